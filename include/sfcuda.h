@@ -1,0 +1,138 @@
+/*
+ * sfcuda.h — C ABI of the ShapeForge B200 (sm_100a) execution backend.
+ *
+ * This is the native boundary the harness binds with ctypes (the B200 counterpart of the
+ * reference's Metal batch encoder, tcenv/backends/metal/native_batch.m).  Every entry point
+ * takes plain device pointers, sizes and a CUDA stream handle (cudaStream_t passed as void*),
+ * never allocates or frees memory, and follows the native_batch.m status convention
+ * (native_batch.m:43-46, :150, :191-194):
+ *
+ *     0  SF_OK       the work was enqueued (or completed, for calls that say so)
+ *     2  SF_EINVAL   invalid arguments: nothing was launched
+ *     3  SF_EDEVICE  the CUDA runtime reported an error
+ *
+ * On a non-zero status a NUL-terminated message is written into the caller-owned buffer
+ * `err` of `cap` bytes (may be NULL / 0).  Launches are asynchronous on `stream`; only
+ * sf_run_batch and sf_device_info synchronise.
+ *
+ * Tensor arguments are row-major and contiguous, in the ABI order of the task's OpSpec
+ * `tensors` block (inputs, then outputs).  dtype codes are SF_DTYPE_*.
+ */
+#ifndef SFCUDA_H
+#define SFCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SF_API __attribute__((visibility("default")))
+#else
+#define SF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SF_OK 0
+#define SF_EINVAL 2
+#define SF_EDEVICE 3
+
+#define SF_DTYPE_F16 0
+#define SF_DTYPE_BF16 1
+#define SF_DTYPE_F32 2
+#define SF_DTYPE_I32 3
+
+/* Library version string, e.g. "0.1.0+sm_100a". */
+SF_API const char* sf_version(void);
+
+/*
+ * Device probe: replaces the Metal device probe behind Backend.probe
+ * (tcenv/backends/base.py:223).  Synchronous.  `name` receives the device name.
+ */
+typedef struct sf_device_info {
+    int32_t device;
+    int32_t cc_major;
+    int32_t cc_minor;
+    int32_t sm_count;
+    int64_t global_mem_bytes;
+    int64_t l2_bytes;
+    int32_t max_smem_per_block_optin;
+    int32_t max_threads_per_block;
+    int32_t clock_khz;
+    int32_t mem_clock_khz;
+    int32_t mem_bus_width_bits;
+    char name[128];
+} sf_device_info;
+
+SF_API int sf_device_info_get(int32_t device, sf_device_info* out, char* err, uint64_t cap);
+
+/*
+ * Fill `nbytes` bytes at `dst` with the byte `value` (the guard 0xCD / poison 0xFF / zero
+ * fills of tcenv/track/protocol.py:43-47, 107-143).  Asynchronous on `stream`.
+ */
+SF_API int sf_fill_bytes(void* dst, uint64_t nbytes, int32_t value, void* stream, char* err, uint64_t cap);
+
+/*
+ * Count the bytes in [ptr, ptr+nbytes) that differ from `value` into *count (device
+ * uint64 counter, caller zeroes it).  Used to check guard bands and unwritten poison on the
+ * device instead of copying whole buffers to the host.
+ */
+SF_API int sf_count_mismatch(const void* ptr, uint64_t nbytes, int32_t value, uint64_t* count_dev,
+                      void* stream, char* err, uint64_t cap);
+
+/* ---------------------------------------------------------------------------------------
+ * Task operators.  Each replaces the candidate kernel dispatch of one OpSpec v2 task.
+ * ------------------------------------------------------------------------------------- */
+
+/*
+ * rmsnorm: y[r,:] = x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w   (fp32 accumulation, one
+ * rounding).  tasks/rmsnorm/reference.py:110-115, opspec.json:5.  x,y [rows, hidden], w [hidden].
+ * dtype F16 or BF16.  rows >= 0, hidden >= 1.
+ */
+SF_API int sf_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
+               int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/* ---------------------------------------------------------------------------------------
+ * Generic dispatch + timed batches (the taic_metal_run_batch replacement).
+ * ------------------------------------------------------------------------------------- */
+
+#define SF_OP_RMSNORM 1
+
+typedef struct sf_op_desc {
+    int32_t op;       /* SF_OP_* */
+    int32_t dtype;    /* SF_DTYPE_* of the task's type variable T */
+    int32_t variant;  /* 0 = default dispatch; op-specific forced variant otherwise */
+    int32_t flags;    /* op-specific (e.g. causal) */
+    int64_t dims[8];  /* op-specific sizes, see sf_run_op */
+    double attrs[4];  /* op-specific scalar attributes (eps, scale, ...) */
+} sf_op_desc;
+
+/* Number of tensor arguments op `op` takes (0 for an unknown op). */
+SF_API int32_t sf_op_nargs(int32_t op);
+
+/*
+ * Enqueue one launch of `desc` with tensor pointers `args` (sf_op_nargs(desc->op) entries,
+ * ABI order).  dims/attrs per op:
+ *   SF_OP_RMSNORM   dims = {rows, hidden}          attrs = {eps}       args = {x, w, y}
+ */
+SF_API int sf_run_op(const sf_op_desc* desc, const void* const* args, uint64_t nargs, void* stream,
+              char* err, uint64_t cap);
+
+/*
+ * Timed batch (mirror of taic_metal_run_batch, native_batch.m:128): enqueue `iters`
+ * launches of `desc`, launch i binding argument set (i % nsets) from `args`
+ * ([nsets][nargs] flattened), bracketed by two CUDA events on `stream`; synchronise and
+ * write the elapsed device seconds to *gpu_s.  With use_graph != 0 the `iters` launches are
+ * captured once into a CUDA graph (outside the timed region) and the graph launch is timed,
+ * which removes per-launch CPU overhead for launch-bound shards.
+ */
+SF_API int sf_run_batch(const sf_op_desc* desc, const void* const* args, uint64_t nargs, uint64_t nsets,
+                 uint64_t iters, int32_t use_graph, void* stream, double* gpu_s, char* err,
+                 uint64_t cap);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SFCUDA_H */

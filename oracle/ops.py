@@ -1,0 +1,192 @@
+"""fp64 numpy restatements of the task operators (test infrastructure only).
+
+Every function takes float64 arrays (already widened from the storage dtype) and returns
+float64 results, like the reference's ``reference(inputs, attrs)`` functions, which widen the
+rounded inputs and apply the formula once in fp64.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+def _err():
+    return np.errstate(all="ignore")
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """tasks/rmsnorm/reference.py:110-115: ``x * rsqrt(mean(x*x, -1) + eps) * w``."""
+    with _err():
+        ms = np.mean(x * x, axis=-1, keepdims=True)
+        return x * (1.0 / np.sqrt(ms + eps)) * w
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    """tasks/softmax/reference.py:104-106: row softmax over the last axis (torch.softmax rules:
+    the row max is subtracted first; a NaN or +Inf in a row makes the row NaN, -Inf entries
+    get weight 0, an all -Inf row is NaN)."""
+    with _err():
+        m = np.max(x, axis=-1, keepdims=True)
+        nan_row = np.isnan(x).any(axis=-1, keepdims=True)
+        e = np.exp(x - m)
+        y = e / np.sum(e, axis=-1, keepdims=True)
+        return np.where(nan_row, np.nan, y)
+
+
+def reduction_sum(x: np.ndarray) -> np.ndarray:
+    """tasks/reduction_sum/reference.py:104-106: row sum in fp64."""
+    with _err():
+        return np.sum(x, axis=-1)
+
+
+def reduction_sum_error_scale(x: np.ndarray) -> np.ndarray:
+    """tasks/reduction_sum/reference.py:109-113: per-row ``sum |x|`` over the finite inputs."""
+    fin = np.where(np.isfinite(x), x, 0.0)
+    return np.sum(np.abs(fin), axis=-1)
+
+
+def _sigmoid(x):
+    with _err():
+        return np.where(x >= 0, 1.0 / (1.0 + np.exp(-x)), np.exp(x) / (1.0 + np.exp(x)))
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    """tasks/silu/reference.py:105-108: ``x * sigmoid(x)``."""
+    with _err():
+        return x * _torch_sigmoid(x)
+
+
+def _torch_sigmoid(x):
+    # torch.sigmoid(x) in fp64 is 1 / (1 + exp(-x)); keep that exact form so +-Inf and NaN map
+    # the way the reference's fp64 tensors do (sigmoid(-inf) = 0, sigmoid(inf) = 1).
+    with _err():
+        return 1.0 / (1.0 + np.exp(-x))
+
+
+def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """tasks/swiglu/reference.py:109-113: ``gate * sigmoid(gate) * up``."""
+    with _err():
+        return gate * _torch_sigmoid(gate) * up
+
+
+def rope(x: np.ndarray, base: float) -> np.ndarray:
+    """tasks/rope/reference.py:105-115: rotate-half RoPE over ``[..., S, D]``; the position is
+    the index along S and ``inv_freq = base ** (-arange(D/2) / (D/2))``."""
+    half = x.shape[-1] // 2
+    seq = x.shape[-2]
+    inv_freq = base ** (-np.arange(half, dtype=np.float64) / half)
+    ang = np.arange(seq, dtype=np.float64)[:, None] * inv_freq[None, :]
+    c, s = np.cos(ang), np.sin(ang)
+    x1, x2 = x[..., :half], x[..., half:]
+    with _err():
+        return np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=-1)
+
+
+def gemm_nn(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """tasks/gemm/reference.py:110-114: ``C = A @ B`` with B ``[K, N]`` (computed in fp64; the
+    reference's fp32 product widened to fp64 agrees to fp32 accumulation error)."""
+    with _err():
+        return a @ b
+
+
+def gemm_nt(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """``C = A @ B^T`` with B ``[N, K]``: the pinned NN product applied to ``B^T``."""
+    return gemm_nn(a, b.T)
+
+
+def unpack_pm1_kn(words: np.ndarray) -> np.ndarray:
+    """tasks/bitdelta_gemm/reference.py:108-116: ``[KB, N]`` 32-bit words -> ``[K, N]`` of +-1,
+    bit j of ``words[kb, n]`` is row ``kb*32 + j`` (+1 when set)."""
+    w = np.asarray(words).astype(np.int64) & 0xFFFFFFFF
+    j = np.arange(32, dtype=np.int64).reshape(1, 32, 1)
+    bit = (w[:, None, :] >> j) & 1
+    return (bit.astype(np.float64) * 2 - 1).reshape(-1, w.shape[-1])
+
+
+def bitdelta_gemm(x: np.ndarray, bits: np.ndarray, scale: float) -> np.ndarray:
+    """tasks/bitdelta_gemm/reference.py:127-130: ``y = SCALE * (x @ W)``, W = unpack(bits)."""
+    with _err():
+        return (x @ unpack_pm1_kn(bits)) * scale
+
+
+def unpack_pm1_nk(words: np.ndarray) -> np.ndarray:
+    """``[N, K/32]`` words packed along K -> ``[N, K]`` of +-1 (bit j of ``words[n, kb]`` is
+    column ``kb*32 + j``), the same bit order as :func:`unpack_pm1_kn` transposed."""
+    return unpack_pm1_kn(np.asarray(words).T).T
+
+
+def bitdelta_gemm_base(x: np.ndarray, w_base: np.ndarray, s_words: np.ndarray, alpha: np.ndarray) -> np.ndarray:
+    """``y = x @ (W_base + diag(alpha) S)^T = x @ W_base^T + alpha * (x @ S^T)`` with S in
+    {-1,+1} packed ``[N, K/32]`` along K; alpha scales output column n."""
+    s = unpack_pm1_nk(s_words)
+    with _err():
+        return x @ w_base.T + (x @ s.T) * alpha[None, :]
+
+
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float, causal: bool = False) -> np.ndarray:
+    """tasks/flash_attention/reference.py:113-119: ``softmax(q k^T * scale [+ causal mask]) v``
+    over ``[B, H, S, D]`` (scaled_dot_product_attention semantics; the causal mask keeps key
+    j <= query i)."""
+    with _err():
+        s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+        if causal:
+            sq, sk = s.shape[-2], s.shape[-1]
+            mask = np.tril(np.ones((sq, sk), dtype=bool))
+            s = np.where(mask, s, -np.inf)
+        p = softmax(s)
+        return np.einsum("bhqk,bhkd->bhqd", p, v)
+
+
+def _sigmoid_t(x):
+    with _err():
+        return 1.0 / (1.0 + np.exp(-x))
+
+
+def delta_rule(q: np.ndarray, k: np.ndarray, v: np.ndarray, log_decay: np.ndarray, beta: np.ndarray,
+               state0: np.ndarray, cu_seqlens: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The per-token gated delta-rule core of tasks/varlen_kda/reference.py:352-368.
+
+    Inputs are already prepared: ``q``/``k`` ``[T, H, D]`` (normalised; q carries the scale),
+    ``log_decay`` ``[T, H, Dk]``, ``beta`` ``[T, H]`` (already sigmoided), ``state0``
+    ``[N, H, Dv, Dk]`` (V-first).  Per sequence s and token t:
+    ``S *= exp(ld_t)`` along the key axis; ``r = (v_t - S k_t) * beta_t``; ``S += r (x) k_t``;
+    ``o_t = S q_t``.  Returns ``(output [T, H, Dv], final_state [N, H, Dv, Dk])``.
+    """
+    state = np.array(state0, dtype=np.float64, copy=True)
+    out = np.zeros(v.shape, dtype=np.float64)
+    cu = [int(c) for c in cu_seqlens]
+    with _err():
+        for s in range(len(cu) - 1):
+            st = state[s]
+            for t in range(cu[s], cu[s + 1]):
+                st = st * np.exp(log_decay[t])[:, None, :]
+                r = v[t] - np.einsum("hvk,hk->hv", st, k[t])
+                r = r * beta[t][:, None]
+                st = st + r[:, :, None] * k[t][:, None, :]
+                out[t] = np.einsum("hvk,hk->hv", st, q[t])
+            state[s] = st
+    return out, state
+
+
+def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, lower_bound):
+    """tasks/varlen_kda/reference.py:323-374: q/k L2 normalisation (``rsqrt(sum x^2 + 1e-6)``,
+    q times ``scale``), log-decay ``LOWER_BOUND * sigmoid(exp(A_log) * (g + dt_bias))``,
+    ``sigmoid(beta)``, then :func:`delta_rule` per sequence from ``initial_state``."""
+    heads, dim = q.shape[1], q.shape[2]
+    with _err():
+        qn = q / np.sqrt(np.sum(q * q, axis=-1, keepdims=True) + 1e-6) * float(scale)
+        kn = k / np.sqrt(np.sum(k * k, axis=-1, keepdims=True) + 1e-6)
+        gate = g + np.asarray(dt_bias).reshape(heads, dim)[None]
+        ld = float(lower_bound) * _sigmoid_t(np.exp(np.asarray(a_log))[None, :, None] * gate)
+        b = _sigmoid_t(beta)
+    return delta_rule(qn, kn, v, ld, b, initial_state, cu_seqlens)
+
+
+def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale, state0=None):
+    """Gated variant: q/k already L2-normalised, ``g`` is the fp32 per-channel log-decay used
+    directly, ``beta`` is already sigmoided, the initial state is zero unless given; q is
+    multiplied by ``scale`` (1/sqrt(D)) as in the task op."""
+    n = len(cu_seqlens) - 1
+    heads, dim = q.shape[1], q.shape[2]
+    if state0 is None:
+        state0 = np.zeros((n, heads, v.shape[2], dim), dtype=np.float64)
+    return delta_rule(q * float(scale), k, v, g, beta, state0, cu_seqlens)

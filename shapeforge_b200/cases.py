@@ -1,0 +1,124 @@
+"""Seeded correctness-case input streams of the OpSpec tasks (the harness side of ``gen_inputs``).
+
+The adversarial sampler is the frozen G0 block that every migrated task carries
+(tasks/rmsnorm/reference.py:12-84: ``_sample`` with the normal / wide_range / large / tiny /
+outlier / cancel / const distributions and ``_inject`` planting NaN, +-Inf and -0.0), restated
+here on torch's CPU generator so the same seeds give the same tensors as the task modules on
+the same torch build.  Per-task magnitudes and seed offsets follow each task's reference.py.
+Case seeds follow the harness rule ``seed + 7919 * (case_index + 1)``
+(tcenv/backends/metal/v2_runtime.py:1602); the search seed is 7.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+FLOAT_MAX = {"fp16": 65504.0, "bf16": 3.3895313892515355e38, "fp32": 3.4028234663852886e38}
+TINY_NORMAL = {"fp16": 2.0**-14, "bf16": 2.0**-126, "fp32": 2.0**-126}
+TINY_SUBNORMAL = {"fp16": 2.0**-24, "bf16": 2.0**-133, "fp32": 2.0**-149}
+SPECIALS = (float("nan"), float("inf"), float("-inf"), -0.0)
+IEEE_SEED_STRIDE = 104_729
+CASE_SEED_STRIDE = 7919
+SEARCH_SEED = 7
+
+TORCH_DTYPE = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32, "i32": torch.int32}
+
+
+def case_seed(base_seed: int, case_index: int) -> int:
+    return int(base_seed) + CASE_SEED_STRIDE * (int(case_index) + 1)
+
+
+def generator(seed: int) -> torch.Generator:
+    g = torch.Generator(device="cpu")
+    g.manual_seed(int(seed) & 0x7FFFFFFFFFFFFFFF)
+    return g
+
+
+def sample(case: str, shape, seed: int, dtype: str, *, mag: float = 1.0, large: float | None = None, spike: float = 100.0) -> torch.Tensor:
+    """One adversarial float32 sample (tasks/rmsnorm/reference.py:28-67)."""
+    g = generator(seed)
+    shape = tuple(int(s) for s in shape)
+    dmax = FLOAT_MAX.get(dtype, 3.0e38)
+    if case == "normal":
+        return torch.randn(shape, generator=g) * mag
+    if case == "wide_range":
+        e = torch.rand(shape, generator=g) * 5 - 3
+        s = torch.where(torch.rand(shape, generator=g) < 0.5, -1.0, 1.0)
+        return s * torch.pow(10.0, e) * mag
+    if case == "large":
+        top = large if large is not None else min(dmax * 0.25, 1.0e4)
+        return (torch.rand(shape, generator=g) * 2 - 1) * top
+    if case == "tiny":
+        if dtype == "fp16":
+            lo, hi = TINY_SUBNORMAL["fp16"], TINY_NORMAL["fp16"] * 4
+        else:
+            lo = TINY_NORMAL.get(dtype, 1.2e-38) * 2.0
+            hi = lo * 4096.0
+        e = torch.rand(shape, generator=g) * (math.log10(hi) - math.log10(lo)) + math.log10(lo)
+        s = torch.where(torch.rand(shape, generator=g) < 0.5, -1.0, 1.0)
+        return s * torch.pow(10.0, e)
+    if case == "outlier":
+        x = torch.randn(shape, generator=g) * mag
+        mask = torch.rand(shape, generator=g) < 1e-3
+        return torch.where(mask, x * spike, x)
+    if case == "cancel":
+        x = torch.randn(shape, generator=g) * mag
+        big = (torch.rand(shape, generator=g) * 0.5 + 0.5) * 512.0
+        s = torch.where(torch.rand(shape, generator=g) < 0.5, -1.0, 1.0)
+        v = big * s
+        if shape and shape[-1] % 2 == 0:
+            vv = v.reshape(*shape[:-1], shape[-1] // 2, 2)
+            vv[..., 1] = -vv[..., 0]
+            v = vv.reshape(shape)
+        return x + v
+    if case == "const":
+        return torch.full(shape, 1.0 * mag if mag != 1.0 else 0.75)
+    raise ValueError(f"unknown case {case!r}")
+
+
+def inject(t: torch.Tensor, seed: int, max_n: int | None = None) -> torch.Tensor:
+    """Plant NaN/+Inf/-Inf/-0.0 (tasks/rmsnorm/reference.py:70-84; first and last element always)."""
+    flat = t.reshape(-1).clone()
+    numel = flat.numel()
+    last = t.shape[-1] if t.dim() else 1
+    rows = max(1, numel // max(1, last))
+    n = int(min(256, max(8, 0.1 * rows, numel / 65536), max(1, numel // 4)))
+    if max_n is not None:
+        n = max(2, min(n, max_n))
+    perm = torch.randperm(numel, generator=generator(seed))
+    perm = perm[(perm != 0) & (perm != numel - 1)]
+    pos = torch.cat([torch.tensor([0, numel - 1]), perm[: n - 2]])[:n]
+    kinds = torch.randperm(n, generator=generator(seed + 1)) % len(SPECIALS)
+    flat[pos] = torch.tensor([SPECIALS[int(k)] for k in kinds], dtype=flat.dtype)
+    return flat.reshape(t.shape)
+
+
+def round_to(t: torch.Tensor, dtype: str) -> torch.Tensor:
+    """Round float values to the storage dtype (returned in that dtype)."""
+    return t.to(TORCH_DTYPE[dtype])
+
+
+# ---- per-task streams ------------------------------------------------------------------------
+
+RMSNORM_CASES = ("normal", "wide_range", "large", "tiny", "outlier", "ieee")
+
+
+def rmsnorm_inputs(case: str, seed: int, rows: int, hidden: int, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/rmsnorm/reference.py:97-107 (mag 1, large 300, w = 1 + 0.1 N(0,1) at seed+99)."""
+    base = "normal" if case == "ieee" else case
+    x = sample(base, (rows, hidden), seed, dtype, mag=1.0, large=300.0)
+    w = 1.0 + 0.1 * sample("normal", (hidden,), seed + 99, dtype)
+    if case == "ieee":
+        x = inject(x, seed + IEEE_SEED_STRIDE)
+        w = inject(w, seed + 2 * IEEE_SEED_STRIDE)
+    return {"x": round_to(x, dtype), "w": round_to(w, dtype)}
+
+
+def rmsnorm_bench_inputs(rows: int, hidden: int, dtype: str, seed: int = SEARCH_SEED) -> dict[str, torch.Tensor]:
+    """Timing inputs of the rmsnorm workload: x ~ N(0,1), w ~ U(0.5, 1.5)."""
+    g = generator(seed)
+    x = torch.randn((rows, hidden), generator=g)
+    w = torch.rand((hidden,), generator=g) + 0.5
+    return {"x": round_to(x, dtype), "w": round_to(w, dtype)}

@@ -1,0 +1,91 @@
+// Shared helpers of the sm_100a kernels: status reporting, dtype traits, vector IO.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+
+#include "../../include/sfcuda.h"
+
+namespace sf {
+
+// Write a formatted message into the caller's error buffer (may be NULL/0) and return `code`.
+static inline int fail(int code, char* err, uint64_t cap, const char* fmt, ...) {
+    if (err && cap) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(err, (size_t)cap, fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+
+// Map the last CUDA runtime error (after an asynchronous launch) to SF_EDEVICE.
+static inline int check_launch(const char* what, char* err, uint64_t cap) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        return fail(SF_EDEVICE, err, cap, "%s: %s", what, cudaGetErrorString(e));
+    }
+    return SF_OK;
+}
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+template <typename T> struct Dt;
+template <> struct Dt<__half> {
+    static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Dt<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// 8 x 16-bit values packed in one 128-bit word.
+template <typename T>
+struct alignas(16) Vec8 {
+    T v[8];
+};
+
+template <typename T>
+__device__ __forceinline__ Vec8<T> ld_global_nc_v8(const T* p) {
+    uint4 raw;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
+                 : "l"(p));
+    Vec8<T> out;
+    *reinterpret_cast<uint4*>(&out) = raw;
+    return out;
+}
+
+template <typename T>
+__device__ __forceinline__ void st_global_v8(T* p, const Vec8<T>& v) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(&v);
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(raw.x), "r"(raw.y),
+                 "r"(raw.z), "r"(raw.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace sf
+
+// Per-op launchers (defined in the op's .cu file) used by sf_run_op.
+int sf_rmsnorm_launch(const void* x, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
+                      int32_t dtype, int32_t variant, cudaStream_t stream, char* err, uint64_t cap);

@@ -1,0 +1,69 @@
+"""The C-ABI library loads and exports every symbol ``include/sfcuda.h`` declares (no GPU needed)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from shapeforge_b200 import _native
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols() -> set[str]:
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names |= set(re.findall(r"SF_API\s+[\w\s\*]+?\b(sf_\w+)\s*\(", text))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert {"sf_rmsnorm", "sf_run_op", "sf_run_batch", "sf_device_info_get"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    missing = [n for n in sorted(declared_symbols()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    assert declared_symbols() == set(_native.SIGNATURES)
+
+
+def test_version_string():
+    assert _native.version().endswith("sm_100a")
+
+
+def test_op_table_matches_library():
+    lib = _native.load()
+    for name, op in _native.OPS.items():
+        assert lib.sf_op_nargs(op) > 0, name
+    assert lib.sf_op_nargs(9999) == 0
+
+
+def test_invalid_arguments_are_rejected_without_a_device():
+    """Argument validation happens before any CUDA call: status 2 and a message."""
+    with pytest.raises(_native.SfError) as exc:
+        _native.call("sf_rmsnorm", None, None, None, 4, 0, 1e-6, 0, None)
+    assert exc.value.code == _native.SF_EINVAL
+    assert "hidden" in exc.value.message
+    with pytest.raises(_native.SfError) as exc:
+        _native.call("sf_rmsnorm", 16, 16, 16, 4, 8, 1e-6, 7, None)
+    assert exc.value.code == _native.SF_EINVAL
+    d = _native.op_desc("rmsnorm", "fp16", dims=(4, 8), attrs=(1e-6,))
+    with pytest.raises(_native.SfError) as exc:
+        _native.run_op(d, [16, 16], 0)
+    assert exc.value.code == _native.SF_EINVAL
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    monkeypatch.setattr(_native, "LIB_PATH", tmp_path / "nope.so")
+    monkeypatch.setattr(_native, "_lib", None)
+    with pytest.raises(_native.NativeUnavailable):
+        _native.load()
