@@ -93,11 +93,41 @@ SF_API int sf_count_mismatch(const void* ptr, uint64_t nbytes, int32_t value, ui
 SF_API int sf_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
                int32_t dtype, void* stream, char* err, uint64_t cap);
 
+/*
+ * gemm_nt: C[M,N] = A[M,K] . B[N,K]^T, fp16 or bf16 in, fp32 accumulation, one rounding
+ * (the dense-gemm workload; the oracle is tasks/gemm/reference.py:110-114 applied to B^T).
+ * tcgen05/TMEM/TMA kernel when the bases are 16-byte aligned and K % 8 == 0, else the general
+ * fallback kernel.  Any M, N, K >= 0 (K == 0 writes zeros).
+ */
+SF_API int sf_gemm_nt(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+               void* stream, char* err, uint64_t cap);
+
+/*
+ * gemm_nn: C[M,N] = A[M,K] . B[K,N] — the tasks/gemm contract (reference.py:110-114,
+ * opspec.json:5: B row-major [K,N]).  With a workspace of at least
+ * sf_gemm_nn_workspace_bytes(M,N,K,dtype) bytes (16-byte aligned, caller-owned) B is
+ * transposed into it and the tensor-core kernel runs; with workspace == NULL the general
+ * fallback kernel runs.
+ */
+SF_API uint64_t sf_gemm_nn_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t dtype);
+SF_API int sf_gemm_nn(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+               void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap);
+
+/*
+ * Read and clear the sticky status word of the tcgen05 kernels: code 0 = ok, 1 = a bounded
+ * pipeline wait gave up (the launch's output is invalid); `where` names the wait.  Synchronises
+ * `stream`.  Replaces the reference's launch watchdog verdict for device-side stalls
+ * (tcenv/evaluate.py:1029-1051) without trapping the GPU.
+ */
+SF_API int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char* err, uint64_t cap);
+
 /* ---------------------------------------------------------------------------------------
  * Generic dispatch + timed batches (the taic_metal_run_batch replacement).
  * ------------------------------------------------------------------------------------- */
 
 #define SF_OP_RMSNORM 1
+#define SF_OP_GEMM_NT 2
+#define SF_OP_GEMM_NN 3
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -115,6 +145,10 @@ SF_API int32_t sf_op_nargs(int32_t op);
  * Enqueue one launch of `desc` with tensor pointers `args` (sf_op_nargs(desc->op) entries,
  * ABI order).  dims/attrs per op:
  *   SF_OP_RMSNORM   dims = {rows, hidden}          attrs = {eps}       args = {x, w, y}
+ *   SF_OP_GEMM_NT   dims = {M, N, K}                                   args = {A, B, C}
+ *   SF_OP_GEMM_NN   dims = {M, N, K, ws_bytes}                         args = {A, B, C, ws}
+ * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
+ * vectorised) kernel, 2 = force the general fallback kernel.
  */
 SF_API int sf_run_op(const sf_op_desc* desc, const void* const* args, uint64_t nargs, void* stream,
               char* err, uint64_t cap);

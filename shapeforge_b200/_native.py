@@ -67,6 +67,8 @@ class SfOpDesc(ctypes.Structure):
 # Operator ids (SF_OP_* in include/sfcuda.h).
 OPS = {
     "rmsnorm": 1,
+    "gemm_nt": 2,
+    "gemm_nn": 3,
 }
 
 _P = ctypes.c_void_p
@@ -83,6 +85,10 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_fill_bytes": (ctypes.c_int, (_P, _U64, _I32, _P, *_ERR)),
     "sf_count_mismatch": (ctypes.c_int, (_P, _U64, _I32, _P, _P, *_ERR)),
     "sf_rmsnorm": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _F32, _I32, _P, *_ERR)),
+    "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
+    "sf_gemm_nn_workspace_bytes": (_U64, (_I64, _I64, _I64, _I32)),
+    "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),
+    "sf_kernel_status": (ctypes.c_int, (ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), _P, *_ERR)),
     "sf_op_nargs": (ctypes.c_int32, (_I32,)),
     "sf_run_op": (ctypes.c_int, (ctypes.POINTER(SfOpDesc), ctypes.POINTER(_P), _U64, _P, *_ERR)),
     "sf_run_batch": (
@@ -183,6 +189,14 @@ def device_info(device: int = 0) -> dict:
     out = {name: getattr(info, name) for name, _ in SfDeviceInfo._fields_}
     out["name"] = info.name.decode(errors="replace")
     return out
+
+
+def kernel_status(stream: int = 0) -> tuple[int, int]:
+    """Read and clear the sticky status word of the tensor-core kernels: (code, where)."""
+    code = ctypes.c_uint32(0)
+    where = ctypes.c_uint32(0)
+    call("sf_kernel_status", ctypes.byref(code), ctypes.byref(where), ctypes.c_void_p(stream))
+    return int(code.value), int(where.value)
 
 
 def version() -> str:

@@ -82,6 +82,8 @@ def inject(t: torch.Tensor, seed: int, max_n: int | None = None) -> torch.Tensor
     """Plant NaN/+Inf/-Inf/-0.0 (tasks/rmsnorm/reference.py:70-84; first and last element always)."""
     flat = t.reshape(-1).clone()
     numel = flat.numel()
+    if numel == 0:
+        return flat.reshape(t.shape)
     last = t.shape[-1] if t.dim() else 1
     rows = max(1, numel // max(1, last))
     n = int(min(256, max(8, 0.1 * rows, numel / 65536), max(1, numel // 4)))
@@ -122,3 +124,27 @@ def rmsnorm_bench_inputs(rows: int, hidden: int, dtype: str, seed: int = SEARCH_
     x = torch.randn((rows, hidden), generator=g)
     w = torch.rand((hidden,), generator=g) + 0.5
     return {"x": round_to(x, dtype), "w": round_to(w, dtype)}
+
+
+GEMM_CASES = ("normal", "wide_range", "large", "tiny", "outlier", "ieee")
+
+
+def gemm_inputs(case: str, seed: int, a_shape, b_shape, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/gemm/reference.py:86-107: A at seed+0, B at seed+31; mags normal 1 / wide_range
+    0.1, large 20, spike 5; the ieee case injects specials into both operands."""
+    base = "normal" if case == "ieee" else case
+    mag = {"normal": 1.0, "wide_range": 0.1}.get(base, 1.0)
+    a = sample(base, a_shape, seed, dtype, mag=mag, large=20.0, spike=5.0)
+    b = sample(base, b_shape, seed + 31, dtype, mag=mag, large=20.0, spike=5.0)
+    if case == "ieee":
+        a = inject(a, seed + IEEE_SEED_STRIDE)
+        b = inject(b, seed + 2 * IEEE_SEED_STRIDE)
+    return {"A": round_to(a, dtype), "B": round_to(b, dtype)}
+
+
+def gemm_bench_inputs(m: int, n: int, k: int, dtype: str, seed: int = SEARCH_SEED) -> dict[str, torch.Tensor]:
+    """Timing inputs of the dense-gemm workload: A [M,K], B [N,K], both U(-1, 1)."""
+    g = generator(seed)
+    a = torch.rand((m, k), generator=g) * 2 - 1
+    b = torch.rand((n, k), generator=g) * 2 - 1
+    return {"A": round_to(a, dtype), "B": round_to(b, dtype)}

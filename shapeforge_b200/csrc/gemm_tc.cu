@@ -1,0 +1,336 @@
+// Dense GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   C[M,N] = A[M,K] . B[N,K]^T      (both operands K-major; fp16 or bf16 in, fp32 accumulate,
+//                                    one rounding to the input dtype at the output)
+//
+// This is the gemm_nt workload (BASELINE config "dense gemm", C = A.B^T); the reference task
+// tasks/gemm (B stored [K,N]) reaches it after a transpose of B (gemm_nn.cu).
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 KB of pipeline shared memory):
+//   warp 0      TMA producer: 128x64 A box + 256x64 B box per K-block, 128-byte swizzle,
+//               into a 4-stage ring of shared memory guarded by full/empty mbarriers;
+//   warp 1      MMA issuer: one thread issues 4 x tcgen05.mma (M=128, N=256, K=16) per
+//               K-block into a TMEM accumulator, tcgen05.commit releases the smem stage;
+//   warps 2..5  epilogue: tcgen05.ld of the 128x256 fp32 accumulator (each warp its 32-lane
+//               TMEM quadrant), convert, 16-byte stores to C.
+// The TMEM accumulator is double-buffered (2 x 256 columns), so the epilogue of tile i
+// overlaps the main loop of tile i+1.  Every mbarrier wait is bounded (sm100::mbar_wait):
+// a wait that gives up records a status word and the CTA drains to its teardown.
+#include "sf_common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+// Status word of the tcgen05 kernels in this file: a bounded wait that gave up records where.
+// Sticky until read by sf_gemm_status_read (a module global: the library allocates nothing).
+__device__ sm100::KernelStatus g_gemm_status;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;  // 64 x 16-bit = 128 bytes: one swizzle row
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
+
+struct __align__(8) Barriers {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t acc_full[NUM_ACC];
+    uint64_t acc_empty[NUM_ACC];
+    uint32_t tmem_base;
+};
+
+// Grouped rasterisation: tiles are visited in column-major groups of GROUP_M tile rows so
+// concurrently running CTAs share A and B panels in L2.
+constexpr int GROUP_M = 8;
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+    const int per_group = GROUP_M * tiles_n;
+    const int group = tile / per_group;
+    const int first_m = group * GROUP_M;
+    const int rows = min(tiles_m - first_m, GROUP_M);
+    const int in_group = tile - group * per_group;
+    tm = first_m + in_group % rows;
+    tn = in_group / rows;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_nt_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      T* __restrict__ C, int M, int N, int K, sm100::KernelStatus* status) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the 128-byte swizzle atoms.
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tiles_m = (M + BM - 1) / BM;
+    const int tiles_n = (N + BN - 1) / BN;
+    const int num_tiles = tiles_m * tiles_n;
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            sm100::mbar_init(&bars->full[s], 1);
+            sm100::mbar_init(&bars->empty[s], 1);
+        }
+        for (int a = 0; a < NUM_ACC; ++a) {
+            sm100::mbar_init(&bars->acc_full[a], 1);
+            sm100::mbar_init(&bars->acc_empty[a], 4 * 32);
+        }
+        sm100::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        sm100::tma_prefetch_desc(&tmap_a);
+        sm100::tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                int tm, tn;
+                tile_coords(tile, tiles_m, tiles_n, tm, tn);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!sm100::mbar_wait(&bars->empty[stage], phase ^ 1u, status, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * STAGE_BYTES;
+                    uint8_t* sb = sa + A_BYTES;
+                    sm100::mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
+                    sm100::tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * BK, tm * BM);
+                    sm100::tma_load_2d(sb, &tmap_b, &bars->full[stage], kb * BK, tn * BN);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: wait (bounded) until the MMA warp has released every stage, so no TMA
+            // write into shared memory is still in flight at teardown.
+            for (int s = 0; s < STAGES && ok; ++s) {
+                if (!sm100::mbar_wait(&bars->empty[stage], phase ^ 1u, status, 2)) break;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = sm100::idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                if (!sm100::mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, status, 3)) break;
+                sm100::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!sm100::mbar_wait(&bars->full[stage], phase, status, 4)) {
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    const uint32_t sa = sm100::smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint64_t ad = sm100::smem_desc_k_sw128(sa + k * 32);
+                        const uint64_t bd = sm100::smem_desc_k_sw128(sb + k * 32);
+                        sm100::mma_f16(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    sm100::mma_commit(&bars->empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                sm100::mma_commit(&bars->acc_full[acc]);
+                if (++acc == NUM_ACC) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row_in_tile = quad * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        const bool vec_ok = (N % 8) == 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            int tm, tn;
+            tile_coords(tile, tiles_m, tiles_n, tm, tn);
+            if (!sm100::mbar_wait(&bars->acc_full[acc], acc_phase, status, 5)) break;
+            sm100::tc_fence_after();
+            const int row = tm * BM + row_in_tile;
+            const uint32_t t_base = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(t_base + (uint32_t)c, r);
+                sm100::tmem_ld_wait();
+                const int col0 = tn * BN + c;
+                if (row < M) {
+                    T* dst = C + (size_t)row * (size_t)N + col0;
+                    if (vec_ok && col0 + 32 <= N) {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) p[j] = pack2<T>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) d4[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j < N) dst[j] = sf::Dt<T>::from_f(__uint_as_float(r[j]));
+                        }
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&bars->acc_empty[acc]);
+            if (++acc == NUM_ACC) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---- host side ----------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        }
+    });
+    return fn;
+}
+
+// Row-major [rows, K] 16-bit matrix, box = box_rows x 64 elements, 128-byte swizzle.
+int make_kmajor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows, bool bf16, char* err,
+                    uint64_t cap) {
+    auto fn = encode_fn();
+    if (!fn) return sf::fail(SF_EDEVICE, err, cap, "cuTensorMapEncodeTiled is unavailable from the driver");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return sf::fail(SF_EINVAL, err, cap, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SF_OK;
+}
+
+template <typename T>
+int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream, char* err,
+              uint64_t cap) {
+    const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+    CUtensorMap ma, mb;
+    int rc = make_kmajor_map(&ma, A, M, K, BM, bf16, err, cap);
+    if (rc) return rc;
+    rc = make_kmajor_map(&mb, B, N, K, BN, bf16, err, cap);
+    if (rc) return rc;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    sm100::KernelStatus* st = nullptr;
+    if (cudaGetSymbolAddress((void**)&st, g_gemm_status) != cudaSuccess || !st)
+        return sf::fail(SF_EDEVICE, err, cap, "gemm: cannot resolve the status word");
+    static bool attr_set[64] = {false};
+    if (dev < 0 || dev >= 64) return sf::fail(SF_EDEVICE, err, cap, "gemm: device index %d out of range", dev);
+    if (!attr_set[dev]) {
+        cudaFuncSetAttribute(gemm_nt_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        attr_set[dev] = true;
+    }
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = (int)std::min<int64_t>(tiles, sf::sm_count());
+    gemm_nt_tc_kernel<T><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, (T*)C, (int)M, (int)N, (int)K, st);
+    return sf::check_launch("gemm_nt tcgen05 launch", err, cap);
+}
+
+}  // namespace
+
+// True when the tcgen05/TMA path can run this problem: 16-byte aligned bases, K % 8 == 0 (TMA
+// row strides are multiples of 16 bytes) and sizes within the 32-bit coordinate range.
+bool sf_gemm_nt_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K) {
+    return sf::aligned16(A) && sf::aligned16(B) && sf::aligned16(C) && (K % 8) == 0 && M > 0 && N > 0 && K > 0 &&
+           M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31);
+}
+
+int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+                         cudaStream_t stream, char* err, uint64_t cap) {
+    if (dtype == SF_DTYPE_F16) return launch_tc<__half>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_BF16) return launch_tc<__nv_bfloat16>(A, B, C, M, N, K, stream, err, cap);
+    return sf::fail(SF_EINVAL, err, cap, "gemm: dtype %d is not fp16/bf16", dtype);
+}
+
+// Read (and clear) the device status word of the tcgen05 kernels on the current device.
+int sf_gemm_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream) {
+    sm100::KernelStatus h{0, 0};
+    if (cudaMemcpyFromSymbolAsync(&h, g_gemm_status, sizeof(h), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+        return SF_EDEVICE;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return SF_EDEVICE;
+    if (h.code) {
+        const sm100::KernelStatus zero{0, 0};
+        cudaMemcpyToSymbolAsync(g_gemm_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream);
+        cudaStreamSynchronize(stream);
+    }
+    *code = h.code;
+    *where = h.where;
+    return SF_OK;
+}

@@ -89,3 +89,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // Per-op launchers (defined in the op's .cu file) used by sf_run_op.
 int sf_rmsnorm_launch(const void* x, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
                       int32_t dtype, int32_t variant, cudaStream_t stream, char* err, uint64_t cap);
+int sf_gemm_nt_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
+                      cudaStream_t s, char* err, uint64_t cap);
+int sf_gemm_nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
+                      void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap);

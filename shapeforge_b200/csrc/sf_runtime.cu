@@ -107,6 +107,8 @@ extern "C" int sf_count_mismatch(const void* ptr, uint64_t nbytes, int32_t value
 extern "C" int32_t sf_op_nargs(int32_t op) {
     switch (op) {
         case SF_OP_RMSNORM: return 3;
+        case SF_OP_GEMM_NT: return 3;
+        case SF_OP_GEMM_NN: return 4;
         default: return 0;
     }
 }
@@ -116,6 +118,11 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
         case SF_OP_RMSNORM:
             return sf_rmsnorm_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], (float)d->attrs[0], d->dtype,
                                      d->variant, s, err, cap);
+        case SF_OP_GEMM_NT:
+            return sf_gemm_nt_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dims[2], d->dtype, d->variant, s, err, cap);
+        case SF_OP_GEMM_NN:
+            return sf_gemm_nn_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dims[2], d->dtype, d->variant, (void*)a[3],
+                                     (uint64_t)d->dims[3], s, err, cap);
         default:
             return sf::fail(SF_EINVAL, err, cap, "unknown op %d", d->op);
     }

@@ -60,3 +60,55 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tens
         _stream(x),
     )
     return out
+
+
+def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``C = A @ B^T`` with A ``[M, K]`` and B ``[N, K]`` (fp32 accumulation, one rounding)."""
+    _check(a, "A")
+    _check(b, "B", a.dtype)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError(f"gemm_nt needs A [M,K] and B [N,K], got {tuple(a.shape)} and {tuple(b.shape)}")
+    m, k = a.shape
+    n = b.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=a.dtype, device=a.device)
+    _check(out, "out", a.dtype)
+    desc = _native.op_desc("gemm_nt", dtype_name(a), dims=(m, n, k), variant=variant)
+    _native.run_op(desc, [a.data_ptr(), b.data_ptr(), out.data_ptr()], _stream(a))
+    return out
+
+
+def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+            variant: int = 0) -> torch.Tensor:
+    """``C = A @ B`` with A ``[M, K]`` and B ``[K, N]`` (tasks/gemm/reference.py:110-114).
+
+    ``workspace`` (uint8, at least ``gemm_nn_workspace_bytes``) lets the tensor-core kernel run on
+    a transposed copy of B; it is allocated here when not given.  Pass ``variant=2`` to force the
+    general kernel without a workspace."""
+    _check(a, "A")
+    _check(b, "B", a.dtype)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"gemm_nn needs A [M,K] and B [K,N], got {tuple(a.shape)} and {tuple(b.shape)}")
+    m, k = a.shape
+    n = b.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=a.dtype, device=a.device)
+    _check(out, "out", a.dtype)
+    need = gemm_nn_workspace_bytes(m, n, k, dtype_name(a))
+    if workspace is None and variant != 2 and need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
+    ws_ptr = workspace.data_ptr() if workspace is not None else 0
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    desc = _native.op_desc("gemm_nn", dtype_name(a), dims=(m, n, k, ws_bytes), variant=variant)
+    _native.run_op(desc, [a.data_ptr(), b.data_ptr(), out.data_ptr(), ws_ptr], _stream(a))
+    return out
+
+
+def gemm_nn_workspace_bytes(m: int, n: int, k: int, dtype: str) -> int:
+    return int(_native.load().sf_gemm_nn_workspace_bytes(m, n, k, _native.DTYPE_CODES[dtype]))
+
+
+def kernel_status(device: torch.device | None = None) -> tuple[int, int]:
+    """Read and clear the tensor-core kernels' status word (synchronises the current stream)."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    return _native.kernel_status(stream)
