@@ -1,0 +1,546 @@
+"""Benchmark of the ShapeForge B200 backend's hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A *step* is one evaluation of the workload's shard: one launch of the task operator over one
+set of synthetic inputs resident in HBM.  Inputs rotate over several sets whose total size is
+larger than the 126 MB L2, so every timed launch reads its operands from HBM (the reference's
+``fresh_rotation`` discipline, tcenv/track/protocol.py:230).  Timing: W untimed warm-up steps,
+then exactly K steps between a barrier + synchronize on both sides, CUDA events on the
+launching stream, max over ranks.
+
+The default workload is the dense-gemm configuration: C = A . B^T with A, B fp16
+[4096, 4096] ~ U(-1, 1), fp32 accumulation, fp16 output.  Other workloads (``--workload``)
+cover the remaining task operators for per-shard reports.
+
+``--impl reference`` times the reference's CPU algorithm for the same workload (the oracle
+port in ``oracle/``, which restates the task's ``reference.py``) on the host cores; under
+torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Callable
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "per-shard latency and % roofline (HBM GB/s or TC TFLOPS) per OpSpec task"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except (OSError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---- clocks ---------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML in a background thread."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000002: "applications_clocks_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # NVML absent (CPU box): no clock record
+            self._nvml = None
+
+    def _sample(self):
+        nv = self._nvml
+        try:
+            mhz = int(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+            reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            self.samples.append((mhz, reasons))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+            self._sample()
+
+    def summary(self) -> dict | None:
+        if self._nvml is None or not self.samples:
+            return None
+        mhz = [s[0] for s in self.samples]
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        reasons = sorted(name for bit, name in self.REASONS.items() if seen & bit)
+        return {"sm_mhz": float(statistics.median(mhz)), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(mhz)}
+
+
+# ---- workloads ------------------------------------------------------------------------------
+
+
+@dataclass
+class Workload:
+    name: str
+    unit: str  # "TFLOP/s" or "GB/s"
+    bound: str  # "tensor" or "hbm"
+    dtype: str
+    units_per_step: float  # algorithmic flops or bytes of one launch
+    config: dict
+    kernel: str  # dominant kernel name (ncu)
+    make_sets: Callable  # (device, nsets) -> list of (tensors tuple, pointer list)
+    desc: Callable  # () -> sf_op_desc
+    host_inputs: Callable  # () -> (list of pinned host input tensors, list of output shapes/dtypes)
+    e2e_step: Callable  # (host inputs, device inputs, device outputs, host outputs) -> None
+    cpu_rows: Callable  # (rows) -> (callable running the oracle on a row sample, units of that call, description)
+    total_rows: int  # rows of the full shard (the sample is a row subset; rows are independent)
+    nsets: int = 4
+    launches_per_step: int = 1
+
+
+def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
+    import numpy as np
+    import torch
+
+    from shapeforge_b200 import _native, cases
+
+    td = cases.TORCH_DTYPE[dtype]
+    per_set = 2 * (m * k + n * k + m * n)
+    nsets = max(2, int(np.ceil(2 * L2_BYTES / per_set)))
+    flops = 2.0 * m * n * k
+
+    def make_sets(dev, count):
+        out = []
+        for s in range(count):
+            inp = cases.gemm_bench_inputs(m, n, k, dtype, seed=cases.SEARCH_SEED + s)
+            a, b = inp["A"].to(dev), inp["B"].to(dev)
+            c = torch.empty((m, n), dtype=td, device=dev)
+            out.append(((a, b, c), [a.data_ptr(), b.data_ptr(), c.data_ptr()]))
+        return out
+
+    def desc():
+        return _native.op_desc("gemm_nt", dtype, dims=(m, n, k))
+
+    def host_inputs():
+        inp = cases.gemm_bench_inputs(m, n, k, dtype, seed=cases.SEARCH_SEED)
+        return [inp["A"].pin_memory(), inp["B"].pin_memory()], [((m, n), td)]
+
+    def e2e_step(h_in, d_in, d_out, h_out, stream):
+        d_in[0].copy_(h_in[0], non_blocking=True)
+        d_in[1].copy_(h_in[1], non_blocking=True)
+        _native.call("sf_gemm_nt", d_in[0].data_ptr(), d_in[1].data_ptr(), d_out[0].data_ptr(), m, n, k,
+                     _native.DTYPE_CODES[dtype], stream)
+        h_out[0].copy_(d_out[0], non_blocking=True)
+
+    def cpu_rows(rows):
+        # The reference's algorithm (tasks/gemm/reference.py:110-114: an fp32 product) through
+        # the oracle port, on a row sample of the same workload (output rows are independent).
+        from oracle import ops as oref
+
+        inp = cases.gemm_bench_inputs(rows, n, k, dtype, seed=cases.SEARCH_SEED)
+        a = inp["A"].float().numpy()
+        b = inp["B"].float().numpy()
+        return (lambda: oref.gemm_nt(a, b)), 2.0 * rows * n * k, f"fp32 A[{rows},{k}] . B[{n},{k}]^T (row sample)"
+
+    return Workload(
+        name=f"gemm_nt_{m}x{n}x{k}",
+        unit="TFLOP/s",
+        bound="tensor",
+        dtype=dtype,
+        units_per_step=flops,
+        config={
+            "workload": f"dense gemm C=A.B^T, A {dtype} [{m},{k}], B {dtype} [{n},{k}], fp32 accumulate, {dtype} out",
+            "shape": [m, n, k],
+            "inputs": "U(-1,1), seed 7",
+            "l2": f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB",
+        },
+        kernel="gemm_nt_tc_kernel",
+        make_sets=make_sets,
+        desc=desc,
+        host_inputs=host_inputs,
+        e2e_step=e2e_step,
+        cpu_rows=cpu_rows,
+        total_rows=m,
+        nsets=nsets,
+    )
+
+
+def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
+    import numpy as np
+    import torch
+
+    from shapeforge_b200 import _native, cases
+
+    td = cases.TORCH_DTYPE[dtype]
+    nbytes = 4.0 * rows * hidden + 2.0 * hidden
+    per_set = nbytes
+    nsets = max(2, int(np.ceil(2 * L2_BYTES / per_set)))
+
+    def make_sets(dev, count):
+        out = []
+        for s in range(count):
+            inp = cases.rmsnorm_bench_inputs(rows, hidden, dtype, seed=cases.SEARCH_SEED + s)
+            x, w = inp["x"].to(dev), inp["w"].to(dev)
+            y = torch.empty_like(x)
+            out.append(((x, w, y), [x.data_ptr(), w.data_ptr(), y.data_ptr()]))
+        return out
+
+    def desc():
+        return _native.op_desc("rmsnorm", dtype, dims=(rows, hidden), attrs=(1e-6,))
+
+    def host_inputs():
+        inp = cases.rmsnorm_bench_inputs(rows, hidden, dtype)
+        return [inp["x"].pin_memory(), inp["w"].pin_memory()], [((rows, hidden), td)]
+
+    def e2e_step(h_in, d_in, d_out, h_out, stream):
+        d_in[0].copy_(h_in[0], non_blocking=True)
+        d_in[1].copy_(h_in[1], non_blocking=True)
+        _native.call("sf_rmsnorm", d_in[0].data_ptr(), d_in[1].data_ptr(), d_out[0].data_ptr(), rows, hidden, 1e-6,
+                     _native.DTYPE_CODES[dtype], stream)
+        h_out[0].copy_(d_out[0], non_blocking=True)
+
+    def cpu_rows(r):
+        from oracle import ops as oref
+
+        inp = cases.rmsnorm_bench_inputs(r, hidden, dtype)
+        x = inp["x"].double().numpy()
+        w = inp["w"].double().numpy()
+        return (lambda: oref.rmsnorm(x, w, 1e-6)), 4.0 * r * hidden + 2.0 * hidden, f"fp64 oracle on [{r},{hidden}] (row sample)"
+
+    return Workload(
+        name=f"rmsnorm_{rows}x{hidden}",
+        unit="GB/s",
+        bound="hbm",
+        dtype=dtype,
+        units_per_step=nbytes,
+        config={
+            "workload": f"rmsnorm x {dtype} [{rows},{hidden}] ~ N(0,1), w U(0.5,1.5), eps 1e-6, fp32 accumulate",
+            "shape": [rows, hidden],
+            "l2": f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB",
+        },
+        kernel="rmsnorm_vec_kernel",
+        make_sets=make_sets,
+        desc=desc,
+        host_inputs=host_inputs,
+        e2e_step=e2e_step,
+        cpu_rows=cpu_rows,
+        total_rows=rows,
+        nsets=nsets,
+    )
+
+
+WORKLOADS = {
+    "gemm_nt_4096": lambda: _gemm_nt_workload(4096, 4096, 4096),
+    "gemm_nt_8192": lambda: _gemm_nt_workload(8192, 8192, 8192),
+    "gemm_nt_512": lambda: _gemm_nt_workload(512, 512, 512),
+    "gemm_nt_4095": lambda: _gemm_nt_workload(4095, 4096, 4096),
+    "rmsnorm_4096x4096": lambda: _rmsnorm_workload(4096, 4096),
+    "rmsnorm_4096x1024": lambda: _rmsnorm_workload(4096, 1024),
+    "rmsnorm_4096x8192": lambda: _rmsnorm_workload(4096, 8192),
+    "rmsnorm_4093x4096": lambda: _rmsnorm_workload(4093, 4096),
+}
+DEFAULT_WORKLOAD = "gemm_nt_4096"
+
+
+# ---- helpers --------------------------------------------------------------------------------
+
+
+def _threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        info = threadpool_info()
+        blas = [i for i in info if i.get("user_api") == "blas"]
+        if blas:
+            return int(blas[0].get("num_threads") or os.cpu_count() or 1)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def _sample_rows(wl: Workload, seconds: float) -> int:
+    """Rows of a CPU sample that takes about ``seconds`` (calibrated on a small sample)."""
+    probe = max(1, min(wl.total_rows, 32))
+    fn, _, _ = wl.cpu_rows(probe)
+    fn()
+    t0 = time.perf_counter()
+    fn()
+    per_row = max((time.perf_counter() - t0) / probe, 1e-9)
+    rows = int(seconds / per_row)
+    return max(1, min(wl.total_rows, rows))
+
+
+def cpu_baseline(wl: Workload, budget_s: float = 15.0) -> dict:
+    """The oracle port on a bounded row sample of the workload, repeated for about budget_s."""
+    threads = _threads()
+    rows = _sample_rows(wl, min(2.0, budget_s / 4))
+    fn, units, desc = wl.cpu_rows(rows)
+    fn()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    return {"value": units * reps / el / scale, "unit": wl.unit, "cores": threads, "kind": "port",
+            "sample": f"{desc} x{reps} in {el:.1f} s"}
+
+
+def _traffic(kernel: str, workload: str) -> float | None:
+    """Per-launch DRAM traffic recorded from an ncu capture in profiles/ (``traffic_bytes: N``)."""
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        text = p.read_text(errors="replace")
+        if f"kernel: {kernel}" in text and f"workload: {workload}" in text:
+            for line in text.splitlines():
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    try:
+                        return float(line.split(":", 1)[1].strip())
+                    except ValueError:
+                        return None
+    return None
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---- arms -----------------------------------------------------------------------------------
+
+
+def run_reference(args, wl: Workload) -> dict:
+    """Each step runs the oracle port once on a row sample sized so W + K steps take about a minute."""
+    threads = _threads()
+    per_step_s = max(0.005, 60.0 / (args.steps + args.warmup))
+    rows = _sample_rows(wl, per_step_s)
+    fn, units, desc = wl.cpu_rows(rows)
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    el = time.perf_counter() - t0
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    value = units * args.steps / el / scale
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": wl.unit,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": wl.dtype,
+        "data": "synthetic",
+        "config": wl.config,
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
+                         "sample": f"{desc} per step (oracle/ restatement of the task reference.py)"},
+        "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from shapeforge_b200 import _native
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _native.load()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    sets = wl.make_sets(dev, wl.nsets)
+    ptr_sets = [p for _, p in sets]
+    desc = wl.desc()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # Warm-up (untimed): W steps.
+    _native.run_batch(desc, ptr_sets, args.warmup, sptr)
+    torch.cuda.synchronize(dev)
+
+    # Timed: exactly K steps.  sf_run_batch enqueues the K launches from C (set i % nsets for
+    # launch i) between two CUDA events on this stream and synchronises; it returns the events'
+    # elapsed device time.
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        el_s = _native.run_batch(desc, ptr_sets, args.steps, sptr)
+        torch.cuda.synchronize(dev)
+    barrier()
+    code, where = _native.kernel_status(sptr)
+    if code:
+        raise RuntimeError(f"tensor-core kernel status {code} (wait {where}) during the timed region")
+    t = torch.tensor([el_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_s = float(t.item())
+
+    # End to end through the C ABI with host buffers (pinned), copies inside the timed region.
+    h_in, out_specs = wl.host_inputs()
+    d_in = [h.to(dev) for h in h_in]
+    d_out = [torch.empty(shape, dtype=dt, device=dev) for shape, dt in out_specs]
+    h_out = [torch.empty(shape, dtype=dt).pin_memory() for shape, dt in out_specs]
+    e2e_steps = max(1, min(args.steps, 50))
+    for _ in range(2):
+        wl.e2e_step(h_in, d_in, d_out, h_out, sptr)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        wl.e2e_step(h_in, d_in, d_out, h_out, sptr)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_s = torch.tensor([f0.elapsed_time(f1) * 1e-3], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_time = float(e2e_s.item())
+
+    if rank != 0:
+        return None
+
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    value = world * wl.units_per_step * args.steps / max_s / scale
+    per_launch_s = el_s / (args.steps * wl.launches_per_step)
+    achieved = wl.units_per_step / per_launch_s / scale
+    peaks, peak_src = measured_peaks()
+    if wl.bound == "tensor":
+        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    else:
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    e2e_value = world * wl.units_per_step * e2e_steps / e2e_time / scale
+    h2d = sum(h.numel() * h.element_size() for h in h_in)
+    d2h = sum(h.numel() * h.element_size() for h in h_out)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": wl.unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": max_s / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": wl.dtype,
+        "data": "synthetic",
+        "config": dict(wl.config, parallelism=f"replicas x{world}" if world > 1 else "1 GPU"),
+        "roofline": {
+            "bound": wl.bound,
+            "achieved": achieved,
+            "peak": peak,
+            "unit": wl.unit,
+            "frac": achieved / peak,
+            "peak_source": f"{peak_src} ({'bf16_tflops burst' if wl.bound == 'tensor' else 'hbm_gbs'})",
+            "traffic": _traffic(wl.kernel, wl.name),
+            "kernel": wl.kernel,
+        },
+        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "path": "sf_* C ABI, pinned host buffers, H2D + kernel + D2H per step"},
+        "gpu_launches": args.steps * wl.launches_per_step,
+        "clocks": clocks.summary(),
+        "impl": "ours",
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl)
+    return line
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = _dist()
+    wl = WORKLOADS[args.workload]()
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, wl)), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    try:
+        line = run_ours(args, wl, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
