@@ -114,6 +114,21 @@ SF_API int sf_gemm_nn(const void* A, const void* B, void* C, int64_t M, int64_t 
                void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap);
 
 /*
+ * gemm_nn without any device allocation (no counterpart in the reference).  Same result as
+ * sf_gemm_nn with a workspace, for callers that cannot allocate device memory at call time:
+ * code running inside a host callback (where CUDA API calls are forbidden), hosts whose device
+ * memory is fully reserved by another allocator, and certified/real-time hosts that forbid
+ * allocation after start-up.  The transpose scratch is a fixed file-scope device array of
+ * SF_GEMM_NN_NOALLOC_MAX_SCRATCH_BYTES, held on every GPU that loads the library until exit;
+ * problems with K*N*2 bytes above it are rejected with SF_EINVAL.  The first call on a device
+ * resolves the array's address (cudaGetSymbolAddress) — make it before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race; serialise them on one stream.
+ */
+#define SF_GEMM_NN_NOALLOC_MAX_SCRATCH_BYTES (32ull * 1024ull * 1024ull)
+SF_API int sf_gemm_nn_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+               void* stream, char* err, uint64_t cap);
+
+/*
  * Read and clear the sticky status word of the tcgen05 kernels: code 0 = ok, 1 = a bounded
  * pipeline wait gave up (the launch's output is invalid); `where` names the wait.  Synchronises
  * `stream`.  Replaces the reference's launch watchdog verdict for device-side stalls

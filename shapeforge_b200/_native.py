@@ -88,6 +88,7 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_gemm_nn_workspace_bytes": (_U64, (_I64, _I64, _I64, _I32)),
     "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),
+    "sf_gemm_nn_noalloc": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_kernel_status": (ctypes.c_int, (ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), _P, *_ERR)),
     "sf_op_nargs": (ctypes.c_int32, (_I32,)),
     "sf_run_op": (ctypes.c_int, (ctypes.POINTER(SfOpDesc), ctypes.POINTER(_P), _U64, _P, *_ERR)),
