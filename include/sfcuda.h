@@ -94,6 +94,30 @@ SF_API int sf_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64
                int32_t dtype, void* stream, char* err, uint64_t cap);
 
 /*
+ * silu: y = x * sigmoid(x) over n elements (tasks/silu/reference.py:105-108).
+ * swiglu: y = gate * sigmoid(gate) * up (tasks/swiglu/reference.py:109-113).  F16 / BF16.
+ */
+SF_API int sf_silu(const void* x, void* y, int64_t n, int32_t dtype, void* stream, char* err, uint64_t cap);
+SF_API int sf_swiglu(const void* gate, const void* up, void* y, int64_t n, int32_t dtype, void* stream, char* err,
+               uint64_t cap);
+
+/*
+ * softmax over the last axis of x [m, n] (tasks/softmax/reference.py:104-106) and
+ * reduction_sum y[m] = sum_j x[m, j] (tasks/reduction_sum/reference.py:104-106); fp32
+ * accumulation, F16 / BF16 storage.
+ */
+SF_API int sf_softmax(const void* x, void* y, int64_t m, int64_t n, int32_t dtype, void* stream, char* err, uint64_t cap);
+SF_API int sf_reduction_sum(const void* x, void* y, int64_t m, int64_t n, int32_t dtype, void* stream, char* err,
+               uint64_t cap);
+
+/*
+ * rope: rotate-half rotary embedding of x [B, H, S, D] with position = index along S and
+ * inv_freq = base^(-i / (D/2)) (tasks/rope/reference.py:105-115).  D even.  F16 / BF16.
+ */
+SF_API int sf_rope(const void* x, void* y, int64_t B, int64_t H, int64_t S, int64_t D, double base, int32_t dtype,
+               void* stream, char* err, uint64_t cap);
+
+/*
  * gemm_nt: C[M,N] = A[M,K] . B[N,K]^T, fp16 or bf16 in, fp32 accumulation, one rounding
  * (the dense-gemm workload; the oracle is tasks/gemm/reference.py:110-114 applied to B^T).
  * tcgen05/TMEM/TMA kernel when the bases are 16-byte aligned and K % 8 == 0, else the general
@@ -143,6 +167,11 @@ SF_API int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char*
 #define SF_OP_RMSNORM 1
 #define SF_OP_GEMM_NT 2
 #define SF_OP_GEMM_NN 3
+#define SF_OP_SILU 4
+#define SF_OP_SWIGLU 5
+#define SF_OP_SOFTMAX 6
+#define SF_OP_REDUCTION_SUM 7
+#define SF_OP_ROPE 8
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -162,6 +191,11 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_RMSNORM   dims = {rows, hidden}          attrs = {eps}       args = {x, w, y}
  *   SF_OP_GEMM_NT   dims = {M, N, K}                                   args = {A, B, C}
  *   SF_OP_GEMM_NN   dims = {M, N, K, ws_bytes}                         args = {A, B, C, ws}
+ *   SF_OP_SILU      dims = {n}                                         args = {x, y}
+ *   SF_OP_SWIGLU    dims = {n}                                         args = {gate, up, y}
+ *   SF_OP_SOFTMAX   dims = {m, n}                                      args = {x, y}
+ *   SF_OP_REDUCTION_SUM dims = {m, n}                                  args = {x, y}
+ *   SF_OP_ROPE      dims = {B, H, S, D}            attrs = {base}      args = {x, y}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

@@ -69,6 +69,11 @@ OPS = {
     "rmsnorm": 1,
     "gemm_nt": 2,
     "gemm_nn": 3,
+    "silu": 4,
+    "swiglu": 5,
+    "softmax": 6,
+    "reduction_sum": 7,
+    "rope": 8,
 }
 
 _P = ctypes.c_void_p
@@ -85,6 +90,11 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_fill_bytes": (ctypes.c_int, (_P, _U64, _I32, _P, *_ERR)),
     "sf_count_mismatch": (ctypes.c_int, (_P, _U64, _I32, _P, _P, *_ERR)),
     "sf_rmsnorm": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _F32, _I32, _P, *_ERR)),
+    "sf_silu": (ctypes.c_int, (_P, _P, _I64, _I32, _P, *_ERR)),
+    "sf_swiglu": (ctypes.c_int, (_P, _P, _P, _I64, _I32, _P, *_ERR)),
+    "sf_softmax": (ctypes.c_int, (_P, _P, _I64, _I64, _I32, _P, *_ERR)),
+    "sf_reduction_sum": (ctypes.c_int, (_P, _P, _I64, _I64, _I32, _P, *_ERR)),
+    "sf_rope": (ctypes.c_int, (_P, _P, _I64, _I64, _I64, _I64, ctypes.c_double, _I32, _P, *_ERR)),
     "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_gemm_nn_workspace_bytes": (_U64, (_I64, _I64, _I64, _I32)),
     "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),

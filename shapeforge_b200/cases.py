@@ -148,3 +148,41 @@ def gemm_bench_inputs(m: int, n: int, k: int, dtype: str, seed: int = SEARCH_SEE
     a = torch.rand((m, k), generator=g) * 2 - 1
     b = torch.rand((n, k), generator=g) * 2 - 1
     return {"A": round_to(a, dtype), "B": round_to(b, dtype)}
+
+
+# Sampler parameters of the memory-bound tasks: (magnitudes per base case, default magnitude,
+# LARGE, SPIKE) from each task's reference.py (softmax :86-89, reduction_sum :86-89,
+# silu :86-90, swiglu :86-90, rope :88-91).
+MEMBOUND_PARAMS = {
+    "softmax": ({"normal": 2.0}, 1.0, 10000.0, 100.0),
+    "reduction_sum": ({"normal": 1.0, "wide_range": 0.1}, 1.0, 300.0, 100.0),
+    "silu": ({"normal": 3.0}, 1.0, 10000.0, 100.0),
+    "swiglu": ({"normal": 3.0}, 1.0, 200.0, 100.0),
+    "rope": ({"normal": 1.0, "wide_range": 1.0}, 1.0, 40000.0, 100.0),
+}
+MEMBOUND_CASES = {
+    "softmax": ("normal", "wide_range", "large", "tiny", "outlier", "const", "ieee"),
+    "reduction_sum": ("normal", "wide_range", "large", "tiny", "outlier", "cancel", "ieee"),
+    "silu": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
+    "swiglu": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
+    "rope": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
+}
+SWIGLU_UP_SEED_STRIDE = 1000003
+
+
+def membound_inputs(task: str, case: str, seed: int, shape, dtype: str) -> dict[str, torch.Tensor]:
+    """Inputs of softmax / reduction_sum / silu / rope (``x``) and swiglu (``gate``, ``up``)."""
+    mags, default, large, spike = MEMBOUND_PARAMS[task]
+    base = "normal" if case == "ieee" else case
+    mag = mags.get(base, default)
+    if task == "swiglu":
+        gate = sample(base, shape, seed, dtype, mag=mag, large=large, spike=spike)
+        up = sample(base, shape, seed + SWIGLU_UP_SEED_STRIDE, dtype, mag=mag, large=large, spike=spike)
+        if case == "ieee":
+            gate = inject(gate, seed + IEEE_SEED_STRIDE)
+            up = inject(up, seed + 2 * IEEE_SEED_STRIDE)
+        return {"gate": round_to(gate, dtype), "up": round_to(up, dtype)}
+    x = sample(base, shape, seed, dtype, mag=mag, large=large, spike=spike)
+    if case == "ieee":
+        x = inject(x, seed + IEEE_SEED_STRIDE)
+    return {"x": round_to(x, dtype)}

@@ -93,3 +93,12 @@ int sf_gemm_nt_launch(const void* A, const void* B, void* C, int64_t M, int64_t 
                       cudaStream_t s, char* err, uint64_t cap);
 int sf_gemm_nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
                       void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap);
+int sf_silu_launch(const void* x, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err, uint64_t cap);
+int sf_swiglu_launch(const void* gate, const void* up, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s,
+                     char* err, uint64_t cap);
+int sf_softmax_launch(const void* x, void* y, int64_t m, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err,
+                      uint64_t cap);
+int sf_reduction_sum_launch(const void* x, void* y, int64_t m, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s,
+                            char* err, uint64_t cap);
+int sf_rope_launch(const void* x, void* y, int64_t B, int64_t H, int64_t S, int64_t D, double base, int32_t dtype, int32_t variant,
+                   cudaStream_t st, char* err, uint64_t cap);

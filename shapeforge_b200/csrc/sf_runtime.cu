@@ -109,6 +109,11 @@ extern "C" int32_t sf_op_nargs(int32_t op) {
         case SF_OP_RMSNORM: return 3;
         case SF_OP_GEMM_NT: return 3;
         case SF_OP_GEMM_NN: return 4;
+        case SF_OP_SILU: return 2;
+        case SF_OP_SWIGLU: return 3;
+        case SF_OP_SOFTMAX: return 2;
+        case SF_OP_REDUCTION_SUM: return 2;
+        case SF_OP_ROPE: return 2;
         default: return 0;
     }
 }
@@ -123,6 +128,17 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
         case SF_OP_GEMM_NN:
             return sf_gemm_nn_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dims[2], d->dtype, d->variant, (void*)a[3],
                                      (uint64_t)d->dims[3], s, err, cap);
+        case SF_OP_SILU:
+            return sf_silu_launch(a[0], (void*)a[1], d->dims[0], d->dtype, d->variant, s, err, cap);
+        case SF_OP_SWIGLU:
+            return sf_swiglu_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dtype, d->variant, s, err, cap);
+        case SF_OP_SOFTMAX:
+            return sf_softmax_launch(a[0], (void*)a[1], d->dims[0], d->dims[1], d->dtype, d->variant, s, err, cap);
+        case SF_OP_REDUCTION_SUM:
+            return sf_reduction_sum_launch(a[0], (void*)a[1], d->dims[0], d->dims[1], d->dtype, d->variant, s, err, cap);
+        case SF_OP_ROPE:
+            return sf_rope_launch(a[0], (void*)a[1], d->dims[0], d->dims[1], d->dims[2], d->dims[3], d->attrs[0], d->dtype,
+                                  d->variant, s, err, cap);
         default:
             return sf::fail(SF_EINVAL, err, cap, "unknown op %d", d->op);
     }

@@ -112,3 +112,63 @@ def kernel_status(device: torch.device | None = None) -> tuple[int, int]:
     """Read and clear the tensor-core kernels' status word (synchronises the current stream)."""
     stream = torch.cuda.current_stream(device).cuda_stream
     return _native.kernel_status(stream)
+
+
+def _run(op: str, t: torch.Tensor, ptrs, dims=(), attrs=(), variant: int = 0) -> None:
+    desc = _native.op_desc(op, dtype_name(t), dims=dims, attrs=attrs, variant=variant)
+    _native.run_op(desc, ptrs, _stream(t))
+
+
+def silu(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y = x * sigmoid(x)`` (tasks/silu/reference.py:105-108), any shape, element-wise."""
+    _check(x, "x")
+    out = torch.empty_like(x) if out is None else out
+    _check(out, "out", x.dtype)
+    _run("silu", x, [x.data_ptr(), out.data_ptr()], dims=(x.numel(),), variant=variant)
+    return out
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y = gate * sigmoid(gate) * up`` (tasks/swiglu/reference.py:109-113)."""
+    _check(gate, "gate")
+    _check(up, "up", gate.dtype)
+    if up.numel() != gate.numel():
+        raise ValueError("gate and up must have the same number of elements")
+    out = torch.empty_like(gate) if out is None else out
+    _check(out, "out", gate.dtype)
+    _run("swiglu", gate, [gate.data_ptr(), up.data_ptr(), out.data_ptr()], dims=(gate.numel(),), variant=variant)
+    return out
+
+
+def softmax(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """Row softmax over the last axis (tasks/softmax/reference.py:104-106)."""
+    _check(x, "x")
+    n = x.shape[-1]
+    m = x.numel() // max(n, 1)
+    out = torch.empty_like(x) if out is None else out
+    _check(out, "out", x.dtype)
+    _run("softmax", x, [x.data_ptr(), out.data_ptr()], dims=(m, n), variant=variant)
+    return out
+
+
+def reduction_sum(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """Row sum over the last axis (tasks/reduction_sum/reference.py:104-106)."""
+    _check(x, "x")
+    n = x.shape[-1]
+    m = x.numel() // max(n, 1)
+    out = torch.empty(x.shape[:-1], dtype=x.dtype, device=x.device) if out is None else out
+    _check(out, "out", x.dtype)
+    _run("reduction_sum", x, [x.data_ptr(), out.data_ptr()], dims=(m, n), variant=variant)
+    return out
+
+
+def rope(x: torch.Tensor, base: float = 10000.0, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """Rotate-half RoPE over ``[B, H, S, D]`` (tasks/rope/reference.py:105-115)."""
+    _check(x, "x")
+    if x.dim() != 4:
+        raise ValueError("rope expects x [B, H, S, D]")
+    b, h, s, d = x.shape
+    out = torch.empty_like(x) if out is None else out
+    _check(out, "out", x.dtype)
+    _run("rope", x, [x.data_ptr(), out.data_ptr()], dims=(b, h, s, d), attrs=(base,), variant=variant)
+    return out
