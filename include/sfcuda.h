@@ -118,6 +118,22 @@ SF_API int sf_rope(const void* x, void* y, int64_t B, int64_t H, int64_t S, int6
                void* stream, char* err, uint64_t cap);
 
 /*
+ * bitdelta_gemm (tasks/bitdelta_gemm/reference.py:99-130): y[M,N] = scale * x[M,K] . W[K,N]
+ * with W[k,n] = +1 if bit (k % 32) of bits[k/32, n] is set, else -1.  bits is [K/32, N] 32-bit
+ * words; K % 32 == 0.  tcgen05 kernel with the signs expanded in shared memory.
+ */
+SF_API int sf_bitdelta_gemm(const void* x, const void* bits, void* y, int64_t M, int64_t N, int64_t K, float scale,
+               int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
+ * bitdelta_gemm_base (the 1-bit-delta fine-tune workload): y[M,N] = x[M,K] . (W_base[N,K] +
+ * diag(alpha[N]) S[N,K])^T with S in {-1,+1} packed along K as s_words[N, K/32] (bit j of word
+ * kb is column kb*32 + j, set = +1).  Swap-AB tcgen05 kernel, split-K over a cluster.
+ */
+SF_API int sf_bitdelta_gemm_base(const void* x, const void* w_base, const void* s_words, const void* alpha, void* y,
+               int64_t M, int64_t N, int64_t K, int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
  * gemm_nt: C[M,N] = A[M,K] . B[N,K]^T, fp16 or bf16 in, fp32 accumulation, one rounding
  * (the dense-gemm workload; the oracle is tasks/gemm/reference.py:110-114 applied to B^T).
  * tcgen05/TMEM/TMA kernel when the bases are 16-byte aligned and K % 8 == 0, else the general
@@ -172,6 +188,8 @@ SF_API int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char*
 #define SF_OP_SOFTMAX 6
 #define SF_OP_REDUCTION_SUM 7
 #define SF_OP_ROPE 8
+#define SF_OP_BITDELTA 9
+#define SF_OP_BITDELTA_BASE 10
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -196,6 +214,8 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_SOFTMAX   dims = {m, n}                                      args = {x, y}
  *   SF_OP_REDUCTION_SUM dims = {m, n}                                  args = {x, y}
  *   SF_OP_ROPE      dims = {B, H, S, D}            attrs = {base}      args = {x, y}
+ *   SF_OP_BITDELTA  dims = {M, N, K}               attrs = {scale}     args = {x, bits, y}
+ *   SF_OP_BITDELTA_BASE dims = {M, N, K}                               args = {x, w_base, s_words, alpha, y}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

@@ -186,3 +186,50 @@ def membound_inputs(task: str, case: str, seed: int, shape, dtype: str) -> dict[
     if case == "ieee":
         x = inject(x, seed + IEEE_SEED_STRIDE)
     return {"x": round_to(x, dtype)}
+
+
+# ---- bitdelta ---------------------------------------------------------------------------------
+
+BITDELTA_CASES = ("random", "edge_bits", "large", "tiny", "outlier", "ieee")
+BITDELTA_EDGE_WORDS = (0, -1, 1431655765, -1431655766, 1, -2147483648, 252645135, -252645136)
+
+
+def bitdelta_inputs(case: str, seed: int, m: int, n: int, k: int, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/bitdelta_gemm/reference.py:101-124: packed words [K/32, N] (uniform 32-bit, or the
+    edge words for ``edge_bits``) from a generator at ``seed``, x at ``seed + 5`` (mag 1, large 20,
+    spike 5; edge_bits/random sample x as normal); ieee injects x only."""
+    base = "random" if case == "ieee" else case
+    g = torch.Generator().manual_seed(int(seed) & 2147483647)
+    kb = k // 32
+    if base == "edge_bits":
+        edge = torch.tensor(BITDELTA_EDGE_WORDS, dtype=torch.int64)
+        words = edge[torch.randint(0, len(edge), (kb, n), generator=g)]
+    else:
+        words = torch.randint(-(1 << 31), 1 << 31, (kb, n), generator=g, dtype=torch.int64)
+    xcase = {"edge_bits": "normal", "random": "normal"}.get(base, base)
+    x = sample(xcase, (m, k), seed + 5, dtype, mag=1.0, large=20.0, spike=5.0)
+    if case == "ieee":
+        x = inject(x, seed + IEEE_SEED_STRIDE)
+    return {"x": round_to(x, dtype), "bits": words.to(torch.int32)}
+
+
+BITDELTA_BASE_CASES = ("normal", "large", "ieee")
+
+
+def bitdelta_base_inputs(case: str, seed: int, m: int, n: int, k: int, dtype: str) -> dict[str, torch.Tensor]:
+    """The 1-bit-delta workload: x ~ N(0,1) [M,K], W_base ~ N(0, 0.02) [N,K], S ~ Bernoulli(0.5)
+    packed along K into int32 words [N, K/32], alpha ~ U(1e-3, 1e-2) [N].  ``large`` scales x by
+    20; ``ieee`` plants specials in x."""
+    g = generator(seed)
+    x = torch.randn((m, k), generator=g)
+    if case == "large":
+        x = x * 20.0
+    w = torch.randn((n, k), generator=g) * 0.02
+    s_bits = torch.randint(0, 2, (n, k // 32, 32), generator=g, dtype=torch.int64)
+    shifts = torch.arange(32, dtype=torch.int64)
+    words = (s_bits << shifts).sum(-1)
+    words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32)
+    alpha = torch.rand((n,), generator=g) * (1e-2 - 1e-3) + 1e-3
+    if case == "ieee":
+        x = inject(x, seed + IEEE_SEED_STRIDE)
+    return {"x": round_to(x, dtype), "w_base": round_to(w, dtype), "s_words": words, "alpha": round_to(alpha, dtype)}

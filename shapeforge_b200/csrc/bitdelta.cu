@@ -1,0 +1,606 @@
+// BitDelta GEMMs on the tcgen05 tensor cores, sm_100a.  The +-1 sign operand is never stored
+// in HBM: its packed bits are expanded straight into a 128-byte-swizzled K-major shared-memory
+// tile that tcgen05.mma reads like any TMA-loaded operand.
+//
+// Task contract (tasks/bitdelta_gemm/reference.py:99-130, opspec.json:5):
+//   y[M,N] = SCALE * x[M,K] . W[K,N],  W[k,n] = +1 if bit (k % 32) of bits[k/32, n] is set, else -1
+//   -> bitdelta_task_kernel: 128x128 output tiles, A = x (TMA), B = signs expanded from the
+//      [KB, N] words of each K-block, fp32 accumulation in TMEM, SCALE in the epilogue.
+//
+// W_base variant (the 1-bit-delta fine-tune workload):
+//   y[M,N] = x[M,K] . (W_base[N,K] + diag(alpha[N]) S[N,K])^T = x.W_base^T + alpha (x) (x.S^T)
+//   S in {-1,+1} packed along K: bit j of S_words[n, kb] is S[n, kb*32 + j].
+//   -> bitdelta_base_kernel: M <= 128 rows make the op HBM-bound (W_base is 2*N*K bytes read
+//      once), so the product is computed transposed (swap-AB): each CTA owns 128 output columns
+//      n, A = W_base rows (TMA) and A' = S rows (expanded), B = x (TMA, M padded to a multiple of
+//      16 with zero rows), two TMEM accumulators D1 = W_base.x^T and D2 = S.x^T (the +-1 products
+//      are exact in fp32), epilogue p = D1 + alpha[n] * D2.  K is split over the CTAs of a
+//      thread-block cluster (up to 8) so ~all SMs stream W_base; the partials are reduce-scattered
+//      through distributed shared memory (each CTA sums a slice of the M rows of y from every
+//      peer's partial and writes it).  No workspace.
+//
+// Sign expansion uses a 256-entry shared-memory table: one 16-byte lookup per 8 signs.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2..5
+// expand sign bits for every stage and run the epilogue.  Every mbarrier wait is bounded.
+#include "sf_common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+__device__ sm100::KernelStatus g_bitdelta_status;
+
+namespace {
+
+constexpr int BK = 64;
+constexpr int TILE_ROWS = 128;
+constexpr int ROW_TILE_BYTES = TILE_ROWS * BK * 2;  // 16 KB: 128 rows x 128 bytes
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_LIMIT = 227 * 1024;
+// Dynamic shared memory available next to the 4 KB static sign table.
+constexpr int kMaxDynSmem = SMEM_LIMIT - 4096;
+
+struct __align__(8) Bars {
+    uint64_t full_tma[4];
+    uint64_t full_exp[4];
+    uint64_t empty[4];
+    uint64_t acc_full;
+    uint32_t tmem_base;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t minus_one_pair() {
+    return std::is_same<T, __half>::value ? 0xBC00BC00u : 0xBF80BF80u;
+}
+
+// Lookup table: byte value b -> the 8 16-bit values (+1 where bit j of b is set, else -1) of
+// one 16-byte chunk.  Built once per CTA in shared memory.
+template <typename T>
+__device__ __forceinline__ void build_sign_lut(uint4* lut) {
+    const uint32_t base = minus_one_pair<T>();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t b = ((uint32_t)i >> (2 * q)) & 3u;
+            w[q] = base ^ ((b & 1u) << 15) ^ ((b & 2u) << 30);
+        }
+        lut[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// Row r of a K-major 128-byte-swizzled tile (64 16-bit elements per row) from 64 sign bits:
+// element j = +1 if bit j is set, else -1.  Chunk c (elements 8c..8c+7) lives at chunk c ^ (r%8).
+__device__ __forceinline__ void expand_row_sw128(uint8_t* tile, int r, uint64_t bits, const uint4* lut) {
+    uint8_t* row = tile + r * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) * 16)) = lut[(uint32_t)(bits >> (8 * c)) & 0xFFu];
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ------------------------------------------------------------------------------------------------
+// W_base variant (swap-AB, split-K over a cluster)
+// ------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    bitdelta_base_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                         const uint32_t* __restrict__ s_words, const T* __restrict__ alpha, T* __restrict__ y, int M, int N,
+                         int K, int nm, int stages, sm100::KernelStatus* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int x_bytes = nm * 128;
+    const int stage_bytes = 2 * ROW_TILE_BYTES + x_bytes;
+    Bars* bars = reinterpret_cast<Bars*>(smem + stages * stage_bytes);
+    __shared__ uint4 lut[256];
+    build_sign_lut<T>(lut);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * TILE_ROWS;
+    const int sk = gridDim.y;
+    const uint32_t rank = sm100::cluster_ctarank();
+    const int nkb = (K + BK - 1) / BK;
+    const int kb_begin = (int)((int64_t)nkb * rank / sk);
+    const int kb_end = (int)((int64_t)nkb * (rank + 1) / sk);
+    const int kw = K / 32;  // words per S row
+    const uint32_t tmem_cols = (uint32_t)max(32, 1 << (32 - __clz(2 * nm - 1)));
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            sm100::mbar_init(&bars->full_tma[s], 1);
+            sm100::mbar_init(&bars->full_exp[s], 128);
+            sm100::mbar_init(&bars->empty[s], 1);
+        }
+        sm100::mbar_init(&bars->acc_full, 1);
+        sm100::fence_mbar_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&bars->tmem_base, tmem_cols);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            sm100::tma_prefetch_desc(&tmap_w);
+            sm100::tma_prefetch_desc(&tmap_x);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int kb = kb_begin; kb < kb_end; ++kb) {
+                if (!sm100::mbar_wait(&bars->empty[s], ph ^ 1u, status, 11)) break;
+                uint8_t* st = smem + s * stage_bytes;
+                sm100::mbar_arrive_expect_tx(&bars->full_tma[s], ROW_TILE_BYTES + x_bytes);
+                sm100::tma_load_2d(st, &tmap_w, &bars->full_tma[s], kb * BK, n0);
+                sm100::tma_load_2d(st + 2 * ROW_TILE_BYTES, &tmap_x, &bars->full_tma[s], kb * BK, 0);
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && kb_end > kb_begin) {
+            const uint32_t idesc = sm100::idesc_f16(128, (uint32_t)nm, std::is_same<T, __nv_bfloat16>::value);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int kb = kb_begin; kb < kb_end; ++kb) {
+                if (!sm100::mbar_wait(&bars->full_tma[s], ph, status, 12) || !sm100::mbar_wait(&bars->full_exp[s], ph, status, 13)) {
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t sw = sm100::smem_u32(smem + s * stage_bytes);
+                const uint32_t ss = sw + ROW_TILE_BYTES;
+                const uint32_t sx = sw + 2 * ROW_TILE_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) {
+                    const uint64_t bx = sm100::smem_desc_k_sw128(sx + k * 32);
+                    const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
+                    sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sw + k * 32), bx, idesc, acc);
+                    sm100::mma_f16(tmem + (uint32_t)nm, sm100::smem_desc_k_sw128(ss + k * 32), bx, idesc, acc);
+                }
+                sm100::mma_commit(&bars->empty[s]);
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+            if (ok) sm100::mma_commit(&bars->acc_full);
+        }
+    } else {
+        // Sign expansion: thread t owns row t (output column n0 + t) of every S tile.  The sign
+        // words of 16 K-blocks are loaded up front (independent loads, one memory latency per 16
+        // stages instead of one per stage).
+        const int t = threadIdx.x - 64;
+        const int n = n0 + t;
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int kc = kb_begin; kc < kb_end && ok; kc += 16) {
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int w = 2 * (kc + i);
+                const bool live = n < N && kc + i < kb_end;
+                lo[i] = (live && w < kw) ? s_words[(int64_t)n * kw + w] : 0u;
+                hi[i] = (live && w + 1 < kw) ? s_words[(int64_t)n * kw + w + 1] : 0u;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (kc + i >= kb_end) break;
+                if (!sm100::mbar_wait(&bars->empty[s], ph ^ 1u, status, 14)) {
+                    ok = false;
+                    break;
+                }
+                expand_row_sw128(smem + s * stage_bytes + ROW_TILE_BYTES, t, (uint64_t)lo[i] | ((uint64_t)hi[i] << 32), lut);
+                sm100::fence_proxy_async_smem();
+                sm100::mbar_arrive(&bars->full_exp[s]);
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+        }
+    }
+
+    // ---- epilogue: partial p[row][m] = D1 + alpha[n] * D2 into shared memory (the pipeline
+    // buffers are free once acc_full has fired: every MMA reading them has completed).
+    float* red = reinterpret_cast<float*>(smem);
+    if (warp >= 2) {
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const int n = n0 + row;
+        const float a = n < N ? sf::Dt<T>::to_f(alpha[n]) : 0.f;
+        bool have = kb_end > kb_begin;
+        if (have && !sm100::mbar_wait(&bars->acc_full, 0, status, 15)) have = false;
+        sm100::tc_fence_after();
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        for (int c = 0; c < nm; c += 16) {
+            float p[16];
+            if (have) {
+                uint32_t d1[16], d2[16];
+                sm100::tmem_ld_32x32b_x16(lane_base + (uint32_t)c, d1);
+                sm100::tmem_ld_32x32b_x16(lane_base + (uint32_t)(nm + c), d2);
+                sm100::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) p[j] = __uint_as_float(d1[j]) + a * __uint_as_float(d2[j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) p[j] = 0.f;
+            }
+            float4* dst = reinterpret_cast<float4*>(red + (size_t)row * nm + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = make_float4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+        }
+    }
+    __syncthreads();
+    sm100::cluster_sync();  // every CTA's partial is in its shared memory
+    // Reduce-scatter over the cluster: CTA `rank` sums the columns [c0, c1) of all partials
+    // (16-byte loads through distributed shared memory) and writes those rows of y.
+    if (warp >= 2) {
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const int n = n0 + row;
+        const int per = (((M + sk - 1) / sk) + 3) & ~3;
+        const int c0 = (int)rank * per;
+        const int c1 = min(M, c0 + per);
+        if (n < N) {
+            const uint32_t own = sm100::smem_u32(red + (size_t)row * nm);
+            for (int c = c0; c < c1; c += 4) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < sk; ++r) {
+                    const float4 v = sm100::ld_shared_cluster_v4(sm100::mapa_shared(own + 4u * c, (uint32_t)r));
+                    acc.x += v.x;
+                    acc.y += v.y;
+                    acc.z += v.z;
+                    acc.w += v.w;
+                }
+                const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (c + j < c1) y[(int64_t)(c + j) * N + n] = sf::Dt<T>::from_f(o[j]);
+            }
+        }
+    }
+    sm100::cluster_sync();  // every CTA keeps its shared memory until all peers have read it
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, tmem_cols);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Task contract: y = SCALE * x . W, W from bits [KB, N]
+// ------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    bitdelta_task_kernel(const __grid_constant__ CUtensorMap tmap_x, const uint32_t* __restrict__ bits, T* __restrict__ y, int M,
+                         int N, int K, float scale, int stages, sm100::KernelStatus* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int stage_bytes = 2 * ROW_TILE_BYTES;
+    Bars* bars = reinterpret_cast<Bars*>(smem + stages * stage_bytes);
+    __shared__ uint4 lut[256];
+    build_sign_lut<T>(lut);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * TILE_ROWS, n0 = blockIdx.x * TILE_ROWS;
+    const int nkb = (K + BK - 1) / BK;
+    const int kbw = K / 32;  // rows of the bits array
+    constexpr uint32_t TMEM_COLS = 128;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            sm100::mbar_init(&bars->full_tma[s], 1);
+            sm100::mbar_init(&bars->full_exp[s], 128);
+            sm100::mbar_init(&bars->empty[s], 1);
+        }
+        sm100::mbar_init(&bars->acc_full, 1);
+        sm100::fence_mbar_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            sm100::tma_prefetch_desc(&tmap_x);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (!sm100::mbar_wait(&bars->empty[s], ph ^ 1u, status, 21)) break;
+                sm100::mbar_arrive_expect_tx(&bars->full_tma[s], ROW_TILE_BYTES);
+                sm100::tma_load_2d(smem + s * stage_bytes, &tmap_x, &bars->full_tma[s], kb * BK, m0);
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = sm100::idesc_f16(128, 128, std::is_same<T, __nv_bfloat16>::value);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (!sm100::mbar_wait(&bars->full_tma[s], ph, status, 22) || !sm100::mbar_wait(&bars->full_exp[s], ph, status, 23)) {
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t sa = sm100::smem_u32(smem + s * stage_bytes);
+                const uint32_t sb = sa + ROW_TILE_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sa + k * 32), sm100::smem_desc_k_sw128(sb + k * 32), idesc,
+                                   (kb > 0 || k > 0) ? 1u : 0u);
+                sm100::mma_commit(&bars->empty[s]);
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+            if (ok) sm100::mma_commit(&bars->acc_full);
+        }
+    } else {
+        const int t = threadIdx.x - 64;
+        const int n = n0 + t;
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int kc = 0; kc < nkb && ok; kc += 16) {
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int w = 2 * (kc + i);
+                const bool live = n < N && kc + i < nkb;
+                lo[i] = (live && w < kbw) ? bits[(int64_t)w * N + n] : 0u;
+                hi[i] = (live && w + 1 < kbw) ? bits[(int64_t)(w + 1) * N + n] : 0u;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (kc + i >= nkb) break;
+                if (!sm100::mbar_wait(&bars->empty[s], ph ^ 1u, status, 24)) {
+                    ok = false;
+                    break;
+                }
+                expand_row_sw128(smem + s * stage_bytes + ROW_TILE_BYTES, t, (uint64_t)lo[i] | ((uint64_t)hi[i] << 32), lut);
+                sm100::fence_proxy_async_smem();
+                sm100::mbar_arrive(&bars->full_exp[s]);
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+        }
+        // epilogue: TMEM lane = output row m, columns = n.
+        const int quad = warp & 3;
+        const int m = m0 + quad * 32 + lane;
+        if (sm100::mbar_wait(&bars->acc_full, 0, status, 25)) {
+            sm100::tc_fence_after();
+            const bool vec_ok = (N % 8) == 0;
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, r);
+                sm100::tmem_ld_wait();
+                const int col0 = n0 + c;
+                if (m < M) {
+                    T* dst = y + (int64_t)m * N + col0;
+                    if (vec_ok && col0 + 32 <= N) {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            p[j] = pack2<T>(scale * __uint_as_float(r[2 * j]), scale * __uint_as_float(r[2 * j + 1]));
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) d4[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < N) dst[j] = sf::Dt<T>::from_f(scale * __uint_as_float(r[j]));
+                    }
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------------------------------------
+// General fallbacks (any shape / alignment): one thread per output element, fp32 accumulation.
+// ------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void bitdelta_task_fallback(const T* __restrict__ x, const uint32_t* __restrict__ bits, T* __restrict__ y, int64_t M,
+                                       int64_t N, int64_t K, float scale) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * N) return;
+    const int64_t m = idx / N, n = idx % N;
+    float acc = 0.f;
+    for (int64_t k = 0; k < K; ++k) {
+        const uint32_t w = bits[(k >> 5) * N + n];
+        const float sgn = ((w >> (k & 31)) & 1u) ? 1.f : -1.f;
+        acc = fmaf(sf::Dt<T>::to_f(x[m * K + k]), sgn, acc);
+    }
+    y[idx] = sf::Dt<T>::from_f(scale * acc);
+}
+
+template <typename T>
+__global__ void bitdelta_base_fallback(const T* __restrict__ x, const T* __restrict__ wb, const uint32_t* __restrict__ sw,
+                                       const T* __restrict__ alpha, T* __restrict__ y, int64_t M, int64_t N, int64_t K) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * N) return;
+    const int64_t m = idx / N, n = idx % N;
+    const int64_t kw = K / 32;
+    float a1 = 0.f, a2 = 0.f;
+    for (int64_t k = 0; k < K; ++k) {
+        const float xv = sf::Dt<T>::to_f(x[m * K + k]);
+        a1 = fmaf(xv, sf::Dt<T>::to_f(wb[n * K + k]), a1);
+        const uint32_t w = sw[n * kw + (k >> 5)];
+        a2 += ((w >> (k & 31)) & 1u) ? xv : -xv;
+    }
+    y[idx] = sf::Dt<T>::from_f(a1 + sf::Dt<T>::to_f(alpha[n]) * a2);
+}
+
+// ---- host ----------------------------------------------------------------------------------------
+
+sm100::KernelStatus* status_ptr() {
+    sm100::KernelStatus* p = nullptr;
+    if (cudaGetSymbolAddress((void**)&p, g_bitdelta_status) != cudaSuccess) return nullptr;
+    return p;
+}
+
+template <typename T>
+int launch_base_tc(const void* x, const void* wb, const void* sw, const void* alpha, void* y, int64_t M, int64_t N, int64_t K,
+                   cudaStream_t st, char* err, uint64_t cap) {
+    const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+    sm100::KernelStatus* status = status_ptr();
+    if (!status) return sf::fail(SF_EDEVICE, err, cap, "bitdelta: cannot resolve the status word");
+    CUtensorMap mw;
+    int rc = sf::tmap_kmajor(&mw, wb, N, K, TILE_ROWS, bf16, err, cap);
+    if (rc) return rc;
+    const int64_t tiles = (N + TILE_ROWS - 1) / TILE_ROWS;
+    const int64_t nkb = (K + BK - 1) / BK;
+    int sk = (int)std::max<int64_t>(1, std::min<int64_t>(8, sf::sm_count() / std::max<int64_t>(tiles, 1)));
+    sk = (int)std::min<int64_t>(sk, nkb);
+    // x rows are processed in chunks of at most 256 (the MMA N dimension).
+    for (int64_t mc = 0; mc < M; mc += 256) {
+        const int64_t mrows = std::min<int64_t>(256, M - mc);
+        const int nm = (int)((mrows + 15) / 16 * 16);
+        CUtensorMap mx;
+        rc = sf::tmap_kmajor(&mx, (const T*)x + mc * K, mrows, K, nm, bf16, err, cap);
+        if (rc) return rc;
+        const int stage_bytes = 2 * ROW_TILE_BYTES + nm * 128;
+        int stages = std::min(4, (kMaxDynSmem - 2048) / stage_bytes);
+        // The reduction buffer (128 x nm fp32) reuses the pipeline buffers.
+        while (stages * stage_bytes < 128 * nm * 4) ++stages;
+        const int smem = stages * stage_bytes + 1024 + 256;
+        if (stages > 4 || smem > kMaxDynSmem) return sf::fail(SF_EINVAL, err, cap, "bitdelta: no shared-memory plan for M chunk %d", nm);
+        static std::atomic<uint64_t> attr_done{0};
+        if (sf::once_per_device(attr_done))
+            cudaFuncSetAttribute(bitdelta_base_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)tiles, (unsigned)sk, 1);
+        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = (unsigned)sk;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, bitdelta_base_kernel<T>, mw, mx, (const uint32_t*)sw, (const T*)alpha,
+                                           (T*)y + mc * N, (int)mrows, (int)N, (int)K, nm, stages, status);
+        if (e != cudaSuccess) return sf::fail(SF_EDEVICE, err, cap, "bitdelta_base launch: %s", cudaGetErrorString(e));
+    }
+    return SF_OK;
+}
+
+template <typename T>
+int launch_task_tc(const void* x, const void* bits, void* y, int64_t M, int64_t N, int64_t K, float scale, cudaStream_t st,
+                   char* err, uint64_t cap) {
+    const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+    sm100::KernelStatus* status = status_ptr();
+    if (!status) return sf::fail(SF_EDEVICE, err, cap, "bitdelta: cannot resolve the status word");
+    CUtensorMap mx;
+    int rc = sf::tmap_kmajor(&mx, x, M, K, TILE_ROWS, bf16, err, cap);
+    if (rc) return rc;
+    const int stages = 4;
+    const int smem = stages * 2 * ROW_TILE_BYTES + 1024 + 256;
+    static std::atomic<uint64_t> attr_done{0};
+    if (sf::once_per_device(attr_done))
+        cudaFuncSetAttribute(bitdelta_task_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    const dim3 grid((unsigned)((N + TILE_ROWS - 1) / TILE_ROWS), (unsigned)((M + TILE_ROWS - 1) / TILE_ROWS));
+    if (grid.y > 65535) return sf::fail(SF_EINVAL, err, cap, "bitdelta: M too large");
+    bitdelta_task_kernel<T><<<grid, NUM_THREADS, smem, st>>>(mx, (const uint32_t*)bits, (T*)y, (int)M, (int)N, (int)K, scale, stages,
+                                                             status);
+    return sf::check_launch("bitdelta_task launch", err, cap);
+}
+
+bool tc_ok(const void* x, int64_t M, int64_t N, int64_t K) {
+    return sf::aligned16(x) && K % 32 == 0 && K > 0 && M > 0 && N > 0 && K < (1LL << 31) && N < (1LL << 31) && M < (1LL << 31);
+}
+
+}  // namespace
+
+int sf_bitdelta_base_launch(const void* x, const void* w_base, const void* s_words, const void* alpha, void* y, int64_t M, int64_t N,
+                            int64_t K, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+    if (M < 0 || N < 0 || K < 0 || K % 32) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: need M,N >= 0 and K a multiple of 32");
+    if (dtype != SF_DTYPE_F16 && dtype != SF_DTYPE_BF16) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: dtype %d is not fp16/bf16", dtype);
+    if (M == 0 || N == 0) return SF_OK;
+    if (!x || !w_base || !s_words || !alpha || !y) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: null tensor pointer");
+    const bool tc = tc_ok(x, M, N, K) && sf::aligned16(w_base);
+    if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: the tensor-core variant needs aligned bases");
+    if (tc && variant != 2) {
+        return dtype == SF_DTYPE_F16 ? launch_base_tc<__half>(x, w_base, s_words, alpha, y, M, N, K, st, err, cap)
+                                     : launch_base_tc<__nv_bfloat16>(x, w_base, s_words, alpha, y, M, N, K, st, err, cap);
+    }
+    const int64_t total = M * N;
+    const unsigned blocks = (unsigned)((total + 255) / 256);
+    if (dtype == SF_DTYPE_F16)
+        bitdelta_base_fallback<__half><<<blocks, 256, 0, st>>>((const __half*)x, (const __half*)w_base, (const uint32_t*)s_words,
+                                                               (const __half*)alpha, (__half*)y, M, N, K);
+    else
+        bitdelta_base_fallback<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_base,
+                                                                      (const uint32_t*)s_words, (const __nv_bfloat16*)alpha,
+                                                                      (__nv_bfloat16*)y, M, N, K);
+    return sf::check_launch("bitdelta_base fallback launch", err, cap);
+}
+
+int sf_bitdelta_launch(const void* x, const void* bits, void* y, int64_t M, int64_t N, int64_t K, float scale, int32_t dtype,
+                       int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+    if (M < 0 || N < 0 || K < 0 || K % 32) return sf::fail(SF_EINVAL, err, cap, "bitdelta: need M,N >= 0 and K a multiple of 32");
+    if (dtype != SF_DTYPE_F16 && dtype != SF_DTYPE_BF16) return sf::fail(SF_EINVAL, err, cap, "bitdelta: dtype %d is not fp16/bf16", dtype);
+    if (M == 0 || N == 0) return SF_OK;
+    if (!x || !bits || !y) return sf::fail(SF_EINVAL, err, cap, "bitdelta: null tensor pointer");
+    const bool tc = tc_ok(x, M, N, K);
+    if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "bitdelta: the tensor-core variant needs an aligned x and K %% 32 == 0");
+    if (tc && variant != 2) {
+        return dtype == SF_DTYPE_F16 ? launch_task_tc<__half>(x, bits, y, M, N, K, scale, st, err, cap)
+                                     : launch_task_tc<__nv_bfloat16>(x, bits, y, M, N, K, scale, st, err, cap);
+    }
+    const int64_t total = M * N;
+    const unsigned blocks = (unsigned)((total + 255) / 256);
+    if (dtype == SF_DTYPE_F16)
+        bitdelta_task_fallback<__half><<<blocks, 256, 0, st>>>((const __half*)x, (const uint32_t*)bits, (__half*)y, M, N, K, scale);
+    else
+        bitdelta_task_fallback<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x, (const uint32_t*)bits,
+                                                                      (__nv_bfloat16*)y, M, N, K, scale);
+    return sf::check_launch("bitdelta fallback launch", err, cap);
+}
+
+int sf_bitdelta_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream) {
+    sm100::KernelStatus h{0, 0};
+    if (cudaMemcpyFromSymbolAsync(&h, g_bitdelta_status, sizeof(h), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+        return SF_EDEVICE;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return SF_EDEVICE;
+    if (h.code) {
+        const sm100::KernelStatus zero{0, 0};
+        cudaMemcpyToSymbolAsync(g_bitdelta_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream);
+        cudaStreamSynchronize(stream);
+    }
+    *code = h.code;
+    *where = h.where;
+    return SF_OK;
+}
+
+extern "C" int sf_bitdelta_gemm(const void* x, const void* bits, void* y, int64_t M, int64_t N, int64_t K, float scale, int32_t dtype,
+                                void* stream, char* err, uint64_t cap) {
+    return sf_bitdelta_launch(x, bits, y, M, N, K, scale, dtype, 0, (cudaStream_t)stream, err, cap);
+}
+
+extern "C" int sf_bitdelta_gemm_base(const void* x, const void* w_base, const void* s_words, const void* alpha, void* y, int64_t M,
+                                     int64_t N, int64_t K, int32_t dtype, void* stream, char* err, uint64_t cap) {
+    return sf_bitdelta_base_launch(x, w_base, s_words, alpha, y, M, N, K, dtype, 0, (cudaStream_t)stream, err, cap);
+}

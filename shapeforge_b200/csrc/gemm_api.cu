@@ -193,7 +193,19 @@ extern "C" int sf_gemm_nn(const void* A, const void* B, void* C, int64_t M, int6
 
 extern "C" int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char* err, uint64_t cap) {
     if (!code || !where) return sf::fail(SF_EINVAL, err, cap, "sf_kernel_status: null output");
-    if (sf_gemm_status_read(code, where, (cudaStream_t)stream) != SF_OK)
+    // Each tensor-core module keeps its own status word; the first failure found is reported
+    // (the wait ids are unique across modules) and every word is cleared.
+    uint32_t c[2] = {0, 0}, w[2] = {0, 0};
+    if (sf_gemm_status_read(&c[0], &w[0], (cudaStream_t)stream) != SF_OK ||
+        sf_bitdelta_status_read(&c[1], &w[1], (cudaStream_t)stream) != SF_OK)
         return sf::fail(SF_EDEVICE, err, cap, "sf_kernel_status: reading the status word failed");
+    *code = 0;
+    *where = 0;
+    for (int i = 0; i < 2; ++i) {
+        if (c[i] && !*code) {
+            *code = c[i];
+            *where = w[i];
+        }
+    }
     return SF_OK;
 }

@@ -18,6 +18,7 @@
 // a wait that gives up records a status word and the CTA drains to its teardown.
 #include "sf_common.cuh"
 #include "sm100.cuh"
+#include "tma_host.cuh"
 
 #include <cudaTypedefs.h>
 #include <algorithm>
@@ -247,56 +248,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---- host side ----------------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess) {
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-        }
-    });
-    return fn;
-}
-
-// Row-major [rows, K] 16-bit matrix, box = box_rows x 64 elements, 128-byte swizzle.
-int make_kmajor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows, bool bf16, char* err,
-                    uint64_t cap) {
-    auto fn = encode_fn();
-    if (!fn) return sf::fail(SF_EDEVICE, err, cap, "cuTensorMapEncodeTiled is unavailable from the driver");
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
-                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return sf::fail(SF_EINVAL, err, cap, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-    return SF_OK;
-}
-
 template <typename T>
 int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream, char* err,
               uint64_t cap) {
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     CUtensorMap ma, mb;
-    int rc = make_kmajor_map(&ma, A, M, K, BM, bf16, err, cap);
+    int rc = sf::tmap_kmajor(&ma, A, M, K, BM, bf16, err, cap);
     if (rc) return rc;
-    rc = make_kmajor_map(&mb, B, N, K, BN, bf16, err, cap);
+    rc = sf::tmap_kmajor(&mb, B, N, K, BN, bf16, err, cap);
     if (rc) return rc;
     int dev = 0;
     cudaGetDevice(&dev);
     sm100::KernelStatus* st = nullptr;
     if (cudaGetSymbolAddress((void**)&st, g_gemm_status) != cudaSuccess || !st)
         return sf::fail(SF_EDEVICE, err, cap, "gemm: cannot resolve the status word");
-    static bool attr_set[64] = {false};
-    if (dev < 0 || dev >= 64) return sf::fail(SF_EDEVICE, err, cap, "gemm: device index %d out of range", dev);
-    if (!attr_set[dev]) {
+    static std::atomic<uint64_t> attr_done{0};
+    if (sf::once_per_device(attr_done))
         cudaFuncSetAttribute(gemm_nt_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        attr_set[dev] = true;
-    }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = (int)std::min<int64_t>(tiles, sf::sm_count());
     gemm_nt_tc_kernel<T><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, (T*)C, (int)M, (int)N, (int)K, st);

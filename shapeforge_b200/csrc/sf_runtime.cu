@@ -114,6 +114,8 @@ extern "C" int32_t sf_op_nargs(int32_t op) {
         case SF_OP_SOFTMAX: return 2;
         case SF_OP_REDUCTION_SUM: return 2;
         case SF_OP_ROPE: return 2;
+        case SF_OP_BITDELTA: return 3;
+        case SF_OP_BITDELTA_BASE: return 5;
         default: return 0;
     }
 }
@@ -139,6 +141,12 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
         case SF_OP_ROPE:
             return sf_rope_launch(a[0], (void*)a[1], d->dims[0], d->dims[1], d->dims[2], d->dims[3], d->attrs[0], d->dtype,
                                   d->variant, s, err, cap);
+        case SF_OP_BITDELTA:
+            return sf_bitdelta_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype,
+                                      d->variant, s, err, cap);
+        case SF_OP_BITDELTA_BASE:
+            return sf_bitdelta_base_launch(a[0], a[1], a[2], a[3], (void*)a[4], d->dims[0], d->dims[1], d->dims[2], d->dtype,
+                                           d->variant, s, err, cap);
         default:
             return sf::fail(SF_EINVAL, err, cap, "unknown op %d", d->op);
     }

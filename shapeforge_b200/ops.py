@@ -172,3 +172,39 @@ def rope(x: torch.Tensor, base: float = 10000.0, out: torch.Tensor | None = None
     _check(out, "out", x.dtype)
     _run("rope", x, [x.data_ptr(), out.data_ptr()], dims=(b, h, s, d), attrs=(base,), variant=variant)
     return out
+
+
+def bitdelta_gemm(x: torch.Tensor, bits: torch.Tensor, scale: float = 0.02, out: torch.Tensor | None = None,
+                  variant: int = 0) -> torch.Tensor:
+    """``y = scale * x @ W`` with W ``[K, N]`` of +-1 from ``bits [K/32, N]`` (int32/uint32 words;
+    bit j of ``bits[kb, n]`` is ``W[kb*32 + j, n]``, set = +1) — tasks/bitdelta_gemm/reference.py:99-130."""
+    _check(x, "x")
+    _check(bits, "bits")
+    if bits.element_size() != 4:
+        raise TypeError("bits must hold 32-bit words")
+    m, k = x.shape
+    kb, n = bits.shape
+    if kb * 32 != k:
+        raise ValueError(f"bits has {kb} word rows, expected K/32 = {k // 32}")
+    out = torch.empty((m, n), dtype=x.dtype, device=x.device) if out is None else out
+    _check(out, "out", x.dtype)
+    _run("bitdelta_gemm", x, [x.data_ptr(), bits.data_ptr(), out.data_ptr()], dims=(m, n, k), attrs=(scale,), variant=variant)
+    return out
+
+
+def bitdelta_gemm_base(x: torch.Tensor, w_base: torch.Tensor, s_words: torch.Tensor, alpha: torch.Tensor,
+                       out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y = x @ (W_base + diag(alpha) S)^T`` with S in {-1,+1} packed along K as ``s_words [N, K/32]``."""
+    _check(x, "x")
+    _check(w_base, "w_base", x.dtype)
+    _check(s_words, "s_words")
+    _check(alpha, "alpha", x.dtype)
+    m, k = x.shape
+    n = w_base.shape[0]
+    if w_base.shape[1] != k or s_words.shape != (n, k // 32) or alpha.numel() != n:
+        raise ValueError("bitdelta_gemm_base: inconsistent shapes")
+    out = torch.empty((m, n), dtype=x.dtype, device=x.device) if out is None else out
+    _check(out, "out", x.dtype)
+    _run("bitdelta_gemm_base", x, [x.data_ptr(), w_base.data_ptr(), s_words.data_ptr(), alpha.data_ptr(), out.data_ptr()],
+         dims=(m, n, k), variant=variant)
+    return out
