@@ -134,6 +134,14 @@ SF_API int sf_bitdelta_gemm_base(const void* x, const void* w_base, const void* 
                int64_t M, int64_t N, int64_t K, int32_t dtype, void* stream, char* err, uint64_t cap);
 
 /*
+ * flash_attention forward: o = softmax(q . k^T * scale [+ causal mask]) . v over q, k, v, o
+ * [B, H, S, D] (tasks/flash_attention/reference.py:113-119 with SM_SCALE = scale; causal != 0
+ * keeps key j <= query i).  tcgen05 kernel for D in {64, 128}; general kernel otherwise (D <= 256).
+ */
+SF_API int sf_flash_attention(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H, int64_t S,
+               int64_t D, float scale, int32_t causal, int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
  * gemm_nt: C[M,N] = A[M,K] . B[N,K]^T, fp16 or bf16 in, fp32 accumulation, one rounding
  * (the dense-gemm workload; the oracle is tasks/gemm/reference.py:110-114 applied to B^T).
  * tcgen05/TMEM/TMA kernel when the bases are 16-byte aligned and K % 8 == 0, else the general
@@ -190,6 +198,7 @@ SF_API int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char*
 #define SF_OP_ROPE 8
 #define SF_OP_BITDELTA 9
 #define SF_OP_BITDELTA_BASE 10
+#define SF_OP_ATTENTION 11
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -216,6 +225,7 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_ROPE      dims = {B, H, S, D}            attrs = {base}      args = {x, y}
  *   SF_OP_BITDELTA  dims = {M, N, K}               attrs = {scale}     args = {x, bits, y}
  *   SF_OP_BITDELTA_BASE dims = {M, N, K}                               args = {x, w_base, s_words, alpha, y}
+ *   SF_OP_ATTENTION dims = {B, H, S, D}  attrs = {scale}  flags bit 0 = causal  args = {q, k, v, o}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

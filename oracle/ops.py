@@ -190,3 +190,16 @@ def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale, state0=None):
     if state0 is None:
         state0 = np.zeros((n, heads, v.shape[2], dim), dtype=np.float64)
     return delta_rule(q * float(scale), k, v, g, beta, state0, cu_seqlens)
+
+
+def attention_rows(q, k, v, scale: float, causal: bool, rows) -> np.ndarray:
+    """:func:`attention` for the query rows ``rows`` only (``[B, H, len(rows), D]``); each output
+    row depends only on its own query row, so this equals ``attention(...)[:, :, rows]``."""
+    rows = np.asarray(rows)
+    with _err():
+        s = np.einsum("bhqd,bhkd->bhqk", q[:, :, rows], k) * scale
+        if causal:
+            keys = np.arange(k.shape[2])
+            s = np.where(keys[None, :] <= rows[:, None], s, -np.inf)
+        p = softmax(s)
+        return np.einsum("bhqk,bhkd->bhqd", p, v)

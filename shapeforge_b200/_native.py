@@ -76,6 +76,7 @@ OPS = {
     "rope": 8,
     "bitdelta_gemm": 9,
     "bitdelta_gemm_base": 10,
+    "flash_attention": 11,
 }
 
 _P = ctypes.c_void_p
@@ -99,6 +100,7 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_rope": (ctypes.c_int, (_P, _P, _I64, _I64, _I64, _I64, ctypes.c_double, _I32, _P, *_ERR)),
     "sf_bitdelta_gemm": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_bitdelta_gemm_base": (ctypes.c_int, (_P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
+    "sf_flash_attention": (ctypes.c_int, (_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _I32, _I32, _P, *_ERR)),
     "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_gemm_nn_workspace_bytes": (_U64, (_I64, _I64, _I64, _I32)),
     "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),

@@ -233,3 +233,27 @@ def bitdelta_base_inputs(case: str, seed: int, m: int, n: int, k: int, dtype: st
     if case == "ieee":
         x = inject(x, seed + IEEE_SEED_STRIDE)
     return {"x": round_to(x, dtype), "w_base": round_to(w, dtype), "s_words": words, "alpha": round_to(alpha, dtype)}
+
+
+# ---- attention --------------------------------------------------------------------------------
+
+ATTENTION_CASES = ("normal", "wide_range", "large", "tiny", "outlier", "ieee")
+
+
+def attention_inputs(case: str, seed: int, shape, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/flash_attention/reference.py:88-110: q/k/v at seed + 0/31/62 (mags normal 1 /
+    wide_range 0.1, large 6, spike 5); the ieee case injects specials into q only."""
+    base = "normal" if case == "ieee" else case
+    mag = {"normal": 1.0, "wide_range": 0.1}.get(base, 1.0)
+    out = {}
+    for name, off in (("q", 0), ("k", 31), ("v", 62)):
+        out[name] = sample(base, shape, seed + off, dtype, mag=mag, large=6.0, spike=5.0)
+    if case == "ieee":
+        out["q"] = inject(out["q"], seed + IEEE_SEED_STRIDE)
+    return {k: round_to(v, dtype) for k, v in out.items()}
+
+
+def attention_bench_inputs(shape, dtype: str, seed: int = SEARCH_SEED) -> dict[str, torch.Tensor]:
+    """Timing inputs of the causal attention workload: q, k, v ~ N(0, 1)."""
+    g = generator(seed)
+    return {name: round_to(torch.randn(shape, generator=g), dtype) for name in ("q", "k", "v")}

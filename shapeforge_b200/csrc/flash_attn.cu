@@ -1,0 +1,446 @@
+// Flash-attention forward on the tcgen05 tensor cores, sm_100a.
+//
+//   o[b,h,i,:] = sum_j softmax_j(q[b,h,i,:] . k[b,h,j,:] * scale [+ causal mask j <= i]) v[b,h,j,:]
+//
+// Task contract: tasks/flash_attention/reference.py:113-119 (non-causal scaled_dot_product_attention
+// in fp32, SM_SCALE attr); the causal workload is the same formula with the mask.  q, k, v, o are
+// [B, H, S, D] row-major fp16/bf16, D in {64, 128}; softmax statistics in fp32.
+//
+// One CTA per (b*h, 128-query tile); 192 threads:
+//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring (3-D tensor
+//               maps over [B*H, S, D], so rows past S read as zeros and never spill into the next head);
+//   warp 1      MMA issuer: S_j = Q.K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
+//               issued one tile ahead, and O += P_j.V_j (M=128, N=D, K=128) into a TMEM accumulator;
+//               V is read as an MN-major operand straight from its [keys, D] layout;
+//   warps 2..5  softmax, one thread per query row: tcgen05.ld of the score row, scale + mask,
+//               online max/sum in fp32 with exp2; O is rescaled in TMEM (tcgen05.ld/st) only when
+//               the row max grows by more than 2^8 (the final 1/l cancels any stale max, so this is
+//               exact up to rounding); P_j is written as 16-bit into a 128-byte-swizzled K-major
+//               shared tile for the second MMA.  Final O / l is stored with 16-byte stores.
+// Causal CTAs skip every key tile above the diagonal and are scheduled heaviest first.
+// NaN/Inf follow the fp32 reference: the row max propagates NaN, so a special in a query row makes
+// that output row NaN.  Every mbarrier wait is bounded.
+#include "sf_common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+__device__ sm100::KernelStatus g_attn_status;
+
+namespace {
+
+constexpr int BM = 128, BN = 128;
+constexpr int BOX_BYTES = 128 * 128;  // 128 rows x 64 16-bit elements
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;   // S0 [0,128), S1 [128,256), O [256, 256+D)
+
+struct __align__(8) Bars {
+    uint64_t q_full;
+    uint64_t kv_full[2];
+    uint64_t kv_empty[2];
+    uint64_t s_full[2];
+    uint64_t s_free[2];
+    uint64_t p_full;
+    uint64_t pv_done;
+    uint32_t tmem_base;
+};
+
+__device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// PSPLIT: P is written as a 16-bit high part and a 16-bit residual (P - high), and P.V is issued
+// twice, so the probabilities enter the product with ~16-22 significant bits instead of 8-11.  A
+// single 16-bit rounding of P, amplified by cancellation between large v terms, can exceed the
+// task tolerances.
+template <int D, bool PSPLIT>
+struct Layout {
+    static constexpr int DB = D / 64;  // 64-column boxes per row
+    static constexpr int Q = 0;
+    static constexpr int K = Q + DB * BOX_BYTES;           // K[2][DB] boxes
+    static constexpr int V = K + 2 * DB * BOX_BYTES;       // V[2][DB] boxes
+    static constexpr int P = V + 2 * DB * BOX_BYTES;       // P[2] boxes (128 keys)
+    static constexpr int PLO = P + 2 * BOX_BYTES;          // residual P[2] boxes (PSPLIT only)
+    static constexpr int BARS = PLO + (PSPLIT ? 2 * BOX_BYTES : 0);
+    static constexpr int BYTES = BARS + 256;
+};
+
+template <typename T, int D, bool CAUSAL, bool PSPLIT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                  T* __restrict__ o, int S, float scale_log2, sm100::KernelStatus* status) {
+    using L = Layout<D, PSPLIT>;
+    constexpr int DB = L::DB;
+    constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars* bars = reinterpret_cast<Bars*>(smem + L::BARS);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int nq = (S + BM - 1) / BM;
+    const int qt = CAUSAL ? (nq - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+    const int nkv_all = (S + BN - 1) / BN;
+    const int nkv = CAUSAL ? min(qt + 1, nkv_all) : nkv_all;
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bars->q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            sm100::mbar_init(&bars->kv_full[i], 1);
+            sm100::mbar_init(&bars->kv_empty[i], 1);
+            sm100::mbar_init(&bars->s_full[i], 1);
+            sm100::mbar_init(&bars->s_free[i], 128);
+        }
+        sm100::mbar_init(&bars->p_full, 128);
+        sm100::mbar_init(&bars->pv_done, 1);
+        sm100::fence_mbar_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const uint32_t tmem_o = tmem + 256;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            sm100::tma_prefetch_desc(&tq);
+            sm100::tma_prefetch_desc(&tk);
+            sm100::tma_prefetch_desc(&tv);
+            sm100::mbar_arrive_expect_tx(&bars->q_full, DB * BOX_BYTES);
+            for (int b = 0; b < DB; ++b) sm100::tma_load_3d(smem + L::Q + b * BOX_BYTES, &tq, &bars->q_full, b * 64, qt * BM, bh);
+            for (int j = 0; j < nkv; ++j) {
+                const int st = j & 1;
+                if (!sm100::mbar_wait(&bars->kv_empty[st], ((j >> 1) & 1) ^ 1u, status, 31)) break;
+                sm100::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * DB * BOX_BYTES);
+                for (int b = 0; b < DB; ++b) {
+                    sm100::tma_load_3d(smem + L::K + (st * DB + b) * BOX_BYTES, &tk, &bars->kv_full[st], b * 64, j * BN, bh);
+                    sm100::tma_load_3d(smem + L::V + (st * DB + b) * BOX_BYTES, &tv, &bars->kv_full[st], b * 64, j * BN, bh);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = sm100::idesc_f16(BM, BN, BF16);
+            constexpr uint32_t idesc_o = sm100::idesc_f16_bmn(BM, D, BF16);
+            const uint32_t sq = sm100::smem_u32(smem + L::Q);
+            auto issue_s = [&](int j) {
+                const int st = j & 1;
+                const uint32_t sk = sm100::smem_u32(smem + L::K + st * DB * BOX_BYTES);
+                const uint32_t dst = tmem + (uint32_t)((j & 1) * 128);
+#pragma unroll
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint32_t off = (uint32_t)((k >> 2) * BOX_BYTES + (k & 3) * 32);
+                    sm100::mma_f16(dst, sm100::smem_desc_k_sw128(sq + off), sm100::smem_desc_k_sw128(sk + off), idesc_s, k > 0 ? 1u : 0u);
+                }
+                sm100::mma_commit(&bars->s_full[j & 1]);
+            };
+            bool ok = sm100::mbar_wait(&bars->q_full, 0, status, 32) && sm100::mbar_wait(&bars->kv_full[0], 0, status, 33);
+            if (ok) {
+                sm100::tc_fence_after();
+                issue_s(0);
+            }
+            const uint32_t sp = sm100::smem_u32(smem + L::P);
+            for (int j = 0; j < nkv && ok; ++j) {
+                if (j + 1 < nkv) {
+                    const int jn = j + 1;
+                    if (!sm100::mbar_wait(&bars->kv_full[jn & 1], (jn >> 1) & 1, status, 34) ||
+                        !sm100::mbar_wait(&bars->s_free[jn & 1], ((jn >> 1) & 1) ^ 1u, status, 35)) {
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    issue_s(jn);
+                }
+                if (!sm100::mbar_wait(&bars->p_full, j & 1, status, 36)) {
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t sv = sm100::smem_u32(smem + L::V + (j & 1) * DB * BOX_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    const uint64_t ad = sm100::smem_desc_k_sw128(sp + (uint32_t)((kk >> 2) * BOX_BYTES + (kk & 3) * 32));
+                    const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
+                    sm100::mma_f16(tmem_o, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                if (PSPLIT) {
+                    const uint32_t spl = sm100::smem_u32(smem + L::PLO);
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk) {
+                        const uint64_t ad = sm100::smem_desc_k_sw128(spl + (uint32_t)((kk >> 2) * BOX_BYTES + (kk & 3) * 32));
+                        const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
+                        sm100::mma_f16(tmem_o, ad, bd, idesc_o, 1u);
+                    }
+                }
+                sm100::mma_commit(&bars->pv_done);
+                sm100::mma_commit(&bars->kv_empty[j & 1]);
+            }
+        }
+    } else {
+        // ---------------- softmax: one thread per query row ----------------
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const int q = qt * BM + row;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        uint8_t* pbase = smem + L::P;
+        for (int j = 0; j < nkv; ++j) {
+            if (!sm100::mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 37)) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+            float s[BN];
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * 128 + c * 32), r);
+                sm100::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&bars->s_free[j & 1]);
+
+            const int key0 = j * BN;
+            const bool mask_tail = key0 + BN > S;
+            const bool mask_diag = CAUSAL && (j == qt);
+            float rmax = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                float v = s[c] * scale_log2;
+                if ((mask_tail && key0 + c >= S) || (mask_diag && c > row)) v = -INFINITY;
+                s[c] = v;
+                rmax = nan_max(rmax, v);
+            }
+            const float m_new = nan_max(m, rmax);
+            const bool need = !(m_new <= m + 8.0f);
+            if (j > 0) {
+                if (!sm100::mbar_wait(&bars->pv_done, (j - 1) & 1, status, 38)) {
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                const float alpha = need ? exp2f(m - m_new) : 1.0f;
+                if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t r[32];
+                        sm100::tmem_ld_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+                        sm100::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                        sm100::tmem_st_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+                    }
+                    sm100::tmem_st_wait();
+                }
+                if (need) l *= alpha;
+            }
+            if (need) m = m_new;
+            float rsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                const float p = exp2f(s[c] - m);
+                s[c] = p;
+                rsum += p;
+            }
+            l += rsum;
+            // P row -> K-major swizzled tiles: keys 0..63 in box 0, 64..127 in box 1.
+#pragma unroll
+            for (int cc = 0; cc < BN / 8; ++cc) {
+                const uint4 v = make_uint4(pack2<T>(s[cc * 8 + 0], s[cc * 8 + 1]), pack2<T>(s[cc * 8 + 2], s[cc * 8 + 3]),
+                                           pack2<T>(s[cc * 8 + 4], s[cc * 8 + 5]), pack2<T>(s[cc * 8 + 6], s[cc * 8 + 7]));
+                const int off = (cc >> 3) * BOX_BYTES + row * 128 + (((cc & 7) ^ (row & 7)) * 16);
+                *reinterpret_cast<uint4*>(pbase + off) = v;
+                if (PSPLIT) {
+                    // Residual of the 16-bit rounding of each probability.
+                    float r[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t w = (i & 1) ? ((&v.x)[i >> 1] >> 16) : ((&v.x)[i >> 1] & 0xFFFFu);
+                        r[i] = s[cc * 8 + i] - sf::Dt<T>::to_f(*reinterpret_cast<const T*>(&w));
+                    }
+                    *reinterpret_cast<uint4*>(smem + L::PLO + off) =
+                        make_uint4(pack2<T>(r[0], r[1]), pack2<T>(r[2], r[3]), pack2<T>(r[4], r[5]), pack2<T>(r[6], r[7]));
+                }
+            }
+            sm100::fence_proxy_async_smem();
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&bars->p_full);
+        }
+        // ---------------- epilogue: O / l ----------------
+        if (ok && nkv > 0 && sm100::mbar_wait(&bars->pv_done, (nkv - 1) & 1, status, 39)) {
+            sm100::tc_fence_after();
+            const float inv = 1.0f / l;
+            T* orow = o + ((int64_t)bh * S + q) * D;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+                sm100::tmem_ld_wait();
+                if (q < S) {
+                    uint4* d4 = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        d4[i] = make_uint4(pack2<T>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
+                                           pack2<T>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
+                                           pack2<T>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
+                                           pack2<T>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---- general fallback: one warp per query row, fp32, any D <= 256 / alignment ------------------
+template <typename T>
+__global__ void __launch_bounds__(128) fa_fallback_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                                                          T* __restrict__ o, int64_t BH, int64_t S, int64_t D, float scale, bool causal) {
+    const int64_t rowid = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (rowid >= BH * S) return;
+    const int64_t bh = rowid / S, i = rowid % S;
+    const T* qr = q + rowid * D;
+    const T* kb = k + bh * S * D;
+    const T* vb = v + bh * S * D;
+    float acc[8];  // D <= 256: lane owns d = lane + 32*t
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    const int64_t jend = causal ? i + 1 : S;
+    for (int64_t j = 0; j < jend; ++j) {
+        float part = 0.f;
+        for (int64_t d = lane; d < D; d += 32) part += sf::Dt<T>::to_f(qr[d]) * sf::Dt<T>::to_f(kb[j * D + d]);
+        const float sc = sf::warp_sum(part) * scale;
+        const float m_new = nan_max(m, sc);
+        const float a = exp2f((m - m_new) * 1.4426950408889634f);
+        const float p = exp2f((sc - m_new) * 1.4426950408889634f);
+        l = l * a + p;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int64_t d = lane + 32 * t;
+            const float vv = d < D ? sf::Dt<T>::to_f(vb[j * D + d]) : 0.f;
+            acc[t] = acc[t] * a + p * vv;
+        }
+        m = m_new;
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const int64_t d = lane + 32 * t;
+        if (d < D) o[rowid * D + d] = sf::Dt<T>::from_f(acc[t] / l);
+    }
+}
+
+sm100::KernelStatus* status_ptr() {
+    sm100::KernelStatus* p = nullptr;
+    if (cudaGetSymbolAddress((void**)&p, g_attn_status) != cudaSuccess) return nullptr;
+    return p;
+}
+
+int tmap_bhsd(CUtensorMap* out, const void* base, int64_t BH, int64_t S, int64_t D, bool bf16, char* err, uint64_t cap);
+
+template <typename T, int D, bool CAUSAL>
+int launch_tc_t(const void* q, const void* k, const void* v, void* o, int64_t BH, int64_t S, float scale, cudaStream_t st, char* err,
+                uint64_t cap) {
+    const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+    CUtensorMap mq, mk, mv;
+    int rc = tmap_bhsd(&mq, q, BH, S, D, bf16, err, cap);
+    if (!rc) rc = tmap_bhsd(&mk, k, BH, S, D, bf16, err, cap);
+    if (!rc) rc = tmap_bhsd(&mv, v, BH, S, D, bf16, err, cap);
+    if (rc) return rc;
+    sm100::KernelStatus* status = status_ptr();
+    if (!status) return sf::fail(SF_EDEVICE, err, cap, "attention: cannot resolve the status word");
+    // P is split into high + residual parts for both 16-bit types (see Layout): with a single
+    // rounding, bf16 P errors reach the task tolerance (rtol 1.6e-2 / atol_rel 8e-3) on the
+    // normal case and fp16 P errors exceed its tolerance on the wide_range case.
+    constexpr bool PSPLIT = true;
+    // At least 116 KB so a second CTA (which would wait for TMEM) is never co-resident.
+    const int smem = std::max(Layout<D, PSPLIT>::BYTES + 1024, 116 * 1024);
+    static std::atomic<uint64_t> attr_done{0};
+    if (sf::once_per_device(attr_done))
+        cudaFuncSetAttribute(fa_fwd_kernel<T, D, CAUSAL, PSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    const int64_t nq = (S + BM - 1) / BM;
+    if (BH > 65535 || nq > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "attention: grid too large");
+    fa_fwd_kernel<T, D, CAUSAL, PSPLIT><<<dim3((unsigned)nq, (unsigned)BH), NUM_THREADS, smem, st>>>(
+        mq, mk, mv, (T*)o, (int)S, scale * 1.4426950408889634f, status);
+    return sf::check_launch("attention launch", err, cap);
+}
+
+template <typename T>
+int launch_t(const void* q, const void* k, const void* v, void* o, int64_t BH, int64_t S, int64_t D, float scale, bool causal,
+             int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+    const bool tc = (D == 64 || D == 128) && sf::aligned16(q) && sf::aligned16(k) && sf::aligned16(v) && sf::aligned16(o) &&
+                    S < (1LL << 31) && BH <= 65535;
+    if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "attention: the tensor-core variant needs D in {64,128} and aligned tensors");
+    if (tc && variant != 2) {
+        if (D == 64)
+            return causal ? launch_tc_t<T, 64, true>(q, k, v, o, BH, S, scale, st, err, cap)
+                          : launch_tc_t<T, 64, false>(q, k, v, o, BH, S, scale, st, err, cap);
+        return causal ? launch_tc_t<T, 128, true>(q, k, v, o, BH, S, scale, st, err, cap)
+                      : launch_tc_t<T, 128, false>(q, k, v, o, BH, S, scale, st, err, cap);
+    }
+    if (D > 256) return sf::fail(SF_EINVAL, err, cap, "attention: D=%lld exceeds the general kernel's 256", (long long)D);
+    const int64_t rows = BH * S;
+    fa_fallback_kernel<T><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, BH, S, D, scale, causal);
+    return sf::check_launch("attention fallback launch", err, cap);
+}
+
+int tmap_bhsd(CUtensorMap* out, const void* base, int64_t BH, int64_t S, int64_t D, bool bf16, char* err, uint64_t cap) {
+    return sf::tmap_3d(out, base, D, S, BH, D * 2, S * D * 2, 64, BM, 1, bf16, err, cap);
+}
+
+}  // namespace
+
+int sf_attention_launch(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H, int64_t S, int64_t D, float scale,
+                        int32_t causal, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+    if (B < 0 || H < 0 || S < 0 || D < 1) return sf::fail(SF_EINVAL, err, cap, "attention: bad sizes");
+    if (!(scale > 0.f)) return sf::fail(SF_EINVAL, err, cap, "attention: scale must be > 0");
+    if (B * H * S == 0) return SF_OK;
+    if (!q || !k || !v || !o) return sf::fail(SF_EINVAL, err, cap, "attention: null tensor pointer");
+    if (dtype == SF_DTYPE_F16) return launch_t<__half>(q, k, v, o, B * H, S, D, scale, causal != 0, variant, st, err, cap);
+    if (dtype == SF_DTYPE_BF16) return launch_t<__nv_bfloat16>(q, k, v, o, B * H, S, D, scale, causal != 0, variant, st, err, cap);
+    return sf::fail(SF_EINVAL, err, cap, "attention: dtype %d is not fp16/bf16", dtype);
+}
+
+int sf_attention_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream) {
+    sm100::KernelStatus h{0, 0};
+    if (cudaMemcpyFromSymbolAsync(&h, g_attn_status, sizeof(h), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess) return SF_EDEVICE;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return SF_EDEVICE;
+    if (h.code) {
+        const sm100::KernelStatus zero{0, 0};
+        cudaMemcpyToSymbolAsync(g_attn_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream);
+        cudaStreamSynchronize(stream);
+    }
+    *code = h.code;
+    *where = h.where;
+    return SF_OK;
+}
+
+extern "C" int sf_flash_attention(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H, int64_t S, int64_t D,
+                                  float scale, int32_t causal, int32_t dtype, void* stream, char* err, uint64_t cap) {
+    return sf_attention_launch(q, k, v, o, B, H, S, D, scale, causal, dtype, 0, (cudaStream_t)stream, err, cap);
+}

@@ -107,3 +107,6 @@ int sf_bitdelta_launch(const void* x, const void* bits, void* y, int64_t M, int6
 int sf_bitdelta_base_launch(const void* x, const void* w_base, const void* s_words, const void* alpha, void* y, int64_t M, int64_t N,
                             int64_t K, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);
 int sf_bitdelta_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
+int sf_attention_launch(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H, int64_t S, int64_t D, float scale,
+                        int32_t causal, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);
+int sf_attention_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);

@@ -116,6 +116,7 @@ extern "C" int32_t sf_op_nargs(int32_t op) {
         case SF_OP_ROPE: return 2;
         case SF_OP_BITDELTA: return 3;
         case SF_OP_BITDELTA_BASE: return 5;
+        case SF_OP_ATTENTION: return 4;
         default: return 0;
     }
 }
@@ -147,6 +148,9 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
         case SF_OP_BITDELTA_BASE:
             return sf_bitdelta_base_launch(a[0], a[1], a[2], a[3], (void*)a[4], d->dims[0], d->dims[1], d->dims[2], d->dtype,
                                            d->variant, s, err, cap);
+        case SF_OP_ATTENTION:
+            return sf_attention_launch(a[0], a[1], a[2], (void*)a[3], d->dims[0], d->dims[1], d->dims[2], d->dims[3], (float)d->attrs[0],
+                                       d->flags & 1, d->dtype, d->variant, s, err, cap);
         default:
             return sf::fail(SF_EINVAL, err, cap, "unknown op %d", d->op);
     }

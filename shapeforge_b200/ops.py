@@ -114,8 +114,8 @@ def kernel_status(device: torch.device | None = None) -> tuple[int, int]:
     return _native.kernel_status(stream)
 
 
-def _run(op: str, t: torch.Tensor, ptrs, dims=(), attrs=(), variant: int = 0) -> None:
-    desc = _native.op_desc(op, dtype_name(t), dims=dims, attrs=attrs, variant=variant)
+def _run(op: str, t: torch.Tensor, ptrs, dims=(), attrs=(), variant: int = 0, flags: int = 0) -> None:
+    desc = _native.op_desc(op, dtype_name(t), dims=dims, attrs=attrs, variant=variant, flags=flags)
     _native.run_op(desc, ptrs, _stream(t))
 
 
@@ -207,4 +207,21 @@ def bitdelta_gemm_base(x: torch.Tensor, w_base: torch.Tensor, s_words: torch.Ten
     _check(out, "out", x.dtype)
     _run("bitdelta_gemm_base", x, [x.data_ptr(), w_base.data_ptr(), s_words.data_ptr(), alpha.data_ptr(), out.data_ptr()],
          dims=(m, n, k), variant=variant)
+    return out
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool = False,
+                    out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``softmax(q k^T * scale [+ causal mask]) v`` over ``[B, H, S, D]``
+    (tasks/flash_attention/reference.py:113-119; the causal mask keeps key j <= query i)."""
+    _check(q, "q")
+    _check(k, "k", q.dtype)
+    _check(v, "v", q.dtype)
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("flash_attention expects q, k, v of the same shape [B, H, S, D]")
+    b, h, s, d = q.shape
+    out = torch.empty_like(q) if out is None else out
+    _check(out, "out", q.dtype)
+    _run("flash_attention", q, [q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()], dims=(b, h, s, d), attrs=(scale,),
+         variant=variant, flags=1 if causal else 0)
     return out
