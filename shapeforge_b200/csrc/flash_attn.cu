@@ -51,6 +51,21 @@ struct __align__(8) Bars {
 
 __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
 
+// max that returns NaN if either operand is NaN (one instruction).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
+// 2^x on the special-function unit (approximate, subnormal results flushed to zero; softmax
+// weights below 2^-126 of the row max contribute nothing at fp32 accumulation).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -210,30 +225,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 break;
             }
             sm100::tc_fence_after();
-            float s[BN];
+            // Raw scores: four independent 32-column loads, one wait.
+            uint32_t sr[BN];
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * 128 + c * 32), r);
-                sm100::tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-            }
+            for (int c = 0; c < BN / 32; ++c)
+                sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * 128 + c * 32),
+                                          *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+            sm100::tmem_ld_wait();
             sm100::tc_fence_before();
             sm100::mbar_arrive(&bars->s_free[j & 1]);
+            float* s = reinterpret_cast<float*>(sr);
 
+            // Only the diagonal tile (causal) and the last tile (S tail) need a mask.
             const int key0 = j * BN;
-            const bool mask_tail = key0 + BN > S;
-            const bool mask_diag = CAUSAL && (j == qt);
+            if ((CAUSAL && j == qt) || key0 + BN > S) {
+                const int lim = min(CAUSAL && j == qt ? row : BN - 1, S - 1 - key0);
+#pragma unroll
+                for (int c = 0; c < BN; ++c)
+                    if (c > lim) s[c] = -INFINITY;
+            }
+            // Row max of the raw scores (scale > 0 commutes with max); NaN propagates.
             float rmax = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                float v = s[c] * scale_log2;
-                if ((mask_tail && key0 + c >= S) || (mask_diag && c > row)) v = -INFINITY;
-                s[c] = v;
-                rmax = nan_max(rmax, v);
-            }
-            const float m_new = nan_max(m, rmax);
+            for (int c = 0; c < BN; ++c) rmax = fmax_nan(rmax, s[c]);
+            const float m_new = fmax_nan(m, rmax * scale_log2);
             const bool need = !(m_new <= m + 8.0f);
             if (j > 0) {
                 if (!sm100::mbar_wait(&bars->pv_done, (j - 1) & 1, status, 38)) {
@@ -241,7 +256,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     break;
                 }
                 sm100::tc_fence_after();
-                const float alpha = need ? exp2f(m - m_new) : 1.0f;
+                const float alpha = need ? ex2_approx(m - m_new) : 1.0f;
                 if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
@@ -257,14 +272,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (need) l *= alpha;
             }
             if (need) m = m_new;
-            float rsum = 0.f;
+            // p = 2^(s * scale * log2(e) - m): one FFMA + one MUFU.EX2 per score.
+            const float neg_m = -m;
+            float rsum0 = 0.f, rsum1 = 0.f;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                const float p = exp2f(s[c] - m);
-                s[c] = p;
-                rsum += p;
+            for (int c = 0; c < BN; c += 2) {
+                const float p0 = ex2_approx(fmaf(s[c], scale_log2, neg_m));
+                const float p1 = ex2_approx(fmaf(s[c + 1], scale_log2, neg_m));
+                s[c] = p0;
+                s[c + 1] = p1;
+                rsum0 += p0;
+                rsum1 += p1;
             }
-            l += rsum;
+            l += rsum0 + rsum1;
             // P row -> K-major swizzled tiles: keys 0..63 in box 0, 64..127 in box 1.
 #pragma unroll
             for (int cc = 0; cc < BN / 8; ++cc) {

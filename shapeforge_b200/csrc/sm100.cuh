@@ -69,17 +69,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase of `bar` with parity `parity` to complete.  Gives up after `limit_ns`
-// nanoseconds of wall time (checked every 256 polls), records the timeout in `st` and returns
-// false.  A kernel that sees false stops issuing work and goes to its teardown.
+// try_wait with a suspend-time hint: a thread whose phase is not complete is suspended in
+// hardware (issuing nothing) until the phase completes or about `hint_ns` pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred P;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n"
+        "selp.u32 %0, 1, 0, P;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase of `bar` with parity `parity` to complete.  Waiting threads are suspended
+// (no issue slots taken from the warps doing math on the same scheduler).  Gives up after
+// `limit_ns` nanoseconds of wall time, records the timeout in `st` and returns false.  A kernel
+// that sees false stops issuing work and goes to its teardown.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, KernelStatus* st, uint32_t where,
                                           uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     uint32_t polls = 0;
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((++polls & 255u) == 0) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((++polls & 15u) == 0) {
             if (st && *reinterpret_cast<volatile unsigned int*>(&st->code) != 0) return false;  // another role gave up
             if (globaltimer_ns() - t0 > limit_ns) {
                 if (st) {
