@@ -142,6 +142,27 @@ SF_API int sf_flash_attention(const void* q, const void* k, const void* v, void*
                int64_t D, float scale, int32_t causal, int32_t dtype, void* stream, char* err, uint64_t cap);
 
 /*
+ * varlen_kda (tasks/varlen_kda/reference.py:323-374): packed-varlen Kimi Delta Attention forward.
+ * q, k, v, g [T, H, D] and beta [T, H] in dtype; A_log [H], dt_bias [H*D], initial_state and
+ * final_state [num_seqs, H, D, D] (V-first), scale [1] fp32; cu_seqlens [num_seqs + 1] int32
+ * (negative entries = capacity sentinel: those sequences are skipped and left untouched).
+ * lower_bound is the LOWER_BOUND attr.  D in {8, 16, 32, 64, 128}.
+ */
+SF_API int sf_varlen_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+               const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* output,
+               void* final_state, int64_t num_seqs, int64_t H, int64_t D, float lower_bound, int32_t dtype, void* stream,
+               char* err, uint64_t cap);
+
+/*
+ * varlen_kda_gated (the gated workload): same recurrence with q, k already L2-normalised, g the
+ * fp32 log-decay [T, H, D] used directly, beta the fp32 gate [T, H] used directly, q times
+ * `scale`, state starting at zero when initial_state is NULL.
+ */
+SF_API int sf_varlen_kda_gated(const void* q, const void* k, const void* v, const void* g, const void* beta,
+               const void* cu_seqlens, const void* initial_state, void* output, void* final_state, int64_t num_seqs,
+               int64_t H, int64_t D, float scale, int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
  * gemm_nt: C[M,N] = A[M,K] . B[N,K]^T, fp16 or bf16 in, fp32 accumulation, one rounding
  * (the dense-gemm workload; the oracle is tasks/gemm/reference.py:110-114 applied to B^T).
  * tcgen05/TMEM/TMA kernel when the bases are 16-byte aligned and K % 8 == 0, else the general
@@ -199,6 +220,8 @@ SF_API int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char*
 #define SF_OP_BITDELTA 9
 #define SF_OP_BITDELTA_BASE 10
 #define SF_OP_ATTENTION 11
+#define SF_OP_KDA 12
+#define SF_OP_KDA_GATED 13
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -226,6 +249,10 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_BITDELTA  dims = {M, N, K}               attrs = {scale}     args = {x, bits, y}
  *   SF_OP_BITDELTA_BASE dims = {M, N, K}                               args = {x, w_base, s_words, alpha, y}
  *   SF_OP_ATTENTION dims = {B, H, S, D}  attrs = {scale}  flags bit 0 = causal  args = {q, k, v, o}
+ *   SF_OP_KDA       dims = {num_seqs, H, D}  attrs = {lower_bound}
+ *                   args = {q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state}
+ *   SF_OP_KDA_GATED dims = {num_seqs, H, D}  attrs = {scale}
+ *                   args = {q, k, v, g, beta, cu_seqlens, initial_state (may be NULL), output, final_state}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

@@ -257,3 +257,59 @@ def attention_bench_inputs(shape, dtype: str, seed: int = SEARCH_SEED) -> dict[s
     """Timing inputs of the causal attention workload: q, k, v ~ N(0, 1)."""
     g = generator(seed)
     return {name: round_to(torch.randn(shape, generator=g), dtype) for name in ("q", "k", "v")}
+
+
+# ---- varlen KDA -------------------------------------------------------------------------------
+
+
+def cu_from_lengths(lengths) -> torch.Tensor:
+    offs = [0]
+    for n in lengths:
+        offs.append(offs[-1] + int(n))
+    return torch.tensor(offs, dtype=torch.int32)
+
+
+def kda_gated_lengths(seed: int = SEARCH_SEED, num_seqs: int = 8, lo: int = 256, hi: int = 4096) -> list[int]:
+    """The workload's packed sequence lengths: seeded U(lo, hi) integers."""
+    g = generator(seed)
+    return [int(x) for x in torch.randint(lo, hi + 1, (num_seqs,), generator=g)]
+
+
+def kda_gated_inputs(lengths, heads: int, dim: int, dtype: str, seed: int = SEARCH_SEED) -> dict[str, torch.Tensor]:
+    """The gated KDA workload: q, k ~ N(0,1) then L2-normalised per head (in fp32, then rounded),
+    v ~ N(0,1), beta = sigmoid(N(0,1)) fp32 [T,H], g = logsigmoid(N(0,1)) fp32 [T,H,D]."""
+    g = generator(seed + 1)
+    t = int(sum(lengths))
+    q = torch.randn((t, heads, dim), generator=g)
+    k = torch.randn((t, heads, dim), generator=g)
+    v = torch.randn((t, heads, dim), generator=g)
+    q = q / q.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    k = k / k.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    beta = torch.sigmoid(torch.randn((t, heads), generator=g))
+    gl = torch.nn.functional.logsigmoid(torch.randn((t, heads, dim), generator=g))
+    return {"q": round_to(q, dtype), "k": round_to(k, dtype), "v": round_to(v, dtype), "g": gl.float(), "beta": beta.float(),
+            "cu_seqlens": cu_from_lengths(lengths)}
+
+
+def kda_task_inputs(lengths, heads: int, dim: int, dtype: str, seed: int) -> dict[str, torch.Tensor]:
+    """Task-contract KDA inputs with the distributions of tasks/varlen_kda/reference.py:420-446
+    (0.5 N(0,1) q/k/v/g/beta, A_log = log U(1,16), dt_bias from dt ~ logU(1e-3, 1e-1), a distinct
+    non-zero initial state per sequence, scale = 1/sqrt(D))."""
+    gen = generator(seed)
+    t = int(sum(lengths))
+    n = len(lengths)
+    rn = lambda shape, s=0.5: torch.randn(shape, generator=gen) * s  # noqa: E731
+    a_log = torch.log(torch.empty(heads).uniform_(1.0, 16.0, generator=gen))
+    lo, hi = math.log(0.001), math.log(0.1)
+    dt = torch.exp(torch.rand(heads * dim, generator=gen) * (hi - lo) + lo).clamp_(min=1e-4)
+    dt_bias = dt + torch.log(-torch.expm1(-dt))
+    q, k, v, gg = (rn((t, heads, dim)) for _ in range(4))
+    beta = rn((t, heads))
+    s0 = rn((n, heads, dim, dim), 0.25)
+    for s in range(n):
+        s0[s].diagonal(dim1=-2, dim2=-1).add_(0.5 + 0.25 * s)
+    return {
+        "q": round_to(q, dtype), "k": round_to(k, dtype), "v": round_to(v, dtype), "g": round_to(gg, dtype),
+        "beta": round_to(beta, dtype), "A_log": a_log.float(), "dt_bias": dt_bias.float(), "initial_state": s0.float(),
+        "cu_seqlens": cu_from_lengths(lengths), "scale": torch.tensor([1.0 / math.sqrt(dim)], dtype=torch.float32),
+    }

@@ -1,0 +1,256 @@
+// Packed-varlen Kimi Delta Attention (gated delta rule) forward for sm_100a.
+//
+// Per sequence s (tokens [cu[s], cu[s+1])) and head h, with an fp32 state S [Dv, Dk] (V-first):
+//   S <- S * diag(exp(ld_t))                      (decay along the key axis)
+//   r  = (v_t - S k_t) * b_t                      (delta residual)
+//   S <- S + r k_t^T
+//   o_t = S q_t
+// Task contract (tasks/varlen_kda/reference.py:323-374): q, k are L2-normalised in-op
+// (rsqrt(sum x^2 + 1e-6)), q times `scale`; ld = LOWER_BOUND * sigmoid(exp(A_log[h]) * (g + dt_bias));
+// b = sigmoid(beta); S starts from initial_state[s]; final_state[s] = S at the segment end.
+// Gated workload: q, k arrive normalised, g is the fp32 log-decay used directly, beta is already
+// a gate in (0,1), q times `scale`, S starts at zero (or a given initial state).
+//
+// Parallel structure: the recurrence never mixes state rows (each row v evolves from k, q, ld, b
+// and v_t[v] alone), so a (sequence, head) chain is split over CTAs of 16 state rows each.  A
+// CTA has 128 threads: 8 per row, each holding D/8 key columns of the row in registers (thread
+// part p owns columns p, p+8, ..., so staged rows are read without bank conflicts); per token
+// the row dot products S.k and S.q are 3-shuffle reductions over those 8 threads.  Tokens are
+// staged 16 at a time in shared memory (normalised q/k, exp(ld), b, this CTA's v slice) by all
+// threads, then consumed sequentially; outputs are staged and written 16 tokens at a time.
+// Sentinel offsets (cu < 0, the L2 capacity padding) end the sequence list: such sequences and
+// their final_state rows are left untouched.
+#include "sf_common.cuh"
+
+namespace {
+
+constexpr int VR = 16;       // state rows per CTA
+constexpr int TPR = 8;       // threads per row
+constexpr int TS = 16;       // tokens staged per group
+constexpr int NT = VR * TPR; // 128 threads
+
+template <typename T, int D, bool TASK>
+__global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                                                     const void* __restrict__ g_, const void* __restrict__ beta_,
+                                                     const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                                     const float* __restrict__ state0, const int32_t* __restrict__ cu,
+                                                     const float* __restrict__ scale_ptr, float scale_val, float lower_bound, int H,
+                                                     T* __restrict__ out, float* __restrict__ final_state) {
+    constexpr int CPT = D / TPR;  // key columns per thread
+    __shared__ float ks[TS][D];
+    __shared__ float qs[TS][D];
+    __shared__ float es[TS][D];
+    __shared__ float bs[TS];
+    __shared__ float vs[TS][VR];
+    __shared__ float os[TS][VR];
+
+    const int chain = blockIdx.x;  // s * H + h
+    const int s = chain / H, h = chain % H;
+    const int v0 = blockIdx.y * VR;
+    const int tid = threadIdx.x;
+    const int row = tid / TPR;  // local state row
+    const int part = tid % TPR;  // owns key columns part, part + 8, part + 16, ...
+    const int vrow = v0 + row;
+    const bool row_live = vrow < D;
+
+    const int begin = cu[s];
+    const int end = cu[s + 1];
+    if (begin < 0 || end < 0 || end < begin) return;  // sentinel: not part of this batch
+
+    const float scale = scale_ptr ? scale_ptr[0] : scale_val;
+    float st[CPT];
+    const size_t sbase = (((size_t)s * H + h) * D + (row_live ? vrow : 0)) * D + part;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) st[c] = (state0 && row_live) ? state0[sbase + (size_t)c * TPR] : 0.f;
+
+    // Staging layout: thread = (token tt = tid / 8, lane-part p = tid % 8) covering D/8 columns.
+    const int stt = tid / TPR;
+    const int sp = tid % TPR;
+    float decay_scale = 0.f;
+    if (TASK) decay_scale = __expf(a_log[h]);
+
+    for (int t0 = begin; t0 < end; t0 += TS) {
+        const int nt = min(TS, end - t0);
+        __syncthreads();  // previous group fully consumed
+        {
+            const int t = t0 + stt;
+            const bool live = stt < nt;
+            float qv[CPT], kv[CPT];
+            float qq = 0.f, kk = 0.f;
+            const size_t base = ((size_t)t * H + h) * D + sp;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                qv[c] = live ? sf::Dt<T>::to_f(q[base + (size_t)c * TPR]) : 0.f;
+                kv[c] = live ? sf::Dt<T>::to_f(k[base + (size_t)c * TPR]) : 0.f;
+                qq = fmaf(qv[c], qv[c], qq);
+                kk = fmaf(kv[c], kv[c], kk);
+            }
+            float qn = scale, kn = 1.f;
+            if (TASK) {
+#pragma unroll
+                for (int o = 1; o < TPR; o <<= 1) {
+                    qq += __shfl_xor_sync(0xffffffffu, qq, o);
+                    kk += __shfl_xor_sync(0xffffffffu, kk, o);
+                }
+                qn = rsqrtf(qq + 1e-6f) * scale;
+                kn = rsqrtf(kk + 1e-6f);
+            }
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                const int col = sp + c * TPR;
+                qs[stt][col] = qv[c] * qn;
+                ks[stt][col] = kv[c] * kn;
+                float e = 1.f;
+                if (live) {
+                    if (TASK) {
+                        const float gv = sf::Dt<T>::to_f(reinterpret_cast<const T*>(g_)[base + (size_t)c * TPR]);
+                        const float z = decay_scale * (gv + dt_bias[h * D + col]);
+                        const float ld = lower_bound / (1.f + __expf(-z));
+                        e = __expf(ld);
+                    } else {
+                        e = __expf(reinterpret_cast<const float*>(g_)[base + (size_t)c * TPR]);
+                    }
+                }
+                es[stt][col] = e;
+            }
+            if (sp == 0) {
+                float b = 0.f;
+                if (live) {
+                    if (TASK) {
+                        const float bv = sf::Dt<T>::to_f(reinterpret_cast<const T*>(beta_)[(size_t)t * H + h]);
+                        b = 1.f / (1.f + __expf(-bv));
+                    } else {
+                        b = reinterpret_cast<const float*>(beta_)[(size_t)t * H + h];
+                    }
+                }
+                bs[stt] = b;
+            }
+            // v slice: VR rows of token stt, threads sp 0..7 cover VR columns (2 each).
+#pragma unroll
+            for (int i = 0; i < VR / TPR; ++i) {
+                const int r = sp * (VR / TPR) + i;
+                vs[stt][r] = (live && v0 + r < D) ? sf::Dt<T>::to_f(v[((size_t)t * H + h) * D + v0 + r]) : 0.f;
+            }
+        }
+        __syncthreads();
+        for (int tt = 0; tt < nt; ++tt) {
+            float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < CPT; c += 2) {
+                st[c] *= es[tt][part + c * TPR];
+                acc0 = fmaf(st[c], ks[tt][part + c * TPR], acc0);
+                if (c + 1 < CPT) {
+                    st[c + 1] *= es[tt][part + (c + 1) * TPR];
+                    acc1 = fmaf(st[c + 1], ks[tt][part + (c + 1) * TPR], acc1);
+                }
+            }
+            float acc = acc0 + acc1;
+#pragma unroll
+            for (int o = 1; o < TPR; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            const float r = (vs[tt][row] - acc) * bs[tt];
+            float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < CPT; c += 2) {
+                st[c] = fmaf(r, ks[tt][part + c * TPR], st[c]);
+                o0 = fmaf(st[c], qs[tt][part + c * TPR], o0);
+                if (c + 1 < CPT) {
+                    st[c + 1] = fmaf(r, ks[tt][part + (c + 1) * TPR], st[c + 1]);
+                    o1 = fmaf(st[c + 1], qs[tt][part + (c + 1) * TPR], o1);
+                }
+            }
+            float o = o0 + o1;
+#pragma unroll
+            for (int w = 1; w < TPR; w <<= 1) o += __shfl_xor_sync(0xffffffffu, o, w);
+            if (part == 0) os[tt][row] = o;
+        }
+        __syncthreads();
+        // Write the group's outputs: token-major, VR contiguous values per token.
+        for (int i = tid; i < nt * VR; i += NT) {
+            const int tt = i / VR, r = i % VR;
+            if (v0 + r < D) out[((size_t)(t0 + tt) * H + h) * D + v0 + r] = sf::Dt<T>::from_f(os[tt][r]);
+        }
+    }
+    if (row_live) {
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) final_state[sbase + (size_t)c * TPR] = st[c];
+    }
+}
+
+template <typename T, bool TASK>
+int launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* a_log, const float* dt_bias,
+             const float* state0, const int32_t* cu, const float* scale_ptr, float scale_val, float lower_bound, int64_t N, int64_t H,
+             int64_t D, void* out, float* final_state, cudaStream_t st, char* err, uint64_t cap) {
+    const dim3 grid((unsigned)(N * H), (unsigned)((D + VR - 1) / VR));
+#define SF_KDA_CASE(DD)                                                                                                        \
+    case DD:                                                                                                                   \
+        kda_fwd_kernel<T, DD, TASK><<<grid, NT, 0, st>>>((const T*)q, (const T*)k, (const T*)v, g, beta, a_log, dt_bias, state0, \
+                                                        cu, scale_ptr, scale_val, lower_bound, (int)H, (T*)out, final_state); \
+        break;
+    switch (D) {
+        SF_KDA_CASE(8)
+        SF_KDA_CASE(16)
+        SF_KDA_CASE(32)
+        SF_KDA_CASE(64)
+        SF_KDA_CASE(128)
+        default:
+            return sf::fail(SF_EINVAL, err, cap, "kda: head dim %lld is not one of 8/16/32/64/128", (long long)D);
+    }
+#undef SF_KDA_CASE
+    return sf::check_launch("kda launch", err, cap);
+}
+
+int check(int64_t N, int64_t H, int64_t D, int32_t dtype, char* err, uint64_t cap) {
+    if (N < 0 || H < 1 || D < 1) return sf::fail(SF_EINVAL, err, cap, "kda: need num_seqs >= 0, H >= 1, D >= 1");
+    if (dtype != SF_DTYPE_F16 && dtype != SF_DTYPE_BF16) return sf::fail(SF_EINVAL, err, cap, "kda: dtype %d is not fp16/bf16", dtype);
+    if (N * H > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "kda: too many chains");
+    return SF_OK;
+}
+
+}  // namespace
+
+int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log, const void* dt_bias,
+                  const void* initial_state, const void* cu_seqlens, const void* scale, void* out, void* final_state, int64_t N,
+                  int64_t H, int64_t D, float lower_bound, int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
+    int rc = check(N, H, D, dtype, err, cap);
+    if (rc) return rc;
+    if (N == 0) return SF_OK;
+    if (!q || !k || !v || !g || !beta || !a_log || !dt_bias || !initial_state || !cu_seqlens || !scale || !out || !final_state)
+        return sf::fail(SF_EINVAL, err, cap, "kda: null tensor pointer");
+    if (dtype == SF_DTYPE_F16)
+        return launch_t<__half, true>(q, k, v, g, beta, (const float*)a_log, (const float*)dt_bias, (const float*)initial_state,
+                                      (const int32_t*)cu_seqlens, (const float*)scale, 0.f, lower_bound, N, H, D, out,
+                                      (float*)final_state, st, err, cap);
+    return launch_t<__nv_bfloat16, true>(q, k, v, g, beta, (const float*)a_log, (const float*)dt_bias, (const float*)initial_state,
+                                         (const int32_t*)cu_seqlens, (const float*)scale, 0.f, lower_bound, N, H, D, out,
+                                         (float*)final_state, st, err, cap);
+}
+
+int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                        const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
+                        int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
+    int rc = check(N, H, D, dtype, err, cap);
+    if (rc) return rc;
+    if (N == 0) return SF_OK;
+    if (!q || !k || !v || !g || !beta || !cu_seqlens || !out || !final_state)
+        return sf::fail(SF_EINVAL, err, cap, "kda_gated: null tensor pointer");
+    if (dtype == SF_DTYPE_F16)
+        return launch_t<__half, false>(q, k, v, g, beta, nullptr, nullptr, (const float*)initial_state, (const int32_t*)cu_seqlens,
+                                       nullptr, scale, 0.f, N, H, D, out, (float*)final_state, st, err, cap);
+    return launch_t<__nv_bfloat16, false>(q, k, v, g, beta, nullptr, nullptr, (const float*)initial_state, (const int32_t*)cu_seqlens,
+                                          nullptr, scale, 0.f, N, H, D, out, (float*)final_state, st, err, cap);
+}
+
+extern "C" int sf_varlen_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                             const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* output,
+                             void* final_state, int64_t num_seqs, int64_t H, int64_t D, float lower_bound, int32_t dtype, void* stream,
+                             char* err, uint64_t cap) {
+    return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state, num_seqs, H, D,
+                         lower_bound, dtype, (cudaStream_t)stream, err, cap);
+}
+
+extern "C" int sf_varlen_kda_gated(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                                   const void* initial_state, void* output, void* final_state, int64_t num_seqs, int64_t H, int64_t D,
+                                   float scale, int32_t dtype, void* stream, char* err, uint64_t cap) {
+    return sf_kda_gated_launch(q, k, v, g, beta, cu_seqlens, initial_state, output, final_state, num_seqs, H, D, scale, dtype,
+                               (cudaStream_t)stream, err, cap);
+}

@@ -225,3 +225,44 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     _run("flash_attention", q, [q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()], dims=(b, h, s, d), attrs=(scale,),
          variant=variant, flags=1 if causal else 0)
     return out
+
+
+def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, lower_bound: float = -5.0,
+               output: torch.Tensor | None = None, final_state: torch.Tensor | None = None):
+    """Packed-varlen KDA forward (tasks/varlen_kda/reference.py:323-374).  ``scale`` is the
+    task's one-element fp32 tensor; returns ``(output [T,H,D], final_state [N,H,D,D])``."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
+        _check(t, name, q.dtype)
+    for name, t in (("A_log", a_log), ("dt_bias", dt_bias), ("initial_state", initial_state), ("scale", scale)):
+        _check(t, name, torch.float32)
+    _check(cu_seqlens, "cu_seqlens", torch.int32)
+    t_, h, d = q.shape
+    n = cu_seqlens.numel() - 1
+    output = torch.empty_like(v) if output is None else output
+    final_state = torch.empty((n, h, d, d), dtype=torch.float32, device=q.device) if final_state is None else final_state
+    ptrs = [x.data_ptr() for x in (q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state)]
+    _run("varlen_kda", q, ptrs, dims=(n, h, d), attrs=(lower_bound,))
+    return output, final_state
+
+
+def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: torch.Tensor | None = None,
+                     output: torch.Tensor | None = None, final_state: torch.Tensor | None = None):
+    """Gated KDA workload: q, k pre-normalised, ``g`` fp32 log-decay used directly, ``beta`` fp32
+    gate used directly, state from zero (or ``initial_state``)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check(t, name, q.dtype)
+    _check(g, "g", torch.float32)
+    _check(beta, "beta", torch.float32)
+    _check(cu_seqlens, "cu_seqlens", torch.int32)
+    t_, h, d = q.shape
+    n = cu_seqlens.numel() - 1
+    output = torch.empty_like(v) if output is None else output
+    final_state = torch.empty((n, h, d, d), dtype=torch.float32, device=q.device) if final_state is None else final_state
+    s0 = 0
+    if initial_state is not None:
+        _check(initial_state, "initial_state", torch.float32)
+        s0 = initial_state.data_ptr()
+    ptrs = [q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), cu_seqlens.data_ptr(), s0,
+            output.data_ptr(), final_state.data_ptr()]
+    _run("varlen_kda_gated", q, ptrs, dims=(n, h, d), attrs=(scale,))
+    return output, final_state

@@ -1,0 +1,146 @@
+"""varlen_kda (task contract) and varlen_kda_gated (the gated workload) on the B200.
+
+Tolerances: tasks/varlen_kda/opspec.json numerics — fp16 rtol 1e-2 / atol_rel 5e-3, bf16 rtol
+3e-2 / atol_rel 1.5e-2 — for both the output and the final state, scaled by the RMS of each
+finite reference.  Heads are independent chains, so large shapes are checked on a few heads.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle import ops as oref
+from shapeforge_b200 import cases, compare, ops
+from tests import golden
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp16": dict(rtol=1e-2, atol_rel=5e-3), "bf16": dict(rtol=3e-2, atol_rel=1.5e-2)}
+TD = {"fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _np(t):
+    return t.detach().cpu().to(torch.float64).numpy()
+
+
+def _from_fixture(arr, dtype_name, dev):
+    a = np.ascontiguousarray(arr)
+    if dtype_name in ("fp16", "bf16"):
+        return torch.from_numpy(a.view(np.int16)).view(TD[dtype_name]).to(dev)
+    if dtype_name == "fp32":
+        return torch.from_numpy(a.astype(np.float32)).to(dev)
+    return torch.from_numpy(a.astype(np.int32)).to(dev)
+
+
+def _verdict(got, ref, dtype, out_dtype):
+    return compare.check(got, ref, compare.rms_scale(ref), dtype=out_dtype, **TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("tier", ["mixed", "fixed", "uniform"])
+def test_reference_vectors(cuda_device, tier, dtype):
+    """All 9 correctness cases of the reference's own varlen planner, on its own input bytes."""
+    doc = golden.load(f"ref_varlen_kda_{tier}_{dtype}")
+    tdt = doc["tensor_dtypes"]
+    assert len(doc["records"]) == 9
+    for rec in doc["records"]:
+        d = {k: _from_fixture(v, tdt[k], cuda_device) for k, v in rec["inputs"].items()}
+        out, fin = ops.varlen_kda(d["q"], d["k"], d["v"], d["g"], d["beta"], d["A_log"], d["dt_bias"], d["initial_state"],
+                                  d["cu_seqlens"], d["scale"], lower_bound=-5.0)
+        torch.cuda.synchronize()
+        v1 = _verdict(_np(out), rec["refs"]["output"], dtype, dtype)
+        v2 = _verdict(_np(fin), rec["refs"]["final_state"], dtype, "fp32")
+        assert v1.ok, (tier, rec["case"], "output", v1.summary())
+        assert v2.ok, (tier, rec["case"], "final_state", v2.summary())
+
+
+def _oracle_task(inp, heads):
+    f = lambda n: _np(inp[n])  # noqa: E731
+    sel = lambda a: a[:, heads]  # noqa: E731
+    out, fin = oref.varlen_kda(
+        sel(f("q")), sel(f("k")), sel(f("v")), sel(f("g")), sel(f("beta")), f("A_log")[heads],
+        f("dt_bias").reshape(-1, inp["q"].shape[2])[heads].reshape(-1), f("initial_state")[:, heads],
+        inp["cu_seqlens"].cpu().numpy(), float(f("scale")[0]), -5.0)
+    return out, fin
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("dim", [128, 64, 32])
+def test_task_op_large_heads(cuda_device, dtype, dim):
+    lengths = [130, 64, 1, 300, 0, 17]
+    heads = 4
+    inp = cases.kda_task_inputs(lengths, heads, dim, dtype, seed=cases.case_seed(0, 3))
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    out = torch.full_like(d["v"], float("nan"))
+    out, fin = ops.varlen_kda(d["q"], d["k"], d["v"], d["g"], d["beta"], d["A_log"], d["dt_bias"], d["initial_state"],
+                              d["cu_seqlens"], d["scale"], output=out)
+    torch.cuda.synchronize()
+    hs = [0, heads - 1]
+    ro, rf = _oracle_task(d, hs)
+    v1 = _verdict(_np(out)[:, hs], ro, dtype, dtype)
+    v2 = _verdict(_np(fin)[:, hs], rf, dtype, "fp32")
+    assert v1.ok, ("output", v1.summary())
+    assert v2.ok, ("final_state", v2.summary())
+
+
+def test_capacity_sentinel_leaves_padding(cuda_device):
+    """cu_seqlens entries of -1 (the L2 capacity sentinel) end the batch: unused final-state rows
+    and output rows past the resolved total keep their padding bytes."""
+    lengths = [5, 3, 1]
+    inp = cases.kda_task_inputs(lengths, 2, 8, "fp16", seed=11)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    cap_seqs, cap_tokens = 4, 16
+    cu = torch.tensor([0, 5, 8, 9, -1], dtype=torch.int32, device=cuda_device)
+    pad = lambda t, n: torch.cat([t, torch.zeros((n - t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)])  # noqa: E731
+    q, k, v, g = (pad(d[n], cap_tokens) for n in ("q", "k", "v", "g"))
+    beta = pad(d["beta"], cap_tokens)
+    s0 = torch.cat([d["initial_state"], torch.zeros((1, 2, 8, 8), device=cuda_device)])
+    out = torch.full((cap_tokens, 2, 8), 7.0, dtype=torch.float16, device=cuda_device)
+    fin = torch.full((cap_seqs, 2, 8, 8), 7.0, dtype=torch.float32, device=cuda_device)
+    ops.varlen_kda(q, k, v, g, beta, d["A_log"], d["dt_bias"], s0, cu, d["scale"], output=out, final_state=fin)
+    torch.cuda.synchronize()
+    assert torch.all(out[9:] == 7.0)
+    assert torch.all(fin[3] == 7.0)
+    ro, rf = _oracle_task(d, [0, 1])
+    assert _verdict(_np(out[:9]), ro, "fp16", "fp16").ok
+    assert _verdict(_np(fin[:3]), rf, "fp16", "fp32").ok
+
+
+def _oracle_gated(inp, heads, scale):
+    f = lambda n: _np(inp[n])[:, heads]  # noqa: E731
+    return oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), inp["cu_seqlens"].cpu().numpy(), scale)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_gated_workload(cuda_device, dtype):
+    """The gated workload: 8 packed sequences of seeded U(256, 4096) lengths, H=16, D=128."""
+    lengths = cases.kda_gated_lengths()
+    heads, dim = 16, 128
+    inp = cases.kda_gated_inputs(lengths, heads, dim, dtype)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    scale = 1.0 / math.sqrt(dim)
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], scale)
+    torch.cuda.synchronize()
+    hs = [0, 9, 15]
+    ro, rf = _oracle_gated(d, hs, scale)
+    v1 = _verdict(_np(out)[:, hs], ro, dtype, dtype)
+    v2 = _verdict(_np(fin)[:, hs], rf, dtype, "fp32")
+    assert v1.ok, ("output", v1.summary())
+    assert v2.ok, ("final_state", v2.summary())
+    assert not torch.isnan(out).any()
+
+
+def test_gated_small_ragged(cuda_device):
+    lengths = [1, 0, 63, 64, 65, 200]
+    inp = cases.kda_gated_inputs(lengths, 3, 64, "bf16", seed=3)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125)
+    torch.cuda.synchronize()
+    ro, rf = _oracle_gated(d, [0, 1, 2], 0.125)
+    assert _verdict(_np(out), ro, "bf16", "bf16").ok
+    assert _verdict(_np(fin), rf, "bf16", "fp32").ok
