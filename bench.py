@@ -272,7 +272,173 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
     )
 
 
+def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_inputs, in_names, out_specs, dims, attrs=(), flags=0,
+                 cpu_rows=None, total_rows=1, null_args=()) -> Workload:
+    """A workload over one C-ABI operator: ``make_inputs(seed)`` gives CPU tensors named
+    ``in_names`` (ABI order, followed by the outputs ``out_specs`` = [(shape, dtype)]);
+    ``null_args`` are ABI positions passed as NULL (optional tensors)."""
+    import numpy as np
+    import torch
+
+    from shapeforge_b200 import _native
+
+    sample = make_inputs(cases_seed())
+    per_set = sum(t.numel() * t.element_size() for t in sample.values()) + sum(
+        int(np.prod(s)) * torch.tensor([], dtype=dt).element_size() for s, dt in out_specs)
+    nsets = max(2, int(np.ceil(2 * L2_BYTES / per_set)))
+
+    def ptr_list(ins, outs):
+        ptrs = [ins[n].data_ptr() for n in in_names] + [o.data_ptr() for o in outs]
+        for pos in null_args:
+            ptrs.insert(pos, 0)
+        return ptrs
+
+    def make_sets(dev, count):
+        out = []
+        for s in range(count):
+            ins = {k: v.to(dev) for k, v in make_inputs(cases_seed() + s).items()}
+            outs = [torch.empty(shape, dtype=dt, device=dev) for shape, dt in out_specs]
+            out.append(((ins, outs), ptr_list(ins, outs)))
+        return out
+
+    def desc():
+        return _native.op_desc(op, dtype, dims=dims, attrs=attrs, flags=flags)
+
+    def host_inputs():
+        ins = make_inputs(cases_seed())
+        return [ins[n].pin_memory() for n in in_names], list(out_specs)
+
+    def e2e_step(h_in, d_in, d_out, h_out, stream):
+        for d, h in zip(d_in, h_in):
+            d.copy_(h, non_blocking=True)
+        ptrs = [t.data_ptr() for t in d_in] + [o.data_ptr() for o in d_out]
+        for pos in null_args:
+            ptrs.insert(pos, 0)
+        _native.run_op(desc(), ptrs, stream)
+        for h, d in zip(h_out, d_out):
+            h.copy_(d, non_blocking=True)
+
+    return Workload(name=name, unit=unit, bound=bound, dtype=dtype, units_per_step=units,
+                    config=dict(config, l2=f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB"),
+                    kernel=kernel, make_sets=make_sets, desc=desc, host_inputs=host_inputs, e2e_step=e2e_step,
+                    cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets)
+
+
+def cases_seed() -> int:
+    from shapeforge_b200 import cases
+
+    return cases.SEARCH_SEED
+
+
+def _attention_workload(b: int, h: int, s: int, d: int, causal: bool = True, dtype: str = "bf16") -> Workload:
+    import math
+
+    import torch
+
+    from shapeforge_b200 import cases
+
+    scale = 1.0 / math.sqrt(d)
+    flops = 4.0 * b * h * d * (s * (s + 1) / 2 if causal else s * s)
+
+    def make_inputs(seed):
+        return cases.attention_bench_inputs((b, h, s, d), dtype, seed=seed)
+
+    def cpu_rows(rows):
+        # The reference's algorithm (tasks/flash_attention/reference.py:113-119 with the causal
+        # mask) through the oracle port, on the last `rows` query rows of one head.
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        q = inp["q"][:1, :1].float().numpy()
+        k = inp["k"][:1, :1].float().numpy()
+        v = inp["v"][:1, :1].float().numpy()
+        sel = list(range(s - rows, s))
+        fl = sum(4.0 * d * ((i + 1) if causal else s) for i in sel)
+        return (lambda: oref.attention_rows(q, k, v, scale, causal, sel)), fl, f"fp64 attention of {rows} query rows x one head"
+
+    return _op_workload(
+        f"attention_{'causal' if causal else 'full'}_{b}x{h}x{s}x{d}", "TFLOP/s", "tensor", dtype, flops,
+        {"workload": f"flash attention forward {'causal' if causal else 'non-causal'}, q/k/v {dtype} [{b},{h},{s},{d}] ~ N(0,1), "
+                     f"scale 1/sqrt({d}), fp32 softmax statistics", "shape": [b, h, s, d]},
+        "fa_fwd_kernel", "flash_attention", make_inputs, ["q", "k", "v"], [((b, h, s, d), cases.TORCH_DTYPE[dtype])],
+        (b, h, s, d), (scale,), 1 if causal else 0, cpu_rows=cpu_rows, total_rows=s)
+
+
+def _bitdelta_base_workload(m: int, n: int = 4096, k: int = 4096, dtype: str = "fp16") -> Workload:
+    import torch
+
+    from shapeforge_b200 import cases
+
+    nbytes = 2.0 * n * k + n * k / 8 + 2.0 * n + 2.0 * m * k + 2.0 * m * n
+
+    def make_inputs(seed):
+        return cases.bitdelta_base_inputs("normal", seed, m, n, k, dtype)
+
+    def cpu_rows(rows):
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        x = inp["x"][:1].double().numpy()
+        w = inp["w_base"][:rows].double().numpy()
+        sw = inp["s_words"][:rows].numpy()
+        a = inp["alpha"][:rows].double().numpy()
+        fb = 2.0 * rows * k + rows * k / 8 + 2.0 * rows
+        return (lambda: oref.bitdelta_gemm_base(x, w, sw, a)), fb, f"fp64 oracle over {rows} output columns (W_base rows)"
+
+    return _op_workload(
+        f"bitdelta_base_m{m}", "GB/s", "hbm", dtype, nbytes,
+        {"workload": f"bitdelta y = x.(W_base + diag(alpha) S)^T, x {dtype} [{m},{k}] ~ N(0,1), W_base {dtype} [{n},{k}] ~ N(0,0.02), "
+                     f"S Bernoulli(0.5) packed u32 [{n},{k // 32}], alpha {dtype} U(1e-3,1e-2)", "shape": [m, n, k]},
+        "bitdelta_base_kernel", "bitdelta_gemm_base", make_inputs, ["x", "w_base", "s_words", "alpha"],
+        [((m, n), cases.TORCH_DTYPE[dtype])], (m, n, k), cpu_rows=cpu_rows, total_rows=n)
+
+
+def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16") -> Workload:
+    import math
+
+    import torch
+
+    from shapeforge_b200 import cases
+
+    lengths = cases.kda_gated_lengths()
+    total = int(sum(lengths))
+    n = len(lengths)
+    nbytes = (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * heads * total + 4.0 * n * heads * dim * dim
+
+    def make_inputs(seed):
+        return cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed)
+
+    def cpu_rows(rows):
+        # The delta-rule recurrence (tasks/varlen_kda/reference.py:352-368, gate supplied) through
+        # the oracle port on the first `rows` tokens of one (sequence, head) chain.
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        t = min(rows, lengths[0])
+        f = lambda name: inp[name][:t, :1].double().numpy()  # noqa: E731
+        cu = [0, t]
+        return ((lambda: oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), cu, 1.0 / math.sqrt(dim))),
+                (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * float(t), f"fp64 recurrence over {t} tokens of one chain")
+
+    return _op_workload(
+        "kda_gated", "GB/s", "hbm", dtype, nbytes,
+        {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
+                     "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
+         "total_tokens": total},
+        "kda_fwd_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"],
+        [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim),
+        (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,))
+
+
 WORKLOADS = {
+    "attention_causal_4x32x2048x128": lambda: _attention_workload(4, 32, 2048, 128),
+    "attention_causal_4x32x512x128": lambda: _attention_workload(4, 32, 512, 128),
+    "attention_causal_4x32x8192x128": lambda: _attention_workload(4, 32, 8192, 128),
+    "attention_causal_4x32x2048x64": lambda: _attention_workload(4, 32, 2048, 64),
+    "bitdelta_base_m1": lambda: _bitdelta_base_workload(1),
+    "bitdelta_base_m16": lambda: _bitdelta_base_workload(16),
+    "bitdelta_base_m128": lambda: _bitdelta_base_workload(128),
+    "kda_gated": lambda: _kda_gated_workload(),
     "gemm_nt_4096": lambda: _gemm_nt_workload(4096, 4096, 4096),
     "gemm_nt_8192": lambda: _gemm_nt_workload(8192, 8192, 8192),
     "gemm_nt_512": lambda: _gemm_nt_workload(512, 512, 512),
@@ -413,13 +579,14 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
     _native.run_batch(desc, ptr_sets, args.warmup, sptr)
     torch.cuda.synchronize(dev)
 
-    # Timed: exactly K steps.  sf_run_batch enqueues the K launches from C (set i % nsets for
-    # launch i) between two CUDA events on this stream and synchronises; it returns the events'
-    # elapsed device time.
+    # Timed: exactly K steps.  sf_run_batch captures the K launches (set i % nsets for launch i)
+    # into one CUDA graph before the timed region, launches it between two CUDA events on this
+    # stream and synchronises; it returns the events' elapsed device time.  (--no-graph enqueues
+    # the launches one by one from C instead.)
     barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clocks:
-        el_s = _native.run_batch(desc, ptr_sets, args.steps, sptr)
+        el_s = _native.run_batch(desc, ptr_sets, args.steps, sptr, use_graph=not args.no_graph)
         torch.cuda.synchronize(dev)
     barrier()
     code, where = _native.kernel_status(sptr)
@@ -512,6 +679,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="enqueue the K timed launches one by one instead of as one captured CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
