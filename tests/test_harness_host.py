@@ -1,0 +1,222 @@
+"""Host-side harness logic (no GPU): fill plans, timing protocol, exact dispatch, accounts, the
+Backend protocol's text hooks, and the drop-in through the reference's own loaders."""
+
+from __future__ import annotations
+
+import math
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from shapeforge_b200 import compare, portfolio, protocol, runtime
+from shapeforge_b200.backend import CudaBackend, LaunchStage
+
+ROOT = Path(__file__).resolve().parents[1]
+REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+
+
+# ---- fill plans (tcenv/track/protocol.py:107-143) --------------------------------------------------
+
+def test_fill_plan_matches_reference_protocol():
+    import torch
+
+    specs = [runtime.TensorSpec("x", (4,), torch.float16, "input"), runtime.TensorSpec("y", (4,), torch.float16, "output"),
+             runtime.TensorSpec("ws", (8,), torch.float32, "workspace"), runtime.TensorSpec("st", (2,), torch.float32, "read_write")]
+    p1, p2, p3 = (runtime.fill_plan(specs, t) for t in runtime.TRIALS)
+    assert p1 == p3 == {"x": runtime.RESTORE, "y": runtime.POISON, "ws": runtime.POISON, "st": runtime.RESTORE}
+    assert p2 == {"x": runtime.RESTORE, "y": runtime.ZERO, "ws": runtime.ZERO, "st": runtime.RESTORE}
+    with pytest.raises(ValueError):
+        runtime.fill_plan(specs, "out4")
+    assert (runtime.GUARD_PATTERN, runtime.GUARD_BYTES, runtime.POISON_PATTERN) == (0xCD, 16384, 0xFF)
+
+
+def test_fill_plan_agrees_with_reference_module():
+    if not REF.is_dir():
+        pytest.skip("reference checkout not mounted")
+    sys.path.insert(0, str(REF))
+    from tcenv.track import protocol as ref_protocol
+
+    assert ref_protocol.GUARD_PATTERN == runtime.GUARD_PATTERN
+    assert ref_protocol.GUARD_BYTES == runtime.GUARD_BYTES
+    assert ref_protocol.POISON_PATTERN == runtime.POISON_PATTERN
+    assert tuple(ref_protocol.CORRECTNESS_TRIALS) == runtime.TRIALS
+
+
+# ---- comparator (testing.py:140-177) -----------------------------------------------------------------
+
+def test_scaled_error_specials_and_floor():
+    ref = np.array([1.0, np.nan, np.inf, -np.inf, 0.0])
+    ok = np.array([1.001, np.nan, np.inf, -np.inf, 0.0])
+    assert compare.check(ok, ref, 1.0, rtol=2e-3, atol_rel=1e-3, dtype="fp16").ok
+    for bad in ([1.0, 0.0, np.inf, -np.inf, 0.0], [1.0, np.nan, -np.inf, -np.inf, 0.0], [1.0, np.nan, np.inf, -np.inf, np.nan]):
+        assert not compare.check(np.array(bad), ref, 1.0, rtol=2e-3, atol_rel=1e-3, dtype="fp16").ok
+    # A non-finite scale fails everything; exact means bit equality.
+    assert not compare.check(ok, ref, np.nan, rtol=1, atol_rel=1).ok
+    assert np.isinf(compare.scaled_error(np.array([1, 2]), np.array([1, 3]), 0, 0, 0, True)).sum() == 1
+    assert compare.floor_for("fp16") == pytest.approx(0.51 * 2.0**-24)
+
+
+def test_comparator_agrees_with_reference():
+    if not REF.is_dir():
+        pytest.skip("reference checkout not mounted")
+    import torch
+
+    sys.path.insert(0, str(REF))
+    try:
+        from tcenv.backends.metal.testing import scaled_error as ref_scaled_error  # imports Metal
+    except Exception:
+        pytest.skip("the reference comparator module needs Metal (objc) to import")
+    rng = np.random.default_rng(0)
+    o, r = rng.normal(size=100), rng.normal(size=100)
+    ours = compare.scaled_error(o, r, 0.7, 2e-3, 1e-3, False, 1e-8)
+    theirs = ref_scaled_error(torch.tensor(o), torch.tensor(r), 0.7, 2e-3, 1e-3, False, 1e-8).numpy()
+    np.testing.assert_allclose(ours, theirs)
+
+
+# ---- timing protocol (tcenv/bench.py) ----------------------------------------------------------------
+
+def test_choose_iters_targets_batch_duration():
+    per = 1e-5
+    k = protocol.choose_iters(lambda k: k * per, target_s=0.015, kmin=4)
+    assert k in (1499, 1500)  # 0.015 / 1e-5 in floating point
+    assert protocol.choose_iters(lambda k: k * 0.5, target_s=0.015, kmin=4) == 3  # slow: bounded by the watchdog budget
+    assert protocol.choose_iters(lambda k: k * 1e-9, target_s=0.015, kmin=4, kmax=4000) == 4000
+
+
+def test_interleaved_and_attempt_selection():
+    calls = []
+
+    def runner(name, per):
+        def run_k(k):
+            calls.append(name)
+            return per * k
+        return run_k
+
+    noise, stats, attempts = protocol.measure_interleaved({"candidate": runner("c", 2e-6), "torch": runner("t", 3e-6)}, reps=5)
+    assert attempts == 1 and noise == 0.0
+    assert stats["candidate"].median_s == pytest.approx(2e-6)
+    assert stats["torch"].reps == 5
+    assert protocol.select_attempt([(0.2, "a"), (0.04, "b"), (0.01, "c")]) == (0.04, "b")
+    assert protocol.select_attempt([(0.2, "a"), (0.1, "b")]) == (0.1, "b")
+
+
+def test_protocol_agrees_with_reference_bench():
+    if not REF.is_dir():
+        pytest.skip("reference checkout not mounted")
+    sys.path.insert(0, str(REF))
+    from tcenv import bench as ref_bench
+
+    for per in (1e-7, 1e-5, 1e-3, 0.05, 0.3):
+        run = lambda k, per=per: k * per  # noqa: E731
+        assert protocol.choose_iters(run) == ref_bench.choose_iters(run)
+    assert ref_bench.QUIET_CV == protocol.QUIET_CV and ref_bench.BENCH_ATTEMPTS == protocol.BENCH_ATTEMPTS
+
+
+# ---- exact dispatch and accounts -----------------------------------------------------------------------
+
+def test_exact_dispatch_outcomes():
+    p = portfolio.gemm_nt_portfolio()
+    r = p.resolve({"M": 4096, "N": 4096, "K": 4096, "aligned": True})
+    assert (r.outcome, r.provider, r.variant) == ("candidate", "candidate", 1)
+    r = p.resolve({"M": 64, "N": 64, "K": 60, "aligned": True})
+    assert (r.outcome, r.provider, r.variant) == ("fallback", "fallback", 2)
+    assert r.detail == "outside_candidate_coverage"
+    assert p.resolve({"M": -1, "N": 4, "K": 8, "aligned": True}).outcome == "unsupported_contract_capability"
+    overlap = portfolio.Portfolio((portfolio.Variant("a", lambda n: True), portfolio.Variant("b", lambda n: True)))
+    assert overlap.resolve({}).outcome == "dispatch_overlap"
+    unknown = portfolio.Portfolio((portfolio.Variant("a", lambda n: n["missing"] > 0),), portfolio.Fallback("f"))
+    assert unknown.resolve({}).outcome == "dispatch_unknown"
+    assert portfolio.Portfolio((portfolio.Variant("a", lambda n: False),)).resolve({}).outcome == "dispatch_unmatched"
+
+
+def _m(key, provider, cand, base, **kw):
+    return portfolio.ShardMeasurement(key, key.split("/")[2], provider, cand, base, **kw)
+
+
+def test_accounts_specialized_and_effective():
+    rows = [_m("gemm/4096/benchmark", "candidate", 100.0, 120.0), _m("gemm/512/benchmark", "candidate", 8.0, 10.0),
+            _m("gemm/odd/benchmark", "fallback", 50.0, 50.0), _m("gemm/small/golden", "candidate", 1.0, 1.0)]
+    rep = portfolio.PerformanceReport.evaluate(rows)
+    assert rep.publishable
+    assert rep.specialized_hit_latency_ratio == pytest.approx(np.median([100 / 120, 8 / 10]))
+    assert rep.effective_end_to_end_latency_ratio == pytest.approx(158.0 / 180.0)
+    assert rep.fallback_count_fraction == pytest.approx(1 / 3)
+    assert rep.fallback_time_fraction == pytest.approx(50 / 158)
+    slow = portfolio.PerformanceReport.evaluate(rows + [_m("gemm/big/benchmark", "candidate", 120.0, 100.0)])
+    assert not slow.publishable and any("ratio>1.10" in f for f in slow.failure_reasons)
+    with pytest.raises(portfolio.ContractError):
+        _m("gemm/x/benchmark", "other", 1.0, 1.0)
+
+
+def test_accounts_agree_with_reference():
+    if not REF.is_dir():
+        pytest.skip("reference checkout not mounted")
+    sys.path.insert(0, str(REF))
+    from tcenv.portfolio_performance import performance as ref_perf
+
+    spec = [("t/a/benchmark", "candidate", 10.0, 12.0), ("t/b/benchmark", "fallback", 5.0, 4.8), ("t/c/benchmark", "candidate", 3.0, 3.3)]
+    ours = portfolio.PerformanceReport.evaluate([_m(*s) for s in spec])
+    theirs = ref_perf.PerformanceReport.evaluate([ref_perf.ShardMeasurement(k, k.split("/")[2], p, c, b) for k, p, c, b in spec])
+    for name in ("specialized_hit_speedup", "effective_end_to_end_speedup", "fallback_time_fraction", "fallback_count_fraction",
+                 "publishable"):
+        assert getattr(ours, name) == pytest.approx(getattr(theirs, name)), name
+
+
+# ---- Backend protocol text hooks --------------------------------------------------------------------
+
+def test_backend_text_hooks():
+    b = CudaBackend()
+    assert (b.id, b.version, b.file_ext, b.language) == ("cuda-sm100", "1", ".cu", "cuda")
+    src = 'extern "C" __global__ void k(const __half* x, __half* y) {}\n/* taic-launch\nkernel k grid=64,2 threads=256 smem=1024\n*/'
+    stages = b.parse_launch(src)
+    assert stages == [LaunchStage("k", (64, 2, 1), (256, 1, 1), 1024)]
+    assert b.validate_launch(stages, {"max_threads_per_threadgroup": 1024, "max_threadgroup_memory_bytes": 232448}) == []
+    assert b.validate_launch([LaunchStage("k", (1, 1, 1), (2048, 1, 1))], {}) != []
+    assert b.screen(src) == []
+    assert b.screen(src + "\nvoid f(){ __trap(); }")
+    assert b.device_matches({"match_name_contains": "B200"}, {"name": "NVIDIA B200", "cc_major": 10})
+    assert not b.device_matches({"match_name_contains": "B200"}, {"name": "NVIDIA H100", "cc_major": 9})
+    cal = b.calibration("b200")
+    roof = b.roofline({"min_bytes": 67117056, "flops": 4 * 4096 * 4096, "dtype": "fp16"}, 12.8e-6, cal)
+    assert roof["bound"] == "memory"
+    assert roof["bandwidth_fraction"] == pytest.approx(67117056 / 12.8e-6 / (cal["copy_gbs"] * 1e9))
+    assert "const __half* __restrict__ x" in b.abi_stub({"tensors": [{"name": "x", "dtype": "fp16", "access": "read"}]})
+
+
+def test_plugin_loads_through_reference_registry_and_target():
+    """The drop-in: the reference's own load_backend / load_target resolve cuda-sm100 / b200."""
+    if not REF.is_dir():
+        pytest.skip("reference checkout not mounted")
+    sys.path.insert(0, str(REF))
+    import tcenv.backends.registry as registry
+    import tcenv.target as target
+
+    from shapeforge_b200 import bootstrap
+
+    saved = (registry.BACKENDS, target.BACKENDS, target.TARGETS)
+    try:
+        bootstrap.install()
+        b = registry.load_backend("cuda-sm100")
+        assert isinstance(b, CudaBackend) and b.version == "1"
+        prof = target.load_target("b200")
+        assert prof.backend == "cuda-sm100" and prof.status == "active"
+        assert int(prof.raw_limits["max_threadgroup_memory_bytes"]) == 232448
+        from tcenv.track.abi import REQUIRED_TARGET_LIMITS
+
+        assert set(REQUIRED_TARGET_LIMITS) <= set(prof.raw_limits)
+    finally:
+        registry.BACKENDS, target.BACKENDS, target.TARGETS = saved
+        registry.load_backend.cache_clear()
+
+
+def test_track_registry_file_loads_with_reference_loader():
+    if not REF.is_dir():
+        pytest.skip("reference checkout not mounted")
+    sys.path.insert(0, str(REF))
+    from tcenv.track.registry import load_track_registry
+
+    reg = load_track_registry(ROOT / "backends" / "cuda-sm100" / "tracks.json")
+    assert "cuda-single" in {t.track_id for t in reg.tracks}
