@@ -139,6 +139,11 @@ class Workload:
     total_rows: int  # rows of the full shard (the sample is a row subset; rows are independent)
     nsets: int = 4
     launches_per_step: int = 1
+    # Head-sharded workloads (attention, KDA): this rank's share of the job and the whole job's
+    # units per step; replicated workloads leave these at their defaults.
+    sharded: bool = False
+    total_units: float | None = None
+    shard_note: str = ""
 
 
 def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
@@ -330,18 +335,28 @@ def cases_seed() -> int:
     return cases.SEARCH_SEED
 
 
-def _attention_workload(b: int, h: int, s: int, d: int, causal: bool = True, dtype: str = "bf16") -> Workload:
+def _attention_workload(b: int, h: int, s: int, d: int, causal: bool = True, dtype: str = "bf16", world: int = 1,
+                        rank: int = 0) -> Workload:
+    """With world > 1 the b*h heads are split into contiguous ranges, one per rank (each rank's
+    slice is a [1, n_r, s, d] problem); the job's units are the full problem's flops."""
     import math
 
     import torch
 
-    from shapeforge_b200 import cases
+    from shapeforge_b200 import cases, shard
 
     scale = 1.0 / math.sqrt(d)
-    flops = 4.0 * b * h * d * (s * (s + 1) / 2 if causal else s * s)
+    total_flops = 4.0 * b * h * d * (s * (s + 1) / 2 if causal else s * s)
+    full_shape = (b, h, s, d)
+    if world > 1:
+        h0, h1 = shard.head_ranges(b * h, world)[rank]
+        shape = (1, h1 - h0, s, d)
+    else:
+        shape = full_shape
+    flops = total_flops * (shape[0] * shape[1]) / (b * h)
 
     def make_inputs(seed):
-        return cases.attention_bench_inputs((b, h, s, d), dtype, seed=seed)
+        return cases.attention_bench_inputs(shape, dtype, seed=seed + 1000 * rank)
 
     def cpu_rows(rows):
         # The reference's algorithm (tasks/flash_attention/reference.py:113-119 with the causal
@@ -356,12 +371,16 @@ def _attention_workload(b: int, h: int, s: int, d: int, causal: bool = True, dty
         fl = sum(4.0 * d * ((i + 1) if causal else s) for i in sel)
         return (lambda: oref.attention_rows(q, k, v, scale, causal, sel)), fl, f"fp64 attention of {rows} query rows x one head"
 
-    return _op_workload(
+    wl = _op_workload(
         f"attention_{'causal' if causal else 'full'}_{b}x{h}x{s}x{d}", "TFLOP/s", "tensor", dtype, flops,
         {"workload": f"flash attention forward {'causal' if causal else 'non-causal'}, q/k/v {dtype} [{b},{h},{s},{d}] ~ N(0,1), "
                      f"scale 1/sqrt({d}), fp32 softmax statistics", "shape": [b, h, s, d]},
-        "fa_fwd_kernel", "flash_attention", make_inputs, ["q", "k", "v"], [((b, h, s, d), cases.TORCH_DTYPE[dtype])],
-        (b, h, s, d), (scale,), 1 if causal else 0, cpu_rows=cpu_rows, total_rows=s)
+        "fa_fwd_kernel", "flash_attention", make_inputs, ["q", "k", "v"], [(shape, cases.TORCH_DTYPE[dtype])],
+        shape, (scale,), 1 if causal else 0, cpu_rows=cpu_rows, total_rows=s)
+    if world > 1:
+        wl.sharded, wl.total_units = True, total_flops
+        wl.shard_note = f"b*h={b * h} heads split into {world} contiguous ranges (rank {rank}: {shape[1]} heads)"
+    return wl
 
 
 def _bitdelta_base_workload(m: int, n: int = 4096, k: int = 4096, dtype: str = "fp16") -> Workload:
@@ -393,20 +412,28 @@ def _bitdelta_base_workload(m: int, n: int = 4096, k: int = 4096, dtype: str = "
         [((m, n), cases.TORCH_DTYPE[dtype])], (m, n, k), cpu_rows=cpu_rows, total_rows=n)
 
 
-def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16") -> Workload:
+def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", world: int = 1, rank: int = 0) -> Workload:
+    """With world > 1 the heads are split into contiguous ranges (every rank runs all sequences
+    for its heads); the job's units are the full problem's bytes."""
     import math
 
     import torch
 
-    from shapeforge_b200 import cases
+    from shapeforge_b200 import cases, shard
 
     lengths = cases.kda_gated_lengths()
     total = int(sum(lengths))
     n = len(lengths)
-    nbytes = (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * heads * total + 4.0 * n * heads * dim * dim
+    per_head = lambda hh: (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * hh * total + 4.0 * n * hh * dim * dim  # noqa: E731
+    total_bytes = per_head(heads)
+    full_heads = heads
+    if world > 1:
+        h0, h1 = shard.head_ranges(heads, world)[rank]
+        heads = h1 - h0
+    nbytes = per_head(heads)
 
     def make_inputs(seed):
-        return cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed)
+        return cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed + 1000 * rank)
 
     def cpu_rows(rows):
         # The delta-rule recurrence (tasks/varlen_kda/reference.py:352-368, gate supplied) through
@@ -420,7 +447,7 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16") ->
         return ((lambda: oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), cu, 1.0 / math.sqrt(dim))),
                 (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * float(t), f"fp64 recurrence over {t} tokens of one chain")
 
-    return _op_workload(
+    wl = _op_workload(
         "kda_gated", "GB/s", "hbm", dtype, nbytes,
         {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
                      "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
@@ -428,25 +455,29 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16") ->
         "kda_fwd_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"],
         [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim),
         (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,))
+    if world > 1:
+        wl.sharded, wl.total_units = True, total_bytes
+        wl.shard_note = f"H={full_heads} heads split into {world} contiguous ranges (rank {rank}: {heads} heads, all sequences)"
+    return wl
 
 
 WORKLOADS = {
-    "attention_causal_4x32x2048x128": lambda: _attention_workload(4, 32, 2048, 128),
-    "attention_causal_4x32x512x128": lambda: _attention_workload(4, 32, 512, 128),
-    "attention_causal_4x32x8192x128": lambda: _attention_workload(4, 32, 8192, 128),
-    "attention_causal_4x32x2048x64": lambda: _attention_workload(4, 32, 2048, 64),
-    "bitdelta_base_m1": lambda: _bitdelta_base_workload(1),
-    "bitdelta_base_m16": lambda: _bitdelta_base_workload(16),
-    "bitdelta_base_m128": lambda: _bitdelta_base_workload(128),
-    "kda_gated": lambda: _kda_gated_workload(),
-    "gemm_nt_4096": lambda: _gemm_nt_workload(4096, 4096, 4096),
-    "gemm_nt_8192": lambda: _gemm_nt_workload(8192, 8192, 8192),
-    "gemm_nt_512": lambda: _gemm_nt_workload(512, 512, 512),
-    "gemm_nt_4095": lambda: _gemm_nt_workload(4095, 4096, 4096),
-    "rmsnorm_4096x4096": lambda: _rmsnorm_workload(4096, 4096),
-    "rmsnorm_4096x1024": lambda: _rmsnorm_workload(4096, 1024),
-    "rmsnorm_4096x8192": lambda: _rmsnorm_workload(4096, 8192),
-    "rmsnorm_4093x4096": lambda: _rmsnorm_workload(4093, 4096),
+    "attention_causal_4x32x2048x128": lambda w, r: _attention_workload(4, 32, 2048, 128, world=w, rank=r),
+    "attention_causal_4x32x512x128": lambda w, r: _attention_workload(4, 32, 512, 128, world=w, rank=r),
+    "attention_causal_4x32x8192x128": lambda w, r: _attention_workload(4, 32, 8192, 128, world=w, rank=r),
+    "attention_causal_4x32x2048x64": lambda w, r: _attention_workload(4, 32, 2048, 64, world=w, rank=r),
+    "bitdelta_base_m1": lambda w, r: _bitdelta_base_workload(1),
+    "bitdelta_base_m16": lambda w, r: _bitdelta_base_workload(16),
+    "bitdelta_base_m128": lambda w, r: _bitdelta_base_workload(128),
+    "kda_gated": lambda w, r: _kda_gated_workload(world=w, rank=r),
+    "gemm_nt_4096": lambda w, r: _gemm_nt_workload(4096, 4096, 4096),
+    "gemm_nt_8192": lambda w, r: _gemm_nt_workload(8192, 8192, 8192),
+    "gemm_nt_512": lambda w, r: _gemm_nt_workload(512, 512, 512),
+    "gemm_nt_4095": lambda w, r: _gemm_nt_workload(4095, 4096, 4096),
+    "rmsnorm_4096x4096": lambda w, r: _rmsnorm_workload(4096, 4096),
+    "rmsnorm_4096x1024": lambda w, r: _rmsnorm_workload(4096, 1024),
+    "rmsnorm_4096x8192": lambda w, r: _rmsnorm_workload(4096, 8192),
+    "rmsnorm_4093x4096": lambda w, r: _rmsnorm_workload(4093, 4096),
 }
 DEFAULT_WORKLOAD = "gemm_nt_4096"
 
@@ -625,7 +656,8 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
         return None
 
     scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
-    value = world * wl.units_per_step * args.steps / max_s / scale
+    job_units = wl.total_units if wl.sharded else world * wl.units_per_step
+    value = job_units * args.steps / max_s / scale
     per_launch_s = el_s / (args.steps * wl.launches_per_step)
     achieved = wl.units_per_step / per_launch_s / scale
     peaks, peak_src = measured_peaks()
@@ -633,7 +665,7 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     else:
         peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-    e2e_value = world * wl.units_per_step * e2e_steps / e2e_time / scale
+    e2e_value = job_units * e2e_steps / e2e_time / scale
     h2d = sum(h.numel() * h.element_size() for h in h_in)
     d2h = sum(h.numel() * h.element_size() for h in h_out)
     line = {
@@ -645,11 +677,11 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
         "warmup": args.warmup,
         "ms_per_step": max_s / args.steps * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if wl.sharded else "weak",
         "vs_baseline": None,
         "dtype": wl.dtype,
         "data": "synthetic",
-        "config": dict(wl.config, parallelism=f"replicas x{world}" if world > 1 else "1 GPU"),
+        "config": dict(wl.config, parallelism=(wl.shard_note if wl.sharded else f"replicas x{world}") if world > 1 else "1 GPU"),
         "roofline": {
             "bound": wl.bound,
             "achieved": achieved,
@@ -685,7 +717,7 @@ def main() -> None:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = _dist()
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](world, rank)
 
     if args.impl == "reference":
         if rank == 0:
@@ -695,6 +727,8 @@ def main() -> None:
     if world > 1:
         import datetime
 
+        # Keep stdout to the one JSON line (NCCL's version banner goes to stdout at INFO/VERSION).
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         import torch
         import torch.distributed as dist
 

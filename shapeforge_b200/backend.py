@@ -110,8 +110,8 @@ class CudaBackend:
         problems = []
         if re.search(r"\b__trap\s*\(|\basm\s*\(\s*\"trap", source):
             problems.append("trap is not allowed: report failures through a status word")
-        if ".multicast::cluster" in source:
-            problems.append("TMA loads with cluster multicast are not allowed")
+        if re.search(r"multicast\s*::\s*cluster", source):
+            problems.append("cluster-multicast bulk copies are not allowed on this backend")
         if "__global__" not in source:
             problems.append("no __global__ kernel in the candidate")
         return problems
