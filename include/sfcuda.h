@@ -206,6 +206,21 @@ SF_API int sf_gemm_nn_noalloc(const void* A, const void* B, void* C, int64_t M, 
 SF_API int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char* err, uint64_t cap);
 
 /* ---------------------------------------------------------------------------------------
+ * Compiled candidate kernels (the Candidate/Harness split).  The harness compiles a candidate
+ * CUDA source to an sm_100a cubin, loads it here and launches its kernels; replaces the Metal
+ * pipeline creation and dispatch (tcenv/backends/metal/runtime.py:306, :593).
+ * ------------------------------------------------------------------------------------- */
+
+/* Load a cubin/fatbin image; *module receives an opaque handle (cudaLibrary_t). */
+SF_API int sf_module_load(const void* image, uint64_t size, void** module, char* err, uint64_t cap);
+SF_API int sf_module_unload(void* module, char* err, uint64_t cap);
+/* Resolve an extern "C" kernel by name; *function receives an opaque handle (cudaKernel_t). */
+SF_API int sf_module_get_function(void* module, const char* name, void** function, char* err, uint64_t cap);
+/* Launch `function` with cudaLaunchKernel semantics: args[i] points at the i-th parameter's value. */
+SF_API int sf_launch_kernel(void* function, uint32_t gx, uint32_t gy, uint32_t gz, uint32_t bx, uint32_t by, uint32_t bz,
+               uint32_t smem, void* stream, void** args, char* err, uint64_t cap);
+
+/* ---------------------------------------------------------------------------------------
  * Generic dispatch + timed batches (the taic_metal_run_batch replacement).
  * ------------------------------------------------------------------------------------- */
 

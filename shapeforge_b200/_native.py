@@ -110,6 +110,14 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),
     "sf_gemm_nn_noalloc": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_kernel_status": (ctypes.c_int, (ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), _P, *_ERR)),
+    "sf_module_load": (ctypes.c_int, (_P, _U64, ctypes.POINTER(_P), *_ERR)),
+    "sf_module_unload": (ctypes.c_int, (_P, *_ERR)),
+    "sf_module_get_function": (ctypes.c_int, (_P, ctypes.c_char_p, ctypes.POINTER(_P), *_ERR)),
+    "sf_launch_kernel": (
+        ctypes.c_int,
+        (_P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+         _P, ctypes.POINTER(_P), *_ERR),
+    ),
     "sf_op_nargs": (ctypes.c_int32, (_I32,)),
     "sf_run_op": (ctypes.c_int, (ctypes.POINTER(SfOpDesc), ctypes.POINTER(_P), _U64, _P, *_ERR)),
     "sf_run_batch": (

@@ -1,0 +1,88 @@
+"""Build, load and launch candidate CUDA sources (the harness side of the Candidate/Harness split).
+
+A candidate is a single CUDA source whose ``extern "C" __global__`` kernels take the task's ABI
+tensors in order.  The harness compiles it for sm_100a with nvcc (``-cubin``), loads the image
+through the C ABI (``sf_module_load``) and launches kernels by name (``sf_launch_kernel``).
+Compiled images are cached by the hash of source + flags.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import subprocess
+import tempfile
+from pathlib import Path
+from typing import Sequence
+
+from . import _native
+from .build import ARCH, nvcc
+
+CACHE = Path(os.environ.get("SF_CANDIDATE_CACHE", Path(tempfile.gettempdir()) / "shapeforge_b200_candidates"))
+
+
+class CandidateCompileError(RuntimeError):
+    """nvcc rejected the candidate; ``log`` holds the compiler output."""
+
+    def __init__(self, message: str, log: str):
+        super().__init__(message)
+        self.log = log
+
+
+def compile_source(source: str, extra_flags: Sequence[str] = (), name: str = "candidate") -> bytes:
+    """Compile ``source`` to an sm_100a cubin (cached) and return the image bytes."""
+    flags = [*ARCH, "-O3", "-std=c++17", "-cubin", *extra_flags]
+    key = hashlib.sha256((source + "\0" + " ".join(flags)).encode()).hexdigest()[:24]
+    CACHE.mkdir(parents=True, exist_ok=True)
+    out = CACHE / f"{name}-{key}.cubin"
+    if out.is_file():
+        return out.read_bytes()
+    with tempfile.TemporaryDirectory() as d:
+        src = Path(d) / f"{name}.cu"
+        src.write_text(source)
+        tmp = Path(d) / "out.cubin"
+        proc = subprocess.run([nvcc(), *flags, str(src), "-o", str(tmp)], capture_output=True, text=True)
+        if proc.returncode != 0:
+            raise CandidateCompileError(f"nvcc failed for {name}", proc.stdout + proc.stderr)
+        data = tmp.read_bytes()
+    out.write_bytes(data)
+    return data
+
+
+class Module:
+    """A loaded image; kernels are launched by name with cudaLaunchKernel argument semantics."""
+
+    def __init__(self, image: bytes):
+        self._image = ctypes.create_string_buffer(image, len(image))
+        handle = ctypes.c_void_p()
+        _native.call("sf_module_load", ctypes.cast(self._image, ctypes.c_void_p), len(image), ctypes.byref(handle))
+        self.handle = handle
+        self._functions: dict[str, ctypes.c_void_p] = {}
+
+    def function(self, name: str) -> ctypes.c_void_p:
+        if name not in self._functions:
+            fn = ctypes.c_void_p()
+            _native.call("sf_module_get_function", self.handle, name.encode(), ctypes.byref(fn))
+            self._functions[name] = fn
+        return self._functions[name]
+
+    def launch(self, name: str, grid, block, args: Sequence[object], smem: int = 0, stream: int = 0) -> None:
+        """``args``: ctypes scalars (c_int, c_float, ...) or ints (device pointers)."""
+        holders = [a if isinstance(a, ctypes._SimpleCData) else ctypes.c_void_p(int(a)) for a in args]
+        argv = (ctypes.c_void_p * len(holders))(*[ctypes.cast(ctypes.pointer(h), ctypes.c_void_p) for h in holders])
+        g = tuple(grid) + (1,) * (3 - len(tuple(grid)))
+        b = tuple(block) + (1,) * (3 - len(tuple(block)))
+        _native.call("sf_launch_kernel", self.function(name), *[int(v) for v in g], *[int(v) for v in b], int(smem),
+                     ctypes.c_void_p(stream), argv)
+
+    def close(self) -> None:
+        if self.handle:
+            _native.call("sf_module_unload", self.handle)
+            self.handle = None
+
+    def __del__(self):  # best effort: a module outlives no process
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass

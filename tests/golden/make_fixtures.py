@@ -239,10 +239,24 @@ def write(doc: dict, name: str) -> Path:
     return path
 
 
+def sem_int_program(task: str) -> dict:
+    """The task's int32 program document (the ``_PROGRAM`` JSON of tasks/<t>/reference.py)."""
+    import re
+
+    text = (REF / "tasks" / task / "reference.py").read_text(encoding="utf-8")
+    m = re.search(r"_PROGRAM = json\.loads\(r'''(.*?)'''\)", text, re.S)
+    return json.loads(m.group(1))
+
+
 def main() -> None:
     if not REF.is_dir():
         raise SystemExit(f"reference checkout not found at {REF}")
     outs = []
+    for task in ("sem_int_1", "sem_int_2", "sem_int_3", "sem_int_4", "sem_int_5", "sem_int_7"):
+        doc = from_reference(task, "i32", "small")
+        doc["program"] = sem_int_program(task)
+        doc["attrs"] = {"SCALAR_K": 12345}
+        outs.append(write(doc, f"ref_{task}_i32"))
     for task in G0_TASKS:
         for dtype in ("fp16", "bf16"):
             outs.append(write(from_g0(task, dtype), f"g0_{task}_{dtype}"))
