@@ -461,7 +461,43 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
     return wl
 
 
+def _mamba2_workload(b: int = 2, l: int = 2048, h: int = 8, p: int = 64, n: int = 64, c: int = 64, dtype: str = "fp16") -> Workload:
+    """The mamba2_chunk_scan paper size (tasks/mamba2_chunk_scan/opspec.json sizes.paper)."""
+    from shapeforge_b200 import cases
+
+    nc = l // c
+
+    def nbytes(bb, chunks):
+        rows = bb * chunks * c
+        return 2.0 * (2 * rows * h * p + 2 * rows * h + 2 * rows * n + h + bb * chunks * h * p * n)
+
+    def make_inputs(seed):
+        return cases.mamba2_inputs("normal", seed, b, l, h, p, n, c, dtype)
+
+    def cpu_rows(rows):
+        # tasks/mamba2_chunk_scan/reference.py:106-127 through the oracle port, on the first `rows`
+        # chunks of batch 0 (chunks are independent).
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        k = min(rows, nc)
+        t = k * c
+        a = [inp["x"][:1, :t], inp["dt"][:1, :t], inp["dA_cumsum"][:1, :, :k], inp["Bmat"][:1, :t], inp["Cmat"][:1, :t],
+             inp["Dskip"], inp["states"][:1, :k]]
+        a = [v.double().numpy() for v in a]
+        return (lambda: oref.mamba2_chunk_scan(*a)), nbytes(1, k), f"fp64 oracle over {k} chunks of batch 0"
+
+    return _op_workload(
+        f"mamba2_chunk_scan_b{b}_l{l}_h{h}", "GB/s", "hbm", dtype, nbytes(b, nc),
+        {"workload": f"mamba2 SSD chunk scan, B={b} L={l} H={h} P={p} N={n} CHUNK={c}, {dtype}, task input stream "
+                     "(normal case: x/B/C/D/states ~ N(0,1), dt in [0.001,0.05], A in [-8,-1])", "shape": [b, l, h, p, n, c]},
+        "mamba2_tc_kernel", "mamba2_chunk_scan", make_inputs, ["x", "dt", "dA_cumsum", "Bmat", "Cmat", "Dskip", "states"],
+        [((b, l, h, p), cases.TORCH_DTYPE[dtype])], (b, l, h, p, n, c), cpu_rows=cpu_rows, total_rows=nc)
+
+
 WORKLOADS = {
+    "mamba2_chunk_scan_paper": lambda w, r: _mamba2_workload(),
+    "mamba2_chunk_scan_b8_l8192": lambda w, r: _mamba2_workload(8, 8192, 16),
     "attention_causal_4x32x2048x128": lambda w, r: _attention_workload(4, 32, 2048, 128, world=w, rank=r),
     "attention_causal_4x32x512x128": lambda w, r: _attention_workload(4, 32, 512, 128, world=w, rank=r),
     "attention_causal_4x32x8192x128": lambda w, r: _attention_workload(4, 32, 8192, 128, world=w, rank=r),

@@ -163,6 +163,17 @@ SF_API int sf_varlen_kda_gated(const void* q, const void* k, const void* v, cons
                int64_t H, int64_t D, float scale, int32_t dtype, void* stream, char* err, uint64_t cap);
 
 /*
+ * mamba2_chunk_scan (tasks/mamba2_chunk_scan/reference.py:106-127): the Mamba-2 SSD chunk scan of
+ * one B/C group.  x [B,L,H,P], dt [B,L,H], dA_cumsum [B,H,NC,chunk] (NC = L / chunk),
+ * Bmat/Cmat [B,L,N], Dskip [H], states [B,NC,H,P,N] in, y [B,L,H,P] out, all in dtype, fp32
+ * arithmetic, one rounding of y.  tcgen05 kernel when chunk = P = N = 64 and x, Bmat, Cmat,
+ * states, y are 16-byte aligned; general fp32 kernel otherwise.  L must be a multiple of chunk.
+ */
+SF_API int sf_mamba2_chunk_scan(const void* x, const void* dt, const void* dA_cumsum, const void* Bmat, const void* Cmat,
+               const void* Dskip, const void* states, void* y, int64_t B, int64_t L, int64_t H, int64_t P, int64_t N,
+               int64_t chunk, int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
  * gemm_nt: C[M,N] = A[M,K] . B[N,K]^T, fp16 or bf16 in, fp32 accumulation, one rounding
  * (the dense-gemm workload; the oracle is tasks/gemm/reference.py:110-114 applied to B^T).
  * tcgen05/TMEM/TMA kernel when the bases are 16-byte aligned and K % 8 == 0, else the general
@@ -237,6 +248,7 @@ SF_API int sf_launch_kernel(void* function, uint32_t gx, uint32_t gy, uint32_t g
 #define SF_OP_ATTENTION 11
 #define SF_OP_KDA 12
 #define SF_OP_KDA_GATED 13
+#define SF_OP_MAMBA2 14
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -268,6 +280,8 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *                   args = {q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state}
  *   SF_OP_KDA_GATED dims = {num_seqs, H, D}  attrs = {scale}
  *                   args = {q, k, v, g, beta, cu_seqlens, initial_state (may be NULL), output, final_state}
+ *   SF_OP_MAMBA2    dims = {B, L, H, P, N, chunk}
+ *                   args = {x, dt, dA_cumsum, Bmat, Cmat, Dskip, states, y}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

@@ -203,3 +203,36 @@ def attention_rows(q, k, v, scale: float, causal: bool, rows) -> np.ndarray:
             s = np.where(keys[None, :] <= rows[:, None], s, -np.inf)
         p = softmax(s)
         return np.einsum("bhqk,bhkd->bhqd", p, v)
+
+
+def mamba2_chunk_scan(x, dt, dA_cumsum, b_mat, c_mat, d_skip, states):
+    """tasks/mamba2_chunk_scan/reference.py:106-127 (the Mamba-2 SSD chunk scan, paper listing 1,
+    one B/C group), in fp64.  Per batch b, chunk c (rows t = c*CHUNK + l), head h:
+
+        w[l, s]  = (C[t_l] . B[t_s]) * exp(cs[b,h,c,l] - cs[b,h,c,s]) * dt[b,t_s,h]   if s <= l else 0
+        y[t_l,h] = sum_s w[l, s] x[t_s, h]
+                 + exp(cs[b,h,c,l]) * sum_n C[t_l, n] states[b,c,h,:,n]  +  D[h] x[t_l, h]
+
+    Shapes: x [B,L,H,P], dt [B,L,H], dA_cumsum [B,H,NC,CHUNK], b_mat/c_mat [B,L,N], d_skip [H],
+    states [B,NC,H,P,N]; y [B,L,H,P].  Masked entries are exactly zero (``where``) and still multiply
+    x, so a non-finite x element makes every row of its chunk non-finite, as in the reference.
+    """
+    bsz, seq, heads, hd = x.shape
+    nc, chunk = dA_cumsum.shape[2], dA_cumsum.shape[3]
+    if nc * chunk != seq:
+        raise ValueError(f"SEQLEN {seq} != NCHUNKS {nc} * CHUNK {chunk}")
+    x5 = np.asarray(x, np.float64).reshape(bsz, nc, chunk, heads, hd)
+    dt4 = np.asarray(dt, np.float64).reshape(bsz, nc, chunk, heads).transpose(0, 3, 1, 2)  # [B,H,NC,C]
+    cs = np.asarray(dA_cumsum, np.float64)
+    br = np.asarray(b_mat, np.float64).reshape(bsz, nc, chunk, -1)
+    cr = np.asarray(c_mat, np.float64).reshape(bsz, nc, chunk, -1)
+    st = np.asarray(states, np.float64)
+    causal = np.tril(np.ones((chunk, chunk), dtype=bool))
+    with _err():
+        cb = np.einsum("bcln,bcsn->bcls", cr, br)
+        decay = np.exp(cs[..., :, None] - cs[..., None, :])                      # [B,H,NC,l,s]
+        w = np.where(causal, cb[:, None] * decay * dt4[..., None, :], 0.0)
+        y = np.einsum("bhcls,bcshp->bclhp", w, x5)
+        y = y + np.einsum("bcln,bchpn->bclhp", cr, st) * np.exp(cs).transpose(0, 2, 3, 1)[..., None]
+        y = y + np.asarray(d_skip, np.float64)[:, None] * x5
+    return y.reshape(bsz, seq, heads, hd)

@@ -79,6 +79,7 @@ OPS = {
     "flash_attention": 11,
     "varlen_kda": 12,
     "varlen_kda_gated": 13,
+    "mamba2_chunk_scan": 14,
 }
 
 _P = ctypes.c_void_p
@@ -105,6 +106,7 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_flash_attention": (ctypes.c_int, (_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _I32, _I32, _P, *_ERR)),
     "sf_varlen_kda": (ctypes.c_int, (_P,) * 12 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_varlen_kda_gated": (ctypes.c_int, (_P,) * 9 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
+    "sf_mamba2_chunk_scan": (ctypes.c_int, (_P,) * 8 + (_I64,) * 6 + (_I32, _P, *_ERR)),
     "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_gemm_nn_workspace_bytes": (_U64, (_I64, _I64, _I64, _I32)),
     "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),

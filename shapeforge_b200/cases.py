@@ -313,3 +313,37 @@ def kda_task_inputs(lengths, heads: int, dim: int, dtype: str, seed: int) -> dic
         "beta": round_to(beta, dtype), "A_log": a_log.float(), "dt_bias": dt_bias.float(), "initial_state": s0.float(),
         "cu_seqlens": cu_from_lengths(lengths), "scale": torch.tensor([1.0 / math.sqrt(dim)], dtype=torch.float32),
     }
+
+
+# ---- mamba2 chunk scan ------------------------------------------------------------------------
+
+MAMBA2_CASES = ("normal", "wide_range", "large", "tiny", "outlier", "ieee")
+MAMBA2_OFFSETS = {"x": 0, "Bmat": 31, "Cmat": 62, "states": 93, "Dskip": 124, "dt": 155, "decay": 186}
+
+
+def mamba2_inputs(case: str, seed: int, batch: int, seq: int, heads: int, headdim: int, dstate: int, chunk: int,
+                  dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/mamba2_chunk_scan/reference.py:199-223: dt = round(0.001 + 0.049 sigmoid(N(0,1))),
+    A = -(1 + 7 sigmoid(N(0,1))) per head, dA_cumsum = the in-chunk cumulative sum of dt*A laid out
+    [B,H,NC,CHUNK]; x/B/C/D/states from the case sampler (mags normal 1 / wide_range 0.1, large 4,
+    spike 5); the ieee case injects specials into states only."""
+    base = "normal" if case == "ieee" else case
+    mag = {"normal": 1.0, "wide_range": 0.1}.get(base, 1.0)
+    nc = seq // chunk
+    off = MAMBA2_OFFSETS
+    dt = round_to(0.001 + 0.049 * torch.sigmoid(sample("normal", (batch, seq, heads), seed + off["dt"], dtype)), dtype).float()
+    a = -(1.0 + 7.0 * torch.sigmoid(sample("normal", (heads,), seed + off["decay"], dtype)))
+    cs = (dt.reshape(batch, nc, chunk, heads) * a).cumsum(dim=2).permute(0, 3, 1, 2).contiguous()
+    kw = dict(mag=mag, large=4.0, spike=5.0)
+    out = {
+        "x": sample(base, (batch, seq, heads, headdim), seed + off["x"], dtype, **kw),
+        "dt": dt,
+        "dA_cumsum": cs,
+        "Bmat": sample(base, (batch, seq, dstate), seed + off["Bmat"], dtype, **kw),
+        "Cmat": sample(base, (batch, seq, dstate), seed + off["Cmat"], dtype, **kw),
+        "Dskip": sample(base, (heads,), seed + off["Dskip"], dtype, **kw),
+        "states": sample(base, (batch, nc, heads, headdim, dstate), seed + off["states"], dtype, **kw),
+    }
+    if case == "ieee":
+        out["states"] = inject(out["states"], seed + 7 * IEEE_SEED_STRIDE)
+    return {k: round_to(v, dtype) for k, v in out.items()}

@@ -162,6 +162,22 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
         : "memory");
 }
 
+// mma_f16 that leaves some accumulator rows untouched: TMEM lane i (row i of D) is not written
+// when bit (i % 32) of disable[i / 32] is set.  Lets one M=128 MMA serve two independent 64-row
+// problems stacked in A (each half masked in turn) without their products mixing.
+__device__ __forceinline__ void mma_f16_lanes(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate, const uint32_t (&disable)[4]) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(disable[0]), "r"(disable[1]), "r"(disable[2]),
+        "r"(disable[3])
+        : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -266,3 +266,32 @@ def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: 
             output.data_ptr(), final_state.data_ptr()]
     _run("varlen_kda_gated", q, ptrs, dims=(n, h, d), attrs=(scale,))
     return output, final_state
+
+
+def mamba2_chunk_scan(x, dt, dA_cumsum, b_mat, c_mat, d_skip, states, out: torch.Tensor | None = None,
+                      variant: int = 0) -> torch.Tensor:
+    """Mamba-2 SSD chunk scan of one B/C group (tasks/mamba2_chunk_scan/reference.py:106-127).
+
+    x [B,L,H,P], dt [B,L,H], dA_cumsum [B,H,NC,CHUNK], b_mat/c_mat [B,L,N], d_skip [H],
+    states [B,NC,H,P,N], all of one 16-bit dtype; returns y [B,L,H,P]."""
+    tensors = (("x", x), ("dt", dt), ("dA_cumsum", dA_cumsum), ("Bmat", b_mat), ("Cmat", c_mat), ("Dskip", d_skip),
+               ("states", states))
+    for name, t in tensors:
+        _check(t, name, x.dtype)
+    if x.dim() != 4 or dA_cumsum.dim() != 4 or states.dim() != 5:
+        raise ValueError("mamba2_chunk_scan expects x [B,L,H,P], dA_cumsum [B,H,NC,CHUNK], states [B,NC,H,P,N]")
+    bsz, seq, heads, hd = x.shape
+    nc, chunk = dA_cumsum.shape[2], dA_cumsum.shape[3]
+    n = b_mat.shape[-1]
+    want = {"dt": (bsz, seq, heads), "dA_cumsum": (bsz, heads, nc, chunk), "Bmat": (bsz, seq, n), "Cmat": (bsz, seq, n),
+            "Dskip": (heads,), "states": (bsz, nc, heads, hd, n)}
+    for name, t in tensors[1:]:
+        if tuple(t.shape) != want[name]:
+            raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {want[name]}")
+    if nc * chunk != seq:
+        raise ValueError(f"SEQLEN {seq} != NCHUNKS {nc} * CHUNK {chunk}")
+    out = torch.empty_like(x) if out is None else out
+    _check(out, "out", x.dtype)
+    ptrs = [t.data_ptr() for _, t in tensors] + [out.data_ptr()]
+    _run("mamba2_chunk_scan", x, ptrs, dims=(bsz, seq, heads, hd, n, chunk), variant=variant)
+    return out

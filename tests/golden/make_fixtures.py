@@ -15,7 +15,7 @@ Two sources, both produced by the reference itself:
   ``tcenv.taskcontract.load_task_contract``): inputs from the task's own ``gen_inputs`` at the
   harness case seeds ``seed + 7919 * (i + 1)`` (``tcenv/backends/metal/v2_runtime.py:1602``), rounded
   to storage dtype, and the task's fp64 ``reference`` outputs, for bitdelta_gemm,
-  flash_attention, rope and varlen_kda.
+  flash_attention, rope, varlen_kda and mamba2_chunk_scan.
 
 Large tensors are sliced to a few rows/columns (the slice is recorded) so the fixtures stay
 small; the reference outputs of the kept rows/columns depend only on kept inputs.  Storage
@@ -217,6 +217,23 @@ def _rope_slice(inputs, refs, scales):
     return inputs, {"y": refs["y"][:, :, np.array(pos)]}, scales, {"ref_positions": pos}
 
 
+def _mamba2_slice(inputs, refs, scales):
+    """Keep the first and the last chunk (chunks are independent: y of chunk c reads only chunk c's
+    rows of x/dt/B/C, cs[:, :, c] and states[:, c]) and a few output rows of each."""
+    cs = inputs["dA_cumsum"]
+    nc, chunk = cs.shape[2], cs.shape[3]
+    keep = [0, nc - 1]
+    rows = np.concatenate([np.arange(c * chunk, (c + 1) * chunk) for c in keep])
+    i2 = dict(inputs)
+    for k in ("x", "dt", "Bmat", "Cmat"):
+        i2[k] = inputs[k][:, rows]
+    i2["dA_cumsum"] = cs[:, :, keep]
+    i2["states"] = inputs["states"][:, keep]
+    local = [0, 1, 2, chunk // 2 - 1, chunk - 1, chunk, chunk + 1, 2 * chunk - 2, 2 * chunk - 1]
+    y = refs["y"][:, rows][:, np.array(local)]
+    return i2, {"y": y}, scales, {"chunks": keep, "ref_rows": local}
+
+
 def write(doc: dict, name: str) -> Path:
     arrays = {}
     meta = {k: v for k, v in doc.items() if k != "records"}
@@ -264,6 +281,7 @@ def main() -> None:
         outs.append(write(from_reference("bitdelta_gemm", dtype, "small", _bitdelta_slice), f"ref_bitdelta_gemm_{dtype}"))
         outs.append(write(from_reference("flash_attention", dtype, "small", _fa_slice), f"ref_flash_attention_{dtype}"))
         outs.append(write(from_reference("rope", dtype, "small", _rope_slice), f"ref_rope_{dtype}"))
+        outs.append(write(from_reference("mamba2_chunk_scan", dtype, "small", _mamba2_slice), f"ref_mamba2_chunk_scan_{dtype}"))
         for size in ("mixed", "fixed", "uniform"):
             outs.append(write(from_reference("varlen_kda", dtype, size), f"ref_varlen_kda_{size}_{dtype}"))
     total = 0
