@@ -7,13 +7,13 @@
 // sums); x [B,L,H,P], dt [B,L,H], dA_cumsum [B,H,NC,CHUNK], Bmat/Cmat [B,L,N], Dskip [H],
 // states [B,NC,H,P,N], y [B,L,H,P], all fp16 or bf16, L = NC * CHUNK.
 //
-// Tensor-core kernel (CHUNK = P = N = 64): one CTA of 128 threads per (two consecutive chunks,
-// head, batch).  The two chunks are stacked into the 128 rows of one M=128 MMA; every MMA is
+// Tensor-core kernel (CHUNK = P = N = 64): one CTA of 256 threads per (two consecutive chunks,
+// head, batch); warp w serves the 32 rows (w % 4) * 32 + lane and the 32 columns (w / 4) * 32 + i.  The two chunks are stacked into the 128 rows of one M=128 MMA; every MMA is
 // issued twice with half of the accumulator lanes disabled (tcgen05.mma disable-output-lane), so
 // a row only ever meets its own chunk's operands:
 //   TMA    C, B rows [128 x 64], x rows [128 s x 64 p] and the two state tiles [64 p x 64 n];
 //   MMA    CB = C . B^T (per chunk, TMEM cols [0,64)),  S = C . states^T (cols [64,128));
-//   rows   thread l: w[l,s] = CB[l,s] exp(cs_l - cs_s) dt_s for s <= l else 0, in fp32, written as a
+//   rows   w[l,s] = CB[l,s] exp(cs_l - cs_s) dt_s for s <= l else 0, in fp32, written as a
 //          16-bit high part and a 16-bit residual (fp16: after a power-of-two row scale that puts
 //          the row maximum in [2^14, 2^15), so neither overflow nor underflow loses it);
 //   MMA    Yh = Wh . x and Yl = Wl . x (x read MN-major straight from its [s, p] rows);
@@ -43,7 +43,7 @@ constexpr int CH = 64;                // chunk length, head dim and state dim of
 constexpr int ROWS = 2 * CH;          // two chunks per CTA = M of every MMA
 constexpr int TILE = ROWS * 128;      // 128 rows of 64 16-bit elements (one 128-byte swizzle row each)
 constexpr int HALF = CH * 128;        // 64 such rows
-constexpr int NUM_THREADS = 128;
+constexpr int NUM_THREADS = 256;
 constexpr uint32_t TMEM_COLS = 256;   // CB [0,64), S [64,128), Yh [128,192), Yl [192,256)
 
 struct Layout {
@@ -53,9 +53,10 @@ struct Layout {
     static constexpr int ST = X + TILE;     // states [chunk][p][n]: K-major B operand of C.states^T
     static constexpr int WH = ST + TILE;    // W high part, K-major over s (row l: its own chunk's s)
     static constexpr int WL = WH + TILE;    // W residual
-    static constexpr int CS = WL + TILE;    // float cs[128]
+    static constexpr int CS = WL + TILE;    // float cs[128] * log2(e)
     static constexpr int DT = CS + 512;     // float dt[128]
-    static constexpr int BARS = DT + 512;
+    static constexpr int MX = DT + 512;     // float row max of |w| over each column half [2][128]
+    static constexpr int BARS = MX + 1024;
     static constexpr int BYTES = BARS + 64;
 };
 
@@ -98,7 +99,7 @@ __device__ __forceinline__ float resid(float v, float hv) { return isfinite(hv) 
 __device__ __forceinline__ int sw128(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
 
 template <typename T>
-__global__ void __launch_bounds__(NUM_THREADS)
+__global__ void __launch_bounds__(NUM_THREADS, 2)
     mamba2_tc_kernel(const __grid_constant__ CUtensorMap tcm, const __grid_constant__ CUtensorMap tbm,
                      const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tst, const T* __restrict__ dt,
                      const T* __restrict__ cs, const T* __restrict__ dskip, T* __restrict__ y, int L, int H, int NC,
@@ -110,39 +111,23 @@ __global__ void __launch_bounds__(NUM_THREADS)
     float* cs_s = reinterpret_cast<float*>(smem + Layout::CS);
     float* dt_s = reinterpret_cast<float*>(smem + Layout::DT);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    float* mx_s = reinterpret_cast<float*>(smem + Layout::MX);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, colh = warp >> 2;  // TMEM lane quarter, column half
     const int pair = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int c0 = 2 * pair;
     const bool has1 = c0 + 1 < NC;
     const int t0 = c0 * CH;
+    const int l = quad * 32 + lane, half = l >> 6, ll = l & (CH - 1);
+    const bool row_ok = (c0 + half) < NC;
 
     if (tid == 0) {
         sm100::mbar_init(&bars->load_full, 1);
         sm100::mbar_init(&bars->cb_full, 1);
         sm100::mbar_init(&bars->y_full, 1);
         sm100::fence_mbar_init();
-    }
-    if (warp == 0) {
-        sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
-        sm100::tmem_relinquish();
-    }
-    // Per-row scalars: cs and dt of row l (chunk c0 + l / 64), zero for a missing second chunk.
-    const int l = tid, half = l >> 6, ll = l & (CH - 1);
-    const bool row_ok = (c0 + half) < NC;
-    cs_s[l] = row_ok ? sf::Dt<T>::to_f(cs[(((int64_t)b * H + h) * NC + c0 + half) * CH + ll]) : 0.f;
-    dt_s[l] = row_ok ? sf::Dt<T>::to_f(dt[((int64_t)b * L + t0 + l) * H + h]) : 0.f;
-    const float dh = sf::Dt<T>::to_f(dskip[h]);
-    sm100::tc_fence_before();
-    __syncthreads();
-    sm100::tc_fence_after();
-    const uint32_t tmem = bars->tmem_base;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-
-    // Lanes of chunk 0 are rows [0,64), of chunk 1 rows [64,128): disable the other half.
-    const uint32_t only0[4] = {0u, 0u, 0xFFFFFFFFu, 0xFFFFFFFFu};
-    const uint32_t only1[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0u, 0u};
-
-    if (tid == 0) {
+        // Tiles first: their latency overlaps everything up to the first MMA.
         sm100::tma_prefetch_desc(&tcm);
         sm100::tma_prefetch_desc(&tbm);
         sm100::tma_prefetch_desc(&tx);
@@ -150,64 +135,91 @@ __global__ void __launch_bounds__(NUM_THREADS)
         sm100::mbar_arrive_expect_tx(&bars->load_full, 3 * TILE + (has1 ? 2 : 1) * HALF);
         sm100::tma_load_3d(smem + Layout::CM, &tcm, &bars->load_full, 0, t0, b);
         sm100::tma_load_3d(smem + Layout::BM, &tbm, &bars->load_full, 0, t0, b);
-        sm100::tma_load_3d(smem + Layout::X, &tx, &bars->load_full, h * CH, t0, b);
         sm100::tma_load_2d(smem + Layout::ST, &tst, &bars->load_full, 0, (int)((((int64_t)b * NC + c0) * H + h) * CH));
         if (has1)
             sm100::tma_load_2d(smem + Layout::ST + HALF, &tst, &bars->load_full, 0, (int)((((int64_t)b * NC + c0 + 1) * H + h) * CH));
-        if (sm100::mbar_wait(&bars->load_full, 0, status, 61)) {
-            sm100::tc_fence_after();
-            constexpr uint32_t idesc = sm100::idesc_f16(ROWS, CH, BF16);
-            const uint32_t scm = sm100::smem_u32(smem + Layout::CM);
-            const uint32_t sbm = sm100::smem_u32(smem + Layout::BM);
-            const uint32_t sst = sm100::smem_u32(smem + Layout::ST);
-            for (int q = 0; q < (has1 ? 2 : 1); ++q) {
-                const uint32_t(&mask)[4] = q == 0 ? only0 : only1;
+        sm100::tma_load_3d(smem + Layout::X, &tx, &bars->load_full, h * CH, t0, b);
+    }
+    if (warp == 0) {
+        sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    // Per-row scalars (zero for a missing second chunk): cs * log2(e) by the first 128 threads,
+    // dt by the other 128.
+    if (colh == 0)
+        cs_s[l] = row_ok ? sf::Dt<T>::to_f(cs[(((int64_t)b * H + h) * NC + c0 + half) * CH + ll]) * 1.4426950408889634f : 0.f;
+    else
+        dt_s[l] = row_ok ? sf::Dt<T>::to_f(dt[((int64_t)b * L + t0 + l) * H + h]) : 0.f;
+    const float dh = sf::Dt<T>::to_f(dskip[h]);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+
+    // Lanes of chunk 0 are rows [0,64), of chunk 1 rows [64,128): disable the other half.
+    const uint32_t only0[4] = {0u, 0u, 0xFFFFFFFFu, 0xFFFFFFFFu};
+    const uint32_t only1[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0u, 0u};
+
+    if (tid == 0 && sm100::mbar_wait(&bars->load_full, 0, status, 61)) {
+        sm100::tc_fence_after();
+        constexpr uint32_t idesc = sm100::idesc_f16(ROWS, CH, BF16);
+        const uint32_t scm = sm100::smem_u32(smem + Layout::CM);
+        const uint32_t sbm = sm100::smem_u32(smem + Layout::BM);
+        const uint32_t sst = sm100::smem_u32(smem + Layout::ST);
+        for (int q = 0; q < (has1 ? 2 : 1); ++q) {
+            const uint32_t(&mask)[4] = q == 0 ? only0 : only1;
 #pragma unroll
-                for (int k = 0; k < CH / 16; ++k) {
-                    const uint64_t ad = sm100::smem_desc_k_sw128(scm + (uint32_t)(k * 32));
-                    sm100::mma_f16_lanes(tmem, ad, sm100::smem_desc_k_sw128(sbm + (uint32_t)(q * HALF + k * 32)), idesc,
-                                         k > 0 ? 1u : 0u, mask);
-                    sm100::mma_f16_lanes(tmem + 64, ad, sm100::smem_desc_k_sw128(sst + (uint32_t)(q * HALF + k * 32)), idesc,
-                                         k > 0 ? 1u : 0u, mask);
-                }
+            for (int k = 0; k < CH / 16; ++k) {
+                const uint64_t ad = sm100::smem_desc_k_sw128(scm + (uint32_t)(k * 32));
+                sm100::mma_f16_lanes(tmem, ad, sm100::smem_desc_k_sw128(sbm + (uint32_t)(q * HALF + k * 32)), idesc, k > 0 ? 1u : 0u,
+                                     mask);
+                sm100::mma_f16_lanes(tmem + 64, ad, sm100::smem_desc_k_sw128(sst + (uint32_t)(q * HALF + k * 32)), idesc,
+                                     k > 0 ? 1u : 0u, mask);
             }
-            sm100::mma_commit(&bars->cb_full);
         }
+        sm100::mma_commit(&bars->cb_full);
     }
 
-    // ---- W rows: one thread per row ----
+    // ---- W: thread (l, colh) builds w[l, s] for its 32 columns s ----
     bool ok = sm100::mbar_wait(&bars->cb_full, 0, status, 62);
-    float rinv = 1.f;
+    float w[32];
     if (ok) {
         sm100::tc_fence_after();
-        uint32_t cb[CH];
-        sm100::tmem_ld_32x32b_x32(tmem + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&cb[0]));
-        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&cb[32]));
+        uint32_t cb[32];
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(colh * 32), cb);
         sm100::tmem_ld_wait();
         const float csl = cs_s[l];
-        const float* csc = cs_s + half * CH;
-        const float* dtc = dt_s + half * CH;
-        float w[CH];
+        const float* csc = cs_s + half * CH + colh * 32;
+        const float* dtc = dt_s + half * CH + colh * 32;
         float m = 0.f;
 #pragma unroll
-        for (int s = 0; s < CH; ++s) {
-            w[s] = s <= ll ? __uint_as_float(cb[s]) * __expf(csl - csc[s]) * dtc[s] : 0.f;
-            m = fmaxf(m, fabsf(w[s]));
+        for (int i = 0; i < 32; ++i) {
+            w[i] = colh * 32 + i <= ll ? __uint_as_float(cb[i]) * exp2f(csl - csc[i]) * dtc[i] : 0.f;
+            m = fmaxf(m, fabsf(w[i]));
         }
+        if (!BF16) mx_s[colh * ROWS + l] = m;
+    }
+    __syncthreads();
+    float rinv = 1.f;
+    if (ok) {
         float rs = 1.f;
-        if (!BF16 && m > 0.f && m <= FLT_MAX) {
-            // Power-of-two scale putting the row maximum into [2^14, 2^15).
-            int e = (int)((__float_as_uint(m) >> 23) & 0xFFu);
-            if (e == 0) e = 1;
-            int sx = 141 - e;
-            sx = sx > 126 ? 126 : sx;
-            rs = __uint_as_float((uint32_t)(sx + 127) << 23);
-            rinv = __uint_as_float((uint32_t)(127 - sx) << 23);
+        if (!BF16) {
+            const float m = fmaxf(mx_s[l], mx_s[ROWS + l]);
+            if (m > 0.f && m <= FLT_MAX) {
+                // Power-of-two scale putting the row maximum into [2^14, 2^15).
+                int e = (int)((__float_as_uint(m) >> 23) & 0xFFu);
+                if (e == 0) e = 1;
+                int sx = 141 - e;
+                sx = sx > 126 ? 126 : sx;
+                rs = __uint_as_float((uint32_t)(sx + 127) << 23);
+                rinv = __uint_as_float((uint32_t)(127 - sx) << 23);
+            }
         }
         uint8_t* wh = smem + Layout::WH;
         uint8_t* wl = smem + Layout::WL;
 #pragma unroll
-        for (int j = 0; j < CH / 8; ++j) {
+        for (int j = 0; j < 4; ++j) {
             float v[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = w[j * 8 + i] * rs;
@@ -216,8 +228,8 @@ __global__ void __launch_bounds__(NUM_THREADS)
                                         pack2<T>(resid(v[2], lo16<T>(hv.y)), resid(v[3], hi16<T>(hv.y))),
                                         pack2<T>(resid(v[4], lo16<T>(hv.z)), resid(v[5], hi16<T>(hv.z))),
                                         pack2<T>(resid(v[6], lo16<T>(hv.w)), resid(v[7], hi16<T>(hv.w))));
-            *reinterpret_cast<uint4*>(wh + sw128(l, j)) = hv;
-            *reinterpret_cast<uint4*>(wl + sw128(l, j)) = lv;
+            *reinterpret_cast<uint4*>(wh + sw128(l, colh * 4 + j)) = hv;
+            *reinterpret_cast<uint4*>(wl + sw128(l, colh * 4 + j)) = lv;
         }
     }
     sm100::fence_proxy_async_smem();
@@ -243,41 +255,38 @@ __global__ void __launch_bounds__(NUM_THREADS)
         sm100::mma_commit(&bars->y_full);
     }
 
-    // ---- epilogue: y = (Yh + Yl) / rowscale + exp(cs_l) S + D x, 32 columns at a time ----
+    // ---- epilogue: y = (Yh + Yl) / rowscale + exp(cs_l) S + D x for the thread's 32 columns ----
     ok = ok && sm100::mbar_wait(&bars->y_full, 0, status, 63);
     if (ok) {
         sm100::tc_fence_after();
-        const float ecs = expf(cs_s[l]);
-        const uint8_t* xs = smem + Layout::X;
-        uint4* dst = reinterpret_cast<uint4*>(y + (((int64_t)b * L + t0 + l) * H + h) * CH);
-#pragma unroll 1
-        for (int g = 0; g < 2; ++g) {
-            uint32_t yh[32], yl[32], sr[32];
-            sm100::tmem_ld_32x32b_x32(tmem + lane_off + 128 + g * 32, yh);
-            sm100::tmem_ld_32x32b_x32(tmem + lane_off + 192 + g * 32, yl);
-            sm100::tmem_ld_32x32b_x32(tmem + lane_off + 64 + g * 32, sr);
-            sm100::tmem_ld_wait();
-            if (row_ok) {
+        uint32_t yh[32], yl[32], sr[32];
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (uint32_t)(colh * 32), yh);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 192 + (uint32_t)(colh * 32), yl);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 64 + (uint32_t)(colh * 32), sr);
+        sm100::tmem_ld_wait();
+        if (row_ok) {
+            const float ecs = exp2f(cs_s[l]);
+            const uint8_t* xs = smem + Layout::X;
+            uint4* dst = reinterpret_cast<uint4*>(y + (((int64_t)b * L + t0 + l) * H + h) * CH) + colh * 4;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint4 xv = *reinterpret_cast<const uint4*>(xs + sw128(l, g * 4 + j));
-                    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-                    uint32_t o[4];
+            for (int j = 0; j < 4; ++j) {
+                const uint4 xv = *reinterpret_cast<const uint4*>(xs + sw128(l, colh * 4 + j));
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+                uint32_t o[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        float v[2];
+                for (int i = 0; i < 4; ++i) {
+                    float v[2];
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int c = j * 8 + 2 * i + e;
-                            const float hv = __uint_as_float(yh[c]);
-                            const float wx = isfinite(hv) ? hv + __uint_as_float(yl[c]) : hv;
-                            const float xe = e ? hi16<T>(xw[i]) : lo16<T>(xw[i]);
-                            v[e] = wx * rinv + ecs * __uint_as_float(sr[c]) + dh * xe;
-                        }
-                        o[i] = pack2<T>(v[0], v[1]);
+                    for (int e = 0; e < 2; ++e) {
+                        const int c = j * 8 + 2 * i + e;
+                        const float hv = __uint_as_float(yh[c]);
+                        const float wx = isfinite(hv) ? hv + __uint_as_float(yl[c]) : hv;
+                        const float xe = e ? hi16<T>(xw[i]) : lo16<T>(xw[i]);
+                        v[e] = wx * rinv + ecs * __uint_as_float(sr[c]) + dh * xe;
                     }
-                    dst[g * 4 + j] = make_uint4(o[0], o[1], o[2], o[3]);
+                    o[i] = pack2<T>(v[0], v[1]);
                 }
+                dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
             }
         }
     }
