@@ -85,3 +85,57 @@ def test_oracle_rejects_bad_chunking():
     a[2] = a[2][:, :, :1]  # NC * CHUNK != SEQLEN
     with pytest.raises(ValueError):
         ops.mamba2_chunk_scan(*a)
+
+
+def _sequential(x, dt, cs, bm, cm, d, st):
+    """The SSM recurrence token by token: per chunk the state starts at states[b, c], each token
+    decays it by exp(cs_t - cs_{t-1}) (cs_{-1} = 0), adds dt_t x_t B_t^T, and emits C_t . h + D x_t."""
+    bsz, seq, heads, hd = x.shape
+    nc, chunk = cs.shape[2], cs.shape[3]
+    y = np.zeros((bsz, seq, heads, hd))
+    for b in range(bsz):
+        for c in range(nc):
+            hs = st[b, c].copy()                         # [H, P, N]
+            prev = np.zeros(heads)
+            for l in range(chunk):
+                t = c * chunk + l
+                cur = cs[b, :, c, l]
+                hs = np.exp(cur - prev)[:, None, None] * hs + dt[b, t][:, None, None] * x[b, t][:, :, None] * bm[b, t][None, None, :]
+                y[b, t] = hs @ cm[b, t] + d[:, None] * x[b, t]
+                prev = cur
+    return y
+
+
+@pytest.mark.parametrize("case", ["normal", "wide_range", "large", "outlier"])
+def test_oracle_equals_the_sequential_state_recurrence(case):
+    """The chunked form (intra-chunk C.B^T with decay mask + carried-in states) is the same
+    operator as the token-by-token recurrence (the reference's own check, on the small size)."""
+    inp = cases.mamba2_inputs(case, 21, dtype="fp16", **SMALL)
+    a = _f64(inp)
+    y = ops.mamba2_chunk_scan(*a)
+    seq = _sequential(*a)
+    np.testing.assert_allclose(seq, y, rtol=1e-9, atol=1e-9 * float(np.abs(y).max()))
+
+
+def test_paper_flops_count_the_shared_bc_product_once():
+    """Work accounting of the paper size: C.B^T once per (batch, chunk), W.x and C.states^T per head."""
+    batch, seq, heads, headdim, dstate, chunk = 2, 2048, 8, 64, 64, 64
+    chunks = seq // chunk
+    shared = batch * chunks * (2 * chunk * chunk * dstate)
+    per_head = batch * heads * chunks * (2 * chunk * chunk * headdim + 2 * chunk * headdim * dstate)
+    assert shared + per_head == 570_425_344
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("case", list(cases.MAMBA2_CASES))
+def test_inputs_keep_the_ssm_invariants(dtype, case):
+    """dt in [0.001, 0.05], dA_cumsum finite, non-increasing and <= 0 inside every chunk (every
+    decay <= 1, and exp(cs) never flushes to zero); the ieee case puts specials only in states."""
+    inp = cases.mamba2_inputs(case, 5, dtype=dtype, **SMALL)
+    dt, cs = inp["dt"].double(), inp["dA_cumsum"].double()
+    assert bool((dt > 0).all()) and float(dt.min()) >= 0.001 * 0.99 and float(dt.max()) <= 0.05 * 1.01
+    assert bool(torch.isfinite(cs).all()) and bool((cs[..., 1:] <= cs[..., :-1]).all()) and bool((cs <= 0).all())
+    assert float(cs.min()) > -8.0 * 0.05 * 64 * 1.01
+    others = [inp[n] for n in NAMES if n != "states"]
+    assert all(bool(torch.isfinite(t).all()) for t in others)
+    assert bool(torch.isfinite(inp["states"]).all()) == (case != "ieee")
