@@ -105,6 +105,12 @@ class CudaBackend:
 
     # ---- parent-process, text-only hooks -------------------------------------------------------
 
+    def track_adapter(self, track):
+        """Construct the adapter for an already-selected TrackSpec, lazily and fail-closed."""
+        from .track_factory import adapter_for_track
+
+        return adapter_for_track(track)
+
     def screen(self, source: str, task: Any = None) -> list[str]:
         """Static refusals before any build: forbidden constructs on this pool."""
         problems = []
