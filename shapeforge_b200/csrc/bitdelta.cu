@@ -19,10 +19,15 @@
 //      through distributed shared memory (each CTA sums a slice of the M rows of y from every
 //      peer's partial and writes it).  No workspace.
 //
-// Sign expansion uses a 256-entry shared-memory table: one 16-byte lookup per 8 signs.
+// Sign expansion uses a 256-entry shared-memory table: one 16-byte lookup per 8 signs.  The
+// base kernel keeps 8 interleaved copies of the table (entry e of copy k at 16-byte slot
+// 8e + k) and lane L reads copy L % 8, so the 8 lanes of each 128-bit shared-memory phase hit 8
+// different bank groups whatever bytes they look up.
 //
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2..5
 // expand sign bits for every stage and run the epilogue.  Every mbarrier wait is bounded.
+// The base kernel streams W_base (+ x) through a deep TMA ring (up to 8 stages) and the expanded
+// signs through a separate 3-entry ring, so DRAM sees up to 8 W_base tiles in flight per SM.
 #include "sf_common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -43,11 +48,27 @@ constexpr int NUM_THREADS = 192;
 constexpr int SMEM_LIMIT = 227 * 1024;
 // Dynamic shared memory available next to the 4 KB static sign table.
 constexpr int kMaxDynSmem = SMEM_LIMIT - 4096;
+// The base kernel has no static shared memory (its table is dynamic).
+constexpr int BASE_SMEM_LIMIT = SMEM_LIMIT;
 
 struct __align__(8) Bars {
     uint64_t full_tma[4];
     uint64_t full_exp[4];
     uint64_t empty[4];
+    uint64_t acc_full;
+    uint32_t tmem_base;
+};
+
+constexpr int BASE_MAX_STAGES = 8;  // W_base + x ring
+constexpr int BASE_SSTAGES = 3;     // expanded-sign ring
+constexpr int LUT_COPIES = 8;
+constexpr int LUT8_BYTES = 256 * LUT_COPIES * 16;
+
+struct __align__(8) BaseBars {
+    uint64_t full_w[BASE_MAX_STAGES];
+    uint64_t empty_w[BASE_MAX_STAGES];
+    uint64_t full_s[BASE_SSTAGES];
+    uint64_t empty_s[BASE_SSTAGES];
     uint64_t acc_full;
     uint32_t tmem_base;
 };
@@ -70,6 +91,31 @@ __device__ __forceinline__ void build_sign_lut(uint4* lut) {
             w[q] = base ^ ((b & 1u) << 15) ^ ((b & 2u) << 30);
         }
         lut[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// The same table, LUT_COPIES interleaved copies: slot 8e + k holds entry e.
+template <typename T>
+__device__ __forceinline__ void build_sign_lut8(uint4* lut) {
+    const uint32_t base = minus_one_pair<T>();
+    for (int i = threadIdx.x; i < 256 * LUT_COPIES; i += blockDim.x) {
+        const uint32_t e = (uint32_t)i / LUT_COPIES;
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t b = (e >> (2 * q)) & 3u;
+            w[q] = base ^ ((b & 1u) << 15) ^ ((b & 2u) << 30);
+        }
+        lut[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// expand_row_sw128 reading copy `copy` of the interleaved table.
+__device__ __forceinline__ void expand_row_sw128_lut8(uint8_t* tile, int r, uint64_t bits, const uint4* lut, int copy) {
+    uint8_t* row = tile + r * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) * 16)) = lut[(((uint32_t)(bits >> (8 * c)) & 0xFFu) << 3) + copy];
     }
 }
 
@@ -103,17 +149,18 @@ template <typename T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     bitdelta_base_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                          const uint32_t* __restrict__ s_words, const T* __restrict__ alpha, T* __restrict__ y, int M, int N,
-                         int K, int nm, int stages, sm100::KernelStatus* status) {
+                         int K, int nm, int stages, int vec_words, int tile_n, sm100::KernelStatus* status) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int x_bytes = nm * 128;
-    const int stage_bytes = 2 * ROW_TILE_BYTES + x_bytes;
-    Bars* bars = reinterpret_cast<Bars*>(smem + stages * stage_bytes);
-    __shared__ uint4 lut[256];
-    build_sign_lut<T>(lut);
+    const int w_bytes = tile_n * 128;                         // rows of W_base this CTA owns
+    const int stage_bytes = ROW_TILE_BYTES + x_bytes;        // W_base tile + x tile
+    uint8_t* sring = smem + stages * stage_bytes;             // expanded signs
+    uint4* lut = reinterpret_cast<uint4*>(sring + BASE_SSTAGES * ROW_TILE_BYTES);
+    BaseBars* bars = reinterpret_cast<BaseBars*>(reinterpret_cast<uint8_t*>(lut) + LUT8_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * TILE_ROWS;
+    const int n0 = blockIdx.x * tile_n;
     const int sk = gridDim.y;
     const uint32_t rank = sm100::cluster_ctarank();
     const int nkb = (K + BK - 1) / BK;
@@ -124,13 +171,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
-            sm100::mbar_init(&bars->full_tma[s], 1);
-            sm100::mbar_init(&bars->full_exp[s], 128);
-            sm100::mbar_init(&bars->empty[s], 1);
+            sm100::mbar_init(&bars->full_w[s], 1);
+            sm100::mbar_init(&bars->empty_w[s], 1);
+        }
+        for (int s = 0; s < BASE_SSTAGES; ++s) {
+            sm100::mbar_init(&bars->full_s[s], 128);
+            sm100::mbar_init(&bars->empty_s[s], 1);
         }
         sm100::mbar_init(&bars->acc_full, 1);
         sm100::fence_mbar_init();
     }
+    // The first ring of W_base / x tiles is requested before anything else (the slots start
+    // empty), so DRAM latency overlaps the table build and TMEM allocation.
+    const int pre = min(stages, max(kb_end - kb_begin, 0));
+    auto issue = [&](int kb, int s) {
+        uint8_t* st = smem + s * stage_bytes;
+        sm100::mbar_arrive_expect_tx(&bars->full_w[s], w_bytes + x_bytes);
+        sm100::tma_load_2d(st, &tmap_w, &bars->full_w[s], kb * BK, n0);
+        sm100::tma_load_2d(st + ROW_TILE_BYTES, &tmap_x, &bars->full_w[s], kb * BK, 0);
+    };
+    if (threadIdx.x == 0) {
+        sm100::tma_prefetch_desc(&tmap_w);
+        sm100::tma_prefetch_desc(&tmap_x);
+        for (int i = 0; i < pre; ++i) issue(kb_begin + i, i);
+    }
+    // Sign words of the first 16 K-blocks: requested before the set-up barrier as well.
+    const int t = threadIdx.x - 64;
+    const int n = n0 + t;
+    const bool row_live = warp >= 2 && t < tile_n && n < N;
+    uint32_t wv[32];
+    auto load_words = [&](int kc) {
+        const int w0 = 2 * kc;
+        const uint32_t* src = s_words + (int64_t)n * kw + w0;
+        if (vec_words && row_live && kc + 16 <= kb_end && (w0 & 3) == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + i);
+                wv[4 * i] = v.x;
+                wv[4 * i + 1] = v.y;
+                wv[4 * i + 2] = v.z;
+                wv[4 * i + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) wv[i] = (row_live && w0 + i < 2 * kb_end && w0 + i < kw) ? __ldg(src + i) : 0u;
+        }
+    };
+    if (warp >= 2 && kb_end > kb_begin) load_words(kb_begin);
+    build_sign_lut8<T>(lut);
     if (warp == 1) {
         sm100::tmem_alloc(&bars->tmem_base, tmem_cols);
         sm100::tmem_relinquish();
@@ -142,34 +230,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            sm100::tma_prefetch_desc(&tmap_w);
-            sm100::tma_prefetch_desc(&tmap_x);
-            int s = 0;
-            uint32_t ph = 0;
-            for (int kb = kb_begin; kb < kb_end; ++kb) {
-                if (!sm100::mbar_wait(&bars->empty[s], ph ^ 1u, status, 11)) break;
-                uint8_t* st = smem + s * stage_bytes;
-                sm100::mbar_arrive_expect_tx(&bars->full_tma[s], ROW_TILE_BYTES + x_bytes);
-                sm100::tma_load_2d(st, &tmap_w, &bars->full_tma[s], kb * BK, n0);
-                sm100::tma_load_2d(st + 2 * ROW_TILE_BYTES, &tmap_x, &bars->full_tma[s], kb * BK, 0);
+            int s = pre % stages;
+            uint32_t ph = pre == stages ? 1u : 0u;
+            for (int kb = kb_begin + pre; kb < kb_end; ++kb) {
+                if (!sm100::mbar_wait(&bars->empty_w[s], ph ^ 1u, status, 11)) break;
+                issue(kb, s);
                 if (++s == stages) { s = 0; ph ^= 1u; }
             }
         }
     } else if (warp == 1) {
         if (lane == 0 && kb_end > kb_begin) {
             const uint32_t idesc = sm100::idesc_f16(128, (uint32_t)nm, std::is_same<T, __nv_bfloat16>::value);
-            int s = 0;
-            uint32_t ph = 0;
+            int s = 0, e = 0;
+            uint32_t ph = 0, phe = 0;
             bool ok = true;
             for (int kb = kb_begin; kb < kb_end; ++kb) {
-                if (!sm100::mbar_wait(&bars->full_tma[s], ph, status, 12) || !sm100::mbar_wait(&bars->full_exp[s], ph, status, 13)) {
+                if (!sm100::mbar_wait(&bars->full_w[s], ph, status, 12) || !sm100::mbar_wait(&bars->full_s[e], phe, status, 13)) {
                     ok = false;
                     break;
                 }
                 sm100::tc_fence_after();
                 const uint32_t sw = sm100::smem_u32(smem + s * stage_bytes);
-                const uint32_t ss = sw + ROW_TILE_BYTES;
-                const uint32_t sx = sw + 2 * ROW_TILE_BYTES;
+                const uint32_t sx = sw + ROW_TILE_BYTES;
+                const uint32_t ss = sm100::smem_u32(sring + e * ROW_TILE_BYTES);
 #pragma unroll
                 for (int k = 0; k < BK / 16; ++k) {
                     const uint64_t bx = sm100::smem_desc_k_sw128(sx + k * 32);
@@ -177,40 +260,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sw + k * 32), bx, idesc, acc);
                     sm100::mma_f16(tmem + (uint32_t)nm, sm100::smem_desc_k_sw128(ss + k * 32), bx, idesc, acc);
                 }
-                sm100::mma_commit(&bars->empty[s]);
+                sm100::mma_commit(&bars->empty_w[s]);
+                sm100::mma_commit(&bars->empty_s[e]);
                 if (++s == stages) { s = 0; ph ^= 1u; }
+                if (++e == BASE_SSTAGES) { e = 0; phe ^= 1u; }
             }
             if (ok) sm100::mma_commit(&bars->acc_full);
         }
     } else {
         // Sign expansion: thread t owns row t (output column n0 + t) of every S tile.  The sign
         // words of 16 K-blocks are loaded up front (independent loads, one memory latency per 16
-        // stages instead of one per stage).
-        const int t = threadIdx.x - 64;
-        const int n = n0 + t;
-        int s = 0;
-        uint32_t ph = 0;
+        // stages instead of one per stage), as 16-byte vectors when the rows allow it.  Rows at
+        // or past tile_n are not this CTA's: their S rows are left as they are (the MMA rows
+        // they feed are never read).
+        const int copy = lane & (LUT_COPIES - 1);
+        int e = 0;
+        uint32_t phe = 0;
         bool ok = true;
         for (int kc = kb_begin; kc < kb_end && ok; kc += 16) {
-            uint32_t lo[16], hi[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int w = 2 * (kc + i);
-                const bool live = n < N && kc + i < kb_end;
-                lo[i] = (live && w < kw) ? s_words[(int64_t)n * kw + w] : 0u;
-                hi[i] = (live && w + 1 < kw) ? s_words[(int64_t)n * kw + w + 1] : 0u;
-            }
+            if (kc != kb_begin) load_words(kc);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 if (kc + i >= kb_end) break;
-                if (!sm100::mbar_wait(&bars->empty[s], ph ^ 1u, status, 14)) {
+                if (!sm100::mbar_wait(&bars->empty_s[e], phe ^ 1u, status, 14)) {
                     ok = false;
                     break;
                 }
-                expand_row_sw128(smem + s * stage_bytes + ROW_TILE_BYTES, t, (uint64_t)lo[i] | ((uint64_t)hi[i] << 32), lut);
+                if (t < tile_n)
+                    expand_row_sw128_lut8(sring + e * ROW_TILE_BYTES, t, (uint64_t)wv[2 * i] | ((uint64_t)wv[2 * i + 1] << 32), lut, copy);
                 sm100::fence_proxy_async_smem();
-                sm100::mbar_arrive(&bars->full_exp[s]);
-                if (++s == stages) { s = 0; ph ^= 1u; }
+                sm100::mbar_arrive(&bars->full_s[e]);
+                if (++e == BASE_SSTAGES) { e = 0; phe ^= 1u; }
             }
         }
     }
@@ -222,7 +302,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const int n = n0 + row;
-        const float a = n < N ? sf::Dt<T>::to_f(alpha[n]) : 0.f;
+        const float a = (row < tile_n && n < N) ? sf::Dt<T>::to_f(alpha[n]) : 0.f;
         bool have = kb_end > kb_begin;
         if (have && !sm100::mbar_wait(&bars->acc_full, 0, status, 15)) have = false;
         sm100::tc_fence_after();
@@ -256,7 +336,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int per = (((M + sk - 1) / sk) + 3) & ~3;
         const int c0 = (int)rank * per;
         const int c1 = min(M, c0 + per);
-        if (n < N) {
+        if (row < tile_n && n < N) {
             const uint32_t own = sm100::smem_u32(red + (size_t)row * nm);
             for (int c = c0; c < c1; c += 4) {
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -465,13 +545,21 @@ int launch_base_tc(const void* x, const void* wb, const void* sw, const void* al
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     sm100::KernelStatus* status = status_ptr();
     if (!status) return sf::fail(SF_EDEVICE, err, cap, "bitdelta: cannot resolve the status word");
-    CUtensorMap mw;
-    int rc = sf::tmap_kmajor(&mw, wb, N, K, TILE_ROWS, bf16, err, cap);
-    if (rc) return rc;
-    const int64_t tiles = (N + TILE_ROWS - 1) / TILE_ROWS;
     const int64_t nkb = (K + BK - 1) / BK;
-    int sk = (int)std::max<int64_t>(1, std::min<int64_t>(8, sf::sm_count() / std::max<int64_t>(tiles, 1)));
+    // Tiling: 128 rows of W_base per CTA (the MMA instruction count per CTA depends only on its
+    // share of K, so tiles are kept as tall as the MMA allows) and K split over a cluster of sk
+    // CTAs, as many as still fit in one wave (clusters are placed within GPCs, so 4 x 32 = 128
+    // CTAs fit on 148 SMs where 4 x 37 do not).
+    int tile_n = (int)std::min<int64_t>(TILE_ROWS, std::max<int64_t>(16, (N + 7) / 8 * 8));
+    const int64_t ntiles = (N + tile_n - 1) / tile_n;
+    int sk = (int)std::max<int64_t>(1, std::min<int64_t>(8, sf::sm_count() / std::max<int64_t>(ntiles, 1)));
     sk = (int)std::min<int64_t>(sk, nkb);
+    const int64_t tiles = (N + tile_n - 1) / tile_n;
+    CUtensorMap mw;
+    int rc = sf::tmap_kmajor(&mw, wb, N, K, tile_n, bf16, err, cap);
+    if (rc) return rc;
+    // 16-byte sign-word loads when every S row starts on a 16-byte boundary.
+    const int vec_words = ((K / 32) % 4 == 0 && sf::aligned16(sw)) ? 1 : 0;
     // x rows are processed in chunks of at most 256 (the MMA N dimension).
     for (int64_t mc = 0; mc < M; mc += 256) {
         const int64_t mrows = std::min<int64_t>(256, M - mc);
@@ -479,15 +567,16 @@ int launch_base_tc(const void* x, const void* wb, const void* sw, const void* al
         CUtensorMap mx;
         rc = sf::tmap_kmajor(&mx, (const T*)x + mc * K, mrows, K, nm, bf16, err, cap);
         if (rc) return rc;
-        const int stage_bytes = 2 * ROW_TILE_BYTES + nm * 128;
-        int stages = std::min(4, (kMaxDynSmem - 2048) / stage_bytes);
-        // The reduction buffer (128 x nm fp32) reuses the pipeline buffers.
-        while (stages * stage_bytes < 128 * nm * 4) ++stages;
-        const int smem = stages * stage_bytes + 1024 + 256;
-        if (stages > 4 || smem > kMaxDynSmem) return sf::fail(SF_EINVAL, err, cap, "bitdelta: no shared-memory plan for M chunk %d", nm);
+        const int stage_bytes = ROW_TILE_BYTES + nm * 128;
+        const int fixed = BASE_SSTAGES * ROW_TILE_BYTES + LUT8_BYTES + (int)sizeof(BaseBars) + 1024;
+        const int stages = std::min(BASE_MAX_STAGES, (BASE_SMEM_LIMIT - fixed) / stage_bytes);
+        const int smem = stages * stage_bytes + fixed;
+        // The reduction buffer (128 x nm fp32) reuses the W_base/x ring and the sign ring.
+        if (stages < 2 || 128 * nm * 4 > stages * stage_bytes + BASE_SSTAGES * ROW_TILE_BYTES)
+            return sf::fail(SF_EINVAL, err, cap, "bitdelta: no shared-memory plan for M chunk %d", nm);
         static std::atomic<uint64_t> attr_done{0};
         if (sf::once_per_device(attr_done))
-            cudaFuncSetAttribute(bitdelta_base_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+            cudaFuncSetAttribute(bitdelta_base_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, BASE_SMEM_LIMIT);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)tiles, (unsigned)sk, 1);
         cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -501,7 +590,7 @@ int launch_base_tc(const void* x, const void* wb, const void* sw, const void* al
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t e = cudaLaunchKernelEx(&cfg, bitdelta_base_kernel<T>, mw, mx, (const uint32_t*)sw, (const T*)alpha,
-                                           (T*)y + mc * N, (int)mrows, (int)N, (int)K, nm, stages, status);
+                                           (T*)y + mc * N, (int)mrows, (int)N, (int)K, nm, stages, vec_words, tile_n, status);
         if (e != cudaSuccess) return sf::fail(SF_EDEVICE, err, cap, "bitdelta_base launch: %s", cudaGetErrorString(e));
     }
     return SF_OK;
