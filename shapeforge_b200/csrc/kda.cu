@@ -227,12 +227,19 @@ int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, co
 
 int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                         const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
-                        int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
+                        int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
     int rc = check(N, H, D, dtype, err, cap);
     if (rc) return rc;
     if (N == 0) return SF_OK;
     if (!q || !k || !v || !g || !beta || !cu_seqlens || !out || !final_state)
         return sf::fail(SF_EINVAL, err, cap, "kda_gated: null tensor pointer");
+    // Variant 0: the chunked tensor-core kernel when it applies (D = 128, aligned rows), else the
+    // recurrent one; 1 forces the chunked kernel, 2 the recurrent kernel.
+    if (variant != 2) {
+        rc = sf_kda_gated_chunk_launch(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, D, scale, dtype, st,
+                                       variant == 1 ? err : nullptr, variant == 1 ? cap : 0);
+        if (rc == SF_OK || variant == 1 || rc != SF_EINVAL) return rc;
+    }
     if (dtype == SF_DTYPE_F16)
         return launch_t<__half, false>(q, k, v, g, beta, nullptr, nullptr, (const float*)initial_state, (const int32_t*)cu_seqlens,
                                        nullptr, scale, 0.f, N, H, D, out, (float*)final_state, st, err, cap);
@@ -251,6 +258,6 @@ extern "C" int sf_varlen_kda(const void* q, const void* k, const void* v, const 
 extern "C" int sf_varlen_kda_gated(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                                    const void* initial_state, void* output, void* final_state, int64_t num_seqs, int64_t H, int64_t D,
                                    float scale, int32_t dtype, void* stream, char* err, uint64_t cap) {
-    return sf_kda_gated_launch(q, k, v, g, beta, cu_seqlens, initial_state, output, final_state, num_seqs, H, D, scale, dtype,
+    return sf_kda_gated_launch(q, k, v, g, beta, cu_seqlens, initial_state, output, final_state, num_seqs, H, D, scale, dtype, 0,
                                (cudaStream_t)stream, err, cap);
 }

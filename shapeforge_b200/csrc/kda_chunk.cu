@@ -1,0 +1,473 @@
+// Chunked gated delta rule (KDA) forward on the tcgen05 tensor cores, sm_100a, D = 128.
+//
+// Per (sequence, head) chain the recurrence of kda.cu is evaluated 16 tokens at a time.  With
+// b_t = sum_{i<=t} g_i (per key channel, cumulative log-decay inside the chunk), the state after
+// token t of a chunk that starts from S0 is
+//   S_t = S0 diag(e^{b_t}) + sum_{i<=t} w_i (k_i * e^{b_t - b_i})^T
+// where the rows w_i [Dv] solve the unit lower-triangular system
+//   w_t = beta_t (v_t - S0 (k_t * e^{b_t}) - sum_{i<t} A[t,i] w_i),  A[t,i] = <k_t e^{b_t}, k_i e^{-b_i}>
+// and the outputs are
+//   o_t = S0 (q~_t * e^{b_t}) + sum_{i<=t} M[t,i] w_i,               M[t,i] = <q~_t e^{b_t}, k_i e^{-b_i}>
+// (q~ = q * scale); the chunk ends with S = S0 diag(e^{b_15}) + W^T Kend, Kend_i = k_i e^{b_15 - b_i}.
+// The factor e^{-b_i} stays finite while the log-decay summed over 16 tokens stays above -87 per
+// channel (always true for decays bounded by -5 per token; for N(0,1) logits it would take 16
+// successive values below -5.4).
+//
+// One CTA of 256 threads per chain; the 128 x 128 fp32 state lives in TMEM (lane = value row v,
+// column = key channel k) and is never written to memory until the chain ends.  Two warpgroups:
+// warpgroup 1 (prep) works up to two chunks ahead of warpgroup 0 (state) through double buffers:
+//   prep   thread = key channel: cumulative decay, the factored keys/queries (fp32 for the CUDA-core
+//          products, 16-bit for the MMAs), the chunk decay e^{b_15}; then the 16 x 16 decayed
+//          key.key (A) and query.key (M) products in fp32; the next chunk's inputs are loaded
+//          into registers meanwhile;
+//   state  thread = value row: S0 is read from TMEM, written as a 16-bit MMA operand and written
+//          back decayed (S0 diag(e^{b_15}));
+//          MMA 1  [U' | O'] = S0 . [Kp ; Qp]^T   (M=128 rows v, N=32, K=128);
+//          u = v - U', forward substitution for w, o = O' + M w (fp32), outputs stored, w written
+//          as a 16-bit high part and residual;
+//          MMA 2  S += W^T . Kend (high and residual parts; M=128, N=128, K=16), whose completion
+//          also hands the chunk's buffers back to the prep warpgroup.
+// Every mbarrier wait is bounded; a timeout is reported through sf_kernel_status.
+#include "sf_common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+#include <atomic>
+#include <type_traits>
+
+__device__ sm100::KernelStatus g_kda_status;
+
+namespace {
+
+constexpr int D = 128;       // head dim (key and value)
+constexpr int C = 16;        // tokens per chunk
+constexpr int NT = 256;      // threads: two warpgroups
+constexpr int WG = 128;      // threads per warpgroup
+constexpr int KP = D + 4;    // fp32 staging row stride: 16-byte rows, rows r and r+8 in distinct bank groups
+constexpr uint32_t TMEM_COLS = 256;  // S [0,128), [U'|O'] [128,160)
+
+struct Layout {
+    static constexpr int SA = 0;                   // S0 operand [128 v x 128 k], 2 K-blocks x 16 KB
+    static constexpr int WH = SA + 32768;          // W^T high [128 v x 64 (t < 16 used)]
+    static constexpr int WL = WH + 16384;          // W^T residual
+    static constexpr int B1 = WL + 16384;          // [Kp ; Qp] [32 x 128], 2 K-blocks x 4 KB; x2 buffers
+    static constexpr int KE = B1 + 2 * 8192;       // Kend [16 t x 128 k] MN-major, 2 blocks x 2 KB; x2
+    static constexpr int KP32 = KE + 2 * 4096;     // fp32 [16][KP] Kp, Kn, Qp, Kend (prep only)
+    static constexpr int KN32 = KP32 + C * KP * 4;
+    static constexpr int QP32 = KN32 + C * KP * 4;
+    static constexpr int KE32 = QP32 + C * KP * 4;
+    static constexpr int AM = KE32 + C * KP * 4;   // fp32 A [16][17], M [16][17]; x2
+    static constexpr int AM_BYTES = 2 * C * 17 * 4;
+    static constexpr int EB = AM + 2 * AM_BYTES;   // fp32 chunk decay e^{b_15} [128]; x2
+    static constexpr int BETA = EB + 2 * D * 4;    // fp32 beta [16]; x2
+    static constexpr int VS = BETA + 2 * 64;       // staged v (16-bit) [16][128]; x2
+    static constexpr int QS = VS + 2 * C * D * 2;  // staged q, k (16-bit) [16][128], g fp32 (prep only)
+    static constexpr int KS = QS + C * D * 2;
+    static constexpr int GS = KS + C * D * 2;
+    static constexpr int BARS = GS + C * D * 4;
+    static constexpr int BYTES = BARS + 64;
+};
+
+struct __align__(8) Bars {
+    uint64_t m1;
+    uint64_t m2;
+    uint64_t pfull[2];   // prep -> state: chunk buffers ready (128 arrivals)
+    uint64_t pempty[2];  // state -> prep: chunk buffers consumed (the update MMA's commit)
+    uint32_t tmem_base;
+};
+
+template <typename T>
+__device__ __forceinline__ uint16_t to16(float x) {
+    const T h = sf::Dt<T>::from_f(x);
+    return *reinterpret_cast<const uint16_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ float from16(uint16_t u) {
+    return sf::Dt<T>::to_f(*reinterpret_cast<const T*>(&u));
+}
+
+// Byte offset of element (row r, column c) of a K-major 128-byte-swizzled operand whose K-blocks of
+// 64 columns are `blk` bytes apart.
+__device__ __forceinline__ int kmaj(int r, int c, int blk) {
+    return (c >> 6) * blk + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1);
+}
+
+// Next chunk's raw inputs, held in registers while the current chunk computes.  Thread tid covers
+// token tid / 8 and the 16 columns (tid % 8) * 16 .. +15.
+struct Prefetch {
+    uint4 q[2], k[2], v[2];
+    float4 g[4];
+    float beta;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_chunk(Prefetch& p, const T* q, const T* k, const T* v, const float* g, const float* beta, int t0,
+                                           int nt, int H, int h, int tid) {
+    const int tt = tid >> 3, part = tid & 7;
+    const bool live = tt < nt;
+    const size_t base = ((size_t)(t0 + tt) * H + h) * D + part * 16;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        p.q[i] = live ? __ldg(reinterpret_cast<const uint4*>(q + base) + i) : make_uint4(0, 0, 0, 0);
+        p.k[i] = live ? __ldg(reinterpret_cast<const uint4*>(k + base) + i) : make_uint4(0, 0, 0, 0);
+        p.v[i] = live ? __ldg(reinterpret_cast<const uint4*>(v + base) + i) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p.g[i] = live ? __ldg(reinterpret_cast<const float4*>(g + base) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    p.beta = (tid < nt) ? __ldg(beta + (size_t)(t0 + tid) * H + h) : 0.f;
+}
+
+__device__ __forceinline__ void store_chunk(const Prefetch& p, uint8_t* smem, int tid, int b) {
+    const int tt = tid >> 3, part = tid & 7;
+    const int off = (tt * D + part * 16) * 2;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        *reinterpret_cast<uint4*>(smem + Layout::QS + off + 16 * i) = p.q[i];
+        *reinterpret_cast<uint4*>(smem + Layout::KS + off + 16 * i) = p.k[i];
+        *reinterpret_cast<uint4*>(smem + Layout::VS + b * C * D * 2 + off + 16 * i) = p.v[i];
+    }
+    float* gs = reinterpret_cast<float*>(smem + Layout::GS) + tt * D + part * 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(gs)[i] = p.g[i];
+    if (tid < C) reinterpret_cast<float*>(smem + Layout::BETA + b * 64)[tid] = p.beta;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT, 1)
+    kda_chunk_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ g,
+                     const float* __restrict__ beta, const int32_t* __restrict__ cu, const float* __restrict__ state0, float scale,
+                     int H, T* __restrict__ out, float* __restrict__ final_state, sm100::KernelStatus* status) {
+    constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars* bars = reinterpret_cast<Bars*>(smem + Layout::BARS);
+    float* kp32 = reinterpret_cast<float*>(smem + Layout::KP32);
+    float* kn32 = reinterpret_cast<float*>(smem + Layout::KN32);
+    float* qp32 = reinterpret_cast<float*>(smem + Layout::QP32);
+    float* ke32 = reinterpret_cast<float*>(smem + Layout::KE32);
+    float* am = reinterpret_cast<float*>(smem + Layout::AM);  // A [16][17] then M [16][17]
+    float* eb = reinterpret_cast<float*>(smem + Layout::EB);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int wg = warp >> 2, wtid = tid & (WG - 1);
+    const int chain = blockIdx.x;
+    const int s = chain / H, h = chain % H;
+    const int begin = cu[s], end = cu[s + 1];
+    if (begin < 0 || end < 0 || end < begin) return;  // sentinel: not part of this batch
+
+    if (tid == 0) {
+        sm100::mbar_init(&bars->m1, 1);
+        sm100::mbar_init(&bars->m2, 1);
+        for (int b = 0; b < 2; ++b) {
+            sm100::mbar_init(&bars->pfull[b], WG);
+            sm100::mbar_init(&bars->pempty[b], 1);
+        }
+        sm100::fence_mbar_init();
+    }
+    if (warp == 0) {
+        sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    const int nchunks = (end - begin + C - 1) / C;
+    Prefetch pf;
+    if (wg == 1 && nchunks > 0) load_chunk<T>(pf, q, k, v, g, beta, begin, min(C, end - begin), H, h, wtid);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int vrow = wtid;  // value row owned by a state thread (TMEM lane)
+    const size_t srow = (((size_t)s * H + h) * D + vrow) * D;
+    bool ok = true;
+
+    if (wg == 1) {
+        // ================= prep warpgroup =================
+        for (int ci = 0; ci < nchunks && ok; ++ci) {
+            const int b = ci & 1;
+            const int t0 = begin + ci * C;
+            if (ci >= 2 && !sm100::mbar_wait(&bars->pempty[b], ((ci >> 1) - 1) & 1, status, 74)) {
+                ok = false;
+                break;
+            }
+            sm100::named_barrier_sync(1, WG);  // previous iteration's reads of the prep scratch are done
+            store_chunk(pf, smem, wtid, b);
+            sm100::named_barrier_sync(1, WG);
+            if (ci + 1 < nchunks) load_chunk<T>(pf, q, k, v, g, beta, t0 + C, min(C, end - t0 - C), H, h, wtid);
+            {
+                // Factors in fp32, thread = key channel c.
+                const int c = wtid;
+                const float* gs = reinterpret_cast<const float*>(smem + Layout::GS);
+                const uint16_t* ks = reinterpret_cast<const uint16_t*>(smem + Layout::KS);
+                const uint16_t* qs = reinterpret_cast<const uint16_t*>(smem + Layout::QS);
+                float bcum[C];
+                float bacc = 0.f;
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    bacc += gs[t * D + c];
+                    bcum[t] = bacc;
+                }
+                const float elast = __expf(bacc);
+                eb[b * D + c] = elast;
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    const float kv = from16<T>(ks[t * D + c]);
+                    const float qv = from16<T>(qs[t * D + c]) * scale;
+                    const float e = __expf(bcum[t]), en = __expf(-bcum[t]);
+                    kp32[t * KP + c] = kv * e;
+                    kn32[t * KP + c] = kv * en;
+                    qp32[t * KP + c] = qv * e;
+                    ke32[t * KP + c] = kv * (elast * en);
+                }
+            }
+            sm100::named_barrier_sync(1, WG);
+            {
+                // 16-bit MMA operands, 16 bytes at a time: B1 = [Kp ; Qp] (K-major) and Kend (MN-major).
+                uint8_t* b1 = smem + Layout::B1 + b * 8192;
+                uint8_t* ke = smem + Layout::KE + b * 4096;
+#pragma unroll 1
+                for (int idx = wtid; idx < 3 * C * (D / 8); idx += WG) {
+                    const int which = idx / (C * (D / 8)), row = (idx / (D / 8)) % C, ch = idx % (D / 8);
+                    const float* src = (which == 0 ? kp32 : which == 1 ? qp32 : ke32) + row * KP + ch * 8;
+                    const float4 f0 = *reinterpret_cast<const float4*>(src);
+                    const float4 f1 = *reinterpret_cast<const float4*>(src + 4);
+                    const uint4 w = make_uint4((uint32_t)to16<T>(f0.x) | ((uint32_t)to16<T>(f0.y) << 16),
+                                               (uint32_t)to16<T>(f0.z) | ((uint32_t)to16<T>(f0.w) << 16),
+                                               (uint32_t)to16<T>(f1.x) | ((uint32_t)to16<T>(f1.y) << 16),
+                                               (uint32_t)to16<T>(f1.z) | ((uint32_t)to16<T>(f1.w) << 16));
+                    if (which < 2)
+                        *reinterpret_cast<uint4*>(b1 + kmaj(which * C + row, ch * 8, 4096)) = w;
+                    else
+                        *reinterpret_cast<uint4*>(ke + kmaj(row, ch * 8, 2048)) = w;
+                }
+                // A[t][i] (i < t) and M[t][i] (i <= t): thread -> rows t of Kp and Qp, columns i and i + 8.
+                const int t = wtid >> 3, i0c = wtid & 7;
+                const float* lk = kp32 + t * KP;
+                const float* lq = qp32 + t * KP;
+                const float* r0 = kn32 + i0c * KP;
+                const float* r1 = kn32 + (i0c + 8) * KP;
+                float a00 = 0.f, a01 = 0.f, m00 = 0.f, m01 = 0.f;
+#pragma unroll 4
+                for (int cc = 0; cc < D; cc += 4) {
+                    const float4 x = *reinterpret_cast<const float4*>(lk + cc);
+                    const float4 y = *reinterpret_cast<const float4*>(lq + cc);
+                    const float4 u = *reinterpret_cast<const float4*>(r0 + cc);
+                    const float4 w = *reinterpret_cast<const float4*>(r1 + cc);
+                    a00 = fmaf(x.x, u.x, fmaf(x.y, u.y, fmaf(x.z, u.z, fmaf(x.w, u.w, a00))));
+                    a01 = fmaf(x.x, w.x, fmaf(x.y, w.y, fmaf(x.z, w.z, fmaf(x.w, w.w, a01))));
+                    m00 = fmaf(y.x, u.x, fmaf(y.y, u.y, fmaf(y.z, u.z, fmaf(y.w, u.w, m00))));
+                    m01 = fmaf(y.x, w.x, fmaf(y.y, w.y, fmaf(y.z, w.z, fmaf(y.w, w.w, m01))));
+                }
+                float* amb = am + b * (Layout::AM_BYTES / 4);
+                amb[t * 17 + i0c] = i0c < t ? a00 : 0.f;
+                amb[t * 17 + i0c + 8] = i0c + 8 < t ? a01 : 0.f;
+                amb[C * 17 + t * 17 + i0c] = i0c <= t ? m00 : 0.f;
+                amb[C * 17 + t * 17 + i0c + 8] = i0c + 8 <= t ? m01 : 0.f;
+            }
+            sm100::fence_proxy_async_smem();  // B1 / KE are read by the MMAs
+            sm100::mbar_arrive(&bars->pfull[b]);
+        }
+    } else {
+        // ================= state warpgroup =================
+        // Initial state -> TMEM (zero when none is given).
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(state0 ? state0[srow + cb * 32 + j] : 0.f);
+            sm100::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r);
+        }
+        sm100::tmem_st_wait();
+        for (int ci = 0; ci < nchunks && ok; ++ci) {
+            const int b = ci & 1;
+            const int t0 = begin + ci * C;
+            const int nt = min(C, end - t0);
+            if (!sm100::mbar_wait(&bars->pfull[b], (ci >> 1) & 1, status, 75) ||
+                (ci > 0 && !sm100::mbar_wait(&bars->m2, (ci - 1) & 1, status, 71))) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+            // S0: 16-bit operand copy, and the decayed state written back for the update.
+            {
+                const float* ebb = eb + b * D;
+                uint32_t r[4][32];
+#pragma unroll
+                for (int cb = 0; cb < 4; ++cb) sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r[cb]);
+                sm100::tmem_ld_wait();
+#pragma unroll
+                for (int cb = 0; cb < 4; ++cb) {
+#pragma unroll
+                    for (int j8 = 0; j8 < 4; ++j8) {
+                        uint32_t w4[4];
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; ++e2) {
+                            const float x0 = __uint_as_float(r[cb][j8 * 8 + 2 * e2]), x1 = __uint_as_float(r[cb][j8 * 8 + 2 * e2 + 1]);
+                            w4[e2] = (uint32_t)to16<T>(x0) | ((uint32_t)to16<T>(x1) << 16);
+                        }
+                        const int col = cb * 32 + j8 * 8;
+                        *reinterpret_cast<uint4*>(smem + Layout::SA + kmaj(vrow, col, 16384)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[cb][j] = __float_as_uint(__uint_as_float(r[cb][j]) * ebb[cb * 32 + j]);
+                    sm100::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r[cb]);
+                }
+                sm100::tmem_st_wait();
+            }
+            sm100::fence_proxy_async_smem();
+            sm100::tc_fence_before();
+            sm100::named_barrier_sync(2, WG);
+
+            // ---- MMA 1: [U' | O'] = S0 . [Kp ; Qp]^T ----
+            if (wtid == 0) {
+                sm100::tc_fence_after();
+                constexpr uint32_t idesc = sm100::idesc_f16(128, 2 * C, BF16);
+                const uint32_t sa = sm100::smem_u32(smem + Layout::SA);
+                const uint32_t sb = sm100::smem_u32(smem + Layout::B1 + b * 8192);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint64_t ad = sm100::smem_desc_k_sw128(sa + (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32));
+                    const uint64_t bd = sm100::smem_desc_k_sw128(sb + (uint32_t)((kk >> 2) * 4096 + (kk & 3) * 32));
+                    sm100::mma_f16(tmem + 128, ad, bd, idesc, kk > 0 ? 1u : 0u);
+                }
+                sm100::mma_commit(&bars->m1);
+            }
+            if (!sm100::mbar_wait(&bars->m1, ci & 1, status, 72)) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+
+            // ---- rows: u = v - U', w by forward substitution, o = O' + M w ----
+            {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem + lane_off + 128, r);
+                sm100::tmem_ld_wait();
+                const uint16_t* vs = reinterpret_cast<const uint16_t*>(smem + Layout::VS + b * C * D * 2);
+                const float* bsb = reinterpret_cast<const float*>(smem + Layout::BETA + b * 64);
+                const float* A = am + b * (Layout::AM_BYTES / 4);
+                const float* M = A + C * 17;
+                float w[C];
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    float u = from16<T>(vs[t * D + vrow]) - __uint_as_float(r[t]);
+#pragma unroll
+                    for (int i = 0; i < t; ++i) u = fmaf(-A[t * 17 + i], w[i], u);
+                    w[t] = bsb[t] * u;
+                }
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    float o = __uint_as_float(r[C + t]);
+#pragma unroll
+                    for (int i = 0; i <= t; ++i) o = fmaf(M[t * 17 + i], w[i], o);
+                    if (t < nt) out[((size_t)(t0 + t) * H + h) * D + vrow] = sf::Dt<T>::from_f(o);
+                }
+                // W^T row v: t = 0..15 is K of the update MMA (16-byte groups 0 and 1 of the row).
+                uint32_t hi[8], lo[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint16_t h0 = to16<T>(w[2 * j]), h1 = to16<T>(w[2 * j + 1]);
+                    const float f0 = from16<T>(h0), f1 = from16<T>(h1);
+                    hi[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                    const float r0 = isfinite(f0) ? w[2 * j] - f0 : 0.f, r1 = isfinite(f1) ? w[2 * j + 1] - f1 : 0.f;
+                    lo[j] = (uint32_t)to16<T>(r0) | ((uint32_t)to16<T>(r1) << 16);
+                }
+#pragma unroll
+                for (int grp = 0; grp < 2; ++grp) {
+                    const int off = vrow * 128 + ((grp ^ (vrow & 7)) << 4);
+                    *reinterpret_cast<uint4*>(smem + Layout::WH + off) = make_uint4(hi[4 * grp], hi[4 * grp + 1], hi[4 * grp + 2], hi[4 * grp + 3]);
+                    *reinterpret_cast<uint4*>(smem + Layout::WL + off) = make_uint4(lo[4 * grp], lo[4 * grp + 1], lo[4 * grp + 2], lo[4 * grp + 3]);
+                }
+            }
+            sm100::fence_proxy_async_smem();
+            sm100::tc_fence_before();
+            sm100::named_barrier_sync(2, WG);
+
+            // ---- MMA 2: S += W^T . Kend (high + residual); its completion frees buffer b ----
+            if (wtid == 0) {
+                sm100::tc_fence_after();
+                constexpr uint32_t idesc = sm100::idesc_f16_bmn(128, D, BF16);
+                const uint64_t bd = sm100::smem_desc_mn_sw128(sm100::smem_u32(smem + Layout::KE + b * 4096), 2048, 1024);
+                sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sm100::smem_u32(smem + Layout::WH)), bd, idesc, 1u);
+                sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sm100::smem_u32(smem + Layout::WL)), bd, idesc, 1u);
+                sm100::mma_commit(&bars->m2);
+                sm100::mma_commit(&bars->pempty[b]);
+            }
+        }
+    }
+
+    // ---- final state (state warpgroup) ----
+    if (wg == 0 && ok && nchunks > 0 && !sm100::mbar_wait(&bars->m2, (nchunks - 1) & 1, status, 73)) ok = false;
+    sm100::tc_fence_after();
+    if (wg == 0 && ok) {
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t r[32];
+            sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r);
+            sm100::tmem_ld_wait();
+            float4* dst = reinterpret_cast<float4*>(final_state + srow + cb * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                                     __uint_as_float(r[4 * j + 3]));
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 0) sm100::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+sm100::KernelStatus* status_ptr() {
+    sm100::KernelStatus* p = nullptr;
+    if (cudaGetSymbolAddress((void**)&p, g_kda_status) != cudaSuccess) return nullptr;
+    return p;
+}
+
+}  // namespace
+
+// Chunked kernel for D = 128 with 16-byte-aligned q/k/v/g rows; returns SF_EINVAL (without
+// launching) when the shape or alignment does not qualify.
+int sf_kda_gated_chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                              const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t Dd, float scale,
+                              int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
+    if (Dd != D || !sf::aligned16(q) || !sf::aligned16(k) || !sf::aligned16(v) || !sf::aligned16(g) || !sf::aligned16(final_state) ||
+        (initial_state && !sf::aligned16(initial_state)))
+        return sf::fail(SF_EINVAL, err, cap, "kda_gated: the chunked kernel needs D = 128 and 16-byte-aligned tensors");
+    if (N * H > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "kda_gated: too many chains");
+    sm100::KernelStatus* status = status_ptr();
+    if (!status) return sf::fail(SF_EDEVICE, err, cap, "kda_gated: cannot resolve the status word");
+    const int smem = Layout::BYTES + 1024;
+    static std::atomic<uint64_t> attr_done{0};
+    if (dtype == SF_DTYPE_F16) {
+        if (sf::once_per_device(attr_done)) {
+            cudaFuncSetAttribute(kda_chunk_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            cudaFuncSetAttribute(kda_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        }
+        kda_chunk_kernel<__half><<<(unsigned)(N * H), NT, smem, st>>>((const __half*)q, (const __half*)k, (const __half*)v, (const float*)g,
+                                                                    (const float*)beta, (const int32_t*)cu_seqlens, (const float*)initial_state,
+                                                                    scale, (int)H, (__half*)out, (float*)final_state, status);
+    } else {
+        if (sf::once_per_device(attr_done)) {
+            cudaFuncSetAttribute(kda_chunk_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            cudaFuncSetAttribute(kda_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        }
+        kda_chunk_kernel<__nv_bfloat16><<<(unsigned)(N * H), NT, smem, st>>>(
+            (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (const float*)g, (const float*)beta,
+            (const int32_t*)cu_seqlens, (const float*)initial_state, scale, (int)H, (__nv_bfloat16*)out, (float*)final_state, status);
+    }
+    return sf::check_launch("kda_gated chunk launch", err, cap);
+}
+
+int sf_kda_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream) {
+    sm100::KernelStatus hs{0, 0};
+    if (cudaMemcpyFromSymbolAsync(&hs, g_kda_status, sizeof(hs), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess) return SF_EDEVICE;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return SF_EDEVICE;
+    if (hs.code) {
+        const sm100::KernelStatus zero{0, 0};
+        cudaMemcpyToSymbolAsync(g_kda_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream);
+        cudaStreamSynchronize(stream);
+    }
+    *code = hs.code;
+    *where = hs.where;
+    return SF_OK;
+}

@@ -159,7 +159,7 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
                                  d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype, s, err, cap);
         case SF_OP_KDA_GATED:
             return sf_kda_gated_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], (void*)a[7], (void*)a[8], d->dims[0], d->dims[1],
-                                       d->dims[2], (float)d->attrs[0], d->dtype, s, err, cap);
+                                       d->dims[2], (float)d->attrs[0], d->dtype, d->variant, s, err, cap);
         case SF_OP_MAMBA2:
             return sf_mamba2_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], (void*)a[7], d->dims[0], d->dims[1], d->dims[2], d->dims[3],
                                     d->dims[4], d->dims[5], d->dtype, d->variant, s, err, cap);

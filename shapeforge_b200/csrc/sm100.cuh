@@ -229,6 +229,12 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // tcgen05.mma operand reads).  Executed by every writing thread before it signals the consumer.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Barrier `id` (1..15; 0 is __syncthreads) over the first `nthreads` threads that reach it: a
+// warpgroup-local synchronisation for warp-specialised kernels.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- thread-block clusters ------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

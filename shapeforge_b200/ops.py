@@ -246,7 +246,7 @@ def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scal
 
 
 def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: torch.Tensor | None = None,
-                     output: torch.Tensor | None = None, final_state: torch.Tensor | None = None):
+                     output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0):
     """Gated KDA workload: q, k pre-normalised, ``g`` fp32 log-decay used directly, ``beta`` fp32
     gate used directly, state from zero (or ``initial_state``)."""
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -264,7 +264,7 @@ def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: 
         s0 = initial_state.data_ptr()
     ptrs = [q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), cu_seqlens.data_ptr(), s0,
             output.data_ptr(), final_state.data_ptr()]
-    _run("varlen_kda_gated", q, ptrs, dims=(n, h, d), attrs=(scale,))
+    _run("varlen_kda_gated", q, ptrs, dims=(n, h, d), attrs=(scale,), variant=variant)
     return output, final_state
 
 

@@ -144,3 +144,37 @@ def test_gated_small_ragged(cuda_device):
     ro, rf = _oracle_gated(d, [0, 1, 2], 0.125)
     assert _verdict(_np(out), ro, "bf16", "bf16").ok
     assert _verdict(_np(fin), rf, "bf16", "fp32").ok
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_gated_chunked_ragged_with_state(cuda_device, dtype):
+    """The chunked tensor-core kernel (variant 1): lengths around the 16-token chunk edges, an
+    empty sequence, and a non-zero initial state, against the fp64 recurrence."""
+    lengths = [1, 0, 15, 16, 17, 33, 200]
+    heads = 2
+    inp = cases.kda_gated_inputs(lengths, heads, 128, dtype, seed=5)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    g = torch.Generator().manual_seed(11)
+    s0 = (0.1 * torch.randn((len(lengths), heads, 128, 128), generator=g)).to(cuda_device)
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, initial_state=s0, variant=1)
+    torch.cuda.synchronize()
+    code, where = ops.kernel_status()
+    assert code == 0, (code, where)
+    f = lambda n: _np(d[n])  # noqa: E731
+    ro, rf = oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), inp["cu_seqlens"].numpy(), 0.125, state0=_np(s0))
+    v1 = _verdict(_np(out), ro, dtype, dtype)
+    v2 = _verdict(_np(fin), rf, dtype, "fp32")
+    assert v1.ok, ("output", v1.summary())
+    assert v2.ok, ("final_state", v2.summary())
+
+
+def test_gated_recurrent_variant_still_matches(cuda_device):
+    """variant=2 keeps the recurrent CUDA-core kernel reachable (and correct) for D = 128."""
+    lengths = [40, 7]
+    inp = cases.kda_gated_inputs(lengths, 2, 128, "bf16", seed=9)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, variant=2)
+    torch.cuda.synchronize()
+    ro, rf = _oracle_gated(d, [0, 1], 0.125)
+    assert _verdict(_np(out), ro, "bf16", "bf16").ok
+    assert _verdict(_np(fin), rf, "bf16", "fp32").ok
