@@ -7,7 +7,7 @@
 // [B, H, S, D] row-major fp16/bf16, D in {64, 128}; softmax statistics in fp32.
 //
 // One CTA per (b*h, 128-query tile); 192 threads:
-//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring (3-D tensor
+//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a 3-stage ring (3-D tensor
 //               maps over [B*H, S, D], so rows past S read as zeros and never spill into the next head);
 //   warp 1      MMA issuer: S_j = Q.K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
 //               issued one tile ahead, and O += P_j.V_j (M=128, N=D, K=128) into a TMEM accumulator;
@@ -15,8 +15,9 @@
 //   warps 2..5  softmax, one thread per query row: tcgen05.ld of the score row, scale + mask,
 //               online max/sum in fp32 with exp2; O is rescaled in TMEM (tcgen05.ld/st) only when
 //               the row max grows by more than 2^8 (the final 1/l cancels any stale max, so this is
-//               exact up to rounding); P_j is written as 16-bit into a 128-byte-swizzled K-major
-//               shared tile for the second MMA.  Final O / l is stored with 16-byte stores.
+//               exact up to rounding); P_j is written as 16-bit into tensor memory (tcgen05.st) and
+//               read from there as the A operand of the second MMA, which keeps shared memory for a
+//               deeper K/V ring.  Final O / l is stored with 16-byte stores.
 // Causal CTAs skip every key tile above the diagonal and are scheduled heaviest first.
 // NaN/Inf follow the fp32 reference: the row max propagates NaN, so a special in a query row makes
 // that output row NaN.  Every mbarrier wait is bounded.
@@ -36,12 +37,14 @@ namespace {
 constexpr int BM = 128, BN = 128;
 constexpr int BOX_BYTES = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;   // S0 [0,128), S1 [128,256), O [256, 256+D)
+constexpr uint32_t TMEM_COLS = 512;   // S0 [0,128), S1 [128,256), O [256, 256+D), P [384,448) + residual [448,512)
+constexpr int KV_STAGES = 3;
+constexpr uint32_t P_COL = 384, PLO_COL = 448;
 
 struct __align__(8) Bars {
     uint64_t q_full;
-    uint64_t kv_full[2];
-    uint64_t kv_empty[2];
+    uint64_t kv_full[KV_STAGES];
+    uint64_t kv_empty[KV_STAGES];
     uint64_t s_full[2];
     uint64_t s_free[2];
     uint64_t p_full;
@@ -87,11 +90,9 @@ template <int D, bool PSPLIT>
 struct Layout {
     static constexpr int DB = D / 64;  // 64-column boxes per row
     static constexpr int Q = 0;
-    static constexpr int K = Q + DB * BOX_BYTES;           // K[2][DB] boxes
-    static constexpr int V = K + 2 * DB * BOX_BYTES;       // V[2][DB] boxes
-    static constexpr int P = V + 2 * DB * BOX_BYTES;       // P[2] boxes (128 keys)
-    static constexpr int PLO = P + 2 * BOX_BYTES;          // residual P[2] boxes (PSPLIT only)
-    static constexpr int BARS = PLO + (PSPLIT ? 2 * BOX_BYTES : 0);
+    static constexpr int K = Q + DB * BOX_BYTES;                   // K[KV_STAGES][DB] boxes
+    static constexpr int V = K + KV_STAGES * DB * BOX_BYTES;       // V[KV_STAGES][DB] boxes
+    static constexpr int BARS = V + KV_STAGES * DB * BOX_BYTES;    // P lives in TMEM
     static constexpr int BYTES = BARS + 256;
 };
 
@@ -115,9 +116,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         sm100::mbar_init(&bars->q_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < KV_STAGES; ++i) {
             sm100::mbar_init(&bars->kv_full[i], 1);
             sm100::mbar_init(&bars->kv_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             sm100::mbar_init(&bars->s_full[i], 1);
             sm100::mbar_init(&bars->s_free[i], 128);
         }
@@ -143,8 +146,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             sm100::mbar_arrive_expect_tx(&bars->q_full, DB * BOX_BYTES);
             for (int b = 0; b < DB; ++b) sm100::tma_load_3d(smem + L::Q + b * BOX_BYTES, &tq, &bars->q_full, b * 64, qt * BM, bh);
             for (int j = 0; j < nkv; ++j) {
-                const int st = j & 1;
-                if (!sm100::mbar_wait(&bars->kv_empty[st], ((j >> 1) & 1) ^ 1u, status, 31)) break;
+                const int st = j % KV_STAGES;
+                if (!sm100::mbar_wait(&bars->kv_empty[st], ((j / KV_STAGES) & 1) ^ 1u, status, 31)) break;
                 sm100::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * DB * BOX_BYTES);
                 for (int b = 0; b < DB; ++b) {
                     sm100::tma_load_3d(smem + L::K + (st * DB + b) * BOX_BYTES, &tk, &bars->kv_full[st], b * 64, j * BN, bh);
@@ -158,7 +161,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             constexpr uint32_t idesc_o = sm100::idesc_f16_bmn(BM, D, BF16);
             const uint32_t sq = sm100::smem_u32(smem + L::Q);
             auto issue_s = [&](int j) {
-                const int st = j & 1;
+                const int st = j % KV_STAGES;
                 const uint32_t sk = sm100::smem_u32(smem + L::K + st * DB * BOX_BYTES);
                 const uint32_t dst = tmem + (uint32_t)((j & 1) * 128);
 #pragma unroll
@@ -173,11 +176,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 sm100::tc_fence_after();
                 issue_s(0);
             }
-            const uint32_t sp = sm100::smem_u32(smem + L::P);
             for (int j = 0; j < nkv && ok; ++j) {
                 if (j + 1 < nkv) {
                     const int jn = j + 1;
-                    if (!sm100::mbar_wait(&bars->kv_full[jn & 1], (jn >> 1) & 1, status, 34) ||
+                    if (!sm100::mbar_wait(&bars->kv_full[jn % KV_STAGES], (jn / KV_STAGES) & 1, status, 34) ||
                         !sm100::mbar_wait(&bars->s_free[jn & 1], ((jn >> 1) & 1) ^ 1u, status, 35)) {
                         ok = false;
                         break;
@@ -190,24 +192,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     break;
                 }
                 sm100::tc_fence_after();
-                const uint32_t sv = sm100::smem_u32(smem + L::V + (j & 1) * DB * BOX_BYTES);
+                const uint32_t sv = sm100::smem_u32(smem + L::V + (j % KV_STAGES) * DB * BOX_BYTES);
+                // O += P . V with P (128 rows x 128 keys, two keys per 32-bit column) read from TMEM.
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t ad = sm100::smem_desc_k_sw128(sp + (uint32_t)((kk >> 2) * BOX_BYTES + (kk & 3) * 32));
                     const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
-                    sm100::mma_f16(tmem_o, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    sm100::mma_f16_ta(tmem_o, tmem + P_COL + (uint32_t)(kk * 8), bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 if (PSPLIT) {
-                    const uint32_t spl = sm100::smem_u32(smem + L::PLO);
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk) {
-                        const uint64_t ad = sm100::smem_desc_k_sw128(spl + (uint32_t)((kk >> 2) * BOX_BYTES + (kk & 3) * 32));
                         const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
-                        sm100::mma_f16(tmem_o, ad, bd, idesc_o, 1u);
+                        sm100::mma_f16_ta(tmem_o, tmem + PLO_COL + (uint32_t)(kk * 8), bd, idesc_o, 1u);
                     }
                 }
                 sm100::mma_commit(&bars->pv_done);
-                sm100::mma_commit(&bars->kv_empty[j & 1]);
+                sm100::mma_commit(&bars->kv_empty[j % KV_STAGES]);
             }
         }
     } else {
@@ -218,7 +218,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        uint8_t* pbase = smem + L::P;
         for (int j = 0; j < nkv; ++j) {
             if (!sm100::mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 37)) {
                 ok = false;
@@ -250,13 +249,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int c = 0; c < BN; ++c) rmax = fmax_nan(rmax, s[c]);
             const float m_new = fmax_nan(m, rmax * scale_log2);
             const bool need = !(m_new <= m + 8.0f);
+            const float m_old = m;
+            if (need) m = m_new;
+            // p = 2^(s * scale * log2(e) - m): one FFMA + one MUFU.EX2 per score.  Computed before
+            // waiting for the previous tile's P.V, so the exponentials overlap those MMAs; only the
+            // O rescale and the P write below need P.V(j-1) to have finished.
+            const float neg_m = -m;
+            float rsum0 = 0.f, rsum1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < BN; c += 2) {
+                const float p0 = ex2_approx(fmaf(s[c], scale_log2, neg_m));
+                const float p1 = ex2_approx(fmaf(s[c + 1], scale_log2, neg_m));
+                s[c] = p0;
+                s[c + 1] = p1;
+                rsum0 += p0;
+                rsum1 += p1;
+            }
             if (j > 0) {
                 if (!sm100::mbar_wait(&bars->pv_done, (j - 1) & 1, status, 38)) {
                     ok = false;
                     break;
                 }
                 sm100::tc_fence_after();
-                const float alpha = need ? ex2_approx(m - m_new) : 1.0f;
+                const float alpha = need ? ex2_approx(m_old - m_new) : 1.0f;
                 if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
@@ -271,40 +286,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 if (need) l *= alpha;
             }
-            if (need) m = m_new;
-            // p = 2^(s * scale * log2(e) - m): one FFMA + one MUFU.EX2 per score.
-            const float neg_m = -m;
-            float rsum0 = 0.f, rsum1 = 0.f;
-#pragma unroll
-            for (int c = 0; c < BN; c += 2) {
-                const float p0 = ex2_approx(fmaf(s[c], scale_log2, neg_m));
-                const float p1 = ex2_approx(fmaf(s[c + 1], scale_log2, neg_m));
-                s[c] = p0;
-                s[c + 1] = p1;
-                rsum0 += p0;
-                rsum1 += p1;
-            }
             l += rsum0 + rsum1;
-            // P row -> K-major swizzled tiles: keys 0..63 in box 0, 64..127 in box 1.
+            // P row -> TMEM columns [P_COL, P_COL + 64): keys 2c, 2c+1 packed in column c (and the
+            // residual of the 16-bit rounding at PLO_COL).
 #pragma unroll
-            for (int cc = 0; cc < BN / 8; ++cc) {
-                const uint4 v = make_uint4(pack2<T>(s[cc * 8 + 0], s[cc * 8 + 1]), pack2<T>(s[cc * 8 + 2], s[cc * 8 + 3]),
-                                           pack2<T>(s[cc * 8 + 4], s[cc * 8 + 5]), pack2<T>(s[cc * 8 + 6], s[cc * 8 + 7]));
-                const int off = (cc >> 3) * BOX_BYTES + row * 128 + (((cc & 7) ^ (row & 7)) * 16);
-                *reinterpret_cast<uint4*>(pbase + off) = v;
-                if (PSPLIT) {
-                    // Residual of the 16-bit rounding of each probability.
-                    float r[8];
+            for (int half = 0; half < 2; ++half) {
+                uint32_t hv[32], lv[32];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const uint32_t w = (i & 1) ? ((&v.x)[i >> 1] >> 16) : ((&v.x)[i >> 1] & 0xFFFFu);
-                        r[i] = s[cc * 8 + i] - sf::Dt<T>::to_f(*reinterpret_cast<const T*>(&w));
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = s[half * 64 + 2 * i], p1 = s[half * 64 + 2 * i + 1];
+                    if (PSPLIT && BF16) {
+                        // bf16: the high part is the upper half of the fp32 bits (truncation, one byte
+                        // permute for two values) and the residual p - high is exact in fp32, so only
+                        // the residual is rounded: ~16 significant bits in total.
+                        const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+                        hv[i] = __byte_perm(b0, b1, 0x7632);
+                        lv[i] = pack2<T>(p0 - __uint_as_float(b0 & 0xFFFF0000u), p1 - __uint_as_float(b1 & 0xFFFF0000u));
+                    } else {
+                        hv[i] = pack2<T>(p0, p1);
+                        if (PSPLIT) {
+                            const float h0 = sf::Dt<T>::to_f(*reinterpret_cast<const T*>(reinterpret_cast<const uint16_t*>(&hv[i])));
+                            const float h1 = sf::Dt<T>::to_f(*reinterpret_cast<const T*>(reinterpret_cast<const uint16_t*>(&hv[i]) + 1));
+                            lv[i] = pack2<T>(p0 - h0, p1 - h1);
+                        }
                     }
-                    *reinterpret_cast<uint4*>(smem + L::PLO + off) =
-                        make_uint4(pack2<T>(r[0], r[1]), pack2<T>(r[2], r[3]), pack2<T>(r[4], r[5]), pack2<T>(r[6], r[7]));
                 }
+                sm100::tmem_st_32x32b_x32(tmem + lane_off + P_COL + (uint32_t)(half * 32), hv);
+                if (PSPLIT) sm100::tmem_st_32x32b_x32(tmem + lane_off + PLO_COL + (uint32_t)(half * 32), lv);
             }
-            sm100::fence_proxy_async_smem();
+            sm100::tmem_st_wait();
             sm100::tc_fence_before();
             sm100::mbar_arrive(&bars->p_full);
         }

@@ -162,6 +162,19 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T for kind::f16: A (M rows in TMEM lanes, K along columns, two
+// 16-bit elements per 32-bit column, the lower K index in the low half) is read from tensor memory.
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // mma_f16 that leaves some accumulator rows untouched: TMEM lane i (row i of D) is not written
 // when bit (i % 32) of disable[i / 32] is set.  Lets one M=128 MMA serve two independent 64-row
 // problems stacked in A (each half masked in turn) without their products mixing.
