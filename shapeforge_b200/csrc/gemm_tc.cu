@@ -14,7 +14,10 @@
 //   warps 2..5  epilogue: tcgen05.ld of the 128x256 fp32 accumulator (each warp its 32-lane
 //               TMEM quadrant), convert, 16-byte stores to C.
 // The TMEM accumulator is double-buffered (2 x 256 columns), so the epilogue of tile i
-// overlaps the main loop of tile i+1.  Every mbarrier wait is bounded (sm100::mbar_wait):
+// overlaps the main loop of tile i+1.  Work units are visited round-robin by the persistent
+// CTAs; when the tiles left after the last full round fit twice on the SMs, each of them is split
+// into two 128-column halves (N=128 MMAs), so the last round takes half a tile instead of a whole
+// one (4096^3: 3.5 instead of 4 tile times per CTA).  Every mbarrier wait is bounded (sm100::mbar_wait):
 // a wait that gives up records a status word and the CTA drains to its teardown.
 #include "sf_common.cuh"
 #include "sm100.cuh"
@@ -65,6 +68,19 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
     tn = in_group / rows;
 }
 
+// Work unit u: a full 128 x 256 tile for u < full_units, else half `half` (0/1, 128 columns each)
+// of tile full_units + (u - full_units) / 2.
+__device__ __forceinline__ void unit_coords(int u, int full_units, int tiles_m, int tiles_n, int& tm, int& tn, int& half) {
+    if (u < full_units) {
+        tile_coords(u, tiles_m, tiles_n, tm, tn);
+        half = -1;
+    } else {
+        const int h = u - full_units;
+        tile_coords(full_units + (h >> 1), tiles_m, tiles_n, tm, tn);
+        half = h & 1;
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -81,7 +97,8 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
 template <typename T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_nt_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                      T* __restrict__ C, int M, int N, int K, sm100::KernelStatus* status) {
+                      const __grid_constant__ CUtensorMap tmap_bh, T* __restrict__ C, int M, int N, int K, int full_units,
+                      int total_units, sm100::KernelStatus* status) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -91,7 +108,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int lane = threadIdx.x & 31;
     const int tiles_m = (M + BM - 1) / BM;
     const int tiles_n = (N + BN - 1) / BN;
-    const int num_tiles = tiles_m * tiles_n;
     const int num_kb = (K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -108,6 +124,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0 && lane == 0) {
         sm100::tma_prefetch_desc(&tmap_a);
         sm100::tma_prefetch_desc(&tmap_b);
+        sm100::tma_prefetch_desc(&tmap_bh);
     }
     if (warp == 1) {
         sm100::tmem_alloc(&bars->tmem_base, TMEM_COLS);
@@ -124,9 +141,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                int tm, tn;
-                tile_coords(tile, tiles_m, tiles_n, tm, tn);
+            for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+                int tm, tn, half;
+                unit_coords(u, full_units, tiles_m, tiles_n, tm, tn, half);
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!sm100::mbar_wait(&bars->empty[stage], phase ^ 1u, status, 1)) {
                         ok = false;
@@ -134,9 +151,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + A_BYTES;
-                    sm100::mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
+                    sm100::mbar_arrive_expect_tx(&bars->full[stage], half < 0 ? STAGE_BYTES : A_BYTES + B_BYTES / 2);
                     sm100::tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * BK, tm * BM);
-                    sm100::tma_load_2d(sb, &tmap_b, &bars->full[stage], kb * BK, tn * BN);
+                    if (half < 0)
+                        sm100::tma_load_2d(sb, &tmap_b, &bars->full[stage], kb * BK, tn * BN);
+                    else
+                        sm100::tma_load_2d(sb, &tmap_bh, &bars->full[stage], kb * BK, tn * BN + half * (BN / 2));
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -156,13 +176,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = sm100::idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+            constexpr uint32_t idesc_full = sm100::idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+            constexpr uint32_t idesc_half = sm100::idesc_f16(BM, BN / 2, std::is_same<T, __nv_bfloat16>::value);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+                const uint32_t idesc = u < full_units ? idesc_full : idesc_half;
                 if (!sm100::mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, status, 3)) break;
                 sm100::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -201,19 +223,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         const bool vec_ok = (N % 8) == 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            int tm, tn;
-            tile_coords(tile, tiles_m, tiles_n, tm, tn);
+        for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+            int tm, tn, half;
+            unit_coords(u, full_units, tiles_m, tiles_n, tm, tn, half);
+            const int width = half < 0 ? BN : BN / 2;
+            const int col_base = tn * BN + (half < 0 ? 0 : half * (BN / 2));
             if (!sm100::mbar_wait(&bars->acc_full[acc], acc_phase, status, 5)) break;
             sm100::tc_fence_after();
             const int row = tm * BM + row_in_tile;
             const uint32_t t_base = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = 0; c < width; c += 32) {
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(t_base + (uint32_t)c, r);
                 sm100::tmem_ld_wait();
-                const int col0 = tn * BN + c;
+                const int col0 = col_base + c;
                 if (row < M) {
                     T* dst = C + (size_t)row * (size_t)N + col0;
                     if (vec_ok && col0 + 32 <= N) {
@@ -252,10 +276,12 @@ template <typename T>
 int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream, char* err,
               uint64_t cap) {
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mbh;
     int rc = sf::tmap_kmajor(&ma, A, M, K, BM, bf16, err, cap);
     if (rc) return rc;
     rc = sf::tmap_kmajor(&mb, B, N, K, BN, bf16, err, cap);
+    if (rc) return rc;
+    rc = sf::tmap_kmajor(&mbh, B, N, K, BN / 2, bf16, err, cap);
     if (rc) return rc;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -266,8 +292,19 @@ int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     if (sf::once_per_device(attr_done))
         cudaFuncSetAttribute(gemm_nt_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const int grid = (int)std::min<int64_t>(tiles, sf::sm_count());
-    gemm_nt_tc_kernel<T><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, (T*)C, (int)M, (int)N, (int)K, st);
+    const int64_t sms = std::max(1, sf::sm_count());
+    // Tiles left over after the last full round of the persistent CTAs are split into halves when
+    // the halves still fit in one round.
+    const int64_t rounds = tiles / sms, tail = tiles - rounds * sms;
+    int64_t full_units = tiles, total_units = tiles;
+    if (tail > 0 && 2 * tail <= sms) {
+        full_units = rounds * sms;
+        total_units = full_units + 2 * tail;
+    }
+    if (total_units > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "gemm: too many tiles");
+    const int grid = (int)std::min<int64_t>(total_units, sms);
+    gemm_nt_tc_kernel<T><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, mbh, (T*)C, (int)M, (int)N, (int)K, (int)full_units,
+                                                                    (int)total_units, st);
     return sf::check_launch("gemm_nt tcgen05 launch", err, cap);
 }
 
