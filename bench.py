@@ -134,7 +134,7 @@ class Workload:
     make_sets: Callable  # (device, nsets) -> list of (tensors tuple, pointer list)
     desc: Callable  # () -> sf_op_desc
     host_inputs: Callable  # () -> (list of pinned host input tensors, list of output shapes/dtypes)
-    e2e_step: Callable  # (host inputs, device inputs, device outputs, host outputs) -> None
+    e2e_launch: Callable  # (device inputs, device outputs, stream) -> None: the public C-ABI call
     cpu_rows: Callable  # (rows) -> (callable running the oracle on a row sample, units of that call, description)
     total_rows: int  # rows of the full shard (the sample is a row subset; rows are independent)
     nsets: int = 4
@@ -173,12 +173,9 @@ def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
         inp = cases.gemm_bench_inputs(m, n, k, dtype, seed=cases.SEARCH_SEED)
         return [inp["A"].pin_memory(), inp["B"].pin_memory()], [((m, n), td)]
 
-    def e2e_step(h_in, d_in, d_out, h_out, stream):
-        d_in[0].copy_(h_in[0], non_blocking=True)
-        d_in[1].copy_(h_in[1], non_blocking=True)
+    def e2e_launch(d_in, d_out, stream):
         _native.call("sf_gemm_nt", d_in[0].data_ptr(), d_in[1].data_ptr(), d_out[0].data_ptr(), m, n, k,
                      _native.DTYPE_CODES[dtype], stream)
-        h_out[0].copy_(d_out[0], non_blocking=True)
 
     def cpu_rows(rows):
         # The reference's algorithm (tasks/gemm/reference.py:110-114: an fp32 product) through
@@ -206,7 +203,7 @@ def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
         make_sets=make_sets,
         desc=desc,
         host_inputs=host_inputs,
-        e2e_step=e2e_step,
+        e2e_launch=e2e_launch,
         cpu_rows=cpu_rows,
         total_rows=m,
         nsets=nsets,
@@ -240,12 +237,9 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
         inp = cases.rmsnorm_bench_inputs(rows, hidden, dtype)
         return [inp["x"].pin_memory(), inp["w"].pin_memory()], [((rows, hidden), td)]
 
-    def e2e_step(h_in, d_in, d_out, h_out, stream):
-        d_in[0].copy_(h_in[0], non_blocking=True)
-        d_in[1].copy_(h_in[1], non_blocking=True)
+    def e2e_launch(d_in, d_out, stream):
         _native.call("sf_rmsnorm", d_in[0].data_ptr(), d_in[1].data_ptr(), d_out[0].data_ptr(), rows, hidden, 1e-6,
                      _native.DTYPE_CODES[dtype], stream)
-        h_out[0].copy_(d_out[0], non_blocking=True)
 
     def cpu_rows(r):
         from oracle import ops as oref
@@ -270,7 +264,7 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
         make_sets=make_sets,
         desc=desc,
         host_inputs=host_inputs,
-        e2e_step=e2e_step,
+        e2e_launch=e2e_launch,
         cpu_rows=cpu_rows,
         total_rows=rows,
         nsets=nsets,
@@ -313,19 +307,15 @@ def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_input
         ins = make_inputs(cases_seed())
         return [ins[n].pin_memory() for n in in_names], list(out_specs)
 
-    def e2e_step(h_in, d_in, d_out, h_out, stream):
-        for d, h in zip(d_in, h_in):
-            d.copy_(h, non_blocking=True)
+    def e2e_launch(d_in, d_out, stream):
         ptrs = [t.data_ptr() for t in d_in] + [o.data_ptr() for o in d_out]
         for pos in null_args:
             ptrs.insert(pos, 0)
         _native.run_op(desc(), ptrs, stream)
-        for h, d in zip(h_out, d_out):
-            h.copy_(d, non_blocking=True)
 
     return Workload(name=name, unit=unit, bound=bound, dtype=dtype, units_per_step=units,
                     config=dict(config, l2=f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB"),
-                    kernel=kernel, make_sets=make_sets, desc=desc, host_inputs=host_inputs, e2e_step=e2e_step,
+                    kernel=kernel, make_sets=make_sets, desc=desc, host_inputs=host_inputs, e2e_launch=e2e_launch,
                     cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets)
 
 
@@ -452,7 +442,7 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
         {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
                      "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
          "total_tokens": total},
-        "kda_fwd_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"],
+        "kda_chunk_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"],
         [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim),
         (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,))
     if world > 1:
@@ -664,29 +654,64 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_s = float(t.item())
 
-    # End to end through the C ABI with host buffers (pinned), copies inside the timed region.
+    # End to end through the C ABI with host buffers (pinned): every step copies its inputs from
+    # host to device, runs the operator and copies its outputs back, all inside the timed region.
+    # Steps are pipelined over two buffer sets and three streams (host->device, compute,
+    # device->host), so the copies of one step overlap the kernel and copies of its neighbours.
     h_in, out_specs = wl.host_inputs()
-    d_in = [h.to(dev) for h in h_in]
-    d_out = [torch.empty(shape, dtype=dt, device=dev) for shape, dt in out_specs]
-    h_out = [torch.empty(shape, dtype=dt).pin_memory() for shape, dt in out_specs]
+    d_in = [[h.to(dev) for h in h_in] for _ in range(2)]
+    d_out = [[torch.empty(shape, dtype=dt, device=dev) for shape, dt in out_specs] for _ in range(2)]
+    h_out = [[torch.empty(shape, dtype=dt).pin_memory() for shape, dt in out_specs] for _ in range(2)]
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     e2e_steps = max(1, min(args.steps, 50))
-    for _ in range(2):
-        wl.e2e_step(h_in, d_in, d_out, h_out, sptr)
+
+    def run_e2e(n_steps):
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for st in (s_in, s_cmp, s_out):
+            st.wait_event(start)
+        in_done, cmp_done, out_done = [], [], []
+        for i in range(n_steps):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(cmp_done[i - 2])  # the kernel of step i-2 has read d_in[b]
+                for d, h in zip(d_in[b], h_in):
+                    d.copy_(h, non_blocking=True)
+                in_done.append(torch.cuda.Event())
+                in_done[-1].record(s_in)
+            s_cmp.wait_event(in_done[i])
+            if i >= 2:
+                s_cmp.wait_event(out_done[i - 2])  # d_out[b] has been copied out
+            wl.e2e_launch(d_in[b], d_out[b], s_cmp.cuda_stream)
+            cmp_done.append(torch.cuda.Event())
+            cmp_done[-1].record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(cmp_done[i])
+                for h, d in zip(h_out[b], d_out[b]):
+                    h.copy_(d, non_blocking=True)
+                out_done.append(torch.cuda.Event())
+                out_done[-1].record(s_out)
+        for st in (s_in, s_cmp, s_out):
+            ev = torch.cuda.Event()
+            ev.record(st)
+            stream.wait_event(ev)
+        stop.record(stream)
+        stop.synchronize()
+        return start.elapsed_time(stop) * 1e-3
+
+    run_e2e(2)
     torch.cuda.synchronize(dev)
     barrier()
     torch.cuda.synchronize(dev)
-    f0 = torch.cuda.Event(enable_timing=True)
-    f1 = torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(e2e_steps):
-        wl.e2e_step(h_in, d_in, d_out, h_out, sptr)
-    f1.record(stream)
+    e2e_s = torch.tensor([run_e2e(e2e_steps)], dtype=torch.float64, device=dev)
     torch.cuda.synchronize(dev)
     barrier()
-    e2e_s = torch.tensor([f0.elapsed_time(f1) * 1e-3], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_time = float(e2e_s.item())
+    h_out = h_out[0]
 
     if rank != 0:
         return None
@@ -736,7 +761,8 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
             "kernel": wl.kernel,
         },
         "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps, "path": "sf_* C ABI, pinned host buffers, H2D + kernel + D2H per step"},
+                "steps": e2e_steps,
+                "path": "sf_* C ABI, pinned host buffers, H2D + kernel + D2H per step, consecutive steps pipelined over two buffer sets"},
         "gpu_launches": args.steps * wl.launches_per_step,
         "clocks": clock_summary,
         "impl": "ours",
