@@ -6,19 +6,25 @@
 // in fp32, SM_SCALE attr); the causal workload is the same formula with the mask.  q, k, v, o are
 // [B, H, S, D] row-major fp16/bf16, D in {64, 128}; softmax statistics in fp32.
 //
-// One CTA per (b*h, 128-query tile); 192 threads:
-//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a 3-stage ring (3-D tensor
-//               maps over [B*H, S, D], so rows past S read as zeros and never spill into the next head);
-//   warp 1      MMA issuer: S_j = Q.K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
-//               issued one tile ahead, and O += P_j.V_j (M=128, N=D, K=128) into a TMEM accumulator;
-//               V is read as an MN-major operand straight from its [keys, D] layout;
-//   warps 2..5  softmax, one thread per query row: tcgen05.ld of the score row, scale + mask,
-//               online max/sum in fp32 with exp2; O is rescaled in TMEM (tcgen05.ld/st) only when
-//               the row max grows by more than 2^8 (the final 1/l cancels any stale max, so this is
-//               exact up to rounding); P_j is written as 16-bit into tensor memory (tcgen05.st) and
-//               read from there as the A operand of the second MMA, which keeps shared memory for a
-//               deeper K/V ring.  Final O / l is stored with 16-byte stores.
-// Causal CTAs skip every key tile above the diagonal and are scheduled heaviest first.
+// One CTA per (b*h, 128-query tile), two CTAs resident per SM (256 TMEM columns, ~97 KB of shared
+// memory each), so one CTA's softmax, prologue and epilogue overlap the other's MMAs; 192 threads:
+//   warp 0      TMA producer: Q once, then K_j and V_j tiles of 128 keys into their own slots
+//               (one slot each for D=128, two for D=64; 3-D tensor maps over [B*H, S, D], so rows
+//               past S read as zeros and never spill into the next head);
+//   warp 1      MMA issuer: S_j = Q.K_j^T (M=128, N=128, K=D) into TMEM columns [0,128), then, once
+//               the softmax has written P_j over those columns, O += P_j.V_j (M=128, N=D, K=128)
+//               with P read from TMEM as the A operand and V as an MN-major operand straight from
+//               its [keys, D] layout.  S_{j+1} is issued after P_j.V_j into the same columns: the
+//               tensor pipe executes one CTA's MMAs in issue order, so P_j is read before it is
+//               overwritten, and the commit that publishes S_{j+1} also covers P_j.V_j;
+//   warps 2..5  softmax, one thread per query row: two passes over the score row in TMEM (row max,
+//               then exp2 and P), online max/sum in fp32; O is rescaled in TMEM (tcgen05.ld/st) only
+//               when the row max grows by more than 2^8 (the final 1/l cancels any stale max, so this
+//               is exact up to rounding); P_j is written as a 16-bit high part and a 16-bit residual
+//               into the score columns it was computed from.  Final O / l is stored with 16-byte
+//               stores.
+// Causal CTAs skip every key tile above the diagonal.  Blocks walk groups of heads whose K/V fit
+// in L2 together, heaviest query tiles first within a group.
 // NaN/Inf follow the fp32 reference: the row max propagates NaN, so a special in a query row makes
 // that output row NaN.  Every mbarrier wait is bounded.
 #include "sf_common.cuh"
@@ -37,18 +43,16 @@ namespace {
 constexpr int BM = 128, BN = 128;
 constexpr int BOX_BYTES = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;   // S0 [0,128), S1 [128,256), O [256, 256+D), P [384,448) + residual [448,512)
-constexpr int KV_STAGES = 3;
-constexpr uint32_t P_COL = 384, PLO_COL = 448;
+constexpr uint32_t TMEM_COLS = 256;   // S_j / P_j [0,128), O [128, 128 + D)
+constexpr uint32_t O_COL = 128;
 
 struct __align__(8) Bars {
     uint64_t q_full;
-    uint64_t kv_full[KV_STAGES];
-    uint64_t kv_empty[KV_STAGES];
-    uint64_t s_full[2];
-    uint64_t s_free[2];
-    uint64_t p_full;
-    uint64_t pv_done;
+    uint64_t k_full[2], k_empty[2];
+    uint64_t v_full[2], v_empty[2];
+    uint64_t s_full;
+    uint64_t p_full[2];  // keys [0,64) and [64,128) of P_j written
+    uint64_t o_done;
     uint32_t tmem_base;
 };
 
@@ -69,6 +73,29 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// max of three that returns NaN if any operand is NaN (one instruction on sm_100).
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Packed fp32 pair arithmetic (one FFMA2 / FADD2 for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(reinterpret_cast<uint64_t&>(d))
+        : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)), "l"(reinterpret_cast<const uint64_t&>(c)));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(reinterpret_cast<uint64_t&>(d))
+        : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+    return d;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -82,50 +109,165 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// PSPLIT: P is written as a 16-bit high part and a 16-bit residual (P - high), and P.V is issued
-// twice, so the probabilities enter the product with ~16-22 significant bits instead of 8-11.  A
-// single 16-bit rounding of P, amplified by cancellation between large v terms, can exceed the
-// task tolerances.
-template <int D, bool PSPLIT>
+// P is written as a 16-bit high part and a 16-bit residual (P - high), and P.V is issued twice, so
+// the probabilities enter the product with ~16-22 significant bits instead of 8-11: a single
+// 16-bit rounding of P, amplified by cancellation between large v terms, exceeds the task
+// tolerances.  Keys [32q, 32q + 32) of a tile go to TMEM columns [32q, 32q + 16) (high, two keys
+// per column) and [32q + 16, 32q + 32) (residual): each quarter overwrites only the score columns
+// it was computed from.
+__device__ __forceinline__ uint32_t p_hi_col(int kk) { return (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1)); }
+__device__ __forceinline__ uint32_t p_lo_col(int kk) { return p_hi_col(kk) + 16u; }
+
+template <int D>
 struct Layout {
-    static constexpr int DB = D / 64;  // 64-column boxes per row
+    static constexpr int DB = D / 64;                  // 64-column boxes per row
+    static constexpr int NST = D == 64 ? 2 : 1;        // K (and V) slots
+    static constexpr int TILE = DB * BOX_BYTES;        // one 128-row tile
     static constexpr int Q = 0;
-    static constexpr int K = Q + DB * BOX_BYTES;                   // K[KV_STAGES][DB] boxes
-    static constexpr int V = K + KV_STAGES * DB * BOX_BYTES;       // V[KV_STAGES][DB] boxes
-    static constexpr int BARS = V + KV_STAGES * DB * BOX_BYTES;    // P lives in TMEM
+    static constexpr int K = Q + TILE;                 // K[NST]
+    static constexpr int V = K + NST * TILE;           // V[NST]
+    static constexpr int BARS = V + NST * TILE;
     static constexpr int BYTES = BARS + 256;
 };
 
-template <typename T, int D, bool CAUSAL, bool PSPLIT>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// One score tile of one query row (the calling thread's TMEM lane): row max, lazy rescale of O,
+// exponentials, P_j (high + residual) over the score columns, published a half at a time on
+// p_full[0] / p_full[1].  MASK: keys past `lim` (tile-relative) score -inf.
+template <typename T, int D, bool MASK>
+__device__ __forceinline__ void softmax_tile(uint32_t tmem, uint32_t tmem_o, uint32_t lane_off, int lim, int j, float scale_log2,
+                                             float& m, float& l, uint64_t* p_full) {
+    constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+    // Pass 1: row max of the raw scores (scale > 0 commutes with max); NaN propagates.
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t r[64];
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(64 * h), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(64 * h + 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        sm100::tmem_ld_wait();
+        if (MASK) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (64 * h + c > lim) r[c] = 0xff800000u;  // -inf
+        }
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+            const float a = fmax3_nan(__uint_as_float(r[c]), __uint_as_float(r[c + 1]), __uint_as_float(r[c + 2]));
+            const float b = fmax3_nan(__uint_as_float(r[c + 3]), __uint_as_float(r[c + 4]), __uint_as_float(r[c + 5]));
+            const int k = (c >> 3) & 3;
+            mx[k] = fmax3_nan(mx[k], a, fmax3_nan(b, __uint_as_float(r[c + 6]), __uint_as_float(r[c + 7])));
+        }
+    }
+    const float rmax = fmax3_nan(mx[0], mx[1], fmax_nan(mx[2], mx[3]));
+    const float m_new = fmax_nan(m, rmax * scale_log2);
+    const bool need = !(m_new <= m + 8.0f);
+    const float m_old = m;
+    if (need) m = m_new;
+    // P.V_{j-1} has completed: the commit that published S_j was issued after it.
+    if (j > 0) {
+        const float alpha = need ? ex2_approx(m_old - m_new) : 1.0f;
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+                sm100::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                sm100::tmem_st_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+            }
+        }
+        if (need) l *= alpha;
+    }
+    // Pass 2: p = 2^(s * scale * log2(e) - m), one FFMA2 per two scores and one MUFU.EX2 per score;
+    // P over the score columns just read, a quarter of the keys at a time; each half of the keys is
+    // published as soon as it is in TMEM.
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
+    const float2 nm2 = make_float2(-m, -m);
+    const float2 neg1 = make_float2(-1.f, -1.f);
+    float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+        uint32_t r[64];
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(64 * h), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(64 * h + 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        sm100::tmem_ld_wait();
+        if (MASK) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (64 * h + c > lim) r[c] = 0xff800000u;
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            uint32_t hv[16], lv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float2 x = ffma2(make_float2(__uint_as_float(r[32 * e + 2 * i]), __uint_as_float(r[32 * e + 2 * i + 1])), sc2, nm2);
+                const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                acc[i & 3] = fadd2(acc[i & 3], pp);
+                if (BF16) {
+                    // bf16: the high part is the upper half of the fp32 bits (truncation, one byte
+                    // permute for two values) and the residual p - high is exact in fp32, so only the
+                    // residual is rounded: ~16 significant bits in total.
+                    const uint32_t b0 = __float_as_uint(pp.x), b1 = __float_as_uint(pp.y);
+                    hv[i] = __byte_perm(b0, b1, 0x7632);
+                    const float2 res = ffma2(make_float2(__uint_as_float(b0 & 0xFFFF0000u), __uint_as_float(b1 & 0xFFFF0000u)), neg1, pp);
+                    lv[i] = pack2<T>(res.x, res.y);
+                } else {
+                    hv[i] = pack2<T>(pp.x, pp.y);
+                    const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hv[i]));
+                    const float2 res = ffma2(hf, neg1, pp);
+                    lv[i] = pack2<T>(res.x, res.y);
+                }
+            }
+            const uint32_t col = (uint32_t)(64 * h + 32 * e);
+            sm100::tmem_st_32x32b_x16(tmem + lane_off + col, hv);
+            sm100::tmem_st_32x32b_x16(tmem + lane_off + col + 16u, lv);
+        }
+        sm100::tmem_st_wait();
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&p_full[h]);
+    }
+    const float2 t = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+    l += t.x + t.y;
+}
+
+template <typename T, int D, bool CAUSAL>
+__global__ void __launch_bounds__(NUM_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                  T* __restrict__ o, int S, float scale_log2, sm100::KernelStatus* status) {
-    using L = Layout<D, PSPLIT>;
+                  T* __restrict__ o, int S, int BH, int nq, int group, float scale_log2, sm100::KernelStatus* status) {
+    using L = Layout<D>;
     constexpr int DB = L::DB;
+    constexpr int NST = L::NST;
     constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars* bars = reinterpret_cast<Bars*>(smem + L::BARS);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int nq = (S + BM - 1) / BM;
-    const int qt = CAUSAL ? (nq - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+    // Block -> (head, query tile): groups of `group` heads, heaviest query tiles first in a group.
+    const int64_t per_group = (int64_t)group * nq;
+    const int g = (int)((int64_t)blockIdx.x / per_group);
+    const int hbase = g * group;
+    const int gsize = min(group, BH - hbase);
+    const int rem = (int)((int64_t)blockIdx.x - (int64_t)g * per_group);
+    const int bh = hbase + rem % gsize;
+    const int qt = CAUSAL ? (nq - 1 - rem / gsize) : rem / gsize;
     const int nkv_all = (S + BN - 1) / BN;
     const int nkv = CAUSAL ? min(qt + 1, nkv_all) : nkv_all;
 
     if (threadIdx.x == 0) {
         sm100::mbar_init(&bars->q_full, 1);
-        for (int i = 0; i < KV_STAGES; ++i) {
-            sm100::mbar_init(&bars->kv_full[i], 1);
-            sm100::mbar_init(&bars->kv_empty[i], 1);
+        for (int i = 0; i < NST; ++i) {
+            sm100::mbar_init(&bars->k_full[i], 1);
+            sm100::mbar_init(&bars->k_empty[i], 1);
+            sm100::mbar_init(&bars->v_full[i], 1);
+            sm100::mbar_init(&bars->v_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            sm100::mbar_init(&bars->s_full[i], 1);
-            sm100::mbar_init(&bars->s_free[i], 128);
-        }
-        sm100::mbar_init(&bars->p_full, 128);
-        sm100::mbar_init(&bars->pv_done, 1);
+        sm100::mbar_init(&bars->s_full, 1);
+        sm100::mbar_init(&bars->p_full[0], 128);
+        sm100::mbar_init(&bars->p_full[1], 128);
+        sm100::mbar_init(&bars->o_done, 1);
         sm100::fence_mbar_init();
     }
     if (warp == 1) {
@@ -136,23 +278,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
     sm100::tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    const uint32_t tmem_o = tmem + 256;
+    const uint32_t tmem_o = tmem + O_COL;
 
     if (warp == 0) {
         if (lane == 0) {
             sm100::tma_prefetch_desc(&tq);
             sm100::tma_prefetch_desc(&tk);
             sm100::tma_prefetch_desc(&tv);
-            sm100::mbar_arrive_expect_tx(&bars->q_full, DB * BOX_BYTES);
+            sm100::mbar_arrive_expect_tx(&bars->q_full, L::TILE);
             for (int b = 0; b < DB; ++b) sm100::tma_load_3d(smem + L::Q + b * BOX_BYTES, &tq, &bars->q_full, b * 64, qt * BM, bh);
             for (int j = 0; j < nkv; ++j) {
-                const int st = j % KV_STAGES;
-                if (!sm100::mbar_wait(&bars->kv_empty[st], ((j / KV_STAGES) & 1) ^ 1u, status, 31)) break;
-                sm100::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * DB * BOX_BYTES);
-                for (int b = 0; b < DB; ++b) {
-                    sm100::tma_load_3d(smem + L::K + (st * DB + b) * BOX_BYTES, &tk, &bars->kv_full[st], b * 64, j * BN, bh);
-                    sm100::tma_load_3d(smem + L::V + (st * DB + b) * BOX_BYTES, &tv, &bars->kv_full[st], b * 64, j * BN, bh);
-                }
+                const int st = j % NST;
+                const uint32_t ph = (uint32_t)(j / NST) & 1u;
+                if (!sm100::mbar_wait(&bars->k_empty[st], ph ^ 1u, status, 31)) break;
+                sm100::mbar_arrive_expect_tx(&bars->k_full[st], L::TILE);
+                for (int b = 0; b < DB; ++b)
+                    sm100::tma_load_3d(smem + L::K + st * L::TILE + b * BOX_BYTES, &tk, &bars->k_full[st], b * 64, j * BN, bh);
+                if (!sm100::mbar_wait(&bars->v_empty[st], ph ^ 1u, status, 32)) break;
+                sm100::mbar_arrive_expect_tx(&bars->v_full[st], L::TILE);
+                for (int b = 0; b < DB; ++b)
+                    sm100::tma_load_3d(smem + L::V + st * L::TILE + b * BOX_BYTES, &tv, &bars->v_full[st], b * 64, j * BN, bh);
             }
         }
     } else if (warp == 1) {
@@ -160,55 +305,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             constexpr uint32_t idesc_s = sm100::idesc_f16(BM, BN, BF16);
             constexpr uint32_t idesc_o = sm100::idesc_f16_bmn(BM, D, BF16);
             const uint32_t sq = sm100::smem_u32(smem + L::Q);
-            auto issue_s = [&](int j) {
-                const int st = j % KV_STAGES;
-                const uint32_t sk = sm100::smem_u32(smem + L::K + st * DB * BOX_BYTES);
-                const uint32_t dst = tmem + (uint32_t)((j & 1) * 128);
-#pragma unroll
-                for (int k = 0; k < D / 16; ++k) {
-                    const uint32_t off = (uint32_t)((k >> 2) * BOX_BYTES + (k & 3) * 32);
-                    sm100::mma_f16(dst, sm100::smem_desc_k_sw128(sq + off), sm100::smem_desc_k_sw128(sk + off), idesc_s, k > 0 ? 1u : 0u);
-                }
-                sm100::mma_commit(&bars->s_full[j & 1]);
-            };
-            bool ok = sm100::mbar_wait(&bars->q_full, 0, status, 32) && sm100::mbar_wait(&bars->kv_full[0], 0, status, 33);
-            if (ok) {
-                sm100::tc_fence_after();
-                issue_s(0);
-            }
+            bool ok = sm100::mbar_wait(&bars->q_full, 0, status, 33);
             for (int j = 0; j < nkv && ok; ++j) {
-                if (j + 1 < nkv) {
-                    const int jn = j + 1;
-                    if (!sm100::mbar_wait(&bars->kv_full[jn % KV_STAGES], (jn / KV_STAGES) & 1, status, 34) ||
-                        !sm100::mbar_wait(&bars->s_free[jn & 1], ((jn >> 1) & 1) ^ 1u, status, 35)) {
-                        ok = false;
-                        break;
-                    }
-                    sm100::tc_fence_after();
-                    issue_s(jn);
-                }
-                if (!sm100::mbar_wait(&bars->p_full, j & 1, status, 36)) {
+                const int st = j % NST;
+                const uint32_t ph = (uint32_t)(j / NST) & 1u;
+                // S_j = Q . K_j^T into columns [0, 128).  Issued after P_{j-1}.V_{j-1}, which read
+                // the same columns: the pipe runs this CTA's MMAs in issue order.
+                if (!sm100::mbar_wait(&bars->k_full[st], ph, status, 34)) {
                     ok = false;
                     break;
                 }
                 sm100::tc_fence_after();
-                const uint32_t sv = sm100::smem_u32(smem + L::V + (j % KV_STAGES) * DB * BOX_BYTES);
-                // O += P . V with P (128 rows x 128 keys, two keys per 32-bit column) read from TMEM.
+                const uint32_t sk = sm100::smem_u32(smem + L::K + st * L::TILE);
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
-                    sm100::mma_f16_ta(tmem_o, tmem + P_COL + (uint32_t)(kk * 8), bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint32_t off = (uint32_t)((k >> 2) * BOX_BYTES + (k & 3) * 32);
+                    sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sq + off), sm100::smem_desc_k_sw128(sk + off), idesc_s, k > 0 ? 1u : 0u);
                 }
-                if (PSPLIT) {
+                sm100::mma_commit(&bars->s_full);
+                sm100::mma_commit(&bars->k_empty[st]);
+                // O += P_j . V_j, each half of the keys as soon as the softmax has written its P
+                // (high part, then the residual).
+                if (!sm100::mbar_wait(&bars->v_full[st], ph, status, 36)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t sv = sm100::smem_u32(smem + L::V + st * L::TILE);
 #pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk) {
+                for (int half = 0; half < 2; ++half) {
+                    if (!sm100::mbar_wait(&bars->p_full[half], (uint32_t)j & 1u, status, 35)) {
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+#pragma unroll
+                    for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
                         const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
-                        sm100::mma_f16_ta(tmem_o, tmem + PLO_COL + (uint32_t)(kk * 8), bd, idesc_o, 1u);
+                        sm100::mma_f16_ta(tmem_o, tmem + p_hi_col(kk), bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    }
+#pragma unroll
+                    for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
+                        const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
+                        sm100::mma_f16_ta(tmem_o, tmem + p_lo_col(kk), bd, idesc_o, 1u);
                     }
                 }
-                sm100::mma_commit(&bars->pv_done);
-                sm100::mma_commit(&bars->kv_empty[j % KV_STAGES]);
+                if (!ok) break;
+                sm100::mma_commit(&bars->v_empty[st]);
             }
+            if (ok) sm100::mma_commit(&bars->o_done);
         }
     } else {
         // ---------------- softmax: one thread per query row ----------------
@@ -219,107 +363,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
-            if (!sm100::mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 37)) {
+            if (!sm100::mbar_wait(&bars->s_full, (uint32_t)j & 1u, status, 37)) {
                 ok = false;
                 break;
             }
             sm100::tc_fence_after();
-            // Raw scores: four independent 32-column loads, one wait.
-            uint32_t sr[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c)
-                sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * 128 + c * 32),
-                                          *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-            sm100::tmem_ld_wait();
-            sm100::tc_fence_before();
-            sm100::mbar_arrive(&bars->s_free[j & 1]);
-            float* s = reinterpret_cast<float*>(sr);
-
             // Only the diagonal tile (causal) and the last tile (S tail) need a mask.
             const int key0 = j * BN;
-            if ((CAUSAL && j == qt) || key0 + BN > S) {
-                const int lim = min(CAUSAL && j == qt ? row : BN - 1, S - 1 - key0);
-#pragma unroll
-                for (int c = 0; c < BN; ++c)
-                    if (c > lim) s[c] = -INFINITY;
-            }
-            // Row max of the raw scores (scale > 0 commutes with max); NaN propagates.
-            float rmax = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < BN; ++c) rmax = fmax_nan(rmax, s[c]);
-            const float m_new = fmax_nan(m, rmax * scale_log2);
-            const bool need = !(m_new <= m + 8.0f);
-            const float m_old = m;
-            if (need) m = m_new;
-            // p = 2^(s * scale * log2(e) - m): one FFMA + one MUFU.EX2 per score.  Computed before
-            // waiting for the previous tile's P.V, so the exponentials overlap those MMAs; only the
-            // O rescale and the P write below need P.V(j-1) to have finished.
-            const float neg_m = -m;
-            float rsum0 = 0.f, rsum1 = 0.f;
-#pragma unroll
-            for (int c = 0; c < BN; c += 2) {
-                const float p0 = ex2_approx(fmaf(s[c], scale_log2, neg_m));
-                const float p1 = ex2_approx(fmaf(s[c + 1], scale_log2, neg_m));
-                s[c] = p0;
-                s[c + 1] = p1;
-                rsum0 += p0;
-                rsum1 += p1;
-            }
-            if (j > 0) {
-                if (!sm100::mbar_wait(&bars->pv_done, (j - 1) & 1, status, 38)) {
-                    ok = false;
-                    break;
-                }
-                sm100::tc_fence_after();
-                const float alpha = need ? ex2_approx(m_old - m_new) : 1.0f;
-                if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-                    for (int c = 0; c < D / 32; ++c) {
-                        uint32_t r[32];
-                        sm100::tmem_ld_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
-                        sm100::tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                        sm100::tmem_st_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
-                    }
-                    sm100::tmem_st_wait();
-                }
-                if (need) l *= alpha;
-            }
-            l += rsum0 + rsum1;
-            // P row -> TMEM columns [P_COL, P_COL + 64): keys 2c, 2c+1 packed in column c (and the
-            // residual of the 16-bit rounding at PLO_COL).
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t hv[32], lv[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float p0 = s[half * 64 + 2 * i], p1 = s[half * 64 + 2 * i + 1];
-                    if (PSPLIT && BF16) {
-                        // bf16: the high part is the upper half of the fp32 bits (truncation, one byte
-                        // permute for two values) and the residual p - high is exact in fp32, so only
-                        // the residual is rounded: ~16 significant bits in total.
-                        const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
-                        hv[i] = __byte_perm(b0, b1, 0x7632);
-                        lv[i] = pack2<T>(p0 - __uint_as_float(b0 & 0xFFFF0000u), p1 - __uint_as_float(b1 & 0xFFFF0000u));
-                    } else {
-                        hv[i] = pack2<T>(p0, p1);
-                        if (PSPLIT) {
-                            const float h0 = sf::Dt<T>::to_f(*reinterpret_cast<const T*>(reinterpret_cast<const uint16_t*>(&hv[i])));
-                            const float h1 = sf::Dt<T>::to_f(*reinterpret_cast<const T*>(reinterpret_cast<const uint16_t*>(&hv[i]) + 1));
-                            lv[i] = pack2<T>(p0 - h0, p1 - h1);
-                        }
-                    }
-                }
-                sm100::tmem_st_32x32b_x32(tmem + lane_off + P_COL + (uint32_t)(half * 32), hv);
-                if (PSPLIT) sm100::tmem_st_32x32b_x32(tmem + lane_off + PLO_COL + (uint32_t)(half * 32), lv);
-            }
-            sm100::tmem_st_wait();
-            sm100::tc_fence_before();
-            sm100::mbar_arrive(&bars->p_full);
+            const bool masked = (CAUSAL && j == qt) || key0 + BN > S;
+            const int lim = masked ? min(CAUSAL && j == qt ? row : BN - 1, S - 1 - key0) : BN - 1;
+            if (masked)
+                softmax_tile<T, D, true>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
+            else
+                softmax_tile<T, D, false>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
         }
         // ---------------- epilogue: O / l ----------------
-        if (ok && nkv > 0 && sm100::mbar_wait(&bars->pv_done, (nkv - 1) & 1, status, 39)) {
+        if (ok && nkv > 0 && sm100::mbar_wait(&bars->o_done, 0, status, 39)) {
             sm100::tc_fence_after();
             const float inv = 1.0f / l;
             T* orow = o + ((int64_t)bh * S + q) * D;
@@ -404,19 +463,19 @@ int launch_tc_t(const void* q, const void* k, const void* v, void* o, int64_t BH
     if (rc) return rc;
     sm100::KernelStatus* status = status_ptr();
     if (!status) return sf::fail(SF_EDEVICE, err, cap, "attention: cannot resolve the status word");
-    // P is split into high + residual parts for both 16-bit types (see Layout): with a single
-    // rounding, bf16 P errors reach the task tolerance (rtol 1.6e-2 / atol_rel 8e-3) on the
-    // normal case and fp16 P errors exceed its tolerance on the wide_range case.
-    constexpr bool PSPLIT = true;
-    // At least 116 KB so a second CTA (which would wait for TMEM) is never co-resident.
-    const int smem = std::max(Layout<D, PSPLIT>::BYTES + 1024, 116 * 1024);
+    // Two CTAs per SM: 2 x 256 TMEM columns, and at least 80 KB of shared memory each so that a
+    // third CTA (which would wait for TMEM) is never co-resident.
+    const int smem = std::max(Layout<D>::BYTES + 1024, 80 * 1024);
     static std::atomic<uint64_t> attr_done{0};
     if (sf::once_per_device(attr_done))
-        cudaFuncSetAttribute(fa_fwd_kernel<T, D, CAUSAL, PSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(fa_fwd_kernel<T, D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     const int64_t nq = (S + BM - 1) / BM;
-    if (BH > 65535 || nq > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "attention: grid too large");
-    fa_fwd_kernel<T, D, CAUSAL, PSPLIT><<<dim3((unsigned)nq, (unsigned)BH), NUM_THREADS, smem, st>>>(
-        mq, mk, mv, (T*)o, (int)S, scale * 1.4426950408889634f, status);
+    if (BH > 0x7fffffffLL || nq > 0x7fffffffLL || BH * nq > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "attention: grid too large");
+    // Heads per group: K and V of a group (2 * S * D * 2 bytes per head) stay within ~32 MB of L2.
+    const int64_t kv_head = 4 * S * D;
+    const int group = (int)std::max<int64_t>(1, std::min<int64_t>({16, BH, (32LL << 20) / std::max<int64_t>(kv_head, 1)}));
+    fa_fwd_kernel<T, D, CAUSAL><<<(unsigned)(BH * nq), NUM_THREADS, smem, st>>>(mq, mk, mv, (T*)o, (int)S, (int)BH, (int)nq, group,
+                                                                               scale * 1.4426950408889634f, status);
     return sf::check_launch("attention launch", err, cap);
 }
 
@@ -424,7 +483,7 @@ template <typename T>
 int launch_t(const void* q, const void* k, const void* v, void* o, int64_t BH, int64_t S, int64_t D, float scale, bool causal,
              int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
     const bool tc = (D == 64 || D == 128) && sf::aligned16(q) && sf::aligned16(k) && sf::aligned16(v) && sf::aligned16(o) &&
-                    S < (1LL << 31) && BH <= 65535;
+                    S < (1LL << 31) && BH < (1LL << 31);
     if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "attention: the tensor-core variant needs D in {64,128} and aligned tensors");
     if (tc && variant != 2) {
         if (D == 64)
