@@ -13,21 +13,29 @@
 // channel (always true for decays bounded by -5 per token; for N(0,1) logits it would take 16
 // successive values below -5.4).
 //
+// Writing B = diag(beta) and T = (I + B A)^-1 B (16 x 16, lower triangular, state-independent),
+// the rows of a chunk are
+//   w = T (V - U'),  U'_t = S0 Kp_t     =>   w_t = Vt_t - S0 K2_t,          Vt = T V,  K2 = T Kp
+//   o_t = S0 Qp_t + (M w)_t             =>   o_t = Ov_t + S0 Q2_t,          Ov = (M T) V,  Q2 = Qp - (M T) Kp
+// so everything the state chain needs besides S0 is prepared ahead.
+//
 // One CTA of 384 threads per chain; the 128 x 128 fp32 state lives in TMEM (lane = value row v,
 // column = key channel k) and is never written to memory until the chain ends.  Warpgroups 1 and 2
 // (prep) take the even and the odd chunks and run up to two chunks ahead of warpgroup 0 (state),
 // each through its own chunk buffer:
-//   prep   thread = key channel: cumulative decay, the factored keys/queries (fp32 for the CUDA-core
-//          products, 16-bit for the MMAs), the chunk decay e^{b_15}; then the 16 x 16 decayed
-//          key.key (A) and query.key (M) products in fp32; the next chunk's inputs are loaded
-//          into registers meanwhile;
-//   state  thread = value row: S0 is read from TMEM, written as a 16-bit MMA operand and written
-//          back decayed (S0 diag(e^{b_15}));
-//          MMA 1  [U' | O'] = S0 . [Kp ; Qp]^T   (M=128 rows v, N=32, K=128);
-//          u = v - U', forward substitution for w, o = O' + M w (fp32), outputs stored, w written
-//          as a 16-bit high part and residual;
+//   prep   thread = key channel: cumulative decay, the factored keys/queries in fp32, the 16 x 16
+//          A and M products, T by forward substitution and M T, all in the warpgroup's own
+//          scratch; only then does it wait for its chunk buffer to be released and write Kend
+//          (16-bit, the update MMA's operand), K2 and Q2 (fp32, the tf32 MMA operand), T, M T, v and
+//          the chunk decay e^{b_15}; the next chunk's inputs are loaded into registers meanwhile;
+//   state  MMA 1  [W' | O'] = S0 . [-K2 ; Q2]^T as tf32 with S0 read straight from TMEM as the A
+//          operand (M=128 rows v, N=32, K=128); while it runs, thread = value row computes
+//          Vt = T v and Ov = (M T) v for its row;
+//          then w = Vt + (-W'), o = Ov + O' (fp32), outputs stored, w written as a 16-bit high part
+//          and residual, S0 decayed in TMEM (S0 diag(e^{b_15}));
 //          MMA 2  S += W^T . Kend (high and residual parts; M=128, N=128, K=16), whose completion
-//          also hands the chunk's buffers back to the prep warpgroup.
+//          also hands the chunk's buffers back to the prep warpgroup.  The next chunk's MMA 1 is
+//          issued behind it: the tensor pipe runs one CTA's MMAs in issue order.
 // Every mbarrier wait is bounded; a timeout is reported through sf_kernel_status.
 #include "sf_common.cuh"
 #include "sm100.cuh"
@@ -45,32 +53,39 @@ constexpr int C = 16;        // tokens per chunk
 constexpr int NT = 384;      // threads: a state warpgroup and two prep warpgroups
 constexpr int WG = 128;      // threads per warpgroup
 constexpr int KP = D + 4;    // fp32 staging row stride: 16-byte rows, rows r and r+8 in distinct bank groups
-constexpr uint32_t TMEM_COLS = 256;  // S [0,128), [U'|O'] [128,160)
+constexpr uint32_t TMEM_COLS = 256;  // S [0,128), [W'|O'] [128,160)
 
 struct Layout {
-    static constexpr int SA = 0;                   // S0 operand [128 v x 128 k], 2 K-blocks x 16 KB
-    static constexpr int WH = SA + 32768;          // W^T high [128 v x 64 (t < 16 used)]
+    static constexpr int WH = 0;                   // W^T high [128 v x 64 (t < 16 used)], 16-bit K-major
     static constexpr int WL = WH + 16384;          // W^T residual
-    static constexpr int B1 = WL + 16384;          // [Kp ; Qp] [32 x 128], 2 K-blocks x 4 KB; x2 buffers
-    static constexpr int KE = B1 + 2 * 8192;       // Kend [16 t x 128 k] MN-major, 2 blocks x 2 KB; x2
-    static constexpr int AM = KE + 2 * 4096;       // fp32 A [16][16], M [16][16]; x2
-    static constexpr int AM_BYTES = 2 * C * C * 4;
-    static constexpr int EB = AM + 2 * AM_BYTES;   // fp32 chunk decay e^{b_15} [128]; x2
-    static constexpr int BETA = EB + 2 * D * 4;    // fp32 beta [16]; x2
-    static constexpr int VS = BETA + 2 * 64;       // staged v (16-bit) [16][128]; x2
-    // Per prep warpgroup: fp32 [16][KP] Kp, Kn, Qp, Kend, then staged q, k (16-bit) and g (fp32).
-    static constexpr int PREP = VS + 2 * C * D * 2;
+    // Chunk buffers (x2, one per prep warpgroup), released by the update MMA's commit.
+    static constexpr int B1 = WL + 16384;          // [-K2 ; Q2] fp32 [32 x 128] K-major, 4 K-blocks x 4 KB
+    static constexpr int B1_BYTES = 16384;
+    static constexpr int KE = B1 + 2 * B1_BYTES;   // Kend [16 t x 128 k] 16-bit MN-major, 2 blocks x 2 KB
+    static constexpr int VB = KE + 2 * 4096;       // v (16-bit) [16][128]
+    static constexpr int TB = VB + 2 * C * D * 2;  // T [16][16] then M T [16][16], fp32
+    static constexpr int EB = TB + 2 * 2 * C * C * 4;  // fp32 chunk decay e^{b_15} [128]
+    // Per prep warpgroup scratch: fp32 [16][KP] Kp, Kn, Qp; staged q, k, v (16-bit), g (fp32), beta;
+    // the 16 x 16 fp32 A, M, T and M T.
+    static constexpr int PREP = EB + 2 * D * 4;
     static constexpr int KP32 = 0;
     static constexpr int KN32 = KP32 + C * KP * 4;
     static constexpr int QP32 = KN32 + C * KP * 4;
-    static constexpr int KE32 = QP32 + C * KP * 4;
-    static constexpr int QS = KE32 + C * KP * 4;
+    static constexpr int QS = QP32 + C * KP * 4;
     static constexpr int KS = QS + C * D * 2;
-    static constexpr int GS = KS + C * D * 2;
-    static constexpr int PREP_BYTES = GS + C * D * 4;
+    static constexpr int VS = KS + C * D * 2;
+    static constexpr int GS = VS + C * D * 2;
+    static constexpr int BS = GS + C * D * 4;
+    static constexpr int TA = BS + 64;
+    static constexpr int TM = TA + C * C * 4;
+    static constexpr int TT = TM + C * C * 4;
+    static constexpr int TMT = TT + C * C * 4;
+    static constexpr int PREP_BYTES = TMT + C * C * 4;
     static constexpr int BARS = PREP + 2 * PREP_BYTES;
     static constexpr int BYTES = BARS + 64;
 };
+static_assert(Layout::B1 % 1024 == 0 && Layout::KE % 1024 == 0, "MMA operands need 1024-byte alignment");
+static_assert(Layout::PREP % 16 == 0 && Layout::PREP_BYTES % 16 == 0, "16-byte staging rows");
 
 struct __align__(8) Bars {
     uint64_t m1;
@@ -90,10 +105,25 @@ __device__ __forceinline__ float from16(uint16_t u) {
     return sf::Dt<T>::to_f(*reinterpret_cast<const T*>(&u));
 }
 
-// Byte offset of element (row r, column c) of a K-major 128-byte-swizzled operand whose K-blocks of
+// Byte offset of 16-bit element (row r, column c) of a 128-byte-swizzled operand whose blocks of
 // 64 columns are `blk` bytes apart.
 __device__ __forceinline__ int kmaj(int r, int c, int blk) {
     return (c >> 6) * blk + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1);
+}
+
+// Byte offset of fp32 element (row r, column c) of a K-major 128-byte-swizzled operand with K-blocks
+// of 32 columns, 32 rows (4 KB) each.
+__device__ __forceinline__ int kmaj32(int r, int c) {
+    return (c >> 5) * 4096 + r * 128 + ((((c & 31) >> 2) ^ (r & 7)) << 4) + ((c & 3) << 2);
+}
+
+// Packed fp32 pair FMA (one FFMA2 for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(reinterpret_cast<uint64_t&>(d))
+        : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)), "l"(reinterpret_cast<const uint64_t&>(c)));
+    return d;
 }
 
 // Next chunk's raw inputs, held in registers while the current chunk computes.  Thread tid covers
@@ -121,19 +151,19 @@ __device__ __forceinline__ void load_chunk(Prefetch& p, const T* q, const T* k, 
     p.beta = (tid < nt) ? __ldg(beta + (size_t)(t0 + tid) * H + h) : 0.f;
 }
 
-__device__ __forceinline__ void store_chunk(const Prefetch& p, uint8_t* smem, uint8_t* prep, int tid, int b) {
+__device__ __forceinline__ void store_chunk(const Prefetch& p, uint8_t* prep, int tid) {
     const int tt = tid >> 3, part = tid & 7;
     const int off = (tt * D + part * 16) * 2;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         *reinterpret_cast<uint4*>(prep + Layout::QS + off + 16 * i) = p.q[i];
         *reinterpret_cast<uint4*>(prep + Layout::KS + off + 16 * i) = p.k[i];
-        *reinterpret_cast<uint4*>(smem + Layout::VS + b * C * D * 2 + off + 16 * i) = p.v[i];
+        *reinterpret_cast<uint4*>(prep + Layout::VS + off + 16 * i) = p.v[i];
     }
     float* gs = reinterpret_cast<float*>(prep + Layout::GS) + tt * D + part * 16;
 #pragma unroll
     for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(gs)[i] = p.g[i];
-    if (tid < C) reinterpret_cast<float*>(smem + Layout::BETA + b * 64)[tid] = p.beta;
+    if (tid < C) reinterpret_cast<float*>(prep + Layout::BS)[tid] = p.beta;
 }
 
 template <typename T>
@@ -145,7 +175,6 @@ __global__ void __launch_bounds__(NT, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars* bars = reinterpret_cast<Bars*>(smem + Layout::BARS);
-    float* am = reinterpret_cast<float*>(smem + Layout::AM);  // A [16][17] then M [16][17]
     float* eb = reinterpret_cast<float*>(smem + Layout::EB);
 
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -170,7 +199,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     const int nchunks = (end - begin + C - 1) / C;
     Prefetch pf;
-    const int pw = wg - 1;  // prep warpgroup index (chunks pw, pw + 2, ...)
+    const int pw = wg - 1;  // prep warpgroup index (chunks pw, pw + 2, ...; buffer pw)
     if (wg >= 1 && pw < nchunks) load_chunk<T>(pf, q, k, v, g, beta, begin + pw * C, min(C, end - begin - pw * C), H, h, wtid);
     sm100::tc_fence_before();
     __syncthreads();
@@ -187,22 +216,25 @@ __global__ void __launch_bounds__(NT, 1)
         float* kp32 = reinterpret_cast<float*>(prep + Layout::KP32);
         float* kn32 = reinterpret_cast<float*>(prep + Layout::KN32);
         float* qp32 = reinterpret_cast<float*>(prep + Layout::QP32);
-        float* ke32 = reinterpret_cast<float*>(prep + Layout::KE32);
+        float* ta = reinterpret_cast<float*>(prep + Layout::TA);
+        float* tm = reinterpret_cast<float*>(prep + Layout::TM);
+        float* tt = reinterpret_cast<float*>(prep + Layout::TT);
+        float* tmt = reinterpret_cast<float*>(prep + Layout::TMT);
+        const float* bs = reinterpret_cast<const float*>(prep + Layout::BS);
         const uint32_t bar_id = 1 + 2 * pw;
+        const int b = pw;
+        const int c = wtid;  // key channel (and value channel)
         for (int ci = pw; ci < nchunks && ok; ci += 2) {
-            const int b = ci & 1;
             const int t0 = begin + ci * C;
-            if (ci >= 2 && !sm100::mbar_wait(&bars->pempty[b], ((ci >> 1) - 1) & 1, status, 74)) {
-                ok = false;
-                break;
-            }
             sm100::named_barrier_sync(bar_id, WG);  // previous iteration's reads of the prep scratch are done
-            store_chunk(pf, smem, prep, wtid, b);
+            store_chunk(pf, prep, wtid);
             sm100::named_barrier_sync(bar_id, WG);
             if (ci + 2 < nchunks) load_chunk<T>(pf, q, k, v, g, beta, t0 + 2 * C, min(C, end - t0 - 2 * C), H, h, wtid);
+
+            // ---- factors in fp32 (thread = key channel c) ----
+            float kp[C], qp[C];
+            float elast;
             {
-                // Factors in fp32, thread = key channel c.
-                const int c = wtid;
                 const float* gs = reinterpret_cast<const float*>(prep + Layout::GS);
                 const uint16_t* ks = reinterpret_cast<const uint16_t*>(prep + Layout::KS);
                 const uint16_t* qs = reinterpret_cast<const uint16_t*>(prep + Layout::QS);
@@ -213,62 +245,108 @@ __global__ void __launch_bounds__(NT, 1)
                     bacc += gs[t * D + c];
                     bcum[t] = bacc;
                 }
-                const float elast = __expf(bacc);
-                eb[b * D + c] = elast;
+                elast = __expf(bacc);
 #pragma unroll
                 for (int t = 0; t < C; ++t) {
                     const float kv = from16<T>(ks[t * D + c]);
                     const float qv = from16<T>(qs[t * D + c]) * scale;
                     const float e = __expf(bcum[t]), en = __expf(-bcum[t]);
-                    kp32[t * KP + c] = kv * e;
+                    kp[t] = kv * e;
+                    qp[t] = qv * e;
+                    kp32[t * KP + c] = kp[t];
                     kn32[t * KP + c] = kv * en;
-                    qp32[t * KP + c] = qv * e;
-                    ke32[t * KP + c] = kv * (elast * en);
+                    qp32[t * KP + c] = qp[t];
                 }
             }
             sm100::named_barrier_sync(bar_id, WG);
             {
-                // 16-bit MMA operands, 16 bytes at a time: B1 = [Kp ; Qp] (K-major) and Kend (MN-major).
-                uint8_t* b1 = smem + Layout::B1 + b * 8192;
-                uint8_t* ke = smem + Layout::KE + b * 4096;
-#pragma unroll 1
-                for (int idx = wtid; idx < 3 * C * (D / 8); idx += WG) {
-                    const int which = idx / (C * (D / 8)), row = (idx / (D / 8)) % C, ch = idx % (D / 8);
-                    const float* src = (which == 0 ? kp32 : which == 1 ? qp32 : ke32) + row * KP + ch * 8;
-                    const float4 f0 = *reinterpret_cast<const float4*>(src);
-                    const float4 f1 = *reinterpret_cast<const float4*>(src + 4);
-                    const uint4 w = make_uint4((uint32_t)to16<T>(f0.x) | ((uint32_t)to16<T>(f0.y) << 16),
-                                               (uint32_t)to16<T>(f0.z) | ((uint32_t)to16<T>(f0.w) << 16),
-                                               (uint32_t)to16<T>(f1.x) | ((uint32_t)to16<T>(f1.y) << 16),
-                                               (uint32_t)to16<T>(f1.z) | ((uint32_t)to16<T>(f1.w) << 16));
-                    if (which < 2)
-                        *reinterpret_cast<uint4*>(b1 + kmaj(which * C + row, ch * 8, 4096)) = w;
-                    else
-                        *reinterpret_cast<uint4*>(ke + kmaj(row, ch * 8, 2048)) = w;
-                }
-                // A[t][i] (i < t) and M[t][i] (i <= t): thread -> rows t of Kp and Qp, columns i and i + 8.
+                // A[t][i] (i < t) and M[t][i] (i <= t): thread -> rows t of Kp and Qp, columns i and
+                // i + 8; even and odd channels accumulate in the two halves of packed pairs.
                 const int t = wtid >> 3, i0c = wtid & 7;
-                const float* lk = kp32 + t * KP;
-                const float* lq = qp32 + t * KP;
-                const float* r0 = kn32 + i0c * KP;
-                const float* r1 = kn32 + (i0c + 8) * KP;
-                float a00 = 0.f, a01 = 0.f, m00 = 0.f, m01 = 0.f;
-#pragma unroll 4
-                for (int cc = 0; cc < D; cc += 4) {
-                    const float4 x = *reinterpret_cast<const float4*>(lk + cc);
-                    const float4 y = *reinterpret_cast<const float4*>(lq + cc);
-                    const float4 u = *reinterpret_cast<const float4*>(r0 + cc);
-                    const float4 w = *reinterpret_cast<const float4*>(r1 + cc);
-                    a00 = fmaf(x.x, u.x, fmaf(x.y, u.y, fmaf(x.z, u.z, fmaf(x.w, u.w, a00))));
-                    a01 = fmaf(x.x, w.x, fmaf(x.y, w.y, fmaf(x.z, w.z, fmaf(x.w, w.w, a01))));
-                    m00 = fmaf(y.x, u.x, fmaf(y.y, u.y, fmaf(y.z, u.z, fmaf(y.w, u.w, m00))));
-                    m01 = fmaf(y.x, w.x, fmaf(y.y, w.y, fmaf(y.z, w.z, fmaf(y.w, w.w, m01))));
+                const float4* lk = reinterpret_cast<const float4*>(kp32 + t * KP);
+                const float4* lq = reinterpret_cast<const float4*>(qp32 + t * KP);
+                const float4* r0 = reinterpret_cast<const float4*>(kn32 + i0c * KP);
+                const float4* r1 = reinterpret_cast<const float4*>(kn32 + (i0c + 8) * KP);
+                float2 a0 = make_float2(0.f, 0.f), a1 = a0, m0 = a0, m1 = a0;
+#pragma unroll 2
+                for (int cc = 0; cc < D / 4; ++cc) {
+                    const float4 x = lk[cc], y = lq[cc], u = r0[cc], w = r1[cc];
+                    a0 = ffma2(make_float2(x.x, x.y), make_float2(u.x, u.y), a0);
+                    a0 = ffma2(make_float2(x.z, x.w), make_float2(u.z, u.w), a0);
+                    a1 = ffma2(make_float2(x.x, x.y), make_float2(w.x, w.y), a1);
+                    a1 = ffma2(make_float2(x.z, x.w), make_float2(w.z, w.w), a1);
+                    m0 = ffma2(make_float2(y.x, y.y), make_float2(u.x, u.y), m0);
+                    m0 = ffma2(make_float2(y.z, y.w), make_float2(u.z, u.w), m0);
+                    m1 = ffma2(make_float2(y.x, y.y), make_float2(w.x, w.y), m1);
+                    m1 = ffma2(make_float2(y.z, y.w), make_float2(w.z, w.w), m1);
                 }
-                float* amb = am + b * (Layout::AM_BYTES / 4);
-                amb[t * C + i0c] = i0c < t ? a00 : 0.f;
-                amb[t * C + i0c + 8] = i0c + 8 < t ? a01 : 0.f;
-                amb[C * C + t * C + i0c] = i0c <= t ? m00 : 0.f;
-                amb[C * C + t * C + i0c + 8] = i0c + 8 <= t ? m01 : 0.f;
+                ta[t * C + i0c] = i0c < t ? a0.x + a0.y : 0.f;
+                ta[t * C + i0c + 8] = i0c + 8 < t ? a1.x + a1.y : 0.f;
+                tm[t * C + i0c] = i0c <= t ? m0.x + m0.y : 0.f;
+                tm[t * C + i0c + 8] = i0c + 8 <= t ? m1.x + m1.y : 0.f;
+            }
+            sm100::named_barrier_sync(bar_id, WG);
+            if (wtid < C) {
+                // T = (I + B A)^-1 B, column j by forward substitution: x_t = [t == j] - beta_t sum_{i<t} A[t][i] x_i.
+                const int j = wtid;
+                float x[C];
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < t; ++i) acc = fmaf(ta[t * C + i], x[i], acc);
+                    x[t] = (t == j ? 1.f : 0.f) - bs[t] * acc;
+                }
+                const float bj = bs[j];
+#pragma unroll
+                for (int t = 0; t < C; ++t) tt[t * C + j] = x[t] * bj;
+            }
+            sm100::named_barrier_sync(bar_id, WG);
+            {
+                // M T (lower triangular): thread -> row t, columns jc and jc + 8.
+                const int t = wtid >> 3, jc = wtid & 7;
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < C; ++i) {
+                    const float mi = tm[t * C + i];
+                    s0 = fmaf(mi, tt[i * C + jc], s0);
+                    s1 = fmaf(mi, tt[i * C + jc + 8], s1);
+                }
+                tmt[t * C + jc] = s0;
+                tmt[t * C + jc + 8] = s1;
+            }
+            sm100::named_barrier_sync(bar_id, WG);
+
+            // ---- the chunk buffer: released by the update MMA of chunk ci - 2 ----
+            if (ci >= 2 && !sm100::mbar_wait(&bars->pempty[b], ((ci >> 1) - 1) & 1, status, 74)) {
+                ok = false;
+                break;
+            }
+            {
+                uint8_t* b1 = smem + Layout::B1 + b * Layout::B1_BYTES;
+                uint8_t* keb = smem + Layout::KE + b * 4096;
+                eb[b * D + c] = elast;
+                // -K2 = -T Kp and Q2 = Qp - (M T) Kp (rows t and 16 + t of the tf32 MMA operand).
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    float k2 = 0.f, q2 = qp[t];
+#pragma unroll
+                    for (int i = 0; i <= t; ++i) {
+                        k2 = fmaf(-tt[t * C + i], kp[i], k2);
+                        q2 = fmaf(-tmt[t * C + i], kp[i], q2);
+                    }
+                    *reinterpret_cast<float*>(b1 + kmaj32(t, c)) = k2;
+                    *reinterpret_cast<float*>(b1 + kmaj32(C + t, c)) = q2;
+                    *reinterpret_cast<uint16_t*>(keb + kmaj(t, c, 2048)) = to16<T>(kn32[t * KP + c] * elast);  // Kend = k e^{b_15 - b_t}
+                }
+                // T, M T and v for the state warpgroup's Vt = T v, Ov = (M T) v.
+                float* tb = reinterpret_cast<float*>(smem + Layout::TB) + b * 2 * C * C;
+                reinterpret_cast<float4*>(tb)[wtid] = wtid < 64 ? reinterpret_cast<const float4*>(tt)[wtid]
+                                                                 : reinterpret_cast<const float4*>(tmt)[wtid - 64];
+                const uint4* vsrc = reinterpret_cast<const uint4*>(prep + Layout::VS);
+                uint4* vdst = reinterpret_cast<uint4*>(smem + Layout::VB + b * C * D * 2);
+                vdst[wtid] = vsrc[wtid];
+                vdst[wtid + WG] = vsrc[wtid + WG];
             }
             sm100::fence_proxy_async_smem();  // B1 / KE are read by the MMAs
             sm100::mbar_arrive(&bars->pfull[b]);
@@ -284,69 +362,48 @@ __global__ void __launch_bounds__(NT, 1)
             sm100::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r);
         }
         sm100::tmem_st_wait();
+        sm100::tc_fence_before();
+        sm100::named_barrier_sync(2, WG);
         for (int ci = 0; ci < nchunks && ok; ++ci) {
             const int b = ci & 1;
             const int t0 = begin + ci * C;
             const int nt = min(C, end - t0);
-            if (!sm100::mbar_wait(&bars->pfull[b], (ci >> 1) & 1, status, 75) ||
-                (ci > 0 && !sm100::mbar_wait(&bars->m2, (ci - 1) & 1, status, 71))) {
+            if (!sm100::mbar_wait(&bars->pfull[b], (ci >> 1) & 1, status, 75)) {
                 ok = false;
                 break;
             }
-            sm100::tc_fence_after();
-            // S0: 16-bit operand copy, and the decayed state written back for the update.
-            {
-                const float* ebb = eb + b * D;
-#pragma unroll 1
-                for (int hh = 0; hh < 2; ++hh) {
-                uint32_t r[2][32];
-#pragma unroll
-                for (int c2 = 0; c2 < 2; ++c2) sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((2 * hh + c2) * 32), r[c2]);
-                sm100::tmem_ld_wait();
-#pragma unroll
-                for (int c2 = 0; c2 < 2; ++c2) {
-                    const int cb = 2 * hh + c2;
-#pragma unroll
-                    for (int j8 = 0; j8 < 4; ++j8) {
-                        uint32_t w4[4];
-#pragma unroll
-                        for (int e2 = 0; e2 < 4; ++e2) {
-                            const float x0 = __uint_as_float(r[c2][j8 * 8 + 2 * e2]), x1 = __uint_as_float(r[c2][j8 * 8 + 2 * e2 + 1]);
-                            w4[e2] = (uint32_t)to16<T>(x0) | ((uint32_t)to16<T>(x1) << 16);
-                        }
-                        const int col = cb * 32 + j8 * 8;
-                        *reinterpret_cast<uint4*>(smem + Layout::SA + kmaj(vrow, col, 16384)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                    }
-#pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 e4 = reinterpret_cast<const float4*>(ebb + cb * 32)[j4];
-                        r[c2][4 * j4] = __float_as_uint(__uint_as_float(r[c2][4 * j4]) * e4.x);
-                        r[c2][4 * j4 + 1] = __float_as_uint(__uint_as_float(r[c2][4 * j4 + 1]) * e4.y);
-                        r[c2][4 * j4 + 2] = __float_as_uint(__uint_as_float(r[c2][4 * j4 + 2]) * e4.z);
-                        r[c2][4 * j4 + 3] = __float_as_uint(__uint_as_float(r[c2][4 * j4 + 3]) * e4.w);
-                    }
-                    sm100::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r[c2]);
-                }
-                }
-                sm100::tmem_st_wait();
-            }
-            sm100::fence_proxy_async_smem();
-            sm100::tc_fence_before();
-            sm100::named_barrier_sync(2, WG);
-
-            // ---- MMA 1: [U' | O'] = S0 . [Kp ; Qp]^T ----
+            // ---- MMA 1: [-W' | O'] = S0 . [-K2 ; Q2]^T, tf32, S0 from TMEM.  Issued behind the
+            // previous chunk's update MMA, which the tensor pipe completes first. ----
             if (wtid == 0) {
                 sm100::tc_fence_after();
-                constexpr uint32_t idesc = sm100::idesc_f16(128, 2 * C, BF16);
-                const uint32_t sa = sm100::smem_u32(smem + Layout::SA);
-                const uint32_t sb = sm100::smem_u32(smem + Layout::B1 + b * 8192);
+                constexpr uint32_t idesc = sm100::idesc_tf32(128, 2 * C);
+                const uint32_t sb = sm100::smem_u32(smem + Layout::B1 + b * Layout::B1_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint64_t ad = sm100::smem_desc_k_sw128(sa + (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32));
+                for (int kk = 0; kk < D / 8; ++kk) {
                     const uint64_t bd = sm100::smem_desc_k_sw128(sb + (uint32_t)((kk >> 2) * 4096 + (kk & 3) * 32));
-                    sm100::mma_f16(tmem + 128, ad, bd, idesc, kk > 0 ? 1u : 0u);
+                    sm100::mma_tf32_ta(tmem + 128, tmem + (uint32_t)(kk * 8), bd, idesc, kk > 0 ? 1u : 0u);
                 }
                 sm100::mma_commit(&bars->m1);
+            }
+            // ---- while MMA 1 runs: Vt = T v and Ov = (M T) v for this value row ----
+            float vt[C], ov[C];
+            {
+                const float* tb = reinterpret_cast<const float*>(smem + Layout::TB) + b * 2 * C * C;
+                const uint16_t* vb = reinterpret_cast<const uint16_t*>(smem + Layout::VB + b * C * D * 2);
+                float vv[C];
+#pragma unroll
+                for (int i = 0; i < C; ++i) vv[i] = from16<T>(vb[i * D + vrow]);
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    float a = 0.f, o = 0.f;
+#pragma unroll
+                    for (int i = 0; i <= t; ++i) {
+                        a = fmaf(tb[t * C + i], vv[i], a);
+                        o = fmaf(tb[C * C + t * C + i], vv[i], o);
+                    }
+                    vt[t] = a;
+                    ov[t] = o;
+                }
             }
             if (!sm100::mbar_wait(&bars->m1, ci & 1, status, 72)) {
                 ok = false;
@@ -354,34 +411,16 @@ __global__ void __launch_bounds__(NT, 1)
             }
             sm100::tc_fence_after();
 
-            // ---- rows: u = v - U', w by forward substitution, o = O' + M w ----
+            // ---- rows: w = Vt - W', o = Ov + O'; S0 decayed in TMEM ----
             {
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(tmem + lane_off + 128, r);
                 sm100::tmem_ld_wait();
-                const uint16_t* vs = reinterpret_cast<const uint16_t*>(smem + Layout::VS + b * C * D * 2);
-                const float* bsb = reinterpret_cast<const float*>(smem + Layout::BETA + b * 64);
-                const float4* A4 = reinterpret_cast<const float4*>(am + b * (Layout::AM_BYTES / 4));
-                const float4* M4 = A4 + C * C / 4;
                 float w[C];
 #pragma unroll
                 for (int t = 0; t < C; ++t) {
-                    float a[C];
-#pragma unroll
-                    for (int j = 0; j < (t + 3) / 4; ++j) *reinterpret_cast<float4*>(&a[4 * j]) = A4[t * (C / 4) + j];
-                    float u = from16<T>(vs[t * D + vrow]) - __uint_as_float(r[t]);
-#pragma unroll
-                    for (int i = 0; i < t; ++i) u = fmaf(-a[i], w[i], u);
-                    w[t] = bsb[t] * u;
-                }
-#pragma unroll
-                for (int t = 0; t < C; ++t) {
-                    float m[C];
-#pragma unroll
-                    for (int j = 0; j < (t + 4) / 4; ++j) *reinterpret_cast<float4*>(&m[4 * j]) = M4[t * (C / 4) + j];
-                    float o = __uint_as_float(r[C + t]);
-#pragma unroll
-                    for (int i = 0; i <= t; ++i) o = fmaf(m[i], w[i], o);
+                    w[t] = vt[t] + __uint_as_float(r[t]);
+                    const float o = ov[t] + __uint_as_float(r[C + t]);
                     if (t < nt) out[((size_t)(t0 + t) * H + h) * D + vrow] = sf::Dt<T>::from_f(o);
                 }
                 // W^T row v: t = 0..15 is K of the update MMA (16-byte groups 0 and 1 of the row).
@@ -400,6 +439,30 @@ __global__ void __launch_bounds__(NT, 1)
                     *reinterpret_cast<uint4*>(smem + Layout::WH + off) = make_uint4(hi[4 * grp], hi[4 * grp + 1], hi[4 * grp + 2], hi[4 * grp + 3]);
                     *reinterpret_cast<uint4*>(smem + Layout::WL + off) = make_uint4(lo[4 * grp], lo[4 * grp + 1], lo[4 * grp + 2], lo[4 * grp + 3]);
                 }
+            }
+            {
+                const float4* e4 = reinterpret_cast<const float4*>(eb + b * D);
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t r[2][32];
+#pragma unroll
+                    for (int c2 = 0; c2 < 2; ++c2) sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((2 * hh + c2) * 32), r[c2]);
+                    sm100::tmem_ld_wait();
+#pragma unroll
+                    for (int c2 = 0; c2 < 2; ++c2) {
+                        const int cb = 2 * hh + c2;
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; ++j4) {
+                            const float4 e = e4[cb * 8 + j4];
+                            r[c2][4 * j4] = __float_as_uint(__uint_as_float(r[c2][4 * j4]) * e.x);
+                            r[c2][4 * j4 + 1] = __float_as_uint(__uint_as_float(r[c2][4 * j4 + 1]) * e.y);
+                            r[c2][4 * j4 + 2] = __float_as_uint(__uint_as_float(r[c2][4 * j4 + 2]) * e.z);
+                            r[c2][4 * j4 + 3] = __float_as_uint(__uint_as_float(r[c2][4 * j4 + 3]) * e.w);
+                        }
+                        sm100::tmem_st_32x32b_x32(tmem + lane_off + (uint32_t)(cb * 32), r[c2]);
+                    }
+                }
+                sm100::tmem_st_wait();
             }
             sm100::fence_proxy_async_smem();
             sm100::tc_fence_before();

@@ -175,6 +175,20 @@ __device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T for kind::tf32: A is M rows (TMEM lanes) of fp32 values, one
+// per column, K = 8 columns per instruction (the tensor core reads them as tf32); B is a K-major
+// fp32 operand in shared memory.
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // mma_f16 that leaves some accumulator rows untouched: TMEM lane i (row i of D) is not written
 // when bit (i % 32) of disable[i / 32] is set.  Lets one M=128 MMA serve two independent 64-row
 // problems stacked in A (each half masked in turn) without their products mixing.
@@ -331,6 +345,12 @@ __host__ __device__ constexpr uint32_t idesc_f16_bmn(uint32_t m, uint32_t n, boo
 //   [15] A major  [16] B major (0 = K)  [17,23) N >> 3  [24,29) M >> 4
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t m, uint32_t n, bool bf16) {
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Instruction descriptor of kind::tf32 with an fp32 accumulator, both operands K-major (A and B
+// format 2 = tf32).
+__host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 }  // namespace sm100
