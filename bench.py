@@ -485,6 +485,161 @@ def _mamba2_workload(b: int = 2, l: int = 2048, h: int = 8, p: int = 64, n: int 
         [((b, l, h, p), cases.TORCH_DTYPE[dtype])], (b, l, h, p, n, c), cpu_rows=cpu_rows, total_rows=nc)
 
 
+def _membound_task_workload(task: str, shape, dtype: str = "fp16", kernel: str = "") -> Workload:
+    """A memory-bound task at its reference paper size (tasks/<task>/opspec.json sizes.paper),
+    inputs from the task's own stream (normal case); units = the opspec's min_bytes (inputs and
+    outputs, each once)."""
+    import math
+
+    import numpy as np
+
+    from shapeforge_b200 import cases
+
+    el = 2
+    n_elem = int(np.prod(shape))
+    if task == "reduction_sum":
+        m, n = shape
+        nbytes, outs, dims = el * m * n + el * m, [((m,), cases.TORCH_DTYPE[dtype])], (m, n)
+    elif task == "swiglu":
+        nbytes, outs, dims = 3 * el * n_elem, [(tuple(shape), cases.TORCH_DTYPE[dtype])], (n_elem,)
+    elif task == "rope":
+        nbytes, outs, dims = 2 * el * n_elem, [(tuple(shape), cases.TORCH_DTYPE[dtype])], tuple(shape)
+    elif task in ("silu",):
+        nbytes, outs, dims = 2 * el * n_elem, [(tuple(shape), cases.TORCH_DTYPE[dtype])], (n_elem,)
+    else:  # softmax
+        m, n = shape
+        nbytes, outs, dims = 2 * el * m * n, [(tuple(shape), cases.TORCH_DTYPE[dtype])], (m, n)
+    names = ["gate", "up"] if task == "swiglu" else ["x"]
+    attrs = (10000.0,) if task == "rope" else ()
+    block = shape[-1] if task in ("softmax", "reduction_sum") else (shape[-2] * shape[-1] if task == "rope" else 65536)
+    total_rows = max(1, n_elem // block)
+
+    def make_inputs(seed):
+        return cases.membound_inputs(task, "normal", seed, shape, dtype)
+
+    def cpu_rows(rows):
+        # The task's reference formula through the oracle port on the first `rows` rows (blocks).
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        k = rows * block
+        if task == "swiglu":
+            g = inp["gate"].reshape(-1)[:k].double().numpy()
+            u = inp["up"].reshape(-1)[:k].double().numpy()
+            return (lambda: oref.swiglu(g, u)), 3.0 * el * k, f"fp64 swiglu of {k} elements"
+        x = inp["x"].reshape(-1)[:k].double().numpy()
+        if task == "rope":
+            xr = x.reshape(rows, shape[-2], shape[-1])
+            return (lambda: oref.rope(xr, 10000.0)), 2.0 * el * k, f"fp64 rope of {rows} heads"
+        if task in ("softmax", "reduction_sum"):
+            xr = x.reshape(rows, shape[-1])
+            fn = oref.softmax if task == "softmax" else oref.reduction_sum
+            per = (2 * el * k) if task == "softmax" else (el * k + el * rows)
+            return (lambda: fn(xr)), float(per), f"fp64 {task} of {rows} rows"
+        return (lambda: oref.silu(x)), 2.0 * el * k, f"fp64 silu of {k} elements"
+
+    label = "x".join(str(v) for v in shape)
+    return _op_workload(
+        f"{task}_{label}", "GB/s", "hbm", dtype, nbytes,
+        {"workload": f"task {task} at the reference paper size {list(shape)}, {dtype}, the task's normal-case input stream",
+         "shape": list(shape)},
+        kernel, task, make_inputs, names, outs, dims, attrs, cpu_rows=cpu_rows, total_rows=total_rows)
+
+
+def _gemm_nn_task_workload(m: int = 2048, n: int = 2048, k: int = 2048, dtype: str = "fp16") -> Workload:
+    """tasks/gemm (C = A.B, B stored [K, N]) at its paper size; the tensor-core path transposes B
+    into a caller workspace (an extra buffer of the launch, K*N 16-bit elements)."""
+    import torch
+
+    from shapeforge_b200 import cases
+
+    ws = 2 * n * k
+
+    def make_inputs(seed):
+        return cases.gemm_inputs("normal", seed, (m, k), (k, n), dtype)
+
+    def cpu_rows(rows):
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        a = inp["A"][:rows].float().numpy()
+        b = inp["B"].float().numpy()
+        return (lambda: a @ b), 2.0 * rows * n * k, f"fp32 A[{rows} rows,{k}] . B[{k},{n}] (row sample)"
+
+    wl = _op_workload(
+        f"gemm_nn_{m}x{n}x{k}", "TFLOP/s", "tensor", dtype, 2.0 * m * n * k,
+        {"workload": f"task gemm C=A.B, A {dtype} [{m},{k}], B {dtype} [{k},{n}] (K x N), fp32 accumulate; B^T staged in a "
+                     f"{ws} B caller workspace (two launches per step: transpose, then the tensor-core GEMM)", "shape": [m, n, k]},
+        "gemm_nt_tc_kernel", "gemm_nn", make_inputs, ["A", "B"], [((m, n), cases.TORCH_DTYPE[dtype]), ((ws,), torch.uint8)],
+        (m, n, k, ws), cpu_rows=cpu_rows, total_rows=m)
+    wl.launches_per_step = 2
+    return wl
+
+
+def _bitdelta_task_workload(m: int = 512, n: int = 4096, k: int = 4096, dtype: str = "fp16", scale: float = 0.02) -> Workload:
+    """tasks/bitdelta_gemm (y = SCALE x.W, W +-1 from bits [K/32, N]) at its paper size."""
+    from shapeforge_b200 import cases
+
+    def make_inputs(seed):
+        return cases.bitdelta_inputs("random", seed, m, n, k, dtype)
+
+    def cpu_rows(rows):
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        x = inp["x"][:rows].double().numpy()
+        bits = inp["bits"].numpy()
+        return (lambda: oref.bitdelta_gemm(x, bits, scale)), 2.0 * rows * n * k, f"fp64 oracle over {rows} rows of x"
+
+    return _op_workload(
+        f"bitdelta_gemm_{m}x{n}x{k}", "TFLOP/s", "tensor", dtype, 2.0 * m * n * k,
+        {"workload": f"task bitdelta_gemm y = {scale} x.W, x {dtype} [{m},{k}] ~ N(0,1), W +-1 from uniform 32-bit words "
+                     f"[{k // 32},{n}]", "shape": [m, n, k]},
+        "bitdelta_task_kernel", "bitdelta_gemm", make_inputs, ["x", "bits"], [((m, n), cases.TORCH_DTYPE[dtype])], (m, n, k),
+        (scale,), cpu_rows=cpu_rows, total_rows=m)
+
+
+def _kda_task_workload(heads: int = 64, dim: int = 128, lengths=(2048, 1024, 1024, 2048, 1024, 1024), dtype: str = "bf16") -> Workload:
+    """tasks/varlen_kda (in-op q/k norms, gates from A_log / dt_bias, sigmoid beta, initial state)
+    at the v6_h64_mixed size; units = the opspec's min_bytes (q, k, v, g, output, initial and final
+    state)."""
+    import math
+
+    import torch
+
+    from shapeforge_b200 import cases
+
+    lengths = list(lengths)
+    t = int(sum(lengths))
+    n = len(lengths)
+    nbytes = 5.0 * 2 * t * heads * dim + 2.0 * 4 * n * heads * dim * dim
+
+    def make_inputs(seed):
+        return cases.kda_task_inputs(lengths, heads, dim, dtype, seed)
+
+    def cpu_rows(rows):
+        # tasks/varlen_kda/reference.py:323-374 through the oracle port on the first `rows` tokens of
+        # one (sequence, head) chain.
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        tt = min(rows, lengths[0])
+        f = lambda name: inp[name][:tt, :1].double().numpy()  # noqa: E731
+        args = (f("q"), f("k"), f("v"), f("g"), inp["beta"][:tt, :1].double().numpy(), inp["A_log"][:1].double().numpy(),
+                inp["dt_bias"][:dim].double().numpy(), inp["initial_state"][:1, :1].double().numpy(), [0, tt],
+                float(inp["scale"][0]), -5.0)
+        return (lambda: oref.varlen_kda(*args)), 5.0 * 2 * tt * dim + 2.0 * 4 * dim * dim, f"fp64 recurrence over {tt} tokens of one chain"
+
+    return _op_workload(
+        f"varlen_kda_h{heads}_mixed", "GB/s", "hbm", dtype, nbytes,
+        {"workload": f"task varlen_kda v6_h64_mixed: {n} sequences {lengths}, H={heads}, D={dim}, {dtype}, the task's input "
+                     "stream (0.5 N(0,1) q/k/v/g/beta, A_log = log U(1,16), dt_bias, non-zero initial state)", "total_tokens": t},
+        "kda_fwd_kernel", "varlen_kda", make_inputs,
+        ["q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "cu_seqlens", "scale"],
+        [((t, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim), (-5.0,),
+        cpu_rows=cpu_rows, total_rows=lengths[0])
+
+
 WORKLOADS = {
     "mamba2_chunk_scan_paper": lambda w, r: _mamba2_workload(),
     "mamba2_chunk_scan_b8_l8192": lambda w, r: _mamba2_workload(8, 8192, 16),
@@ -504,6 +659,16 @@ WORKLOADS = {
     "rmsnorm_4096x1024": lambda w, r: _rmsnorm_workload(4096, 1024),
     "rmsnorm_4096x8192": lambda w, r: _rmsnorm_workload(4096, 8192),
     "rmsnorm_4093x4096": lambda w, r: _rmsnorm_workload(4093, 4096),
+    # The task contracts at their reference paper sizes (tasks/<task>/opspec.json sizes.paper).
+    "softmax_8192x2048": lambda w, r: _membound_task_workload("softmax", (8192, 2048), kernel="softmax_vec_kernel"),
+    "reduction_sum_4096x4096": lambda w, r: _membound_task_workload("reduction_sum", (4096, 4096), kernel="rowsum_vec_kernel"),
+    "rope_2x32x1024x128": lambda w, r: _membound_task_workload("rope", (2, 32, 1024, 128), kernel="rope_vec_kernel"),
+    "silu_16777216": lambda w, r: _membound_task_workload("silu", (16777216,), kernel="act_kernel"),
+    "swiglu_16777216": lambda w, r: _membound_task_workload("swiglu", (16777216,), kernel="act_kernel"),
+    "gemm_nn_2048": lambda w, r: _gemm_nn_task_workload(),
+    "bitdelta_gemm_512x4096x4096": lambda w, r: _bitdelta_task_workload(),
+    "attention_full_2x8x1024x64": lambda w, r: _attention_workload(2, 8, 1024, 64, causal=False, dtype="fp16", world=w, rank=r),
+    "varlen_kda_h64_mixed": lambda w, r: _kda_task_workload(),
 }
 DEFAULT_WORKLOAD = "gemm_nt_4096"
 
@@ -719,8 +884,10 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
     scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
     job_units = wl.total_units if wl.sharded else world * wl.units_per_step
     value = job_units * args.steps / max_s / scale
-    per_launch_s = el_s / (args.steps * wl.launches_per_step)
-    achieved = wl.units_per_step / per_launch_s / scale
+    # Algorithmic units of one step over the step's device time (one launch of the dominant kernel
+    # for every workload but the task gemm, whose step also transposes B).
+    per_step_s = el_s / args.steps
+    achieved = wl.units_per_step / per_step_s / scale
     peaks, peak_src = measured_peaks()
     clock_summary = clocks.summary()
     peak_kind = "hbm_gbs"
