@@ -21,10 +21,7 @@ __global__ void __launch_bounds__(256) act_kernel(const T* __restrict__ x, const
     int64_t done = 0;
     if (vec) {
         const int64_t nv = n >> 3;
-        for (int64_t i = tid; i < nv; i += stride) {
-            const sf::Vec8<T> a = sf::ld_global_nc_v8<T>(x + i * 8);
-            sf::Vec8<T> u;
-            if (GLU) u = sf::ld_global_nc_v8<T>(up + i * 8);
+        auto apply = [&](const sf::Vec8<T>& a, const sf::Vec8<T>& u, int64_t i) {
             sf::Vec8<T> o;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -34,6 +31,25 @@ __global__ void __launch_bounds__(256) act_kernel(const T* __restrict__ x, const
                 o.v[j] = sf::Dt<T>::from_f(r);
             }
             sf::st_global_v8<T>(y + i * 8, o);
+        };
+        // silu: two independent vectors per thread and step, so twice the bytes are in flight
+        // (swiglu already has two input streams per vector).
+        int64_t i = tid;
+        for (; !GLU && i + stride < nv; i += 2 * stride) {
+            const sf::Vec8<T> a0 = sf::ld_global_nc_v8<T>(x + i * 8);
+            const sf::Vec8<T> a1 = sf::ld_global_nc_v8<T>(x + (i + stride) * 8);
+            sf::Vec8<T> u0, u1;
+            if (GLU) {
+                u0 = sf::ld_global_nc_v8<T>(up + i * 8);
+                u1 = sf::ld_global_nc_v8<T>(up + (i + stride) * 8);
+            }
+            apply(a0, u0, i);
+            apply(a1, u1, i + stride);
+        }
+        for (; i < nv; i += stride) {
+            sf::Vec8<T> u0;
+            if (GLU) u0 = sf::ld_global_nc_v8<T>(up + i * 8);
+            apply(sf::ld_global_nc_v8<T>(x + i * 8), u0, i);
         }
         done = nv * 8;
     }

@@ -6,9 +6,15 @@
 //
 // HBM-bound (2 x 16-bit per element in + out).  The angle depends only on (s, i), so a CTA owns a
 // block of 32 positions and a share of the B*H heads: each thread computes the cos/sin of its 8
-// frequencies at its position once (in double precision, so positions in the thousands keep full
-// fp32 accuracy) and then streams its 16-byte x1/x2 vectors through every head of its share.
+// frequencies at its position once and then streams its 16-byte x1/x2 vectors through every head of
+// its share, two heads per step.  inv_freq[i] = r^i with r = BASE^(-1/half) computed once on the
+// host in double precision (a thread's first frequency by repeated squaring, the next ones by
+// repeated multiplication: relative error below 2^-46); the angle s * inv_freq is formed and
+// reduced modulo 2 pi in double precision, so positions in the thousands keep full accuracy, and
+// the reduced angle (|a| <= pi) goes to the special-function sine/cosine (absolute error ~2^-21).
 #include "sf_common.cuh"
+
+#include <cmath>
 
 namespace {
 
@@ -16,7 +22,7 @@ constexpr int POS_PER_CTA = 32;
 
 template <typename T>
 __global__ void __launch_bounds__(256) rope_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t bh, int64_t S,
-                                                       int64_t D, double base, int64_t bh_per_cta) {
+                                                       int64_t D, double ratio, int64_t bh_per_cta) {
     const int64_t half = D / 2;
     const int64_t vec_per_pos = half / 8;
     const int64_t local = threadIdx.x;
@@ -25,22 +31,24 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const T* __restrict__ x, 
     const int64_t s = (int64_t)blockIdx.x * POS_PER_CTA + p;
     if (p >= POS_PER_CTA || s >= S) return;
     float c[8], sn[8];
+    {
+        double f = 1.0, sq = ratio;
+        for (int64_t e = iv * 8; e > 0; e >>= 1) {  // ratio^(8 iv)
+            if (e & 1) f *= sq;
+            sq *= sq;
+        }
+        constexpr double TWO_PI = 6.283185307179586476925286766559;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const double i = (double)(iv * 8 + j);
-        const double ang = (double)s * pow(base, -i / (double)half);
-        double sd, cd;
-        sincos(ang, &sd, &cd);
-        c[j] = (float)cd;
-        sn[j] = (float)sd;
+        for (int j = 0; j < 8; ++j) {
+            const double ang = (double)s * f;
+            const double red = ang - rint(ang * (1.0 / TWO_PI)) * TWO_PI;
+            __sincosf((float)red, &sn[j], &c[j]);
+            f *= ratio;
+        }
     }
     const int64_t h0 = (int64_t)blockIdx.y * bh_per_cta;
     const int64_t h1 = min(bh, h0 + bh_per_cta);
-    for (int64_t h = h0; h < h1; ++h) {
-        const T* xr = x + (h * S + s) * D;
-        T* yr = y + (h * S + s) * D;
-        const sf::Vec8<T> a = sf::ld_global_nc_v8<T>(xr + iv * 8);
-        const sf::Vec8<T> b = sf::ld_global_nc_v8<T>(xr + half + iv * 8);
+    auto rotate = [&](const sf::Vec8<T>& a, const sf::Vec8<T>& b, T* yr) {
         sf::Vec8<T> o1, o2;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -50,6 +58,21 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const T* __restrict__ x, 
         }
         sf::st_global_v8<T>(yr + iv * 8, o1);
         sf::st_global_v8<T>(yr + half + iv * 8, o2);
+    };
+    int64_t h = h0;
+    for (; h + 1 < h1; h += 2) {
+        const T* xa = x + (h * S + s) * D;
+        const T* xb = x + ((h + 1) * S + s) * D;
+        const sf::Vec8<T> a0 = sf::ld_global_nc_v8<T>(xa + iv * 8);
+        const sf::Vec8<T> b0 = sf::ld_global_nc_v8<T>(xa + half + iv * 8);
+        const sf::Vec8<T> a1 = sf::ld_global_nc_v8<T>(xb + iv * 8);
+        const sf::Vec8<T> b1 = sf::ld_global_nc_v8<T>(xb + half + iv * 8);
+        rotate(a0, b0, y + (h * S + s) * D);
+        rotate(a1, b1, y + ((h + 1) * S + s) * D);
+    }
+    if (h < h1) {
+        const T* xr = x + (h * S + s) * D;
+        rotate(sf::ld_global_nc_v8<T>(xr + iv * 8), sf::ld_global_nc_v8<T>(xr + half + iv * 8), y + (h * S + s) * D);
     }
 }
 
@@ -80,7 +103,7 @@ int launch_t(const void* x, void* y, int64_t B, int64_t H, int64_t S, int64_t D,
     if (vec) {
         const int64_t pos_blocks = (S + POS_PER_CTA - 1) / POS_PER_CTA;
         // Enough CTAs to fill the GPU several times over; each walks a share of the heads.
-        int64_t splits = (int64_t)sf::sm_count() * 4 / (pos_blocks > 0 ? pos_blocks : 1);
+        int64_t splits = (int64_t)sf::sm_count() * 8 / (pos_blocks > 0 ? pos_blocks : 1);
         if (splits < 1) splits = 1;
         if (splits > bh) splits = bh;
         if (splits > 65535) splits = 65535;
@@ -88,7 +111,8 @@ int launch_t(const void* x, void* y, int64_t B, int64_t H, int64_t S, int64_t D,
         splits = (bh + per - 1) / per;
         if (pos_blocks > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "rope: S too large");
         const int threads = (int)((half / 8) * POS_PER_CTA);
-        rope_vec_kernel<T><<<dim3((unsigned)pos_blocks, (unsigned)splits), threads, 0, st>>>((const T*)x, (T*)y, bh, S, D, base, per);
+        rope_vec_kernel<T><<<dim3((unsigned)pos_blocks, (unsigned)splits), threads, 0, st>>>((const T*)x, (T*)y, bh, S, D,
+                                                                                             std::pow(base, -1.0 / (double)half), per);
     } else {
         const int64_t total = bh * S * half;
         int64_t blocks = (total + 255) / 256;

@@ -137,12 +137,13 @@ __global__ void __launch_bounds__(256) rowsum_generic_kernel(const T* __restrict
     if (threadIdx.x == 0) y[row] = sf::Dt<T>::from_f(s);
 }
 
-// Vectors per thread: the smallest of 1/2/4/8 giving <= 256 threads (8 may use up to 1024).
+// Vectors per thread: the smallest of 1/2/4/8 giving <= 128 threads (8 may use up to 1024), so up
+// to 16 rows are resident per SM and more of each row's bytes are in flight per thread.
 int pick_nv(int64_t n) {
     const int64_t nvec = n / 8;
     for (int cand : {1, 2, 4, 8}) {
         const int64_t threads = (nvec + cand - 1) / cand;
-        if (threads <= 256 || (cand == 8 && threads <= 1024)) return cand;
+        if (threads <= 128 || (cand == 8 && threads <= 1024)) return cand;
     }
     return 0;
 }
