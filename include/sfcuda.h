@@ -184,10 +184,11 @@ SF_API int sf_gemm_nt(const void* A, const void* B, void* C, int64_t M, int64_t 
 
 /*
  * gemm_nn: C[M,N] = A[M,K] . B[K,N] — the tasks/gemm contract (reference.py:110-114,
- * opspec.json:5: B row-major [K,N]).  With a workspace of at least
- * sf_gemm_nn_workspace_bytes(M,N,K,dtype) bytes (16-byte aligned, caller-owned) B is
- * transposed into it and the tensor-core kernel runs; with workspace == NULL the general
- * fallback kernel runs.
+ * opspec.json:5: B row-major [K,N]).  With 16-byte aligned tensors, K % 8 == 0 and N % 8 == 0 the
+ * tensor-core kernel reads B in place (sf_gemm_nn_workspace_bytes returns 0).  Otherwise, with a
+ * workspace of at least sf_gemm_nn_workspace_bytes(M,N,K,dtype) bytes (16-byte aligned,
+ * caller-owned) B is transposed into it and the tensor-core kernel runs; with workspace == NULL
+ * the general fallback kernel runs.
  */
 SF_API uint64_t sf_gemm_nn_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t dtype);
 SF_API int sf_gemm_nn(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,

@@ -7,8 +7,9 @@
 // (tcenv/portfolio/dispatch.py:595-700): the tcgen05 kernel (gemm_tc.cu) serves every shape it
 // supports (16-byte aligned bases, K % 8 == 0); everything else runs the general fallback below,
 // a tiled fp32-accumulate SIMT kernel valid for any M, N, K >= 0 and any alignment.  The NN
-// layout reaches the tensor-core kernel through a transpose of B into a caller-provided
-// workspace of K*N elements (sf_gemm_nn_workspace_bytes); without one it takes the fallback.
+// layout is read by the tensor-core kernel directly (B as an MN-major operand) when N % 8 == 0;
+// otherwise it goes through a transpose of B into a caller-provided workspace of K*N elements
+// (sf_gemm_nn_workspace_bytes, 0 when no workspace is needed), and without one takes the fallback.
 #include "sf_common.cuh"
 
 #include <algorithm>
@@ -17,6 +18,9 @@ bool sf_gemm_nt_tc_supported(const void* A, const void* B, const void* C, int64_
 int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
                          cudaStream_t stream, char* err, uint64_t cap);
 int sf_gemm_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
+bool sf_gemm_nn_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K);
+int sf_gemm_nn_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+                         cudaStream_t stream, char* err, uint64_t cap);
 
 namespace {
 
@@ -157,12 +161,15 @@ int sf_gemm_nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t 
     if (rc) return rc;
     if (M == 0 || N == 0) return SF_OK;
     if (K == 0) return zero_output(C, M, N, s, err, cap);
+    const bool direct = sf_gemm_nn_tc_supported(A, B, C, M, N, K);
+    if (direct && variant != 2) return sf_gemm_nn_tc_launch(A, B, C, M, N, K, dtype, s, err, cap);
     const uint64_t need = (uint64_t)K * (uint64_t)N * 2u;
     const bool ws_ok = workspace && workspace_bytes >= need && sf::aligned16(workspace);
     const bool tc = ws_ok && sf_gemm_nt_tc_supported(A, workspace, C, M, N, K);
     if (variant == 1 && !tc)
-        return sf::fail(SF_EINVAL, err, cap, "gemm_nn: the tcgen05 variant needs a 16-byte aligned workspace of %llu bytes and K %% 8 == 0",
-                        (unsigned long long)need);
+        return sf::fail(SF_EINVAL, err, cap,
+                        "gemm_nn: the tcgen05 variant needs aligned bases with N %% 8 == 0, or a 16-byte aligned workspace of %llu bytes; "
+                        "and K %% 8 == 0", (unsigned long long)need);
     if (tc && variant != 2) {
         const int64_t gx = (N + 63) / 64, gy = (K + 63) / 64;
         if (gy > 65535) return sf::fail(SF_EINVAL, err, cap, "gemm_nn: K=%lld too large for the transpose grid", (long long)K);
@@ -182,7 +189,8 @@ extern "C" int sf_gemm_nt(const void* A, const void* B, void* C, int64_t M, int6
 extern "C" uint64_t sf_gemm_nn_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t dtype) {
     (void)M;
     (void)dtype;
-    if (N <= 0 || K <= 0) return 0;
+    // N % 8 == 0 (with 16-byte aligned tensors) runs without a workspace.
+    if (N <= 0 || K <= 0 || N % 8 == 0) return 0;
     return (uint64_t)N * (uint64_t)K * 2u;
 }
 

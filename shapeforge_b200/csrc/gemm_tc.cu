@@ -3,8 +3,10 @@
 //   C[M,N] = A[M,K] . B[N,K]^T      (both operands K-major; fp16 or bf16 in, fp32 accumulate,
 //                                    one rounding to the input dtype at the output)
 //
-// This is the gemm_nt workload (BASELINE config "dense gemm", C = A.B^T); the reference task
-// tasks/gemm (B stored [K,N]) reaches it after a transpose of B (gemm_nn.cu).
+// This is the gemm_nt workload (dense gemm, C = A.B^T).  The reference task tasks/gemm stores B as
+// [K, N]; the same kernel reads that layout directly as an MN-major B operand (BMN = true): each
+// K-block of B arrives as 64 x 64 TMA boxes (64 N columns of 128 bytes for 64 K rows) and the
+// MMA's B descriptor walks 16 K rows (2 KB) per instruction with 8 KB between 64-column blocks.
 //
 // Persistent, warp-specialised kernel, one CTA per SM (192 KB of pipeline shared memory):
 //   warp 0      TMA producer: 128x64 A box + 256x64 B box per K-block, 128-byte swizzle,
@@ -94,7 +96,7 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <typename T>
+template <typename T, bool BMN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_nt_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_bh, T* __restrict__ C, int M, int N, int K, int full_units,
@@ -153,10 +155,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     uint8_t* sb = sa + A_BYTES;
                     sm100::mbar_arrive_expect_tx(&bars->full[stage], half < 0 ? STAGE_BYTES : A_BYTES + B_BYTES / 2);
                     sm100::tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * BK, tm * BM);
-                    if (half < 0)
+                    if (BMN) {
+                        // B [K, N]: 64-column boxes of 64 K rows (8 KB each), N-block nb at sb + 8 KB * nb.
+                        const int n0 = tn * BN + (half < 0 ? 0 : half * (BN / 2));
+                        const int nblocks = half < 0 ? BN / 64 : BN / 128;
+                        for (int nb = 0; nb < nblocks; ++nb)
+                            sm100::tma_load_2d(sb + nb * (64 * BK * 2), &tmap_b, &bars->full[stage], n0 + nb * 64, kb * BK);
+                    } else if (half < 0) {
                         sm100::tma_load_2d(sb, &tmap_b, &bars->full[stage], kb * BK, tn * BN);
-                    else
+                    } else {
                         sm100::tma_load_2d(sb, &tmap_bh, &bars->full[stage], kb * BK, tn * BN + half * (BN / 2));
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -176,8 +185,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc_full = sm100::idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
-            constexpr uint32_t idesc_half = sm100::idesc_f16(BM, BN / 2, std::is_same<T, __nv_bfloat16>::value);
+            constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+            constexpr uint32_t idesc_full = BMN ? sm100::idesc_f16_bmn(BM, BN, BF) : sm100::idesc_f16(BM, BN, BF);
+            constexpr uint32_t idesc_half = BMN ? sm100::idesc_f16_bmn(BM, BN / 2, BF) : sm100::idesc_f16(BM, BN / 2, BF);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -199,7 +209,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint64_t ad = sm100::smem_desc_k_sw128(sa + k * 32);
-                        const uint64_t bd = sm100::smem_desc_k_sw128(sb + k * 32);
+                        const uint64_t bd = BMN ? sm100::smem_desc_mn_sw128(sb + (uint32_t)(k * 16 * 128), 64 * BK * 2, 1024)
+                                                : sm100::smem_desc_k_sw128(sb + k * 32);
                         sm100::mma_f16(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                     }
                     sm100::mma_commit(&bars->empty[stage]);
@@ -272,16 +283,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---- host side ----------------------------------------------------------------------------------
 
-template <typename T>
+template <typename T, bool BMN>
 int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream, char* err,
               uint64_t cap) {
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     CUtensorMap ma, mb, mbh;
     int rc = sf::tmap_kmajor(&ma, A, M, K, BM, bf16, err, cap);
     if (rc) return rc;
-    rc = sf::tmap_kmajor(&mb, B, N, K, BN, bf16, err, cap);
-    if (rc) return rc;
-    rc = sf::tmap_kmajor(&mbh, B, N, K, BN / 2, bf16, err, cap);
+    if (BMN) {
+        // B [K, N] row-major: 64-element (128-byte) inner boxes along N, 64 K rows.
+        rc = sf::tmap_kmajor(&mb, B, K, N, BK, bf16, err, cap);
+        mbh = mb;
+    } else {
+        rc = sf::tmap_kmajor(&mb, B, N, K, BN, bf16, err, cap);
+        if (!rc) rc = sf::tmap_kmajor(&mbh, B, N, K, BN / 2, bf16, err, cap);
+    }
     if (rc) return rc;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -290,7 +306,7 @@ int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
         return sf::fail(SF_EDEVICE, err, cap, "gemm: cannot resolve the status word");
     static std::atomic<uint64_t> attr_done{0};
     if (sf::once_per_device(attr_done))
-        cudaFuncSetAttribute(gemm_nt_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaFuncSetAttribute(gemm_nt_tc_kernel<T, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int64_t sms = std::max(1, sf::sm_count());
     // Tiles left over after the last full round of the persistent CTAs are split into halves when
@@ -303,8 +319,8 @@ int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     }
     if (total_units > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "gemm: too many tiles");
     const int grid = (int)std::min<int64_t>(total_units, sms);
-    gemm_nt_tc_kernel<T><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, mbh, (T*)C, (int)M, (int)N, (int)K, (int)full_units,
-                                                                    (int)total_units, st);
+    gemm_nt_tc_kernel<T, BMN><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, mbh, (T*)C, (int)M, (int)N, (int)K, (int)full_units,
+                                                                         (int)total_units, st);
     return sf::check_launch("gemm_nt tcgen05 launch", err, cap);
 }
 
@@ -319,8 +335,21 @@ bool sf_gemm_nt_tc_supported(const void* A, const void* B, const void* C, int64_
 
 int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
                          cudaStream_t stream, char* err, uint64_t cap) {
-    if (dtype == SF_DTYPE_F16) return launch_tc<__half>(A, B, C, M, N, K, stream, err, cap);
-    if (dtype == SF_DTYPE_BF16) return launch_tc<__nv_bfloat16>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_F16) return launch_tc<__half, false>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_BF16) return launch_tc<__nv_bfloat16, false>(A, B, C, M, N, K, stream, err, cap);
+    return sf::fail(SF_EINVAL, err, cap, "gemm: dtype %d is not fp16/bf16", dtype);
+}
+
+// C = A . B with B stored [K, N], read as an MN-major operand: additionally needs N % 8 == 0 (B's
+// rows are TMA strides, multiples of 16 bytes).
+bool sf_gemm_nn_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K) {
+    return sf_gemm_nt_tc_supported(A, B, C, M, N, K) && (N % 8) == 0;
+}
+
+int sf_gemm_nn_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+                         cudaStream_t stream, char* err, uint64_t cap) {
+    if (dtype == SF_DTYPE_F16) return launch_tc<__half, true>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_BF16) return launch_tc<__nv_bfloat16, true>(A, B, C, M, N, K, stream, err, cap);
     return sf::fail(SF_EINVAL, err, cap, "gemm: dtype %d is not fp16/bf16", dtype);
 }
 
