@@ -210,12 +210,19 @@ int check(int64_t N, int64_t H, int64_t D, int32_t dtype, char* err, uint64_t ca
 
 int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log, const void* dt_bias,
                   const void* initial_state, const void* cu_seqlens, const void* scale, void* out, void* final_state, int64_t N,
-                  int64_t H, int64_t D, float lower_bound, int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
+                  int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
     int rc = check(N, H, D, dtype, err, cap);
     if (rc) return rc;
     if (N == 0) return SF_OK;
     if (!q || !k || !v || !g || !beta || !a_log || !dt_bias || !initial_state || !cu_seqlens || !scale || !out || !final_state)
         return sf::fail(SF_EINVAL, err, cap, "kda: null tensor pointer");
+    // Variant 0: the chunked tensor-core kernel when it applies (D = 128, aligned rows,
+    // LOWER_BOUND >= -5.4), else the recurrent one; 1 forces the chunked kernel, 2 the recurrent one.
+    if (variant != 2) {
+        rc = sf_kda_task_chunk_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, out, final_state, N, H, D,
+                                      lower_bound, dtype, st, variant == 1 ? err : nullptr, variant == 1 ? cap : 0);
+        if (rc == SF_OK || variant == 1 || rc != SF_EINVAL) return rc;
+    }
     if (dtype == SF_DTYPE_F16)
         return launch_t<__half, true>(q, k, v, g, beta, (const float*)a_log, (const float*)dt_bias, (const float*)initial_state,
                                       (const int32_t*)cu_seqlens, (const float*)scale, 0.f, lower_bound, N, H, D, out,
@@ -252,7 +259,7 @@ extern "C" int sf_varlen_kda(const void* q, const void* k, const void* v, const 
                              void* final_state, int64_t num_seqs, int64_t H, int64_t D, float lower_bound, int32_t dtype, void* stream,
                              char* err, uint64_t cap) {
     return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state, num_seqs, H, D,
-                         lower_bound, dtype, (cudaStream_t)stream, err, cap);
+                         lower_bound, dtype, 0, (cudaStream_t)stream, err, cap);
 }
 
 extern "C" int sf_varlen_kda_gated(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,

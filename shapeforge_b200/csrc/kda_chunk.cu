@@ -36,6 +36,11 @@
 //          MMA 2  S += W^T . Kend (high and residual parts; M=128, N=128, K=16), whose completion
 //          also hands the chunk's buffers back to the prep warpgroup.  The next chunk's MMA 1 is
 //          issued behind it: the tensor pipe runs one CTA's MMAs in issue order.
+// The task op (tasks/varlen_kda/reference.py:323-374) runs the same kernel with TASK = true: g and beta
+// arrive as 16-bit tensors, each chunk's q and k rows are L2-normalised (rsqrt(sum x^2 + 1e-6), q times
+// the scale tensor) from the staged registers, the log-decay is LOWER_BOUND * sigmoid(exp(A_log[h]) *
+// (g + dt_bias[h, c])) (>= LOWER_BOUND per token, so e^{-b} stays finite over 16 tokens for
+// LOWER_BOUND >= -5.4) and beta is sigmoid(beta).
 // Every mbarrier wait is bounded; a timeout is reported through sf_kernel_status.
 #include "sf_common.cuh"
 #include "sm100.cuh"
@@ -80,7 +85,9 @@ struct Layout {
     static constexpr int TM = TA + C * C * 4;
     static constexpr int TT = TM + C * C * 4;
     static constexpr int TMT = TT + C * C * 4;
-    static constexpr int PREP_BYTES = TMT + C * C * 4;
+    static constexpr int NQ = TMT + C * C * 4;     // task: inverse L2 norms of q and k per token
+    static constexpr int NK = NQ + C * 4;
+    static constexpr int PREP_BYTES = NK + C * 4;
     static constexpr int BARS = PREP + 2 * PREP_BYTES;
     static constexpr int BYTES = BARS + 64;
 };
@@ -130,12 +137,21 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 // token tid / 8 and the 16 columns (tid % 8) * 16 .. +15.
 struct Prefetch {
     uint4 q[2], k[2], v[2];
-    float4 g[4];
+    float4 g[4];   // gated: fp32 log-decay
+    uint4 g16[2];  // task: 16-bit g
     float beta;
 };
 
-template <typename T>
-__device__ __forceinline__ void load_chunk(Prefetch& p, const T* q, const T* k, const T* v, const float* g, const float* beta, int t0,
+// Task inputs that the gated workload does not have.
+struct TaskArgs {
+    const float* a_log;    // [H]
+    const float* dt_bias;  // [H * D]
+    const float* scale;    // [1]
+    float lower_bound;
+};
+
+template <typename T, bool TASK>
+__device__ __forceinline__ void load_chunk(Prefetch& p, const T* q, const T* k, const T* v, const void* g, const void* beta, int t0,
                                            int nt, int H, int h, int tid) {
     const int tt = tid >> 3, part = tid & 7;
     const bool live = tt < nt;
@@ -146,11 +162,37 @@ __device__ __forceinline__ void load_chunk(Prefetch& p, const T* q, const T* k, 
         p.k[i] = live ? __ldg(reinterpret_cast<const uint4*>(k + base) + i) : make_uint4(0, 0, 0, 0);
         p.v[i] = live ? __ldg(reinterpret_cast<const uint4*>(v + base) + i) : make_uint4(0, 0, 0, 0);
     }
+    if (TASK) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) p.g[i] = live ? __ldg(reinterpret_cast<const float4*>(g + base) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    p.beta = (tid < nt) ? __ldg(beta + (size_t)(t0 + tid) * H + h) : 0.f;
+        for (int i = 0; i < 2; ++i)
+            p.g16[i] = live ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(g) + base) + i) : make_uint4(0, 0, 0, 0);
+        p.beta = (tid < nt) ? sf::Dt<T>::to_f(reinterpret_cast<const T*>(beta)[(size_t)(t0 + tid) * H + h]) : -INFINITY;  // sigmoid -> 0
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            p.g[i] = live ? __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + base) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        p.beta = (tid < nt) ? __ldg(reinterpret_cast<const float*>(beta) + (size_t)(t0 + tid) * H + h) : 0.f;
+    }
 }
 
+template <typename T>
+__device__ __forceinline__ float sum_sq16(const uint4 (&w)[2]) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t r[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float a = from16<T>((uint16_t)(r[j] & 0xFFFFu)), b = from16<T>((uint16_t)(r[j] >> 16));
+            s = fmaf(a, a, fmaf(b, b, s));
+        }
+    }
+    return s;
+}
+
+// Staged chunk -> the prep warpgroup's scratch.  Task: g converted to fp32, sigmoid(beta), and the
+// inverse L2 norms of each token's q and k rows (the 8 threads of a token reduce by shuffles).
+template <typename T, bool TASK>
 __device__ __forceinline__ void store_chunk(const Prefetch& p, uint8_t* prep, int tid) {
     const int tt = tid >> 3, part = tid & 7;
     const int off = (tt * D + part * 16) * 2;
@@ -161,16 +203,39 @@ __device__ __forceinline__ void store_chunk(const Prefetch& p, uint8_t* prep, in
         *reinterpret_cast<uint4*>(prep + Layout::VS + off + 16 * i) = p.v[i];
     }
     float* gs = reinterpret_cast<float*>(prep + Layout::GS) + tt * D + part * 16;
+    if (TASK) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(gs)[i] = p.g[i];
-    if (tid < C) reinterpret_cast<float*>(prep + Layout::BS)[tid] = p.beta;
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t r[4] = {p.g16[i].x, p.g16[i].y, p.g16[i].z, p.g16[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                gs[8 * i + 2 * j] = from16<T>((uint16_t)(r[j] & 0xFFFFu));
+                gs[8 * i + 2 * j + 1] = from16<T>((uint16_t)(r[j] >> 16));
+            }
+        }
+        float sq = sum_sq16<T>(p.q), sk = sum_sq16<T>(p.k);
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        if (part == 0) {
+            reinterpret_cast<float*>(prep + Layout::NQ)[tt] = rsqrtf(sq + 1e-6f);
+            reinterpret_cast<float*>(prep + Layout::NK)[tt] = rsqrtf(sk + 1e-6f);
+        }
+        if (tid < C) reinterpret_cast<float*>(prep + Layout::BS)[tid] = 1.0f / (1.0f + __expf(-p.beta));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(gs)[i] = p.g[i];
+        if (tid < C) reinterpret_cast<float*>(prep + Layout::BS)[tid] = p.beta;
+    }
 }
 
-template <typename T>
+template <typename T, bool TASK>
 __global__ void __launch_bounds__(NT, 1)
-    kda_chunk_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ g,
-                     const float* __restrict__ beta, const int32_t* __restrict__ cu, const float* __restrict__ state0, float scale,
-                     int H, T* __restrict__ out, float* __restrict__ final_state, sm100::KernelStatus* status) {
+    kda_chunk_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const void* __restrict__ g,
+                     const void* __restrict__ beta, const int32_t* __restrict__ cu, const float* __restrict__ state0, float scale,
+                     int H, T* __restrict__ out, float* __restrict__ final_state, sm100::KernelStatus* status, TaskArgs task) {
     constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -200,7 +265,7 @@ __global__ void __launch_bounds__(NT, 1)
     const int nchunks = (end - begin + C - 1) / C;
     Prefetch pf;
     const int pw = wg - 1;  // prep warpgroup index (chunks pw, pw + 2, ...; buffer pw)
-    if (wg >= 1 && pw < nchunks) load_chunk<T>(pf, q, k, v, g, beta, begin + pw * C, min(C, end - begin - pw * C), H, h, wtid);
+    if (wg >= 1 && pw < nchunks) load_chunk<T, TASK>(pf, q, k, v, g, beta, begin + pw * C, min(C, end - begin - pw * C), H, h, wtid);
     sm100::tc_fence_before();
     __syncthreads();
     sm100::tc_fence_after();
@@ -224,12 +289,18 @@ __global__ void __launch_bounds__(NT, 1)
         const uint32_t bar_id = 1 + 2 * pw;
         const int b = pw;
         const int c = wtid;  // key channel (and value channel)
+        // Task gate constants of this channel; the q scale (a tensor for the task op).
+        const float task_ea = TASK ? __expf(task.a_log[h]) : 0.f;
+        const float task_dtb = TASK ? task.dt_bias[(size_t)h * D + c] : 0.f;
+        const float task_lb = TASK ? task.lower_bound : 0.f;
+        const float qscale = TASK ? *task.scale : scale;
         for (int ci = pw; ci < nchunks && ok; ci += 2) {
             const int t0 = begin + ci * C;
+            const int nt_chunk = min(C, end - t0);  // tokens past the sequence end contribute no decay
             sm100::named_barrier_sync(bar_id, WG);  // previous iteration's reads of the prep scratch are done
-            store_chunk(pf, prep, wtid);
+            store_chunk<T, TASK>(pf, prep, wtid);
             sm100::named_barrier_sync(bar_id, WG);
-            if (ci + 2 < nchunks) load_chunk<T>(pf, q, k, v, g, beta, t0 + 2 * C, min(C, end - t0 - 2 * C), H, h, wtid);
+            if (ci + 2 < nchunks) load_chunk<T, TASK>(pf, q, k, v, g, beta, t0 + 2 * C, min(C, end - t0 - 2 * C), H, h, wtid);
 
             // ---- factors in fp32 (thread = key channel c) ----
             float kp[C], qp[C];
@@ -242,14 +313,18 @@ __global__ void __launch_bounds__(NT, 1)
                 float bacc = 0.f;
 #pragma unroll
                 for (int t = 0; t < C; ++t) {
-                    bacc += gs[t * D + c];
+                    float gl = gs[t * D + c];
+                    if (TASK) gl = task_lb * (1.0f / (1.0f + __expf(-task_ea * (gl + task_dtb))));
+                    bacc += t < nt_chunk ? gl : 0.f;
                     bcum[t] = bacc;
                 }
                 elast = __expf(bacc);
+                const float* nq = reinterpret_cast<const float*>(prep + Layout::NQ);
+                const float* nk = reinterpret_cast<const float*>(prep + Layout::NK);
 #pragma unroll
                 for (int t = 0; t < C; ++t) {
-                    const float kv = from16<T>(ks[t * D + c]);
-                    const float qv = from16<T>(qs[t * D + c]) * scale;
+                    const float kv = from16<T>(ks[t * D + c]) * (TASK ? nk[t] : 1.0f);
+                    const float qv = from16<T>(qs[t * D + c]) * (TASK ? nq[t] * qscale : qscale);
                     const float e = __expf(bcum[t]), en = __expf(-bcum[t]);
                     kp[t] = kv * e;
                     qp[t] = qv * e;
@@ -511,37 +586,54 @@ sm100::KernelStatus* status_ptr() {
 
 }  // namespace
 
+namespace {
+
+template <bool TASK>
+int chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                 const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t Dd, float scale, TaskArgs task,
+                 int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
+    if (Dd != D || !sf::aligned16(q) || !sf::aligned16(k) || !sf::aligned16(v) || !sf::aligned16(g) || !sf::aligned16(final_state) ||
+        (initial_state && !sf::aligned16(initial_state)))
+        return sf::fail(SF_EINVAL, err, cap, "kda: the chunked kernel needs D = 128 and 16-byte-aligned tensors");
+    if (N * H > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "kda: too many chains");
+    sm100::KernelStatus* status = status_ptr();
+    if (!status) return sf::fail(SF_EDEVICE, err, cap, "kda: cannot resolve the status word");
+    const int smem = Layout::BYTES + 1024;
+    static std::atomic<uint64_t> attr_done{0};
+    if (sf::once_per_device(attr_done)) {
+        cudaFuncSetAttribute(kda_chunk_kernel<__half, TASK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(kda_chunk_kernel<__nv_bfloat16, TASK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    }
+    if (dtype == SF_DTYPE_F16)
+        kda_chunk_kernel<__half, TASK><<<(unsigned)(N * H), NT, smem, st>>>(
+            (const __half*)q, (const __half*)k, (const __half*)v, g, beta, (const int32_t*)cu_seqlens, (const float*)initial_state, scale,
+            (int)H, (__half*)out, (float*)final_state, status, task);
+    else
+        kda_chunk_kernel<__nv_bfloat16, TASK><<<(unsigned)(N * H), NT, smem, st>>>(
+            (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, (const int32_t*)cu_seqlens,
+            (const float*)initial_state, scale, (int)H, (__nv_bfloat16*)out, (float*)final_state, status, task);
+    return sf::check_launch(TASK ? "kda chunk launch" : "kda_gated chunk launch", err, cap);
+}
+
+}  // namespace
+
 // Chunked kernel for D = 128 with 16-byte-aligned q/k/v/g rows; returns SF_EINVAL (without
 // launching) when the shape or alignment does not qualify.
 int sf_kda_gated_chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                               const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t Dd, float scale,
                               int32_t dtype, cudaStream_t st, char* err, uint64_t cap) {
-    if (Dd != D || !sf::aligned16(q) || !sf::aligned16(k) || !sf::aligned16(v) || !sf::aligned16(g) || !sf::aligned16(final_state) ||
-        (initial_state && !sf::aligned16(initial_state)))
-        return sf::fail(SF_EINVAL, err, cap, "kda_gated: the chunked kernel needs D = 128 and 16-byte-aligned tensors");
-    if (N * H > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "kda_gated: too many chains");
-    sm100::KernelStatus* status = status_ptr();
-    if (!status) return sf::fail(SF_EDEVICE, err, cap, "kda_gated: cannot resolve the status word");
-    const int smem = Layout::BYTES + 1024;
-    static std::atomic<uint64_t> attr_done{0};
-    if (dtype == SF_DTYPE_F16) {
-        if (sf::once_per_device(attr_done)) {
-            cudaFuncSetAttribute(kda_chunk_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            cudaFuncSetAttribute(kda_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        }
-        kda_chunk_kernel<__half><<<(unsigned)(N * H), NT, smem, st>>>((const __half*)q, (const __half*)k, (const __half*)v, (const float*)g,
-                                                                    (const float*)beta, (const int32_t*)cu_seqlens, (const float*)initial_state,
-                                                                    scale, (int)H, (__half*)out, (float*)final_state, status);
-    } else {
-        if (sf::once_per_device(attr_done)) {
-            cudaFuncSetAttribute(kda_chunk_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            cudaFuncSetAttribute(kda_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        }
-        kda_chunk_kernel<__nv_bfloat16><<<(unsigned)(N * H), NT, smem, st>>>(
-            (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (const float*)g, (const float*)beta,
-            (const int32_t*)cu_seqlens, (const float*)initial_state, scale, (int)H, (__nv_bfloat16*)out, (float*)final_state, status);
-    }
-    return sf::check_launch("kda_gated chunk launch", err, cap);
+    return chunk_launch<false>(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, Dd, scale, TaskArgs{nullptr, nullptr, nullptr, 0.f},
+                               dtype, st, err, cap);
+}
+
+// The task op (in-op norms and gates) on the chunked kernel; same qualification rules.
+int sf_kda_task_chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                             const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* out,
+                             void* final_state, int64_t N, int64_t H, int64_t Dd, float lower_bound, int32_t dtype, cudaStream_t st,
+                             char* err, uint64_t cap) {
+    if (!(lower_bound >= -5.4f)) return sf::fail(SF_EINVAL, err, cap, "kda: the chunked kernel needs LOWER_BOUND >= -5.4");
+    return chunk_launch<true>(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, Dd, 0.f,
+                              TaskArgs{(const float*)a_log, (const float*)dt_bias, (const float*)scale, lower_bound}, dtype, st, err, cap);
 }
 
 int sf_kda_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream) {

@@ -112,7 +112,11 @@ int sf_attention_launch(const void* q, const void* k, const void* v, void* o, in
 int sf_attention_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
 int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log, const void* dt_bias,
                   const void* initial_state, const void* cu_seqlens, const void* scale, void* out, void* final_state, int64_t N,
-                  int64_t H, int64_t D, float lower_bound, int32_t dtype, cudaStream_t st, char* err, uint64_t cap);
+                  int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);
+int sf_kda_task_chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                             const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* out,
+                             void* final_state, int64_t N, int64_t H, int64_t D, float lower_bound, int32_t dtype, cudaStream_t st,
+                             char* err, uint64_t cap);
 int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                         const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
                         int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);

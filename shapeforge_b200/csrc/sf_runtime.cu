@@ -156,7 +156,7 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
                                        d->flags & 1, d->dtype, d->variant, s, err, cap);
         case SF_OP_KDA:
             return sf_kda_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], a[8], a[9], (void*)a[10], (void*)a[11], d->dims[0],
-                                 d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype, s, err, cap);
+                                 d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype, d->variant, s, err, cap);
         case SF_OP_KDA_GATED:
             return sf_kda_gated_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], (void*)a[7], (void*)a[8], d->dims[0], d->dims[1],
                                        d->dims[2], (float)d->attrs[0], d->dtype, d->variant, s, err, cap);

@@ -228,9 +228,11 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
 
 
 def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, lower_bound: float = -5.0,
-               output: torch.Tensor | None = None, final_state: torch.Tensor | None = None):
+               output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0):
     """Packed-varlen KDA forward (tasks/varlen_kda/reference.py:323-374).  ``scale`` is the
-    task's one-element fp32 tensor; returns ``(output [T,H,D], final_state [N,H,D,D])``."""
+    task's one-element fp32 tensor; returns ``(output [T,H,D], final_state [N,H,D,D])``.
+    ``variant``: 0 = the chunked tensor-core kernel where it applies (D = 128), else the
+    recurrent one; 1 = chunked only; 2 = recurrent only."""
     for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
         _check(t, name, q.dtype)
     for name, t in (("A_log", a_log), ("dt_bias", dt_bias), ("initial_state", initial_state), ("scale", scale)):
@@ -241,7 +243,7 @@ def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scal
     output = torch.empty_like(v) if output is None else output
     final_state = torch.empty((n, h, d, d), dtype=torch.float32, device=q.device) if final_state is None else final_state
     ptrs = [x.data_ptr() for x in (q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state)]
-    _run("varlen_kda", q, ptrs, dims=(n, h, d), attrs=(lower_bound,))
+    _run("varlen_kda", q, ptrs, dims=(n, h, d), attrs=(lower_bound,), variant=variant)
     return output, final_state
 
 

@@ -70,6 +70,31 @@ def _oracle_task(inp, heads):
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("variant", [1, 2])
+def test_task_op_chunked_and_recurrent(cuda_device, dtype, variant):
+    """The task op at D = 128 through the chunked tensor-core kernel (variant 1: in-op q/k norms,
+    gates from A_log / dt_bias, sigmoid beta, initial state) and the recurrent kernel (variant 2),
+    both against the fp64 oracle; a 700-token sequence carries the state through 44 chunks, a
+    zero-length one is skipped."""
+    lengths = [700, 0, 33, 16, 129]
+    heads = 3
+    inp = cases.kda_task_inputs(lengths, heads, 128, dtype, seed=cases.case_seed(11, 2))
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    out = torch.full_like(d["v"], float("nan"))
+    out, fin = ops.varlen_kda(d["q"], d["k"], d["v"], d["g"], d["beta"], d["A_log"], d["dt_bias"], d["initial_state"],
+                              d["cu_seqlens"], d["scale"], output=out, variant=variant)
+    torch.cuda.synchronize()
+    hs = list(range(heads))
+    ro, rf = _oracle_task(d, hs)
+    v1 = _verdict(_np(out), ro, dtype, dtype)
+    v2 = _verdict(_np(fin), rf, dtype, "fp32")
+    assert v1.ok, ("output", variant, v1.summary())
+    assert v2.ok, ("final_state", variant, v2.summary())
+    code, where = ops.kernel_status()
+    assert code == 0, f"tensor-core kernel status {code} at wait {where}"
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
 @pytest.mark.parametrize("dim", [128, 64, 32])
 def test_task_op_large_heads(cuda_device, dtype, dim):
     lengths = [130, 64, 1, 300, 0, 17]
