@@ -46,18 +46,19 @@ constexpr int TILE_ROWS = 128;
 constexpr int ROW_TILE_BYTES = TILE_ROWS * BK * 2;  // 16 KB: 128 rows x 128 bytes
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_LIMIT = 227 * 1024;
-// Dynamic shared memory available next to the 4 KB static sign table.
-constexpr int kMaxDynSmem = SMEM_LIMIT - 4096;
-// The base kernel has no static shared memory (its table is dynamic).
+// Neither kernel has static shared memory (the sign tables are dynamic).
 constexpr int BASE_SMEM_LIMIT = SMEM_LIMIT;
 
+constexpr int TASK_MAX_STAGES = 8;
+
 struct __align__(8) Bars {
-    uint64_t full_tma[4];
-    uint64_t full_exp[4];
-    uint64_t empty[4];
+    uint64_t full_tma[TASK_MAX_STAGES];
+    uint64_t full_exp[TASK_MAX_STAGES];
+    uint64_t empty[TASK_MAX_STAGES];
     uint64_t acc_full;
     uint32_t tmem_base;
 };
+static_assert(sizeof(Bars) <= 256, "the task kernel reserves 256 bytes for its barriers");
 
 constexpr int BASE_MAX_STAGES = 8;  // W_base + x ring
 constexpr int BASE_SSTAGES = 3;     // expanded-sign ring
@@ -78,23 +79,9 @@ __device__ __forceinline__ uint32_t minus_one_pair() {
     return std::is_same<T, __half>::value ? 0xBC00BC00u : 0xBF80BF80u;
 }
 
-// Lookup table: byte value b -> the 8 16-bit values (+1 where bit j of b is set, else -1) of
-// one 16-byte chunk.  Built once per CTA in shared memory.
-template <typename T>
-__device__ __forceinline__ void build_sign_lut(uint4* lut) {
-    const uint32_t base = minus_one_pair<T>();
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-        uint32_t w[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint32_t b = ((uint32_t)i >> (2 * q)) & 3u;
-            w[q] = base ^ ((b & 1u) << 15) ^ ((b & 2u) << 30);
-        }
-        lut[i] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-}
-
-// The same table, LUT_COPIES interleaved copies: slot 8e + k holds entry e.
+// Lookup table: byte value b -> the 8 16-bit values (+1 where bit j of b is set, else -1) of one
+// 16-byte chunk, built once per CTA in shared memory as LUT_COPIES interleaved copies: slot 8e + k
+// holds entry e.
 template <typename T>
 __device__ __forceinline__ void build_sign_lut8(uint4* lut) {
     const uint32_t base = minus_one_pair<T>();
@@ -110,22 +97,14 @@ __device__ __forceinline__ void build_sign_lut8(uint4* lut) {
     }
 }
 
-// expand_row_sw128 reading copy `copy` of the interleaved table.
+// Row r of a K-major 128-byte-swizzled tile (64 16-bit elements per row) from 64 sign bits, reading
+// copy `copy` of the interleaved table: element j = +1 if bit j is set, else -1; chunk c (elements
+// 8c..8c+7) lives at chunk c ^ (r % 8).
 __device__ __forceinline__ void expand_row_sw128_lut8(uint8_t* tile, int r, uint64_t bits, const uint4* lut, int copy) {
     uint8_t* row = tile + r * 128;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) * 16)) = lut[(((uint32_t)(bits >> (8 * c)) & 0xFFu) << 3) + copy];
-    }
-}
-
-// Row r of a K-major 128-byte-swizzled tile (64 16-bit elements per row) from 64 sign bits:
-// element j = +1 if bit j is set, else -1.  Chunk c (elements 8c..8c+7) lives at chunk c ^ (r%8).
-__device__ __forceinline__ void expand_row_sw128(uint8_t* tile, int r, uint64_t bits, const uint4* lut) {
-    uint8_t* row = tile + r * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) * 16)) = lut[(uint32_t)(bits >> (8 * c)) & 0xFFu];
     }
 }
 
@@ -372,8 +351,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int stage_bytes = 2 * ROW_TILE_BYTES;
     Bars* bars = reinterpret_cast<Bars*>(smem + stages * stage_bytes);
-    __shared__ uint4 lut[256];
-    build_sign_lut<T>(lut);
+    // Sign table with LUT_COPIES interleaved copies (lane L reads copy L % 8: the 8 lanes of a
+    // 128-bit shared-memory phase hit 8 bank groups).
+    uint4* lut = reinterpret_cast<uint4*>(smem + stages * stage_bytes + 256);
+    build_sign_lut8<T>(lut);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * TILE_ROWS, n0 = blockIdx.x * TILE_ROWS;
     const int nkb = (K + BK - 1) / BK;
@@ -455,7 +436,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     ok = false;
                     break;
                 }
-                expand_row_sw128(smem + s * stage_bytes + ROW_TILE_BYTES, t, (uint64_t)lo[i] | ((uint64_t)hi[i] << 32), lut);
+                expand_row_sw128_lut8(smem + s * stage_bytes + ROW_TILE_BYTES, t, (uint64_t)lo[i] | ((uint64_t)hi[i] << 32), lut,
+                                      lane & (LUT_COPIES - 1));
                 sm100::fence_proxy_async_smem();
                 sm100::mbar_arrive(&bars->full_exp[s]);
                 if (++s == stages) { s = 0; ph ^= 1u; }
@@ -605,11 +587,12 @@ int launch_task_tc(const void* x, const void* bits, void* y, int64_t M, int64_t 
     CUtensorMap mx;
     int rc = sf::tmap_kmajor(&mx, x, M, K, TILE_ROWS, bf16, err, cap);
     if (rc) return rc;
-    const int stages = 4;
-    const int smem = stages * 2 * ROW_TILE_BYTES + 1024 + 256;
+    const int stages = 5;
+    static_assert(5 <= TASK_MAX_STAGES, "one barrier of each kind per stage");
+    const int smem = stages * 2 * ROW_TILE_BYTES + 256 + LUT8_BYTES + 1024;
     static std::atomic<uint64_t> attr_done{0};
     if (sf::once_per_device(attr_done))
-        cudaFuncSetAttribute(bitdelta_task_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+        cudaFuncSetAttribute(bitdelta_task_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
     const dim3 grid((unsigned)((N + TILE_ROWS - 1) / TILE_ROWS), (unsigned)((M + TILE_ROWS - 1) / TILE_ROWS));
     if (grid.y > 65535) return sf::fail(SF_EINVAL, err, cap, "bitdelta: M too large");
     bitdelta_task_kernel<T><<<grid, NUM_THREADS, smem, st>>>(mx, (const uint32_t*)bits, (T*)y, (int)M, (int)N, (int)K, scale, stages,
