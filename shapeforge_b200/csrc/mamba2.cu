@@ -11,8 +11,11 @@
 // head, batch); warp w serves the 32 rows (w % 4) * 32 + lane and the 32 columns (w / 4) * 32 + i.  The two chunks are stacked into the 128 rows of one M=128 MMA; every MMA is
 // issued twice with half of the accumulator lanes disabled (tcgen05.mma disable-output-lane), so
 // a row only ever meets its own chunk's operands:
-//   TMA    C, B rows [128 x 64], x rows [128 s x 64 p] and the two state tiles [64 p x 64 n];
-//   MMA    CB = C . B^T (per chunk, TMEM cols [0,64)),  S = C . states^T (cols [64,128));
+//   TMA    C rows [128 x 64], x rows [128 s x 64 p], and per chunk c its B rows [64 s x 64 n] and
+//          its state tile [64 p x 64 n], stacked as one 256-row operand [B0; St0; B1; St1];
+//   MMA    [CB | S] = C . [B0; St0; B1; St1]^T (M=128, N=256, no lane masking): a row of chunk c
+//          reads its CB and S from columns [128c, 128c + 64) and [128c + 64, 128c + 128); the other
+//          chunk's columns are never read, so nothing of it mixes into the row;
 //   rows   w[l,s] = CB[l,s] exp(cs_l - cs_s) dt_s for s <= l else 0, in fp32, written as a
 //          16-bit high part and a 16-bit residual (fp16: after a power-of-two row scale that puts
 //          the row maximum in [2^14, 2^15), so neither overflow nor underflow loses it);
@@ -44,14 +47,13 @@ constexpr int ROWS = 2 * CH;          // two chunks per CTA = M of every MMA
 constexpr int TILE = ROWS * 128;      // 128 rows of 64 16-bit elements (one 128-byte swizzle row each)
 constexpr int HALF = CH * 128;        // 64 such rows
 constexpr int NUM_THREADS = 256;
-constexpr uint32_t TMEM_COLS = 256;   // CB [0,64), S [64,128), Yh [128,192), Yl [192,256)
+constexpr uint32_t TMEM_COLS = 256;   // [CB0 | S0 | CB1 | S1]; Yh then overwrites [0,64), Yl [128,192)
 
 struct Layout {
     static constexpr int CM = 0;            // C rows, K-major over n
-    static constexpr int BM = CM + TILE;    // B rows, K-major over n
-    static constexpr int X = BM + TILE;     // x rows [s][p]: MN-major B operand of W.x
-    static constexpr int ST = X + TILE;     // states [chunk][p][n]: K-major B operand of C.states^T
-    static constexpr int WH = ST + TILE;    // W high part, K-major over s (row l: its own chunk's s)
+    static constexpr int BS = CM + TILE;    // [B0; St0; B1; St1]: 4 x 64 rows, K-major over n
+    static constexpr int X = BS + 2 * TILE; // x rows [s][p]: MN-major B operand of W.x
+    static constexpr int WH = X + TILE;     // W high part, K-major over s (row l: its own chunk's s)
     static constexpr int WL = WH + TILE;    // W residual
     static constexpr int CS = WL + TILE;    // float cs[128] * log2(e)
     static constexpr int DT = CS + 512;     // float dt[128]
@@ -132,12 +134,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         sm100::tma_prefetch_desc(&tbm);
         sm100::tma_prefetch_desc(&tx);
         sm100::tma_prefetch_desc(&tst);
-        sm100::mbar_arrive_expect_tx(&bars->load_full, 3 * TILE + (has1 ? 2 : 1) * HALF);
+        sm100::mbar_arrive_expect_tx(&bars->load_full, 2 * TILE + (has1 ? 4 : 2) * HALF);
         sm100::tma_load_3d(smem + Layout::CM, &tcm, &bars->load_full, 0, t0, b);
-        sm100::tma_load_3d(smem + Layout::BM, &tbm, &bars->load_full, 0, t0, b);
-        sm100::tma_load_2d(smem + Layout::ST, &tst, &bars->load_full, 0, (int)((((int64_t)b * NC + c0) * H + h) * CH));
-        if (has1)
-            sm100::tma_load_2d(smem + Layout::ST + HALF, &tst, &bars->load_full, 0, (int)((((int64_t)b * NC + c0 + 1) * H + h) * CH));
+        for (int c = 0; c < (has1 ? 2 : 1); ++c) {
+            sm100::tma_load_3d(smem + Layout::BS + 2 * c * HALF, &tbm, &bars->load_full, 0, t0 + c * CH, b);
+            sm100::tma_load_2d(smem + Layout::BS + (2 * c + 1) * HALF, &tst, &bars->load_full, 0,
+                               (int)((((int64_t)b * NC + c0 + c) * H + h) * CH));
+        }
         sm100::tma_load_3d(smem + Layout::X, &tx, &bars->load_full, h * CH, t0, b);
     }
     if (warp == 0) {
@@ -163,21 +166,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
     if (tid == 0 && sm100::mbar_wait(&bars->load_full, 0, status, 61)) {
         sm100::tc_fence_after();
-        constexpr uint32_t idesc = sm100::idesc_f16(ROWS, CH, BF16);
+        constexpr uint32_t idesc = sm100::idesc_f16(ROWS, 4 * CH, BF16);
         const uint32_t scm = sm100::smem_u32(smem + Layout::CM);
-        const uint32_t sbm = sm100::smem_u32(smem + Layout::BM);
-        const uint32_t sst = sm100::smem_u32(smem + Layout::ST);
-        for (int q = 0; q < (has1 ? 2 : 1); ++q) {
-            const uint32_t(&mask)[4] = q == 0 ? only0 : only1;
+        const uint32_t sbs = sm100::smem_u32(smem + Layout::BS);
 #pragma unroll
-            for (int k = 0; k < CH / 16; ++k) {
-                const uint64_t ad = sm100::smem_desc_k_sw128(scm + (uint32_t)(k * 32));
-                sm100::mma_f16_lanes(tmem, ad, sm100::smem_desc_k_sw128(sbm + (uint32_t)(q * HALF + k * 32)), idesc, k > 0 ? 1u : 0u,
-                                     mask);
-                sm100::mma_f16_lanes(tmem + 64, ad, sm100::smem_desc_k_sw128(sst + (uint32_t)(q * HALF + k * 32)), idesc,
-                                     k > 0 ? 1u : 0u, mask);
-            }
-        }
+        for (int k = 0; k < CH / 16; ++k)
+            sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(scm + (uint32_t)(k * 32)), sm100::smem_desc_k_sw128(sbs + (uint32_t)(k * 32)), idesc,
+                           k > 0 ? 1u : 0u);
         sm100::mma_commit(&bars->cb_full);
     }
 
@@ -187,7 +182,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     if (ok) {
         sm100::tc_fence_after();
         uint32_t cb[32];
-        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(colh * 32), cb);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(128 * half + colh * 32), cb);
         sm100::tmem_ld_wait();
         const float csl = cs_s[l];
         const float* csc = cs_s + half * CH + colh * 32;
@@ -248,7 +243,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                 for (int k = 0; k < CH / 16; ++k) {
                     const uint64_t ad = sm100::smem_desc_k_sw128(wparts[part] + (uint32_t)(k * 32));
                     const uint64_t bd = sm100::smem_desc_mn_sw128(sx + (uint32_t)(q * HALF + k * 16 * 128), TILE, 1024);
-                    sm100::mma_f16_lanes(tmem + 128 + 64 * part, ad, bd, idesc, k > 0 ? 1u : 0u, mask);
+                    sm100::mma_f16_lanes(tmem + 128 * part, ad, bd, idesc, k > 0 ? 1u : 0u, mask);
                 }
             }
         }
@@ -260,9 +255,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     if (ok) {
         sm100::tc_fence_after();
         uint32_t yh[32], yl[32], sr[32];
-        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (uint32_t)(colh * 32), yh);
-        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 192 + (uint32_t)(colh * 32), yl);
-        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 64 + (uint32_t)(colh * 32), sr);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(colh * 32), yh);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (uint32_t)(colh * 32), yl);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(128 * half + 64 + colh * 32), sr);
         sm100::tmem_ld_wait();
         if (row_ok) {
             const float ecs = exp2f(cs_s[l]);
@@ -344,7 +339,7 @@ int launch_tc(const void* x, const void* dt, const void* cs, const void* bm, con
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     CUtensorMap mc, mb, mx, ms;
     int rc = sf::tmap_3d(&mc, cm, CH, L, B, CH * 2, L * CH * 2, 64, ROWS, 1, bf16, err, cap);
-    if (!rc) rc = sf::tmap_3d(&mb, bm, CH, L, B, CH * 2, L * CH * 2, 64, ROWS, 1, bf16, err, cap);
+    if (!rc) rc = sf::tmap_3d(&mb, bm, CH, L, B, CH * 2, L * CH * 2, 64, CH, 1, bf16, err, cap);
     if (!rc) rc = sf::tmap_3d(&mx, x, H * CH, L, B, H * CH * 2, L * H * CH * 2, 64, ROWS, 1, bf16, err, cap);
     if (!rc) rc = sf::tmap_2d(&ms, states, B * NC * H * CH, CH, CH * 2, 64, CH, 2, bf16, err, cap);
     if (rc) return rc;
