@@ -82,9 +82,9 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, w
             variant: int = 0) -> torch.Tensor:
     """``C = A @ B`` with A ``[M, K]`` and B ``[K, N]`` (tasks/gemm/reference.py:110-114).
 
-    ``workspace`` (uint8, at least ``gemm_nn_workspace_bytes``) lets the tensor-core kernel run on
-    a transposed copy of B; it is allocated here when not given.  Pass ``variant=2`` to force the
-    general kernel without a workspace."""
+    The tensor-core kernel reads B in place when N % 8 == 0; otherwise ``workspace`` (uint8, at
+    least ``gemm_nn_workspace_bytes``, allocated here when not given) receives a transposed copy of
+    B first.  Pass ``variant=2`` to force the general kernel."""
     _check(a, "A")
     _check(b, "B", a.dtype)
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:

@@ -55,7 +55,7 @@ def test_golden_vectors_nn(cuda_device, dtype):
         a = torch.from_numpy(rec["inputs"]["A"].view(np.int16)).view(TD[dtype]).to(cuda_device)
         b = torch.from_numpy(np.ascontiguousarray(rec["inputs"]["B"]).view(np.int16)).view(TD[dtype]).to(cuda_device)
         b = b.contiguous()
-        for variant in (0, 2):  # tensor-core path through the transpose workspace, and the fallback
+        for variant in (0, 2):  # the tensor-core path (B read in place as an MN-major operand), and the fallback
             c = ops.gemm_nn(a, b, variant=variant)
             torch.cuda.synchronize()
             ref = rec["refs"]["C"]
@@ -124,6 +124,23 @@ def test_gemm_nn_task_sizes(cuda_device, dtype):
             ref = oref.gemm_nn(_np(a)[rows], _np(b))
             v = compare.check(_np(c)[rows], ref, compare.rms_scale(ref), dtype=dtype, **TOL[dtype])
             assert v.ok, (case, (m, n, k), v.summary())
+    _status_ok()
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_gemm_nn_direct_and_transposed(cuda_device, dtype):
+    """Both tensor-core routes of the NN layout: N % 8 == 0 reads B [K, N] in place (no workspace:
+    the size query returns 0); N % 8 != 0 transposes B into the caller's workspace first."""
+    for (m, n, k) in [(256, 200, 136), (300, 512, 64), (256, 196, 128), (130, 20, 72)]:
+        need = ops.gemm_nn_workspace_bytes(m, n, k, dtype)
+        assert need == (0 if n % 8 == 0 else n * k * 2)
+        inp = cases.gemm_inputs("normal", cases.case_seed(3, n), (m, k), (k, n), dtype)
+        a, b = inp["A"].to(cuda_device), inp["B"].to(cuda_device)
+        c = ops.gemm_nn(a, b, variant=1)
+        torch.cuda.synchronize()
+        ref = oref.gemm_nn(_np(a), _np(b))
+        v = compare.check(_np(c), ref, compare.rms_scale(ref), dtype=dtype, **TOL[dtype])
+        assert v.ok, ((m, n, k), v.summary())
     _status_ok()
 
 
