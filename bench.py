@@ -504,7 +504,7 @@ def _membound_task_workload(task: str, shape, dtype: str = "fp16", kernel: str =
         nbytes, outs, dims = 3 * el * n_elem, [(tuple(shape), cases.TORCH_DTYPE[dtype])], (n_elem,)
     elif task == "rope":
         nbytes, outs, dims = 2 * el * n_elem, [(tuple(shape), cases.TORCH_DTYPE[dtype])], tuple(shape)
-    elif task in ("silu",):
+    elif task in ("silu", "relu", "sigmoid", "sigmoid_shift"):
         nbytes, outs, dims = 2 * el * n_elem, [(tuple(shape), cases.TORCH_DTYPE[dtype])], (n_elem,)
     else:  # softmax
         m, n = shape
@@ -536,7 +536,8 @@ def _membound_task_workload(task: str, shape, dtype: str = "fp16", kernel: str =
             fn = oref.softmax if task == "softmax" else oref.reduction_sum
             per = (2 * el * k) if task == "softmax" else (el * k + el * rows)
             return (lambda: fn(xr)), float(per), f"fp64 {task} of {rows} rows"
-        return (lambda: oref.silu(x)), 2.0 * el * k, f"fp64 silu of {k} elements"
+        fn = {"silu": oref.silu, "relu": oref.relu, "sigmoid": oref.sigmoid, "sigmoid_shift": oref.sigmoid_shift}[task]
+        return (lambda: fn(x)), 2.0 * el * k, f"fp64 {task} of {k} elements"
 
     label = "x".join(str(v) for v in shape)
     return _op_workload(
@@ -573,6 +574,86 @@ def _gemm_nn_task_workload(m: int = 2048, n: int = 2048, k: int = 2048, dtype: s
         "gemm_nt_tc_kernel", "gemm_nn", make_inputs, ["A", "B"], [((m, n), cases.TORCH_DTYPE[dtype]), ((ws,), torch.uint8)],
         (m, n, k, ws), cpu_rows=cpu_rows, total_rows=m)
     return wl
+
+
+def _lion_task_workload(n: int = 8388608, dtype: str = "fp16") -> Workload:
+    """tasks/lion at its paper size: one optimizer step over N parameters (p, g, m in; p_out, m_out
+    out); units = the opspec's min_bytes, 5 tensors of N 16-bit elements."""
+    from shapeforge_b200 import cases
+
+    el = 2
+    a = cases.LION_DEFAULTS
+
+    def make_inputs(seed):
+        return cases.lion_inputs("normal", seed, n, dtype)
+
+    def cpu_rows(rows):
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        k = rows * 65536
+        p, g, m = (inp[name][:k].double().numpy() for name in ("p", "g", "m"))
+        return (lambda: oref.lion(p, g, m, a["LR"], a["WD"], a["BETA1"], a["BETA2"])), 5.0 * el * k, f"fp64 lion step of {k} elements"
+
+    td = cases.TORCH_DTYPE[dtype]
+    return _op_workload(
+        f"lion_{n}", "GB/s", "hbm", dtype, 5.0 * el * n,
+        {"workload": f"task lion (one Lion step, LR/WD/BETA1/BETA2 = opspec defaults) over N={n} {dtype} parameters, "
+                     "the task's normal-case input stream", "shape": [n]},
+        "lion_kernel", "lion", make_inputs, ["p", "g", "m"], [((n,), td), ((n,), td)], (n,),
+        (a["LR"], a["WD"], a["BETA1"], a["BETA2"]), cpu_rows=cpu_rows, total_rows=max(1, n // 65536))
+
+
+def _gemv_task_workload(m: int = 4096, k: int = 4096, dtype: str = "fp16") -> Workload:
+    """tasks/gemv at its paper size; units = the opspec's min_bytes (A, x, y once)."""
+    from shapeforge_b200 import cases
+
+    el = 2
+
+    def make_inputs(seed):
+        return cases.gemv_inputs("normal", seed, m, k, dtype)
+
+    def cpu_rows(rows):
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        a_np = inp["A"][:rows].double().numpy()
+        x_np = inp["x"].double().numpy()
+        return (lambda: oref.gemv(a_np, x_np)), float(el * (rows * k + k + rows)), f"fp64 gemv of {rows} rows x K={k}"
+
+    return _op_workload(
+        f"gemv_{m}x{k}", "GB/s", "hbm", dtype, float(el * (m * k + k + m)),
+        {"workload": f"task gemv y = A.x, A {dtype} [{m},{k}], the task's normal-case input stream", "shape": [m, k]},
+        "gemv_kernel", "gemv", make_inputs, ["A", "x"], [((m,), cases.TORCH_DTYPE[dtype])], (m, k),
+        cpu_rows=cpu_rows, total_rows=m)
+
+
+def _gemm_silu_task_workload(m: int = 2048, n: int = 2048, k: int = 2048, dtype: str = "fp16") -> Workload:
+    """tasks/gemm_silu (C = silu(A.B), B stored [K, N]) at its paper size; units = the opspec's
+    flops 2*M*N*K + 5*M*N."""
+    import torch
+
+    from shapeforge_b200 import cases
+
+    ws = 2 * n * k
+
+    def make_inputs(seed):
+        return cases.gemm_inputs("normal", seed, (m, k), (k, n), dtype)
+
+    def cpu_rows(rows):
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        a = inp["A"][:rows].double().numpy()
+        b = inp["B"].double().numpy()
+        return (lambda: oref.gemm_silu(a, b)), 2.0 * rows * n * k + 5.0 * rows * n, f"fp64 silu(A[{rows} rows,{k}] . B[{k},{n}])"
+
+    return _op_workload(
+        f"gemm_silu_{m}x{n}x{k}", "TFLOP/s", "tensor", dtype, 2.0 * m * n * k + 5.0 * m * n,
+        {"workload": f"task gemm_silu C=silu(A.B), A {dtype} [{m},{k}], B {dtype} [{k},{n}] read in place as an MN-major "
+                     "operand, SiLU fused into the tensor-core epilogue", "shape": [m, n, k]},
+        "gemm_nt_tc_kernel", "gemm_silu", make_inputs, ["A", "B"], [((m, n), cases.TORCH_DTYPE[dtype]), ((ws,), torch.uint8)],
+        (m, n, k, ws), cpu_rows=cpu_rows, total_rows=m)
 
 
 def _bitdelta_task_workload(m: int = 512, n: int = 4096, k: int = 4096, dtype: str = "fp16", scale: float = 0.02) -> Workload:
@@ -668,6 +749,12 @@ WORKLOADS = {
     "bitdelta_gemm_512x4096x4096": lambda w, r: _bitdelta_task_workload(),
     "attention_full_2x8x1024x64": lambda w, r: _attention_workload(2, 8, 1024, 64, causal=False, dtype="fp16", world=w, rank=r),
     "varlen_kda_h64_mixed": lambda w, r: _kda_task_workload(),
+    "relu_16777216": lambda w, r: _membound_task_workload("relu", (16777216,), kernel="act_kernel"),
+    "sigmoid_16777216": lambda w, r: _membound_task_workload("sigmoid", (16777216,), kernel="act_kernel"),
+    "sigmoid_shift_16777216": lambda w, r: _membound_task_workload("sigmoid_shift", (16777216,), kernel="act_kernel"),
+    "lion_8388608": lambda w, r: _lion_task_workload(),
+    "gemv_4096x4096": lambda w, r: _gemv_task_workload(),
+    "gemm_silu_2048": lambda w, r: _gemm_silu_task_workload(),
 }
 DEFAULT_WORKLOAD = "gemm_nt_4096"
 

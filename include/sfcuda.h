@@ -102,6 +102,32 @@ SF_API int sf_swiglu(const void* gate, const void* up, void* y, int64_t n, int32
                uint64_t cap);
 
 /*
+ * relu: y = max(x, 0), values <= 0 map to +0 and NaN propagates (tasks/relu/reference.py, reference()).
+ * sigmoid: y = 1 / (1 + exp(-x)) (tasks/sigmoid/reference.py, reference()).
+ * sigmoid_shift: y = sigmoid(x) + 1 (tasks/sigmoid_shift/reference.py, reference()).
+ * fp32 arithmetic, one rounding to the F16 / BF16 output.
+ */
+SF_API int sf_relu(const void* x, void* y, int64_t n, int32_t dtype, void* stream, char* err, uint64_t cap);
+SF_API int sf_sigmoid(const void* x, void* y, int64_t n, int32_t dtype, void* stream, char* err, uint64_t cap);
+SF_API int sf_sigmoid_shift(const void* x, void* y, int64_t n, int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
+ * lion: one Lion optimizer step over n elements (tasks/lion/reference.py, reference();
+ * opspec.json formula): c = BETA1*m + (1-BETA1)*g, p_out = p*(1 - LR*WD) - LR*sign(c),
+ * m_out = BETA2*m + (1-BETA2)*g.  Attribute domains LR > 0, WD >= 0, 0 < BETA1, BETA2 < 1
+ * (SF_EINVAL otherwise).  F16 / BF16 tensors, fp32 arithmetic.
+ */
+SF_API int sf_lion(const void* p, const void* g, const void* m, void* p_out, void* m_out, int64_t n, double lr, double wd,
+               double beta1, double beta2, int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
+ * gemv: y[r] = sum_k A[r, k] * x[k], A [M, K] row-major, x [K], y [M] (tasks/gemv/reference.py,
+ * reference()).  fp32 accumulation, F16 / BF16 storage; K == 0 writes +0.
+ */
+SF_API int sf_gemv(const void* A, const void* x, void* y, int64_t M, int64_t K, int32_t dtype, void* stream, char* err,
+               uint64_t cap);
+
+/*
  * softmax over the last axis of x [m, n] (tasks/softmax/reference.py:104-106) and
  * reduction_sum y[m] = sum_j x[m, j] (tasks/reduction_sum/reference.py:104-106); fp32
  * accumulation, F16 / BF16 storage.
@@ -195,6 +221,15 @@ SF_API int sf_gemm_nn(const void* A, const void* B, void* C, int64_t M, int64_t 
                void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap);
 
 /*
+ * gemm_silu: C[M,N] = silu(A[M,K] . B[K,N]), silu(v) = v * sigmoid(v) on the fp32 product
+ * (tasks/gemm_silu/reference.py, reference(); opspec.json formula).  Same layouts, dispatch and
+ * workspace rule as sf_gemm_nn (sf_gemm_nn_workspace_bytes sizes it); the SiLU is the epilogue
+ * of whichever kernel runs.
+ */
+SF_API int sf_gemm_silu(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+               void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap);
+
+/*
  * gemm_nn without any device allocation (no counterpart in the reference).  Same result as
  * sf_gemm_nn with a workspace, for callers that cannot allocate device memory at call time:
  * code running inside a host callback (where CUDA API calls are forbidden), hosts whose device
@@ -250,6 +285,12 @@ SF_API int sf_launch_kernel(void* function, uint32_t gx, uint32_t gy, uint32_t g
 #define SF_OP_KDA 12
 #define SF_OP_KDA_GATED 13
 #define SF_OP_MAMBA2 14
+#define SF_OP_RELU 15
+#define SF_OP_SIGMOID 16
+#define SF_OP_SIGMOID_SHIFT 17
+#define SF_OP_LION 18
+#define SF_OP_GEMV 19
+#define SF_OP_GEMM_SILU 20
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -283,6 +324,10 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *                   args = {q, k, v, g, beta, cu_seqlens, initial_state (may be NULL), output, final_state}
  *   SF_OP_MAMBA2    dims = {B, L, H, P, N, chunk}
  *                   args = {x, dt, dA_cumsum, Bmat, Cmat, Dskip, states, y}
+ *   SF_OP_RELU / SF_OP_SIGMOID / SF_OP_SIGMOID_SHIFT  dims = {n}       args = {x, y}
+ *   SF_OP_LION      dims = {n}   attrs = {LR, WD, BETA1, BETA2}        args = {p, g, m, p_out, m_out}
+ *   SF_OP_GEMV      dims = {M, K}                                      args = {A, x, y}
+ *   SF_OP_GEMM_SILU dims = {M, N, K, ws_bytes}                         args = {A, B, C, ws}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

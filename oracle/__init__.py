@@ -14,7 +14,8 @@ Pinning status per operator (see ``tests/test_oracle_golden.py``):
 
 * pinned by G0 corpus bytes: rmsnorm, softmax, reduction_sum, silu, swiglu, gemm (NN);
 * pinned by reference-module outputs: bitdelta_gemm, flash_attention (non-causal), rope,
-  varlen_kda (and through it the shared delta-rule core used by the gated variant);
+  varlen_kda (and through it the shared delta-rule core used by the gated variant), mamba2,
+  relu, sigmoid, sigmoid_shift, lion (and its ``error_scale`` hook), gemv and gemm_silu;
 * variants that exist only as formulas (gemm_nt, bitdelta_gemm_base, causal attention,
   varlen_kda_gated) reuse a pinned function on transformed inputs (``A @ B^T`` is the pinned
   NN product with ``B^T``; the causal mask is the pinned attention with a mask; the gated KDA

@@ -68,6 +68,68 @@ def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
         return gate * _torch_sigmoid(gate) * up
 
 
+def relu(x: np.ndarray) -> np.ndarray:
+    """tasks/relu/reference.py ``reference``: ``torch.relu`` in fp64 (x > 0 keeps x, NaN stays
+    NaN, everything else is +0)."""
+    return np.where(np.isnan(x), x, np.where(x > 0, x, 0.0))
+
+
+def sigmoid(x: np.ndarray) -> np.ndarray:
+    """tasks/sigmoid/reference.py ``reference``: ``torch.sigmoid`` in fp64."""
+    return _torch_sigmoid(x)
+
+
+def sigmoid_shift(x: np.ndarray) -> np.ndarray:
+    """tasks/sigmoid_shift/reference.py ``reference``: ``sigmoid(x) + 1`` in fp64 (the module then
+    stores fp32; the harness rounds that to the output dtype)."""
+    with _err():
+        return (_torch_sigmoid(x) + 1.0).astype(np.float32).astype(np.float64)
+
+
+def lion(p: np.ndarray, g: np.ndarray, m: np.ndarray, lr: float, wd: float, beta1: float, beta2: float):
+    """tasks/lion/reference.py ``reference``: one fp64 Lion step; returns ``(p_out, m_out)``.
+    ``torch.sign`` maps NaN to 0 (numpy's sign keeps NaN), so a NaN ``c`` leaves ``p`` decayed only."""
+    with _err():
+        c = beta1 * m + (1 - beta1) * g
+        u = np.where(np.isnan(c), 0.0, np.sign(c))
+        return p * (1 - lr * wd) - lr * u, beta2 * m + (1 - beta2) * g
+
+
+# tasks/lion/reference.py module constants of the sign-discontinuity allowance.
+LION_DISCONTINUITY_REL = 1e-05
+LION_ATOL_STEPS = 2.5
+
+
+def lion_error_scale(p, g, m, p_out_ref, m_out_ref, lr: float, beta1: float, atol_rel: float):
+    """tasks/lion/reference.py ``error_scale``: non-finite inputs/outputs count as 0; ``p_out``'s
+    scale is the RMS of its reference, except where ``|a + b| <= 1e-5 (|a| + |b|)``
+    (a = beta1*m, b = (1-beta1)*g: the sign of c is ambiguous at fp32 precision), where it is
+    ``2.5 * lr / atol_rel`` (2.5 learning-rate steps of slack); ``m_out``'s is its RMS."""
+    fin = lambda t: np.where(np.isfinite(t), t, 0.0)  # noqa: E731
+    p, g, m = fin(p), fin(g), fin(m)
+    rp, rm = fin(p_out_ref), fin(m_out_ref)
+    with _err():
+        a, b = beta1 * m, (1 - beta1) * g
+        amb = np.abs(a + b) <= LION_DISCONTINUITY_REL * (np.abs(a) + np.abs(b))
+    base = np.full(rp.shape, np.sqrt(np.mean(rp**2)) if rp.size else 0.0)
+    base[amb] = LION_ATOL_STEPS * lr / atol_rel
+    return base, np.float64(np.sqrt(np.mean(rm**2)) if rm.size else 0.0)
+
+
+def gemv(a: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """tasks/gemv/reference.py ``reference``: ``A @ x`` in fp64."""
+    with _err():
+        return a @ x
+
+
+def gemm_silu(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """tasks/gemm_silu/reference.py ``reference``: ``c = A @ B`` (the reference forms it in fp32;
+    the fp64 product here agrees to fp32 accumulation error), then ``c * sigmoid(c)`` in fp64."""
+    with _err():
+        c = a @ b
+        return c * _torch_sigmoid(c)
+
+
 def rope(x: np.ndarray, base: float) -> np.ndarray:
     """tasks/rope/reference.py:105-115: rotate-half RoPE over ``[..., S, D]``; the position is
     the index along S and ``inv_freq = base ** (-arange(D/2) / (D/2))``."""

@@ -80,6 +80,12 @@ OPS = {
     "varlen_kda": 12,
     "varlen_kda_gated": 13,
     "mamba2_chunk_scan": 14,
+    "relu": 15,
+    "sigmoid": 16,
+    "sigmoid_shift": 17,
+    "lion": 18,
+    "gemv": 19,
+    "gemm_silu": 20,
 }
 
 _P = ctypes.c_void_p
@@ -98,6 +104,12 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_rmsnorm": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_silu": (ctypes.c_int, (_P, _P, _I64, _I32, _P, *_ERR)),
     "sf_swiglu": (ctypes.c_int, (_P, _P, _P, _I64, _I32, _P, *_ERR)),
+    "sf_relu": (ctypes.c_int, (_P, _P, _I64, _I32, _P, *_ERR)),
+    "sf_sigmoid": (ctypes.c_int, (_P, _P, _I64, _I32, _P, *_ERR)),
+    "sf_sigmoid_shift": (ctypes.c_int, (_P, _P, _I64, _I32, _P, *_ERR)),
+    "sf_lion": (ctypes.c_int, (_P, _P, _P, _P, _P, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I32, _P,
+                               *_ERR)),
+    "sf_gemv": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I32, _P, *_ERR)),
     "sf_softmax": (ctypes.c_int, (_P, _P, _I64, _I64, _I32, _P, *_ERR)),
     "sf_reduction_sum": (ctypes.c_int, (_P, _P, _I64, _I64, _I32, _P, *_ERR)),
     "sf_rope": (ctypes.c_int, (_P, _P, _I64, _I64, _I64, _I64, ctypes.c_double, _I32, _P, *_ERR)),
@@ -110,6 +122,7 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_gemm_nn_workspace_bytes": (_U64, (_I64, _I64, _I64, _I32)),
     "sf_gemm_nn": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),
+    "sf_gemm_silu": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, _U64, _P, *_ERR)),
     "sf_gemm_nn_noalloc": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_kernel_status": (ctypes.c_int, (ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), _P, *_ERR)),
     "sf_module_load": (ctypes.c_int, (_P, _U64, ctypes.POINTER(_P), *_ERR)),

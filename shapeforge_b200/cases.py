@@ -159,6 +159,12 @@ MEMBOUND_PARAMS = {
     "silu": ({"normal": 3.0}, 1.0, 10000.0, 100.0),
     "swiglu": ({"normal": 3.0}, 1.0, 200.0, 100.0),
     "rope": ({"normal": 1.0, "wide_range": 1.0}, 1.0, 40000.0, 100.0),
+    # tasks/relu/reference.py and tasks/sigmoid/reference.py (_MAGS, _DEFAULT_MAG, _LARGE, _SPIKE).
+    "relu": ({"normal": 3.0}, 1.0, 10000.0, 100.0),
+    "sigmoid": ({"normal": 3.0}, 1.0, 10000.0, 100.0),
+    # tasks/sigmoid_shift has no gen_inputs of its own (the harness samples it from the opspec);
+    # timing and large-size parity use the sigmoid stream.
+    "sigmoid_shift": ({"normal": 3.0}, 1.0, 10000.0, 100.0),
 }
 MEMBOUND_CASES = {
     "softmax": ("normal", "wide_range", "large", "tiny", "outlier", "const", "ieee"),
@@ -166,6 +172,9 @@ MEMBOUND_CASES = {
     "silu": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
     "swiglu": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
     "rope": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
+    "relu": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
+    "sigmoid": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
+    "sigmoid_shift": ("normal", "wide_range", "large", "tiny", "outlier", "ieee"),
 }
 SWIGLU_UP_SEED_STRIDE = 1000003
 
@@ -186,6 +195,49 @@ def membound_inputs(task: str, case: str, seed: int, shape, dtype: str) -> dict[
     if case == "ieee":
         x = inject(x, seed + IEEE_SEED_STRIDE)
     return {"x": round_to(x, dtype)}
+
+
+# ---- lion / gemv / gemm_silu ------------------------------------------------------------------
+
+LION_CASES = ("normal", "wide_range", "large", "tiny", "outlier", "ieee")
+# tasks/lion/opspec.json attrs defaults.
+LION_DEFAULTS = {"LR": 0.001, "WD": 0.1, "BETA1": 0.9, "BETA2": 0.99}
+
+
+def lion_inputs(case: str, seed: int, n: int, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/lion/reference.py gen_inputs: p, g, m at seed + 7*index (mag 1, large 1000, spike
+    100); the tiny case is scaled by 1000 off fp16; ieee injects specials into each of p, g, m at
+    seed + 104729*(index+1)."""
+    base = "normal" if case == "ieee" else case
+    out = {}
+    for index, name in enumerate(("p", "g", "m")):
+        out[name] = sample(base, (n,), seed + 7 * index, dtype, mag=1.0, large=1000.0)
+    if case == "tiny" and dtype != "fp16":
+        out = {k: v * 1000.0 for k, v in out.items()}
+    if case == "ieee":
+        for index, name in enumerate(("p", "g", "m")):
+            out[name] = inject(out[name], seed + IEEE_SEED_STRIDE * (index + 1))
+    return {k: round_to(v, dtype) for k, v in out.items()}
+
+
+GEMV_CASES = ("normal", "wide_range", "large", "tiny", "outlier", "ieee")
+
+
+def gemv_inputs(case: str, seed: int, m: int, k: int, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/gemv/reference.py gen_inputs: A at seed, x at seed + 31 (mags normal 1 / wide_range
+    0.1, large 20, spike 5); ieee injects specials into A only."""
+    base = "normal" if case == "ieee" else case
+    mag = {"normal": 1.0, "wide_range": 0.1}.get(base, 1.0)
+    a = sample(base, (m, k), seed, dtype, mag=mag, large=20.0, spike=5.0)
+    x = sample(base, (k,), seed + 31, dtype, mag=mag, large=20.0, spike=5.0)
+    if case == "ieee":
+        a = inject(a, seed + IEEE_SEED_STRIDE)
+    return {"A": round_to(a, dtype), "x": round_to(x, dtype)}
+
+
+# tasks/gemm_silu/reference.py gen_inputs draws A and B exactly like tasks/gemm (same seeds offsets,
+# magnitudes, LARGE/SPIKE and ieee injection), so gemm_inputs serves both.
+GEMM_SILU_CASES = GEMM_CASES
 
 
 # ---- bitdelta ---------------------------------------------------------------------------------

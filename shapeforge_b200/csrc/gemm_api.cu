@@ -2,6 +2,7 @@
 //
 //   sf_gemm_nt  C = A . B^T, B stored [N, K]  (the dense-gemm workload's layout)
 //   sf_gemm_nn  C = A . B,   B stored [K, N]  (tasks/gemm/reference.py:110-114)
+//   sf_gemm_silu C = silu(A . B), B stored [K, N] (tasks/gemm_silu/reference.py), same dispatch
 //
 // Dispatch mirrors the reference portfolio's exact one-of-N + fallback rule
 // (tcenv/portfolio/dispatch.py:595-700): the tcgen05 kernel (gemm_tc.cu) serves every shape it
@@ -15,19 +16,19 @@
 #include <algorithm>
 
 bool sf_gemm_nt_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K);
-int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, bool silu,
                          cudaStream_t stream, char* err, uint64_t cap);
 int sf_gemm_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
 bool sf_gemm_nn_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K);
-int sf_gemm_nn_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+int sf_gemm_nn_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, bool silu,
                          cudaStream_t stream, char* err, uint64_t cap);
 
 namespace {
 
 constexpr int FB_BM = 64, FB_BN = 64, FB_BK = 16;
 
-// B_KN = true: B is [K, N] (NN); false: B is [N, K] (NT).
-template <typename T, bool B_KN>
+// B_KN = true: B is [K, N] (NN); false: B is [N, K] (NT).  SILU = true stores acc * sigmoid(acc).
+template <typename T, bool B_KN, bool SILU>
 __global__ void __launch_bounds__(256) gemm_fallback_kernel(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C,
                                                             int64_t M, int64_t N, int64_t K) {
     __shared__ float As[FB_BK][FB_BM + 1];
@@ -77,25 +78,31 @@ __global__ void __launch_bounds__(256) gemm_fallback_kernel(const T* __restrict_
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int64_t gn = n0 + tx + 16 * j;
-            if (gn < N) C[gm * N + gn] = sf::Dt<T>::from_f(acc[i][j]);
+            float v = acc[i][j];
+            if (SILU) v = v * (1.0f / (1.0f + __expf(-v)));
+            if (gn < N) C[gm * N + gn] = sf::Dt<T>::from_f(v);
         }
     }
 }
 
-template <typename T, bool B_KN>
+template <typename T, bool B_KN, bool SILU>
 int launch_fallback_t(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t s, char* err,
                       uint64_t cap) {
     const int64_t gx = (N + FB_BN - 1) / FB_BN, gy = (M + FB_BM - 1) / FB_BM;
     if (gy > 65535) return sf::fail(SF_EINVAL, err, cap, "gemm fallback: M=%lld too large", (long long)M);
-    gemm_fallback_kernel<T, B_KN><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, s>>>((const T*)A, (const T*)B, (T*)C, M, N, K);
+    gemm_fallback_kernel<T, B_KN, SILU><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, s>>>((const T*)A, (const T*)B, (T*)C, M, N, K);
     return sf::check_launch("gemm fallback launch", err, cap);
 }
 
 template <bool B_KN>
-int launch_fallback(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, cudaStream_t s,
-                    char* err, uint64_t cap) {
-    if (dtype == SF_DTYPE_F16) return launch_fallback_t<__half, B_KN>(A, B, C, M, N, K, s, err, cap);
-    if (dtype == SF_DTYPE_BF16) return launch_fallback_t<__nv_bfloat16, B_KN>(A, B, C, M, N, K, s, err, cap);
+int launch_fallback(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, bool silu,
+                    cudaStream_t s, char* err, uint64_t cap) {
+    if (dtype == SF_DTYPE_F16)
+        return silu ? launch_fallback_t<__half, B_KN, true>(A, B, C, M, N, K, s, err, cap)
+                    : launch_fallback_t<__half, B_KN, false>(A, B, C, M, N, K, s, err, cap);
+    if (dtype == SF_DTYPE_BF16)
+        return silu ? launch_fallback_t<__nv_bfloat16, B_KN, true>(A, B, C, M, N, K, s, err, cap)
+                    : launch_fallback_t<__nv_bfloat16, B_KN, false>(A, B, C, M, N, K, s, err, cap);
     return sf::fail(SF_EINVAL, err, cap, "gemm: dtype %d is not fp16/bf16", dtype);
 }
 
@@ -151,35 +158,55 @@ int sf_gemm_nt_launch(const void* A, const void* B, void* C, int64_t M, int64_t 
     if (K == 0) return zero_output(C, M, N, s, err, cap);
     const bool tc = sf_gemm_nt_tc_supported(A, B, C, M, N, K);
     if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "gemm_nt: the tcgen05 variant needs 16-byte aligned bases and K %% 8 == 0");
-    if (tc && variant != 2) return sf_gemm_nt_tc_launch(A, B, C, M, N, K, dtype, s, err, cap);
-    return launch_fallback<false>(A, B, C, M, N, K, dtype, s, err, cap);
+    if (tc && variant != 2) return sf_gemm_nt_tc_launch(A, B, C, M, N, K, dtype, false, s, err, cap);
+    return launch_fallback<false>(A, B, C, M, N, K, dtype, false, s, err, cap);
 }
 
-int sf_gemm_nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
-                      void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap) {
+namespace {
+
+// C = A . B (silu = false) or C = silu(A . B) (silu = true) with B stored [K, N].
+int nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant, bool silu,
+              void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap) {
+    const char* name = silu ? "gemm_silu" : "gemm_nn";
     int rc = check_common(A, B, C, M, N, K, dtype, err, cap);
     if (rc) return rc;
     if (M == 0 || N == 0) return SF_OK;
+    // K == 0: the empty sum is +0 and silu(+0) = +0.
     if (K == 0) return zero_output(C, M, N, s, err, cap);
     const bool direct = sf_gemm_nn_tc_supported(A, B, C, M, N, K);
-    if (direct && variant != 2) return sf_gemm_nn_tc_launch(A, B, C, M, N, K, dtype, s, err, cap);
+    if (direct && variant != 2) return sf_gemm_nn_tc_launch(A, B, C, M, N, K, dtype, silu, s, err, cap);
     const uint64_t need = (uint64_t)K * (uint64_t)N * 2u;
     const bool ws_ok = workspace && workspace_bytes >= need && sf::aligned16(workspace);
     const bool tc = ws_ok && sf_gemm_nt_tc_supported(A, workspace, C, M, N, K);
     if (variant == 1 && !tc)
         return sf::fail(SF_EINVAL, err, cap,
-                        "gemm_nn: the tcgen05 variant needs aligned bases with N %% 8 == 0, or a 16-byte aligned workspace of %llu bytes; "
-                        "and K %% 8 == 0", (unsigned long long)need);
+                        "%s: the tcgen05 variant needs aligned bases with N %% 8 == 0, or a 16-byte aligned workspace of %llu bytes; "
+                        "and K %% 8 == 0", name, (unsigned long long)need);
     if (tc && variant != 2) {
         const int64_t gx = (N + 63) / 64, gy = (K + 63) / 64;
-        if (gy > 65535) return sf::fail(SF_EINVAL, err, cap, "gemm_nn: K=%lld too large for the transpose grid", (long long)K);
+        if (gy > 65535) return sf::fail(SF_EINVAL, err, cap, "%s: K=%lld too large for the transpose grid", name, (long long)K);
         transpose16_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, s>>>((const uint16_t*)B, (uint16_t*)workspace, K, N);
         rc = sf::check_launch("gemm_nn transpose launch", err, cap);
         if (rc) return rc;
-        return sf_gemm_nt_tc_launch(A, workspace, C, M, N, K, dtype, s, err, cap);
+        return sf_gemm_nt_tc_launch(A, workspace, C, M, N, K, dtype, silu, s, err, cap);
     }
-    return launch_fallback<true>(A, B, C, M, N, K, dtype, s, err, cap);
+    return launch_fallback<true>(A, B, C, M, N, K, dtype, silu, s, err, cap);
 }
+
+}  // namespace
+
+int sf_gemm_nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
+                      void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap) {
+    return nn_launch(A, B, C, M, N, K, dtype, variant, false, workspace, workspace_bytes, s, err, cap);
+}
+
+// gemm_silu (tasks/gemm_silu/reference.py): the gemm_nn dispatch with the SiLU epilogue fused
+// into whichever kernel runs (tcgen05 direct, tcgen05 after the workspace transpose, or fallback).
+int sf_gemm_silu_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
+                        void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap) {
+    return nn_launch(A, B, C, M, N, K, dtype, variant, true, workspace, workspace_bytes, s, err, cap);
+}
+
 
 extern "C" int sf_gemm_nt(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, void* stream,
                           char* err, uint64_t cap) {
@@ -197,6 +224,11 @@ extern "C" uint64_t sf_gemm_nn_workspace_bytes(int64_t M, int64_t N, int64_t K, 
 extern "C" int sf_gemm_nn(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, void* workspace,
                           uint64_t workspace_bytes, void* stream, char* err, uint64_t cap) {
     return sf_gemm_nn_launch(A, B, C, M, N, K, dtype, 0, workspace, workspace_bytes, (cudaStream_t)stream, err, cap);
+}
+
+extern "C" int sf_gemm_silu(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, void* workspace,
+                            uint64_t workspace_bytes, void* stream, char* err, uint64_t cap) {
+    return sf_gemm_silu_launch(A, B, C, M, N, K, dtype, 0, workspace, workspace_bytes, (cudaStream_t)stream, err, cap);
 }
 
 extern "C" int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, char* err, uint64_t cap) {

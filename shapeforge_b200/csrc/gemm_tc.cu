@@ -7,6 +7,8 @@
 // [K, N]; the same kernel reads that layout directly as an MN-major B operand (BMN = true): each
 // K-block of B arrives as 64 x 64 TMA boxes (64 N columns of 128 bytes for 64 K rows) and the
 // MMA's B descriptor walks 16 K rows (2 KB) per instruction with 8 KB between 64-column blocks.
+// With SILU = true the epilogue stores silu(acc) = acc * sigmoid(acc) instead: the gemm_silu task
+// (tasks/gemm_silu/reference.py), fused at no extra memory traffic.
 //
 // Persistent, warp-specialised kernel, one CTA per SM (192 KB of pipeline shared memory):
 //   warp 0      TMA producer: 128x64 A box + 256x64 B box per K-block, 128-byte swizzle,
@@ -96,7 +98,11 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <typename T, bool BMN>
+// SiLU epilogue of gemm_silu: v * sigmoid(v) in fp32 on the accumulator (tasks/gemm_silu/reference.py
+// applies it to the fp32 product); v = -inf gives -inf * 0 = NaN as in the fp64 reference.
+__device__ __forceinline__ float silu_f(float v) { return v * (1.0f / (1.0f + __expf(-v))); }
+
+template <typename T, bool BMN, bool SILU>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_nt_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_bh, T* __restrict__ C, int M, int N, int K, int full_units,
@@ -248,6 +254,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(t_base + (uint32_t)c, r);
                 sm100::tmem_ld_wait();
+                if (SILU) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(silu_f(__uint_as_float(r[j])));
+                }
                 const int col0 = col_base + c;
                 if (row < M) {
                     T* dst = C + (size_t)row * (size_t)N + col0;
@@ -283,7 +293,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---- host side ----------------------------------------------------------------------------------
 
-template <typename T, bool BMN>
+template <typename T, bool BMN, bool SILU>
 int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream, char* err,
               uint64_t cap) {
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -306,7 +316,7 @@ int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
         return sf::fail(SF_EDEVICE, err, cap, "gemm: cannot resolve the status word");
     static std::atomic<uint64_t> attr_done{0};
     if (sf::once_per_device(attr_done))
-        cudaFuncSetAttribute(gemm_nt_tc_kernel<T, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaFuncSetAttribute(gemm_nt_tc_kernel<T, BMN, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int64_t sms = std::max(1, sf::sm_count());
     // Tiles left over after the last full round of the persistent CTAs are split into halves when
@@ -319,7 +329,7 @@ int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     }
     if (total_units > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "gemm: too many tiles");
     const int grid = (int)std::min<int64_t>(total_units, sms);
-    gemm_nt_tc_kernel<T, BMN><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, mbh, (T*)C, (int)M, (int)N, (int)K, (int)full_units,
+    gemm_nt_tc_kernel<T, BMN, SILU><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, mbh, (T*)C, (int)M, (int)N, (int)K, (int)full_units,
                                                                          (int)total_units, st);
     return sf::check_launch("gemm_nt tcgen05 launch", err, cap);
 }
@@ -333,10 +343,15 @@ bool sf_gemm_nt_tc_supported(const void* A, const void* B, const void* C, int64_
            M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31);
 }
 
-int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+// silu = true applies the gemm_silu epilogue to the accumulator before the store.
+int sf_gemm_nt_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, bool silu,
                          cudaStream_t stream, char* err, uint64_t cap) {
-    if (dtype == SF_DTYPE_F16) return launch_tc<__half, false>(A, B, C, M, N, K, stream, err, cap);
-    if (dtype == SF_DTYPE_BF16) return launch_tc<__nv_bfloat16, false>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_F16)
+        return silu ? launch_tc<__half, false, true>(A, B, C, M, N, K, stream, err, cap)
+                    : launch_tc<__half, false, false>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_BF16)
+        return silu ? launch_tc<__nv_bfloat16, false, true>(A, B, C, M, N, K, stream, err, cap)
+                    : launch_tc<__nv_bfloat16, false, false>(A, B, C, M, N, K, stream, err, cap);
     return sf::fail(SF_EINVAL, err, cap, "gemm: dtype %d is not fp16/bf16", dtype);
 }
 
@@ -346,10 +361,14 @@ bool sf_gemm_nn_tc_supported(const void* A, const void* B, const void* C, int64_
     return sf_gemm_nt_tc_supported(A, B, C, M, N, K) && (N % 8) == 0;
 }
 
-int sf_gemm_nn_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
+int sf_gemm_nn_tc_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, bool silu,
                          cudaStream_t stream, char* err, uint64_t cap) {
-    if (dtype == SF_DTYPE_F16) return launch_tc<__half, true>(A, B, C, M, N, K, stream, err, cap);
-    if (dtype == SF_DTYPE_BF16) return launch_tc<__nv_bfloat16, true>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_F16)
+        return silu ? launch_tc<__half, true, true>(A, B, C, M, N, K, stream, err, cap)
+                    : launch_tc<__half, true, false>(A, B, C, M, N, K, stream, err, cap);
+    if (dtype == SF_DTYPE_BF16)
+        return silu ? launch_tc<__nv_bfloat16, true, true>(A, B, C, M, N, K, stream, err, cap)
+                    : launch_tc<__nv_bfloat16, true, false>(A, B, C, M, N, K, stream, err, cap);
     return sf::fail(SF_EINVAL, err, cap, "gemm: dtype %d is not fp16/bf16", dtype);
 }
 

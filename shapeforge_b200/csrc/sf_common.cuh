@@ -96,6 +96,16 @@ int sf_gemm_nn_launch(const void* A, const void* B, void* C, int64_t M, int64_t 
 int sf_silu_launch(const void* x, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err, uint64_t cap);
 int sf_swiglu_launch(const void* gate, const void* up, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s,
                      char* err, uint64_t cap);
+int sf_relu_launch(const void* x, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err, uint64_t cap);
+int sf_sigmoid_launch(const void* x, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err, uint64_t cap);
+int sf_sigmoid_shift_launch(const void* x, void* y, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err,
+                            uint64_t cap);
+int sf_lion_launch(const void* p, const void* g, const void* m, void* p_out, void* m_out, int64_t n, double lr, double wd,
+                   double beta1, double beta2, int32_t dtype, int32_t variant, cudaStream_t s, char* err, uint64_t cap);
+int sf_gemv_launch(const void* A, const void* x, void* y, int64_t M, int64_t K, int32_t dtype, int32_t variant, cudaStream_t s,
+                   char* err, uint64_t cap);
+int sf_gemm_silu_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype, int32_t variant,
+                        void* workspace, uint64_t workspace_bytes, cudaStream_t s, char* err, uint64_t cap);
 int sf_softmax_launch(const void* x, void* y, int64_t m, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s, char* err,
                       uint64_t cap);
 int sf_reduction_sum_launch(const void* x, void* y, int64_t m, int64_t n, int32_t dtype, int32_t variant, cudaStream_t s,

@@ -120,6 +120,12 @@ extern "C" int32_t sf_op_nargs(int32_t op) {
         case SF_OP_KDA: return 12;
         case SF_OP_KDA_GATED: return 9;
         case SF_OP_MAMBA2: return 8;
+        case SF_OP_RELU: return 2;
+        case SF_OP_SIGMOID: return 2;
+        case SF_OP_SIGMOID_SHIFT: return 2;
+        case SF_OP_LION: return 5;
+        case SF_OP_GEMV: return 3;
+        case SF_OP_GEMM_SILU: return 4;
         default: return 0;
     }
 }
@@ -163,6 +169,20 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
         case SF_OP_MAMBA2:
             return sf_mamba2_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], (void*)a[7], d->dims[0], d->dims[1], d->dims[2], d->dims[3],
                                     d->dims[4], d->dims[5], d->dtype, d->variant, s, err, cap);
+        case SF_OP_RELU:
+            return sf_relu_launch(a[0], (void*)a[1], d->dims[0], d->dtype, d->variant, s, err, cap);
+        case SF_OP_SIGMOID:
+            return sf_sigmoid_launch(a[0], (void*)a[1], d->dims[0], d->dtype, d->variant, s, err, cap);
+        case SF_OP_SIGMOID_SHIFT:
+            return sf_sigmoid_shift_launch(a[0], (void*)a[1], d->dims[0], d->dtype, d->variant, s, err, cap);
+        case SF_OP_LION:
+            return sf_lion_launch(a[0], a[1], a[2], (void*)a[3], (void*)a[4], d->dims[0], d->attrs[0], d->attrs[1], d->attrs[2],
+                                  d->attrs[3], d->dtype, d->variant, s, err, cap);
+        case SF_OP_GEMV:
+            return sf_gemv_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dtype, d->variant, s, err, cap);
+        case SF_OP_GEMM_SILU:
+            return sf_gemm_silu_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dims[2], d->dtype, d->variant, (void*)a[3],
+                                       (uint64_t)d->dims[3], s, err, cap);
         default:
             return sf::fail(SF_EINVAL, err, cap, "unknown op %d", d->op);
     }

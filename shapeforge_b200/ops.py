@@ -85,10 +85,22 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, w
     The tensor-core kernel reads B in place when N % 8 == 0; otherwise ``workspace`` (uint8, at
     least ``gemm_nn_workspace_bytes``, allocated here when not given) receives a transposed copy of
     B first.  Pass ``variant=2`` to force the general kernel."""
+    return _gemm_kn("gemm_nn", a, b, out, workspace, variant)
+
+
+def gemm_silu(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+              variant: int = 0) -> torch.Tensor:
+    """``C = silu(A @ B)``, silu(v) = v * sigmoid(v) on the fp32 product (tasks/gemm_silu/reference.py,
+    ``reference``).  Layouts, workspace and variants as :func:`gemm_nn`; the SiLU is fused into the
+    GEMM's epilogue."""
+    return _gemm_kn("gemm_silu", a, b, out, workspace, variant)
+
+
+def _gemm_kn(op: str, a: torch.Tensor, b: torch.Tensor, out, workspace, variant: int) -> torch.Tensor:
     _check(a, "A")
     _check(b, "B", a.dtype)
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
-        raise ValueError(f"gemm_nn needs A [M,K] and B [K,N], got {tuple(a.shape)} and {tuple(b.shape)}")
+        raise ValueError(f"{op} needs A [M,K] and B [K,N], got {tuple(a.shape)} and {tuple(b.shape)}")
     m, k = a.shape
     n = b.shape[1]
     if out is None:
@@ -99,7 +111,7 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, w
         workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
     ws_ptr = workspace.data_ptr() if workspace is not None else 0
     ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
-    desc = _native.op_desc("gemm_nn", dtype_name(a), dims=(m, n, k, ws_bytes), variant=variant)
+    desc = _native.op_desc(op, dtype_name(a), dims=(m, n, k, ws_bytes), variant=variant)
     _native.run_op(desc, [a.data_ptr(), b.data_ptr(), out.data_ptr(), ws_ptr], _stream(a))
     return out
 
@@ -137,6 +149,64 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None
     out = torch.empty_like(gate) if out is None else out
     _check(out, "out", gate.dtype)
     _run("swiglu", gate, [gate.data_ptr(), up.data_ptr(), out.data_ptr()], dims=(gate.numel(),), variant=variant)
+    return out
+
+
+def _unary(op: str, x: torch.Tensor, out: torch.Tensor | None, variant: int) -> torch.Tensor:
+    _check(x, "x")
+    out = torch.empty_like(x) if out is None else out
+    _check(out, "out", x.dtype)
+    if out.numel() != x.numel():
+        raise ValueError(f"{op}: out has {out.numel()} elements, x has {x.numel()}")
+    _run(op, x, [x.data_ptr(), out.data_ptr()], dims=(x.numel(),), variant=variant)
+    return out
+
+
+def relu(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y = max(x, 0)``; values <= 0 map to +0 and NaN propagates (tasks/relu/reference.py, ``reference``)."""
+    return _unary("relu", x, out, variant)
+
+
+def sigmoid(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y = 1 / (1 + exp(-x))`` (tasks/sigmoid/reference.py, ``reference``)."""
+    return _unary("sigmoid", x, out, variant)
+
+
+def sigmoid_shift(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y = sigmoid(x) + 1`` (tasks/sigmoid_shift/reference.py, ``reference``)."""
+    return _unary("sigmoid_shift", x, out, variant)
+
+
+def lion(p: torch.Tensor, g: torch.Tensor, m: torch.Tensor, lr: float = 1e-3, wd: float = 0.1, beta1: float = 0.9,
+         beta2: float = 0.99, p_out: torch.Tensor | None = None, m_out: torch.Tensor | None = None,
+         variant: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """One Lion step (tasks/lion/reference.py, ``reference``; defaults from tasks/lion/opspec.json attrs):
+    ``c = beta1*m + (1-beta1)*g``, ``p_out = p*(1 - lr*wd) - lr*sign(c)``, ``m_out = beta2*m + (1-beta2)*g``.
+    Returns ``(p_out, m_out)``."""
+    _check(p, "p")
+    _check(g, "g", p.dtype)
+    _check(m, "m", p.dtype)
+    if g.numel() != p.numel() or m.numel() != p.numel():
+        raise ValueError("p, g and m must have the same number of elements")
+    p_out = torch.empty_like(p) if p_out is None else p_out
+    m_out = torch.empty_like(p) if m_out is None else m_out
+    _check(p_out, "p_out", p.dtype)
+    _check(m_out, "m_out", p.dtype)
+    _run("lion", p, [p.data_ptr(), g.data_ptr(), m.data_ptr(), p_out.data_ptr(), m_out.data_ptr()], dims=(p.numel(),),
+         attrs=(float(lr), float(wd), float(beta1), float(beta2)), variant=variant)
+    return p_out, m_out
+
+
+def gemv(a: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """``y[r] = sum_k A[r, k] * x[k]`` with A ``[M, K]`` row-major (tasks/gemv/reference.py, ``reference``)."""
+    _check(a, "A")
+    _check(x, "x", a.dtype)
+    if a.dim() != 2 or x.numel() != a.shape[1]:
+        raise ValueError(f"gemv needs A [M,K] and x [K], got {tuple(a.shape)} and {tuple(x.shape)}")
+    m, k = a.shape
+    out = torch.empty((m,), dtype=a.dtype, device=a.device) if out is None else out
+    _check(out, "out", a.dtype)
+    _run("gemv", a, [a.data_ptr(), x.data_ptr(), out.data_ptr()], dims=(m, k), variant=variant)
     return out
 
 

