@@ -656,6 +656,43 @@ def _gemm_silu_task_workload(m: int = 2048, n: int = 2048, k: int = 2048, dtype:
         (m, n, k, ws), cpu_rows=cpu_rows, total_rows=m)
 
 
+def _kda_fixed_task_workload(n: int = 256, h: int = 8, d: int = 64, dtype: str = "fp16") -> Workload:
+    """tasks/kda (fixed length, one sequence) at its paper size; units = the opspec's min_bytes:
+    q, k, v, g and output (N*H*D each, 16-bit) plus initial_state and final_state (H*D*D fp32)."""
+    import torch
+
+    from shapeforge_b200 import cases
+
+    el = 2
+    nbytes = 5.0 * el * n * h * d + 2.0 * 4 * h * d * d
+    td = cases.TORCH_DTYPE[dtype]
+
+    def make_inputs(seed):
+        return cases.kda_fixed_inputs("normal", seed, n, h, d, dtype)
+
+    def cpu_rows(rows):
+        # The oracle on the first `rows` heads (heads are independent chains).
+        from oracle import ops as oref
+
+        inp = make_inputs(cases.SEARCH_SEED)
+        f = lambda k: inp[k].double().numpy()  # noqa: E731
+        q, k, v, g, b = (f(x)[:, :rows] for x in ("q", "k", "v", "g", "beta"))
+        a_log = f("A_log")[:rows]
+        dt_bias = f("dt_bias").reshape(h, d)[:rows].reshape(-1)
+        s0 = f("initial_state")[:rows]
+        sc = float(f("scale")[0])
+        units = nbytes * rows / h
+        return (lambda: oref.kda_fixed(q, k, v, g, b, a_log, dt_bias, s0, sc, -5.0)), units, f"fp64 kda of {rows} heads x {n} tokens"
+
+    return _op_workload(
+        f"kda_fixed_{n}x{h}x{d}", "GB/s", "hbm", dtype, nbytes,
+        {"workload": f"task kda (fixed length, one sequence) N={n} H={h} D={d} {dtype}, LOWER_BOUND -5, the task's normal-case "
+                     "input stream", "shape": [n, h, d]},
+        "kda_fwd_kernel", "kda", make_inputs, ["q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "scale"],
+        [((n, h, d), td), ((h, d, d), torch.float32), ((3, 2), torch.int32), ((1,), torch.int32), ((2, h, d, d), torch.float32)],
+        (n, h, d), (-5.0,), cpu_rows=cpu_rows, total_rows=h)
+
+
 def _bitdelta_task_workload(m: int = 512, n: int = 4096, k: int = 4096, dtype: str = "fp16", scale: float = 0.02) -> Workload:
     """tasks/bitdelta_gemm (y = SCALE x.W, W +-1 from bits [K/32, N]) at its paper size."""
     from shapeforge_b200 import cases
@@ -755,6 +792,7 @@ WORKLOADS = {
     "lion_8388608": lambda w, r: _lion_task_workload(),
     "gemv_4096x4096": lambda w, r: _gemv_task_workload(),
     "gemm_silu_2048": lambda w, r: _gemm_silu_task_workload(),
+    "kda_fixed_256x8x64": lambda w, r: _kda_fixed_task_workload(),
 }
 DEFAULT_WORKLOAD = "gemm_nt_4096"
 

@@ -180,6 +180,21 @@ SF_API int sf_varlen_kda(const void* q, const void* k, const void* v, const void
                char* err, uint64_t cap);
 
 /*
+ * kda: fixed-length Kimi Delta Attention forward (tasks/kda/reference.py reference(); opspec.json
+ * formula): the varlen_kda recurrence over ONE sequence of N tokens, without cu_seqlens.
+ * q, k, v, g [N, H, D] and beta [N, H] in dtype; A_log [H], dt_bias [H*D], scale [1] fp32;
+ * initial_state and final_state [H, D, D] fp32 (V-first); lower_bound is the LOWER_BOUND attr.
+ * The candidate-owned outputs of the task's host program: work_items [3, 2] u32 receives the
+ * work list ((0, N) then two empty (N, 0) items), item_counts [1] i32 receives 1, and
+ * handoff_states [2, H, D, D] fp32 (piece-boundary states) is not written, one piece having no
+ * boundary.  D in {8, 16, 32, 64, 128}; work_items 4-byte aligned.
+ */
+SF_API int sf_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+               const void* dt_bias, const void* initial_state, const void* scale, void* output, void* final_state,
+               void* work_items, void* item_counts, void* handoff_states, int64_t N, int64_t H, int64_t D, float lower_bound,
+               int32_t dtype, void* stream, char* err, uint64_t cap);
+
+/*
  * varlen_kda_gated (the gated workload): same recurrence with q, k already L2-normalised, g the
  * fp32 log-decay [T, H, D] used directly, beta the fp32 gate [T, H] used directly, q times
  * `scale`, state starting at zero when initial_state is NULL.
@@ -291,6 +306,7 @@ SF_API int sf_launch_kernel(void* function, uint32_t gx, uint32_t gy, uint32_t g
 #define SF_OP_LION 18
 #define SF_OP_GEMV 19
 #define SF_OP_GEMM_SILU 20
+#define SF_OP_KDA_FIXED 21
 
 typedef struct sf_op_desc {
     int32_t op;       /* SF_OP_* */
@@ -328,6 +344,9 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_LION      dims = {n}   attrs = {LR, WD, BETA1, BETA2}        args = {p, g, m, p_out, m_out}
  *   SF_OP_GEMV      dims = {M, K}                                      args = {A, x, y}
  *   SF_OP_GEMM_SILU dims = {M, N, K, ws_bytes}                         args = {A, B, C, ws}
+ *   SF_OP_KDA_FIXED dims = {N, H, D}  attrs = {lower_bound}
+ *                   args = {q, k, v, g, beta, A_log, dt_bias, initial_state, scale, output, final_state,
+ *                           work_items, item_counts, handoff_states}
  * desc->variant: 0 = exact dispatch with fallback, 1 = force the specialised (tensor-core /
  * vectorised) kernel, 2 = force the general fallback kernel.
  */

@@ -243,6 +243,15 @@ def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scal
     return delta_rule(qn, kn, v, ld, b, initial_state, cu_seqlens)
 
 
+def kda_fixed(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound):
+    """tasks/kda/reference.py ``reference``: the same per-token recurrence as :func:`varlen_kda`
+    (normalisation, gated decay, delta residual, V-first state) over one sequence of all N tokens
+    from ``initial_state [H, D, D]``; returns ``(output [N,H,D], final_state [H,D,D])``."""
+    n = q.shape[0]
+    out, fin = varlen_kda(q, k, v, g, beta, a_log, dt_bias, np.asarray(initial_state)[None], np.array([0, n]), scale, lower_bound)
+    return out, fin[0]
+
+
 def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale, state0=None):
     """Gated variant: q/k already L2-normalised, ``g`` is the fp32 per-channel log-decay used
     directly, ``beta`` is already sigmoided, the initial state is zero unless given; q is

@@ -86,6 +86,7 @@ OPS = {
     "lion": 18,
     "gemv": 19,
     "gemm_silu": 20,
+    "kda": 21,
 }
 
 _P = ctypes.c_void_p
@@ -117,6 +118,7 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_bitdelta_gemm_base": (ctypes.c_int, (_P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),
     "sf_flash_attention": (ctypes.c_int, (_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _I32, _I32, _P, *_ERR)),
     "sf_varlen_kda": (ctypes.c_int, (_P,) * 12 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
+    "sf_kda": (ctypes.c_int, (_P,) * 14 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_varlen_kda_gated": (ctypes.c_int, (_P,) * 9 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_mamba2_chunk_scan": (ctypes.c_int, (_P,) * 8 + (_I64,) * 6 + (_I32, _P, *_ERR)),
     "sf_gemm_nt": (ctypes.c_int, (_P, _P, _P, _I64, _I64, _I64, _I32, _P, *_ERR)),

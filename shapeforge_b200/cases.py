@@ -240,6 +240,48 @@ def gemv_inputs(case: str, seed: int, m: int, k: int, dtype: str) -> dict[str, t
 GEMM_SILU_CASES = GEMM_CASES
 
 
+# ---- kda (fixed length) ------------------------------------------------------------------------
+
+KDA_FIXED_CASES = ("normal", "wide_range", "outlier")
+
+
+def _kda_fixed_sample(case: str, shape, g: torch.Generator) -> torch.Tensor:
+    if case == "normal":
+        return torch.randn(shape, generator=g) * 0.5
+    if case == "wide_range":
+        exponent = torch.rand(shape, generator=g) * 4.0 - 2.0
+        sign = torch.where(torch.rand(shape, generator=g) < 0.5, -1.0, 1.0)
+        return sign * torch.pow(10.0, exponent) * 0.25
+    if case == "outlier":
+        values = torch.randn(shape, generator=g) * 0.5
+        mask = torch.rand(shape, generator=g) < 0.01
+        return torch.where(mask, values * 5.0, values)
+    raise ValueError(f"unknown fixed KDA case {case!r}")
+
+
+def kda_fixed_inputs(case: str, seed: int, n: int, heads: int, dim: int, dtype: str) -> dict[str, torch.Tensor]:
+    """tasks/kda/reference.py gen_inputs: one generator at ``seed`` drawn in order A_log =
+    log U(1, 16) [H]; dt = exp(U(log 1e-3, log 0.1)) clamped >= 1e-4 [H*D] and dt_bias = dt +
+    log(-expm1(-dt)); q, k, v, g [N,H,D] and beta [N,H] from the case sampler; initial_state =
+    0.25 N(0,1) [H,D,D] plus 0.5 on the diagonal; scale = 1/sqrt(D).  q..beta rounded to dtype,
+    the rest fp32."""
+    g = torch.Generator().manual_seed(int(seed))
+    a_log = torch.log(torch.empty(heads).uniform_(1.0, 16.0, generator=g))
+    dt = torch.exp(
+        torch.rand(heads * dim, generator=g) * (torch.log(torch.tensor(0.1)) - torch.log(torch.tensor(0.001)))
+        + torch.log(torch.tensor(0.001))
+    ).clamp_(min=1e-4)
+    dt_bias = dt + torch.log(-torch.expm1(-dt))
+    q, k, v, gg = (_kda_fixed_sample(case, (n, heads, dim), g) for _ in range(4))
+    beta = _kda_fixed_sample(case, (n, heads), g)
+    state0 = torch.randn((heads, dim, dim), generator=g) * 0.25
+    state0.diagonal(dim1=-2, dim2=-1).add_(0.5)
+    out = {name: round_to(t, dtype) for name, t in (("q", q), ("k", k), ("v", v), ("g", gg), ("beta", beta))}
+    out.update({"A_log": a_log.float(), "dt_bias": dt_bias.float(), "initial_state": state0.float(),
+                "scale": torch.tensor([1.0 / (dim ** 0.5)], dtype=torch.float32)})
+    return out
+
+
 # ---- bitdelta ---------------------------------------------------------------------------------
 
 BITDELTA_CASES = ("random", "edge_bits", "large", "tiny", "outlier", "ieee")

@@ -9,16 +9,18 @@
 //                                                 tasks/lion/reference.py (reference())
 //
 // HBM-bound (2 to 5 streams of 16-bit elements, a handful of flops each).  A grid-stride loop of
-// 16-byte vector loads/stores over a grid of 8 CTAs per SM; the element tail and unaligned bases
-// take a scalar loop.  sigmoid is evaluated in fp32 as 1 / (1 + exp(-x)), which maps +-Inf and NaN
-// the way the fp64 reference does (sigmoid(-inf) = 0, so silu(-inf) = -inf * 0 = NaN).
+// 16-byte vector loads/stores over one wave of CTAs (SMs x the CTAs that fit on an SM, from the
+// occupancy calculator: a second, partial wave of a grid-stride grid leaves most SMs idle at the
+// end); the element tail and unaligned bases take a scalar loop.  sigmoid is evaluated in fp32 by sf::sigmoid_nr (one exp and a branch-free
+// Newton reciprocal: the IEEE division's second MUFU op made these kernels issue-bound), which maps
+// +-Inf and NaN the way the fp64 reference does (sigmoid(-inf) = 0, so silu(-inf) = -inf * 0 = NaN).
 #include "sf_common.cuh"
 
 namespace {
 
 enum Act : int { SILU = 0, SWIGLU = 1, RELU = 2, SIGMOID = 3, SIGMOID_SHIFT = 4 };
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return sf::sigmoid_nr(x); }
 
 template <int A>
 __device__ __forceinline__ float act(float x, float up) {
@@ -28,6 +30,18 @@ __device__ __forceinline__ float act(float x, float up) {
     if (A == RELU) return x > 0.f ? x : (x != x ? x : 0.f);
     if (A == SIGMOID) return sigmoidf_(x);
     return sigmoidf_(x) + 1.0f;
+}
+
+// The same on a pair of values with packed fp32 arithmetic (the vector loop's form: these kernels
+// are instruction-issue bound once the sigmoid is in, not HBM bound).
+template <int A>
+__device__ __forceinline__ float2 act2(float2 x, float2 up) {
+    if (A == RELU) return make_float2(act<RELU>(x.x, 0.f), act<RELU>(x.y, 0.f));
+    const float2 s = sf::sigmoid2_nr(x);
+    if (A == SILU) return sf::f2_mul(x, s);
+    if (A == SWIGLU) return sf::f2_mul(sf::f2_mul(x, s), up);
+    if (A == SIGMOID) return s;
+    return sf::f2_add(s, sf::f2(1.0f));
 }
 
 constexpr const char* act_name(int a) {
@@ -45,11 +59,12 @@ __global__ void __launch_bounds__(256) act_kernel(const T* __restrict__ x, const
         const int64_t nv = n >> 3;
         auto apply = [&](const sf::Vec8<T>& a, const sf::Vec8<T>& u, int64_t i) {
             sf::Vec8<T> o;
+            const uint32_t* aw = reinterpret_cast<const uint32_t*>(&a);
+            const uint32_t* uw = reinterpret_cast<const uint32_t*>(&u);
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float f = sf::Dt<T>::to_f(a.v[j]);
-                o.v[j] = sf::Dt<T>::from_f(act<A>(f, GLU ? sf::Dt<T>::to_f(u.v[j]) : 0.f));
-            }
+            for (int j = 0; j < 4; ++j)
+                ow[j] = sf::Pair<T>::from_f2(act2<A>(sf::Pair<T>::to_f2(aw[j]), GLU ? sf::Pair<T>::to_f2(uw[j]) : sf::f2(0.f)));
             sf::st_global_v8<T>(y + i * 8, o);
         };
         // Unary operators: two independent vectors per thread and step, so twice the bytes are in
@@ -75,9 +90,10 @@ __global__ void __launch_bounds__(256) act_kernel(const T* __restrict__ x, const
     }
 }
 
-int64_t grid_for(int64_t work) {
+// One wave of grid-stride CTAs: at most SMs x the CTAs of this kernel that fit on an SM.
+int64_t grid_for(int64_t work, int resident) {
     int64_t blocks = (work + 255) / 256;
-    const int64_t cap_blocks = (int64_t)sf::sm_count() * 8;
+    const int64_t cap_blocks = (int64_t)sf::sm_count() * resident;
     if (blocks > cap_blocks) blocks = cap_blocks;
     return blocks < 1 ? 1 : blocks;
 }
@@ -85,7 +101,8 @@ int64_t grid_for(int64_t work) {
 template <typename T, int A>
 int launch_t(const void* x, const void* up, void* y, int64_t n, int32_t variant, cudaStream_t s, char* err, uint64_t cap) {
     const bool vec = variant != 2 && sf::aligned16(x) && sf::aligned16(y) && (A != SWIGLU || sf::aligned16(up));
-    const int64_t blocks = grid_for(vec ? (n + 7) / 8 : n);
+    static const int resident = sf::resident_ctas(act_kernel<T, A>, 256, 0);
+    const int64_t blocks = grid_for(vec ? (n + 7) / 8 : n, resident);
     act_kernel<T, A><<<(unsigned)blocks, 256, 0, s>>>((const T*)x, (const T*)up, (T*)y, n, vec);
     return sf::check_launch(act_name(A), err, cap);
 }
@@ -151,7 +168,8 @@ int lion_t(const void* p, const void* g, const void* m, void* p_out, void* m_out
            cudaStream_t s, char* err, uint64_t cap) {
     const bool vec = variant != 2 && sf::aligned16(p) && sf::aligned16(g) && sf::aligned16(m) && sf::aligned16(p_out) &&
                      sf::aligned16(m_out);
-    const int64_t blocks = grid_for(vec ? (n + 7) / 8 : n);
+    static const int resident = sf::resident_ctas(lion_kernel<T>, 256, 0);
+    const int64_t blocks = grid_for(vec ? (n + 7) / 8 : n, resident);
     lion_kernel<T><<<(unsigned)blocks, 256, 0, s>>>((const T*)p, (const T*)g, (const T*)m, (T*)p_out, (T*)m_out, n, k, vec);
     return sf::check_launch("lion launch", err, cap);
 }

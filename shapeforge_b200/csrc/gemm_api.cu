@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(256) gemm_fallback_kernel(const T* __restrict_
         for (int j = 0; j < 4; ++j) {
             const int64_t gn = n0 + tx + 16 * j;
             float v = acc[i][j];
-            if (SILU) v = v * (1.0f / (1.0f + __expf(-v)));
+            if (SILU) v = v * sf::sigmoid_nr(v);
             if (gn < N) C[gm * N + gn] = sf::Dt<T>::from_f(v);
         }
     }

@@ -98,10 +98,6 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// SiLU epilogue of gemm_silu: v * sigmoid(v) in fp32 on the accumulator (tasks/gemm_silu/reference.py
-// applies it to the fp32 product); v = -inf gives -inf * 0 = NaN as in the fp64 reference.
-__device__ __forceinline__ float silu_f(float v) { return v * (1.0f / (1.0f + __expf(-v))); }
-
 template <typename T, bool BMN, bool SILU>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_nt_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -254,9 +250,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(t_base + (uint32_t)c, r);
                 sm100::tmem_ld_wait();
+                // gemm_silu: v * sigmoid(v) in fp32 on the accumulator (tasks/gemm_silu/reference.py
+                // applies it to the fp32 product; v = -inf gives -inf * 0 = NaN as there).  The
+                // branch-free packed sigmoid keeps the 32 values of one TMEM load independent.
                 if (SILU) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(silu_f(__uint_as_float(r[j])));
+                    for (int j = 0; j < 32; j += 2) {
+                        const float2 v = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        const float2 o = sf::f2_mul(v, sf::sigmoid2_nr(v));
+                        r[j] = __float_as_uint(o.x);
+                        r[j + 1] = __float_as_uint(o.y);
+                    }
                 }
                 const int col0 = col_base + c;
                 if (row < M) {

@@ -2,10 +2,12 @@
 //
 // A [M, K] row-major, x [K], y [M]; fp16 or bf16 in, fp32 accumulate, one rounding at the output.
 // HBM-bound: A is read exactly once (2 bytes per multiply-add), x (K elements) is re-read by every
-// row out of L1/L2.  One warp per row: each lane streams 16-byte vectors of its row, eight of them
-// in flight before the first multiply (128 bytes per lane, 4 KB per warp), accumulates in fp32 and
-// the warp reduces with shuffles; lane 0 stores y[r].  Rows are visited grid-stride by 8-warp CTAs,
-// at most 8 CTAs per SM.  Unaligned bases or K % 8 != 0 take the scalar loop (same order of
+// row out of L1/L2.  One warp per row: each lane streams 16-byte vectors of its row, four of them
+// in flight before the first multiply (64 bytes per lane, 2 KB per warp; with 8 resident 4-warp
+// CTAs that is 64 KB in flight per SM, above the ~40 KB that HBM bandwidth x latency asks for),
+// accumulates in fp32 and the warp reduces with shuffles; lane 0 stores y[r].  Rows are visited
+// grid-stride by 4-warp CTAs, at most 8 per SM (64 registers per thread, no spills): 4096 rows are
+// 1024 CTAs, one wave of 7 per SM, so the slowest SM reads at most one row more than the average.  Unaligned bases or K % 8 != 0 take the scalar loop (same order of
 // operations per lane, element loads instead of vectors).  NaN/Inf in A or x propagate through the
 // fp32 sums as in the fp64 reference.
 #include "sf_common.cuh"
@@ -14,8 +16,8 @@
 
 namespace {
 
-constexpr int WARPS = 8;
-constexpr int UNROLL = 8;
+constexpr int WARPS = 4;
+constexpr int UNROLL = 4;
 
 // 16-byte load of x through L1 (x is shared by every row).
 template <typename T>
@@ -27,7 +29,7 @@ __device__ __forceinline__ sf::Vec8<T> ld_x_v8(const T* p) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(const T* __restrict__ A, const T* __restrict__ x, T* __restrict__ y,
+__global__ void __launch_bounds__(WARPS * 32, 8) gemv_kernel(const T* __restrict__ A, const T* __restrict__ x, T* __restrict__ y,
                                                           int64_t M, int64_t K, bool vec) {
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);

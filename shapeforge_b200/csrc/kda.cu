@@ -254,6 +254,55 @@ int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void*
                                           nullptr, scale, 0.f, N, H, D, out, (float*)final_state, st, err, cap);
 }
 
+namespace {
+
+// Host program of the fixed-length task: the single sequence is one work item [0, N) (the
+// reference's work list holds at most three [token_begin, token_count] pieces; one piece covers
+// any N here because the recurrence runs inside one launch).  Rows 1 and 2 are empty [N, 0) items.
+__global__ void kda_fixed_items_kernel(uint32_t* __restrict__ work_items, int32_t* __restrict__ item_counts, uint32_t n) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        work_items[0] = 0u;
+        work_items[1] = n;
+        work_items[2] = n;
+        work_items[3] = 0u;
+        work_items[4] = n;
+        work_items[5] = 0u;
+        item_counts[0] = 1;
+    }
+}
+
+}  // namespace
+
+// Fixed-length KDA (tasks/kda/reference.py reference()): the varlen recurrence over one sequence of
+// N tokens.  work_items row 0 = (0, N) read as int32 is exactly the cu_seqlens [0, N] of that one
+// sequence, so the kernel takes it directly and nothing is allocated.  handoff_states (the state
+// at piece boundaries when the work is cut into several pieces) is not written: one piece has no
+// boundary.
+int sf_kda_fixed_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                        const void* dt_bias, const void* initial_state, const void* scale, void* out, void* final_state,
+                        void* work_items, void* item_counts, int64_t N, int64_t H, int64_t D, float lower_bound, int32_t dtype,
+                        int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+    int rc = check(1, H, D, dtype, err, cap);
+    if (rc) return rc;
+    if (N < 0 || N > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "kda: N=%lld out of range", (long long)N);
+    if (!work_items || !item_counts) return sf::fail(SF_EINVAL, err, cap, "kda: null work_items / item_counts");
+    if (reinterpret_cast<uintptr_t>(work_items) & 3u) return sf::fail(SF_EINVAL, err, cap, "kda: work_items is not 4-byte aligned");
+    kda_fixed_items_kernel<<<1, 32, 0, st>>>((uint32_t*)work_items, (int32_t*)item_counts, (uint32_t)N);
+    rc = sf::check_launch("kda work-list launch", err, cap);
+    if (rc) return rc;
+    return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, work_items, scale, out, final_state, 1, H, D, lower_bound,
+                         dtype, variant, st, err, cap);
+}
+
+extern "C" int sf_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                      const void* dt_bias, const void* initial_state, const void* scale, void* output, void* final_state,
+                      void* work_items, void* item_counts, void* handoff_states, int64_t N, int64_t H, int64_t D, float lower_bound,
+                      int32_t dtype, void* stream, char* err, uint64_t cap) {
+    (void)handoff_states;
+    return sf_kda_fixed_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, output, final_state, work_items, item_counts,
+                               N, H, D, lower_bound, dtype, 0, (cudaStream_t)stream, err, cap);
+}
+
 extern "C" int sf_varlen_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
                              const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* output,
                              void* final_state, int64_t num_seqs, int64_t H, int64_t D, float lower_bound, int32_t dtype, void* stream,

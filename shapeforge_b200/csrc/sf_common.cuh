@@ -37,6 +37,19 @@ static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// CTAs of `kernel` resident on one SM at `threads` threads and `smem` bytes of dynamic shared
+// memory (the occupancy calculator; at least 1).  Grid-stride kernels size their grid as
+// sm_count() x this, so the whole grid is one wave and every CTA gets the same share.
+template <typename K>
+int resident_ctas(K kernel, int threads, size_t smem) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 1;
+    }
+    return n;
+}
+
 template <typename T> struct Dt;
 template <> struct Dt<__half> {
     static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
@@ -84,6 +97,76 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Packed fp32 pair arithmetic (sm_100: one FFMA2 / FMUL2 / FADD2 instruction for two values).
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(reinterpret_cast<uint64_t&>(d))
+        : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)), "l"(reinterpret_cast<const uint64_t&>(c)));
+    return d;
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    float2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;"
+        : "=l"(reinterpret_cast<uint64_t&>(d))
+        : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+    return d;
+}
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    float2 d;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(reinterpret_cast<uint64_t&>(d))
+        : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+    return d;
+}
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+
+// sigmoid(x) = 1 / (1 + e^-x) with one MUFU operation per element and no branch.
+// With t = e^-|x| in (0, 1] the denominator d = 1 + t lies in [1, 2], so 1/d comes from the
+// Newton-Raphson division seed 24/17 - 8/17 d (maximum relative error 1/17 on [1, 2]) and three
+// Newton steps r += r (1 - d r) (error 1/17 -> 2^-8.2 -> 2^-16.4 -> below fp32 rounding); then
+// sigmoid(x) = 1/d for x >= 0 and t/d = e^x / (1 + e^x) for x < 0.  Within 3 fp32 ulps of the
+// exact value for |x| <= 80 (below that e^x is subnormal in fp32).  NaN propagates through t;
+// +Inf gives 1 and -Inf gives +0.  sigmoid2_nr does the same for a pair with packed arithmetic
+// (written with nd = -d so that every step is one FFMA2).
+__device__ __forceinline__ float sigmoid_nr(float x) {
+    const float t = __expf(-fabsf(x));
+    const float d = 1.0f + t;
+    float r = fmaf(-8.0f / 17.0f, d, 24.0f / 17.0f);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) r = fmaf(r, fmaf(-d, r, 1.0f), r);
+    return x >= 0.f ? r : t * r;
+}
+
+__device__ __forceinline__ float2 sigmoid2_nr(float2 x) {
+    const float2 t = make_float2(__expf(-fabsf(x.x)), __expf(-fabsf(x.y)));
+    const float2 nd = f2_fma(t, f2(-1.0f), f2(-1.0f));  // -(1 + t)
+    float2 r = f2_fma(f2(8.0f / 17.0f), nd, f2(24.0f / 17.0f));
+#pragma unroll
+    for (int i = 0; i < 3; ++i) r = f2_fma(r, f2_fma(nd, r, f2(1.0f)), r);
+    const float2 tr = f2_mul(t, r);
+    return make_float2(x.x >= 0.f ? r.x : tr.x, x.y >= 0.f ? r.y : tr.y);
+}
+
+// Two 16-bit values packed in a 32-bit word <-> a float pair.
+template <typename T> struct Pair;
+template <> struct Pair<__half> {
+    static __device__ __forceinline__ float2 to_f2(uint32_t w) { return __half22float2(*reinterpret_cast<const __half2*>(&w)); }
+    static __device__ __forceinline__ uint32_t from_f2(float2 v) {
+        const __half2 h = __floats2half2_rn(v.x, v.y);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+};
+template <> struct Pair<__nv_bfloat16> {
+    static __device__ __forceinline__ float2 to_f2(uint32_t w) {
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    }
+    static __device__ __forceinline__ uint32_t from_f2(float2 v) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+};
+
 }  // namespace sf
 
 // Per-op launchers (defined in the op's .cu file) used by sf_run_op.
@@ -123,6 +206,10 @@ int sf_attention_status_read(uint32_t* code, uint32_t* where, cudaStream_t strea
 int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log, const void* dt_bias,
                   const void* initial_state, const void* cu_seqlens, const void* scale, void* out, void* final_state, int64_t N,
                   int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);
+int sf_kda_fixed_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                        const void* dt_bias, const void* initial_state, const void* scale, void* out, void* final_state,
+                        void* work_items, void* item_counts, int64_t N, int64_t H, int64_t D, float lower_bound, int32_t dtype,
+                        int32_t variant, cudaStream_t st, char* err, uint64_t cap);
 int sf_kda_task_chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
                              const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* out,
                              void* final_state, int64_t N, int64_t H, int64_t D, float lower_bound, int32_t dtype, cudaStream_t st,

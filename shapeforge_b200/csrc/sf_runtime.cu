@@ -126,6 +126,7 @@ extern "C" int32_t sf_op_nargs(int32_t op) {
         case SF_OP_LION: return 5;
         case SF_OP_GEMV: return 3;
         case SF_OP_GEMM_SILU: return 4;
+        case SF_OP_KDA_FIXED: return 14;
         default: return 0;
     }
 }
@@ -183,6 +184,10 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
         case SF_OP_GEMM_SILU:
             return sf_gemm_silu_launch(a[0], a[1], (void*)a[2], d->dims[0], d->dims[1], d->dims[2], d->dtype, d->variant, (void*)a[3],
                                        (uint64_t)d->dims[3], s, err, cap);
+        case SF_OP_KDA_FIXED:
+            return sf_kda_fixed_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], a[8], (void*)a[9], (void*)a[10], (void*)a[11],
+                                       (void*)a[12], d->dims[0], d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype, d->variant, s,
+                                       err, cap);
         default:
             return sf::fail(SF_EINVAL, err, cap, "unknown op %d", d->op);
     }

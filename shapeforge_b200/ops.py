@@ -317,6 +317,33 @@ def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scal
     return output, final_state
 
 
+def kda(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound: float = -5.0,
+        output: torch.Tensor | None = None, final_state: torch.Tensor | None = None,
+        work_items: torch.Tensor | None = None, item_counts: torch.Tensor | None = None,
+        handoff_states: torch.Tensor | None = None, variant: int = 0):
+    """Fixed-length KDA forward (tasks/kda/reference.py ``reference``): the varlen recurrence over
+    one sequence of N tokens.  q, k, v, g ``[N, H, D]``, beta ``[N, H]``; A_log ``[H]``, dt_bias
+    ``[H*D]``, initial_state ``[H, D, D]`` and the one-element ``scale`` in fp32.  The task's
+    candidate-owned outputs (``work_items`` u32 ``[3, 2]`` as int32, ``item_counts`` ``[1]``,
+    ``handoff_states`` ``[2, H, D, D]``) are allocated when not given; the work list is written,
+    the hand-off states are not (one piece).  Returns ``(output [N,H,D], final_state [H,D,D])``."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
+        _check(t, name, q.dtype)
+    for name, t in (("A_log", a_log), ("dt_bias", dt_bias), ("initial_state", initial_state), ("scale", scale)):
+        _check(t, name, torch.float32)
+    n, h, d = q.shape
+    dev = q.device
+    output = torch.empty_like(v) if output is None else output
+    final_state = torch.empty((h, d, d), dtype=torch.float32, device=dev) if final_state is None else final_state
+    work_items = torch.empty((3, 2), dtype=torch.int32, device=dev) if work_items is None else work_items
+    item_counts = torch.empty((1,), dtype=torch.int32, device=dev) if item_counts is None else item_counts
+    handoff_states = torch.empty((2, h, d, d), dtype=torch.float32, device=dev) if handoff_states is None else handoff_states
+    ptrs = [x.data_ptr() for x in (q, k, v, g, beta, a_log, dt_bias, initial_state, scale, output, final_state, work_items,
+                                   item_counts, handoff_states)]
+    _run("kda", q, ptrs, dims=(n, h, d), attrs=(lower_bound,), variant=variant)
+    return output, final_state
+
+
 def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: torch.Tensor | None = None,
                      output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0):
     """Gated KDA workload: q, k pre-normalised, ``g`` fp32 log-decay used directly, ``beta`` fp32

@@ -15,8 +15,8 @@ Two sources, both produced by the reference itself:
   ``tcenv.taskcontract.load_task_contract``): inputs from the task's own ``gen_inputs`` at the
   harness case seeds ``seed + 7919 * (i + 1)`` (``tcenv/backends/metal/v2_runtime.py:1602``), rounded
   to storage dtype, and the task's fp64 ``reference`` outputs, for bitdelta_gemm,
-  flash_attention, rope, varlen_kda, mamba2_chunk_scan, relu, sigmoid, sigmoid_shift, lion, gemv
-  and gemm_silu.  Where the task module has an ``error_scale`` hook (lion) the recorded scales are
+  flash_attention, rope, varlen_kda, mamba2_chunk_scan, relu, sigmoid, sigmoid_shift, lion, gemv,
+  gemm_silu and kda (fixed length, sizes single/small/tail).  Where the task module has an ``error_scale`` hook (lion) the recorded scales are
   the hook's, otherwise the RMS of the finite reference.
 
 ``python tests/golden/make_fixtures.py relu lion`` rewrites only the named tasks' fixtures.
@@ -338,6 +338,14 @@ def _new_task(task: str, dtype: str) -> Path:
     return write(from_reference(task, dtype, "small", slicer), f"ref_{task}_{dtype}")
 
 
+KDA_FIXED_SIZES = ("single", "small", "tail")
+
+
+def _kda_fixed(dtype: str) -> list[Path]:
+    """tasks/kda at its three golden sizes (D = 8; the paper size is covered by the oracle)."""
+    return [write(from_reference("kda", dtype, size), f"ref_kda_{size}_{dtype}") for size in KDA_FIXED_SIZES]
+
+
 def main(only=()) -> None:
     if not REF.is_dir():
         raise SystemExit(f"reference checkout not found at {REF}")
@@ -345,7 +353,10 @@ def main(only=()) -> None:
     if only:
         for task in only:
             for dtype in ("fp16", "bf16"):
-                outs.append(_new_task(task, dtype))
+                if task == "kda":
+                    outs.extend(_kda_fixed(dtype))
+                else:
+                    outs.append(_new_task(task, dtype))
         for p in outs:
             print(f"{p.name:40s} {p.stat().st_size:8d} B")
         return
@@ -366,6 +377,7 @@ def main(only=()) -> None:
             outs.append(write(from_reference("varlen_kda", dtype, size), f"ref_varlen_kda_{size}_{dtype}"))
         for task in NEW_TASKS:
             outs.append(_new_task(task, dtype))
+        outs.extend(_kda_fixed(dtype))
     total = 0
     for p in outs:
         total += p.stat().st_size

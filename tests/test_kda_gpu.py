@@ -1,4 +1,5 @@
-"""varlen_kda (task contract) and varlen_kda_gated (the gated workload) on the B200.
+"""varlen_kda (task contract), kda (the fixed-length task) and varlen_kda_gated (the gated
+workload) on the B200.
 
 Tolerances: tasks/varlen_kda/opspec.json numerics — fp16 rtol 1e-2 / atol_rel 5e-3, bf16 rtol
 3e-2 / atol_rel 1.5e-2 — for both the output and the final state, scaled by the RMS of each
@@ -203,3 +204,67 @@ def test_gated_recurrent_variant_still_matches(cuda_device):
     ro, rf = _oracle_gated(d, [0, 1], 0.125)
     assert _verdict(_np(out), ro, "bf16", "bf16").ok
     assert _verdict(_np(fin), rf, "bf16", "fp32").ok
+
+
+# ---- fixed-length kda (tasks/kda) -------------------------------------------------------------
+
+# tasks/kda/opspec.json numerics (tighter than varlen_kda's).
+FIXED_TOL = {"fp16": dict(rtol=2e-3, atol_rel=1e-3), "bf16": dict(rtol=1.6e-2, atol_rel=8e-3)}
+
+
+def _fixed_run(d, lb, variant=0):
+    n = d["q"].shape[0]
+    wi = torch.full((3, 2), -7, dtype=torch.int32, device=d["q"].device)
+    ic = torch.full((1,), -7, dtype=torch.int32, device=d["q"].device)
+    out, fin = ops.kda(d["q"], d["k"], d["v"], d["g"], d["beta"], d["A_log"], d["dt_bias"], d["initial_state"], d["scale"],
+                       lower_bound=lb, work_items=wi, item_counts=ic, variant=variant)
+    torch.cuda.synchronize()
+    # The host program's work list: one piece [0, N) and two empty ones.
+    assert wi.cpu().tolist() == [[0, n], [n, 0], [n, 0]]
+    assert ic.item() == 1
+    return out, fin
+
+
+def _fixed_oracle(d, lb):
+    f = lambda n: _np(d[n])  # noqa: E731
+    return oref.kda_fixed(f("q"), f("k"), f("v"), f("g"), f("beta"), f("A_log"), f("dt_bias"), f("initial_state"),
+                          float(f("scale")[0]), lb)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("size", ["single", "small", "tail"])
+def test_fixed_kda_reference_vectors(cuda_device, size, dtype):
+    """The reference's own inputs and fp64 outputs (D = 8) with its recorded error scales."""
+    doc = golden.load(f"ref_kda_{size}_{dtype}")
+    tdt = doc["tensor_dtypes"]
+    lb = float(doc["attrs"]["LOWER_BOUND"])
+    assert [r["case"] for r in doc["records"]] == list(cases.KDA_FIXED_CASES)
+    for rec in doc["records"]:
+        d = {k: _from_fixture(v, tdt[k], cuda_device) for k, v in rec["inputs"].items()}
+        out, fin = _fixed_run(d, lb)
+        v1 = compare.check(_np(out), rec["refs"]["output"], rec["scales"]["output"], dtype=dtype, **FIXED_TOL[dtype])
+        v2 = compare.check(_np(fin), rec["refs"]["final_state"], rec["scales"]["final_state"], dtype="fp32", **FIXED_TOL[dtype])
+        assert v1.ok, (size, rec["case"], "output", v1.summary())
+        assert v2.ok, (size, rec["case"], "final_state", v2.summary())
+
+
+FIXED_SHAPES = [(256, 8, 64), (17, 2, 8), (100, 3, 32), (1, 1, 16), (300, 2, 128)]
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("shape", FIXED_SHAPES, ids=[f"n{n}h{h}d{d}" for n, h, d in FIXED_SHAPES])
+def test_fixed_kda_against_oracle(cuda_device, dtype, shape):
+    """The task's input stream at the paper size (N=256, H=8, D=64) and other head dims, every case,
+    default dispatch (the chunked tensor-core kernel at D = 128, the recurrent one otherwise) and
+    the recurrent kernel forced."""
+    n, h, dim = shape
+    for ci, case in enumerate(cases.KDA_FIXED_CASES):
+        inp = cases.kda_fixed_inputs(case, cases.case_seed(0, ci), n, h, dim, dtype)
+        d = {k: v.to(cuda_device) for k, v in inp.items()}
+        ref_out, ref_fin = _fixed_oracle(d, -5.0)
+        for variant in (0, 2):
+            out, fin = _fixed_run(d, -5.0, variant)
+            v1 = compare.check(_np(out), ref_out, compare.rms_scale(ref_out), dtype=dtype, **FIXED_TOL[dtype])
+            v2 = compare.check(_np(fin), ref_fin, compare.rms_scale(ref_fin), dtype="fp32", **FIXED_TOL[dtype])
+            assert v1.ok, (shape, case, variant, "output", v1.summary())
+            assert v2.ok, (shape, case, variant, "final_state", v2.summary())

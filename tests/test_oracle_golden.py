@@ -77,6 +77,12 @@ def _run(doc, rec):
         return {"y": ops.gemv(f("A"), f("x"))}, FP64_TOL
     if task == "gemm_silu":
         return {"C": ops.gemm_silu(f("A"), f("B"))}, FP32_TOL
+    if task == "kda":
+        out, fin = ops.kda_fixed(
+            f("q"), f("k"), f("v"), f("g"), f("beta"), f("A_log"), f("dt_bias"), f("initial_state"), float(f("scale")[0]),
+            doc["attrs"]["LOWER_BOUND"],
+        )
+        return {"output": out, "final_state": fin}, FP64_TOL
     if task == "mamba2_chunk_scan":
         # The first and the last chunk were kept; the reference rows are a few rows of each.
         y = ops.mamba2_chunk_scan(f("x"), f("dt"), f("dA_cumsum"), f("Bmat"), f("Cmat"), f("Dskip"), f("states"))
