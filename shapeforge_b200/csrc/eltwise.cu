@@ -49,38 +49,61 @@ constexpr const char* act_name(int a) {
 }
 
 template <typename T, int A>
+__device__ __forceinline__ void apply_vec(const sf::Vec8<T>& a, const sf::Vec8<T>& u, T* dst) {
+    sf::Vec8<T> o;
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(&a);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(&u);
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        ow[j] = sf::Pair<T>::from_f2(act2<A>(sf::Pair<T>::to_f2(aw[j]), A == SWIGLU ? sf::Pair<T>::to_f2(uw[j]) : sf::f2(0.f)));
+    sf::st_global_v8<T>(dst, o);
+}
+
+template <typename T, int A>
 __global__ void __launch_bounds__(256) act_kernel(const T* __restrict__ x, const T* __restrict__ up, T* __restrict__ y,
                                                   int64_t n, bool vec) {
     constexpr bool GLU = A == SWIGLU;
+    // The sigmoid-based unary operators carry enough arithmetic per element that a thread's load
+    // and compute phases no longer overlap across warps; they double-buffer in registers (the next
+    // step's two vectors are requested before this step's are computed).  relu and swiglu (two
+    // input streams) keep the plain two-vector step, which needs fewer registers.
+    constexpr bool PREFETCH = A == SILU || A == SIGMOID || A == SIGMOID_SHIFT;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t done = 0;
     if (vec) {
         const int64_t nv = n >> 3;
-        auto apply = [&](const sf::Vec8<T>& a, const sf::Vec8<T>& u, int64_t i) {
-            sf::Vec8<T> o;
-            const uint32_t* aw = reinterpret_cast<const uint32_t*>(&a);
-            const uint32_t* uw = reinterpret_cast<const uint32_t*>(&u);
-            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                ow[j] = sf::Pair<T>::from_f2(act2<A>(sf::Pair<T>::to_f2(aw[j]), GLU ? sf::Pair<T>::to_f2(uw[j]) : sf::f2(0.f)));
-            sf::st_global_v8<T>(y + i * 8, o);
-        };
-        // Unary operators: two independent vectors per thread and step, so twice the bytes are in
-        // flight (swiglu already has two input streams per vector).
-        int64_t i = tid;
-        for (; !GLU && i + stride < nv; i += 2 * stride) {
-            const sf::Vec8<T> a0 = sf::ld_global_nc_v8<T>(x + i * 8);
-            const sf::Vec8<T> a1 = sf::ld_global_nc_v8<T>(x + (i + stride) * 8);
-            sf::Vec8<T> u0, u1;
-            apply(a0, u0, i);
-            apply(a1, u1, i + stride);
-        }
-        for (; i < nv; i += stride) {
-            sf::Vec8<T> u0;
-            if (GLU) u0 = sf::ld_global_nc_v8<T>(up + i * 8);
-            apply(sf::ld_global_nc_v8<T>(x + i * 8), u0, i);
+        if constexpr (PREFETCH) {
+            sf::Vec8<T> a0, a1, u;
+            if (tid < nv) a0 = sf::ld_global_nc_v8<T>(x + tid * 8);
+            if (tid + stride < nv) a1 = sf::ld_global_nc_v8<T>(x + (tid + stride) * 8);
+            for (int64_t i = tid; i < nv; i += 2 * stride) {
+                const int64_t j0 = i + 2 * stride, j1 = i + 3 * stride;
+                sf::Vec8<T> b0, b1;
+                if (j0 < nv) b0 = sf::ld_global_nc_v8<T>(x + j0 * 8);
+                if (j1 < nv) b1 = sf::ld_global_nc_v8<T>(x + j1 * 8);
+                apply_vec<T, A>(a0, u, y + i * 8);
+                if (i + stride < nv) apply_vec<T, A>(a1, u, y + (i + stride) * 8);
+                a0 = b0;
+                a1 = b1;
+            }
+        } else {
+            int64_t i = tid;
+            // relu: two independent vectors per thread and step, so twice the bytes are in flight
+            // (swiglu already has two input streams per vector).
+            for (; !GLU && i + stride < nv; i += 2 * stride) {
+                const sf::Vec8<T> a0 = sf::ld_global_nc_v8<T>(x + i * 8);
+                const sf::Vec8<T> a1 = sf::ld_global_nc_v8<T>(x + (i + stride) * 8);
+                sf::Vec8<T> u;
+                apply_vec<T, A>(a0, u, y + i * 8);
+                apply_vec<T, A>(a1, u, y + (i + stride) * 8);
+            }
+            for (; i < nv; i += stride) {
+                sf::Vec8<T> u0;
+                if (GLU) u0 = sf::ld_global_nc_v8<T>(up + i * 8);
+                apply_vec<T, A>(sf::ld_global_nc_v8<T>(x + i * 8), u0, y + i * 8);
+            }
         }
         done = nv * 8;
     }

@@ -290,8 +290,12 @@ int sf_kda_fixed_launch(const void* q, const void* k, const void* v, const void*
     kda_fixed_items_kernel<<<1, 32, 0, st>>>((uint32_t*)work_items, (int32_t*)item_counts, (uint32_t)N);
     rc = sf::check_launch("kda work-list launch", err, cap);
     if (rc) return rc;
+    // Default: the recurrent fp32 kernel at every D.  The chunked kernel's TF32 products meet
+    // varlen_kda's tolerance but not always this task's tighter one (fp16 rtol 2e-3 / atol_rel
+    // 1e-3): at D = 128 one output in 76,800 of the wide_range case landed at 1.15x the bound.
+    // variant 1 still forces the chunked kernel.
     return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, work_items, scale, out, final_state, 1, H, D, lower_bound,
-                         dtype, variant, st, err, cap);
+                         dtype, variant == 1 ? 1 : 2, st, err, cap);
 }
 
 extern "C" int sf_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,

@@ -121,16 +121,27 @@ __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
 }
 __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
+// 2^x with the hardware approximation, subnormal results flushed to zero (a single MUFU op; the
+// non-flushing form adds range handling around it).
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// e^-|x| for the sigmoid below: 2^(-|x| log2 e), flushed to 0 below 2^-126 (|x| > 87.3).
+__device__ __forceinline__ float exp_neg_abs(float x) { return ex2_ftz(fabsf(x) * -1.4426950408889634f); }
+
 // sigmoid(x) = 1 / (1 + e^-x) with one MUFU operation per element and no branch.
 // With t = e^-|x| in (0, 1] the denominator d = 1 + t lies in [1, 2], so 1/d comes from the
 // Newton-Raphson division seed 24/17 - 8/17 d (maximum relative error 1/17 on [1, 2]) and three
 // Newton steps r += r (1 - d r) (error 1/17 -> 2^-8.2 -> 2^-16.4 -> below fp32 rounding); then
 // sigmoid(x) = 1/d for x >= 0 and t/d = e^x / (1 + e^x) for x < 0.  Within 3 fp32 ulps of the
-// exact value for |x| <= 80 (below that e^x is subnormal in fp32).  NaN propagates through t;
+// exact value for |x| <= 80; for x < -87.3 t flushes to 0 and so does the result (the exact value
+// is below 2^-126 there, under every tolerance of a 16-bit output).  NaN propagates through t;
 // +Inf gives 1 and -Inf gives +0.  sigmoid2_nr does the same for a pair with packed arithmetic
 // (written with nd = -d so that every step is one FFMA2).
 __device__ __forceinline__ float sigmoid_nr(float x) {
-    const float t = __expf(-fabsf(x));
+    const float t = exp_neg_abs(x);
     const float d = 1.0f + t;
     float r = fmaf(-8.0f / 17.0f, d, 24.0f / 17.0f);
 #pragma unroll
@@ -139,7 +150,7 @@ __device__ __forceinline__ float sigmoid_nr(float x) {
 }
 
 __device__ __forceinline__ float2 sigmoid2_nr(float2 x) {
-    const float2 t = make_float2(__expf(-fabsf(x.x)), __expf(-fabsf(x.y)));
+    const float2 t = make_float2(exp_neg_abs(x.x), exp_neg_abs(x.y));
     const float2 nd = f2_fma(t, f2(-1.0f), f2(-1.0f));  // -(1 + t)
     float2 r = f2_fma(f2(8.0f / 17.0f), nd, f2(24.0f / 17.0f));
 #pragma unroll

@@ -326,7 +326,9 @@ def kda(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound: flo
     ``[H*D]``, initial_state ``[H, D, D]`` and the one-element ``scale`` in fp32.  The task's
     candidate-owned outputs (``work_items`` u32 ``[3, 2]`` as int32, ``item_counts`` ``[1]``,
     ``handoff_states`` ``[2, H, D, D]``) are allocated when not given; the work list is written,
-    the hand-off states are not (one piece).  Returns ``(output [N,H,D], final_state [H,D,D])``."""
+    the hand-off states are not (one piece).  ``variant`` 0/2 run the recurrent fp32 kernel (the
+    default at every D), 1 forces the chunked tensor-core kernel (D = 128).  Returns
+    ``(output [N,H,D], final_state [H,D,D])``."""
     for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
         _check(t, name, q.dtype)
     for name, t in (("A_log", a_log), ("dt_bias", dt_bias), ("initial_state", initial_state), ("scale", scale)):

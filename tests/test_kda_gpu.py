@@ -255,8 +255,8 @@ FIXED_SHAPES = [(256, 8, 64), (17, 2, 8), (100, 3, 32), (1, 1, 16), (300, 2, 128
 @pytest.mark.parametrize("shape", FIXED_SHAPES, ids=[f"n{n}h{h}d{d}" for n, h, d in FIXED_SHAPES])
 def test_fixed_kda_against_oracle(cuda_device, dtype, shape):
     """The task's input stream at the paper size (N=256, H=8, D=64) and other head dims, every case,
-    default dispatch (the chunked tensor-core kernel at D = 128, the recurrent one otherwise) and
-    the recurrent kernel forced."""
+    through the default dispatch (the recurrent fp32 kernel at every D: the chunked kernel's TF32
+    products do not always meet this task's tighter tolerance) and the recurrent variant named."""
     n, h, dim = shape
     for ci, case in enumerate(cases.KDA_FIXED_CASES):
         inp = cases.kda_fixed_inputs(case, cases.case_seed(0, ci), n, h, dim, dtype)
