@@ -64,8 +64,11 @@ class CudaCompileError(RuntimeError):
 
 # The launch block a CUDA candidate carries, like the MSL `/* taic-launch ... */` block
 # (tcenv/backends/metal/launch.py:1-60): `kernel <name> grid=X[,Y[,Z]] threads=X[,Y[,Z]] [smem=B]`.
+# Each value is an integer or an expression over the task's symbols in the guard/geometry language
+# of ``expr`` (``grid=ceil_div(N,256)``), so one source can serve every shape a portfolio variant
+# covers; the expressions are resolved per shape (``LaunchTemplate.resolve``).
 _LAUNCH_BLOCK = re.compile(r"/\*\s*taic-launch(.*?)\*/", re.S)
-_LAUNCH_LINE = re.compile(r"^\s*kernel\s+(\w+)\s+grid=([\d,]+)\s+threads=([\d,]+)(?:\s+smem=(\d+))?\s*$")
+_LAUNCH_LINE = re.compile(r"^\s*kernel\s+(\w+)\s+grid=(.+?)\s+threads=(.+?)(?:\s+smem=(.+?))?\s*$")
 MAX_STAGES = 32
 
 
@@ -77,11 +80,83 @@ class LaunchStage:
     smem: int = 0
 
 
-def _dims(text: str) -> tuple[int, int, int]:
-    parts = [int(p) for p in text.split(",") if p]
-    if not 1 <= len(parts) <= 3 or any(p < 1 for p in parts):
-        raise ValueError(f"bad launch dimensions {text!r}")
-    return tuple(parts + [1] * (3 - len(parts)))  # type: ignore[return-value]
+def _split_top(text: str) -> list[str]:
+    """Split a launch value at commas outside parentheses."""
+    parts, depth, cur = [], 0, ""
+    for ch in text:
+        if ch == "," and depth == 0:
+            parts.append(cur)
+            cur = ""
+            continue
+        depth += ch == "("
+        depth -= ch == ")"
+        cur += ch
+    parts.append(cur)
+    return [p.strip() for p in parts]
+
+
+@dataclass(frozen=True)
+class LaunchTemplate:
+    """One launch line with its values kept as expressions (text) until a shape is known."""
+
+    kernel: str
+    grid: tuple[str, ...]
+    threads: tuple[str, ...]
+    smem: str = "0"
+
+    @property
+    def symbolic(self) -> bool:
+        from . import expr
+
+        return any(expr.names(expr.parse(t)) for t in (*self.grid, *self.threads, self.smem))
+
+    def resolve(self, names: Mapping[str, int] | None = None) -> LaunchStage:
+        from . import expr
+
+        env = dict(names or {})
+
+        def dims(terms: tuple[str, ...], what: str) -> tuple[int, int, int]:
+            vals = [int(expr.evaluate_term(t, env, where=f"{self.kernel} {what}")) for t in terms]
+            if any(v < 1 for v in vals):
+                raise ValueError(f"{self.kernel}: {what} {vals} has a dimension below 1")
+            return tuple(vals + [1] * (3 - len(vals)))  # type: ignore[return-value]
+
+        smem = int(expr.evaluate_term(self.smem, env, where=f"{self.kernel} smem"))
+        if smem < 0:
+            raise ValueError(f"{self.kernel}: negative shared memory")
+        return LaunchStage(self.kernel, dims(self.grid, "grid"), dims(self.threads, "threads"), smem)
+
+
+def parse_launch_templates(source: str) -> list[LaunchTemplate] | None:
+    """The launch block of ``source`` as templates (None without a block); syntax is checked,
+    names are not resolved."""
+    from . import expr
+
+    m = _LAUNCH_BLOCK.search(source)
+    if not m:
+        return None
+    out = []
+    for line in m.group(1).splitlines():
+        if not line.strip():
+            continue
+        lm = _LAUNCH_LINE.match(line)
+        if not lm:
+            raise ValueError(f"unparseable launch line {line.strip()!r}")
+        grid, threads = _split_top(lm.group(2)), _split_top(lm.group(3))
+        if not 1 <= len(grid) <= 3 or not 1 <= len(threads) <= 3:
+            raise ValueError(f"bad launch dimensions in {line.strip()!r}")
+        tpl = LaunchTemplate(lm.group(1), tuple(grid), tuple(threads), (lm.group(4) or "0").strip())
+        for t in (*tpl.grid, *tpl.threads, tpl.smem):
+            try:
+                node = expr.parse(t, f"launch {tpl.kernel}")
+                if expr.kind(node) != expr.INT:
+                    raise ValueError(f"launch value {t!r} is a predicate")
+            except expr.ExprError as exc:
+                raise ValueError(str(exc)) from exc
+        out.append(tpl)
+    if not out or len(out) > MAX_STAGES:
+        raise ValueError(f"a launch block needs 1..{MAX_STAGES} stages")
+    return out
 
 
 class CudaBackend:
@@ -122,21 +197,18 @@ class CudaBackend:
             problems.append("no __global__ kernel in the candidate")
         return problems
 
-    def parse_launch(self, source: str, contract: Any = None) -> list[LaunchStage] | None:
-        m = _LAUNCH_BLOCK.search(source)
-        if not m:
+    def parse_launch(self, source: str, contract: Any = None, names: Mapping[str, int] | None = None) -> list[LaunchStage] | None:
+        """The launch stages resolved on ``names`` (the shape's symbols; a symbolic value without
+        them is an error)."""
+        from . import expr
+
+        templates = parse_launch_templates(source)
+        if templates is None:
             return None
-        stages = []
-        for line in m.group(1).splitlines():
-            if not line.strip():
-                continue
-            lm = _LAUNCH_LINE.match(line)
-            if not lm:
-                raise ValueError(f"unparseable launch line {line.strip()!r}")
-            stages.append(LaunchStage(lm.group(1), _dims(lm.group(2)), _dims(lm.group(3)), int(lm.group(4) or 0)))
-        if not stages or len(stages) > MAX_STAGES:
-            raise ValueError(f"a launch block needs 1..{MAX_STAGES} stages")
-        return stages
+        try:
+            return [t.resolve(names) for t in templates]
+        except expr.ExprError as exc:
+            raise ValueError(str(exc)) from exc
 
     def source_name_pattern(self, kernel_name: str) -> str:
         return r'extern\s+"C"\s+__global__\s+void\s+(?:__launch_bounds__\([^)]*\)\s+)?' + re.escape(kernel_name) + r"\s*\("

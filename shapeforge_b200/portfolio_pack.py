@@ -1,0 +1,479 @@
+"""Shape portfolios of CUDA candidates: pack a source tree, check its coverage, dispatch, account.
+
+The layout and the rules follow the reference's portfolio assembly
+(tcenv/portfolio_assembly/assembly.py:132-345, ``_load_coverage`` / ``_fallback_shape`` /
+``_portfolio_document`` below it) with cuda-single sources in place of Metal ones::
+
+    <src>/coverage.json            {"schema_id": "tcenv.portfolio-assembly.coverage.1",
+                                    "planner": {"id": ..., "version": n},
+                                    "variants": [{"variant_key": k, "guard": <predicate term>,
+                                                  "bucket_key": b (optional)}, ...],
+                                    "fallback": {"kind": "refuse", "reasons": [...]} or
+                                                {"kind": "registered_implementation", "reasons": [...],
+                                                 "implementation_id": ..., "implementation_version": n}}
+    <src>/variants/<k>/kernel.cu   one single-source candidate per variant
+    <src>/fallback/kernel.cu       the registered implementation's source (``fallbacks.render``)
+
+Guards are predicate terms of ``expr`` over the task's symbols.  A portfolio kernel takes the
+task's ABI tensors in opspec order followed by the symbols as ``long long`` in ``spec_params``
+order, and its ``taic-launch`` values may be expressions over the symbols, so one build serves
+every shape its guard admits.
+
+* ``pack`` validates the tree (closed key sets, variant-key pattern, at most 16 variants, unique
+  keys, one guard per bucket, registered fallback reasons, every source through the cuda-single
+  builder's pre-compile checks) and returns the parent: entries plus the ``portfolio.json``
+  document (guard digests, the domain-plan digest of the sizes it was packed for).
+* ``check`` evaluates every guard on every point of the domain (size x usage of the task's
+  opspec): each point must go to exactly one variant, or to an implementation fallback when no
+  guard matches; overlaps, guard errors, variants that match no point and unresolvable launches
+  are problems.
+* ``to_portfolio`` gives the exact-dispatch ``portfolio.Portfolio`` of a parent (overlap and
+  guard errors are dispatch failures, no ranking), and ``measure`` runs and times every benchmark
+  point on the GPU against the task's torch baseline, so ``PerformanceReport``'s
+  ``effective_end_to_end`` account includes the real time of the shards the fallback serves.
+"""
+
+from __future__ import annotations
+
+import base64
+import hashlib
+import json
+import re
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Callable, Mapping, Sequence
+
+from . import expr, fallbacks
+from .portfolio import Fallback, Portfolio, Variant
+
+COVERAGE_SCHEMA_ID = "tcenv.portfolio-assembly.coverage.1"
+PORTFOLIO_SCHEMA_ID = "cuda-sm100.candidate-portfolio.1"
+PORTFOLIO_ENTRY_PATH = "coverage_plan/portfolio.json"
+FALLBACK_REASONS = frozenset({"outside_candidate_coverage", "resource_unavailable", "variant_unavailable"})
+MAX_VARIANTS = 16
+SOURCE_NAME = "kernel.cu"
+_VARIANT_KEY = re.compile(r"[a-z0-9][a-z0-9_-]{0,31}")
+_COVERAGE_KEYS = frozenset({"schema_id", "planner", "variants", "fallback"})
+_VARIANT_ITEM_KEYS = frozenset({"variant_key", "guard", "bucket_key"})
+_REFUSE_KEYS = frozenset({"kind", "reasons"})
+_IMPLEMENTATION_KEYS = frozenset({"kind", "reasons", "implementation_id", "implementation_version"})
+
+
+class PortfolioError(ValueError):
+    """The source tree, its coverage.json or a parent document breaks the packing contract."""
+
+
+# ---- the finite domain ------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class Point:
+    instance_key: str  # "<dtype>/<size>/<usage>"
+    size: str
+    usage: str
+    names: Mapping[str, int]
+
+
+def load_opspec(task_dir: str | Path) -> dict[str, Any]:
+    return json.loads((Path(task_dir) / "opspec.json").read_text(encoding="utf-8"))
+
+
+def symbol_order(opspec: Mapping[str, Any]) -> tuple[str, ...]:
+    """The kernel-argument order of the symbols: ``spec_params``, else the declared symbols."""
+    return tuple(opspec.get("spec_params") or opspec.get("symbols", {}).keys())
+
+
+def domain(opspec: Mapping[str, Any], dtype: str, sizes: Sequence[str] | None = None) -> tuple[Point, ...]:
+    """Every (size, usage) point of the task for ``dtype``, in opspec order."""
+    declared = opspec.get("sizes", {})
+    chosen = list(sizes) if sizes is not None else list(declared)
+    if not chosen or len(set(chosen)) != len(chosen):
+        raise PortfolioError(f"sizes must be non-empty and distinct, got {chosen}")
+    points = []
+    for size in chosen:
+        if size not in declared:
+            raise PortfolioError(f"size {size!r} is not declared by the task (declared: {sorted(declared)})")
+        entry = declared[size]
+        names = {k: int(v) for k, v in entry.items() if k != "usage" and isinstance(v, int) and not isinstance(v, bool)}
+        for usage in entry.get("usage", ["benchmark"]):
+            points.append(Point(f"{dtype}/{size}/{usage}", size, usage, names))
+    return tuple(points)
+
+
+def domain_digest(points: Sequence[Point]) -> str:
+    doc = [{"instance_key": p.instance_key, "names": dict(sorted(p.names.items()))} for p in points]
+    return hashlib.sha256(json.dumps(doc, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
+
+
+# ---- the parent -------------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class Entry:
+    path: str
+    role: str
+    media_type: str
+    data: bytes
+
+
+@dataclass(frozen=True)
+class Parent:
+    entries: tuple[Entry, ...]
+    document: Mapping[str, Any]
+
+    def entry(self, path: str) -> Entry:
+        for e in self.entries:
+            if e.path == path:
+                return e
+        raise PortfolioError(f"the parent has no entry {path!r}")
+
+    def source(self, path: str) -> str:
+        return self.entry(path).data.decode("utf-8")
+
+    def to_json(self) -> str:
+        return json.dumps({
+            "transport": "shape-portfolio",
+            "entries": [{"path": e.path, "role": e.role, "media_type": e.media_type,
+                         "data": base64.b64encode(e.data).decode("ascii")} for e in self.entries],
+        }, sort_keys=True, indent=1)
+
+    @property
+    def sha256(self) -> str:
+        return hashlib.sha256(self.to_json().encode()).hexdigest()
+
+    @classmethod
+    def from_json(cls, text: str) -> "Parent":
+        doc = json.loads(text)
+        if doc.get("transport") != "shape-portfolio":
+            raise PortfolioError("not a shape-portfolio parent")
+        entries = tuple(Entry(e["path"], e["role"], e["media_type"], base64.b64decode(e["data"])) for e in doc["entries"])
+        manifest = [e for e in entries if e.path == PORTFOLIO_ENTRY_PATH]
+        if len(manifest) != 1:
+            raise PortfolioError(f"a parent needs exactly one {PORTFOLIO_ENTRY_PATH}")
+        return cls(entries, json.loads(manifest[0].data))
+
+
+def _read_source(path: Path) -> bytes:
+    if not path.is_file() or path.is_symlink():
+        raise PortfolioError(f"{path}: expected a regular file")
+    data = path.read_bytes()
+    try:
+        data.decode("utf-8")
+    except UnicodeDecodeError as exc:
+        raise PortfolioError(f"{path}: not UTF-8") from exc
+    if not data.strip():
+        raise PortfolioError(f"{path}: empty source")
+    return data
+
+
+def _single_source(directory: Path, where: str) -> bytes:
+    """A variant (or fallback) directory holds exactly one ``kernel.cu``."""
+    if not directory.is_dir() or directory.is_symlink():
+        raise PortfolioError(f"{directory}: expected a directory")
+    files = sorted(p.relative_to(directory).as_posix() for p in directory.rglob("*") if p.is_file() or p.is_symlink())
+    if files != [SOURCE_NAME]:
+        raise PortfolioError(f"{directory}: a cuda-single {where} is exactly {SOURCE_NAME}, found {files}")
+    data = _read_source(directory / SOURCE_NAME)
+    from .track_factory import CudaTrackBuilder, TrackRefused
+
+    try:
+        CudaTrackBuilder().check(data.decode("utf-8"))
+    except TrackRefused as exc:
+        raise PortfolioError(f"{directory / SOURCE_NAME}: {exc}") from exc
+    return data
+
+
+def _load_coverage(path: Path) -> dict[str, Any]:
+    try:
+        doc = json.loads(_read_source(path))
+    except json.JSONDecodeError as exc:
+        raise PortfolioError(f"{path}: not JSON: {exc}") from exc
+    if not isinstance(doc, dict) or set(doc) != _COVERAGE_KEYS:
+        raise PortfolioError(f"{path}: keys must be exactly {sorted(_COVERAGE_KEYS)}")
+    if doc["schema_id"] != COVERAGE_SCHEMA_ID:
+        raise PortfolioError(f"{path}: schema_id must be {COVERAGE_SCHEMA_ID!r}")
+    planner = doc["planner"]
+    if (not isinstance(planner, dict) or set(planner) != {"id", "version"} or not isinstance(planner["id"], str)
+            or not planner["id"].strip() or isinstance(planner["version"], bool) or not isinstance(planner["version"], int)
+            or planner["version"] < 1):
+        raise PortfolioError(f"{path}: planner must be {{id: non-empty string, version: positive integer}}")
+    variants = doc["variants"]
+    if not isinstance(variants, list) or not variants or len(variants) > MAX_VARIANTS:
+        raise PortfolioError(f"{path}: variants must be a list of 1..{MAX_VARIANTS} items")
+    return doc
+
+
+def _fallback(doc: Any, root: Path, path: Path) -> tuple[dict[str, Any], bytes | None]:
+    if not isinstance(doc, dict) or "kind" not in doc:
+        raise PortfolioError(f"{path}: fallback must be an object with a kind")
+    reasons = doc.get("reasons")
+    if (not isinstance(reasons, list) or not reasons or len(set(reasons)) != len(reasons)
+            or any(r not in FALLBACK_REASONS for r in reasons)):
+        raise PortfolioError(f"{path}: fallback reasons must be a non-empty list drawn from {sorted(FALLBACK_REASONS)}")
+    directory = root / "fallback"
+    if doc["kind"] == "refuse":
+        if set(doc) != _REFUSE_KEYS:
+            raise PortfolioError(f"{path}: a refuse fallback has only kind and reasons")
+        if directory.exists():
+            raise PortfolioError(f"{directory}: a refuse fallback has no fallback directory")
+        return {"kind": "refuse", "implementation_id": None, "implementation_version": None, "entries": [],
+                "reasons": list(reasons)}, None
+    if doc["kind"] != "registered_implementation":
+        raise PortfolioError(f"{path}: unknown fallback kind {doc['kind']!r}")
+    if set(doc) != _IMPLEMENTATION_KEYS:
+        raise PortfolioError(f"{path}: a registered_implementation fallback has exactly {sorted(_IMPLEMENTATION_KEYS)}")
+    impl, version = doc["implementation_id"], doc["implementation_version"]
+    if not isinstance(impl, str) or not impl.strip() or isinstance(version, bool) or not isinstance(version, int) or version < 1:
+        raise PortfolioError(f"{path}: implementation_id must be a non-empty string and implementation_version >= 1")
+    data = _single_source(directory, "fallback")
+    return {"kind": "registered_implementation", "implementation_id": impl, "implementation_version": version,
+            "entries": [f"fallback/{SOURCE_NAME}"], "reasons": list(reasons)}, data
+
+
+def pack(src: str | Path, points: Sequence[Point]) -> Parent:
+    """Validate ``src`` and build the parent (sources + ``coverage_plan/portfolio.json``)."""
+    root = Path(src)
+    cov_path = root / "coverage.json"
+    coverage = _load_coverage(cov_path)
+    vdir = root / "variants"
+    if not vdir.is_dir():
+        raise PortfolioError(f"{vdir}: expected a variants directory")
+    on_disk = sorted(p.name for p in vdir.iterdir() if not p.name.startswith("."))
+    declared: dict[str, dict[str, Any]] = {}
+    for i, item in enumerate(coverage["variants"]):
+        where = f"{cov_path}: variants[{i}]"
+        if not isinstance(item, dict) or not set(item) <= _VARIANT_ITEM_KEYS or "variant_key" not in item or "guard" not in item:
+            raise PortfolioError(f"{where}: allows only variant_key, guard and an optional bucket_key")
+        key = item["variant_key"]
+        if not isinstance(key, str) or not _VARIANT_KEY.fullmatch(key):
+            raise PortfolioError(f"{where}: variant_key {key!r} must match [a-z0-9][a-z0-9_-]{{0,31}}")
+        if key in declared:
+            raise PortfolioError(f"{cov_path}: variant_key {key!r} is repeated")
+        declared[key] = item
+    if sorted(declared) != on_disk:
+        raise PortfolioError(f"{cov_path}: variant keys {sorted(declared)} do not match the directories {on_disk}")
+    entries: list[Entry] = []
+    variants_doc = []
+    buckets: dict[str, str] = {}
+    for key, item in declared.items():
+        try:
+            expr.guard(item["guard"], where=f"guard of {key}")
+            gdig = expr.digest(item["guard"])
+        except expr.ExprError as exc:
+            raise PortfolioError(f"{cov_path}: {exc}") from exc
+        bucket = item.get("bucket_key", key)
+        if not isinstance(bucket, str) or not bucket.strip() or len(bucket) > 128:
+            raise PortfolioError(f"{cov_path}: bucket_key of {key} must be a non-empty string of at most 128 characters")
+        if buckets.setdefault(bucket, gdig) != gdig:
+            raise PortfolioError(f"{cov_path}: bucket {bucket!r} is used with two different guards")
+        data = _single_source(vdir / key, f"variant {key}")
+        path = f"variants/{key}/{SOURCE_NAME}"
+        entries.append(Entry(path, "device_kernel", "text/x-cuda", data))
+        variants_doc.append({"variant_key": key, "bucket_key": bucket, "guard": {"expr": item["guard"], "digest": gdig},
+                             "entries": [path]})
+    fb_doc, fb_data = _fallback(coverage["fallback"], root, cov_path)
+    if fb_data is not None:
+        entries.append(Entry(f"fallback/{SOURCE_NAME}", "device_kernel", "text/x-cuda", fb_data))
+    document = {
+        "schema_id": PORTFOLIO_SCHEMA_ID,
+        "domain_plan_digest": domain_digest(points),
+        "domain": [p.instance_key for p in points],
+        "planner": dict(coverage["planner"]),
+        "coverage_plan": {"buckets": [{"bucket_key": b, "guard_digest": d} for b, d in buckets.items()]},
+        "variants": variants_doc,
+        "fallback": fb_doc,
+    }
+    entries.sort(key=lambda e: e.path)
+    entries.append(Entry(PORTFOLIO_ENTRY_PATH, "launch", "application/json",
+                         json.dumps(document, indent=2, sort_keys=True).encode() + b"\n"))
+    return Parent(tuple(entries), document)
+
+
+def write_fallback(src: str | Path, task: str, dtype: str, attrs: Mapping[str, float] | None = None) -> dict[str, Any]:
+    """Materialise the registered fallback of ``task`` as ``<src>/fallback/kernel.cu`` and return the
+    coverage.json ``fallback`` stanza that names it."""
+    directory = Path(src) / "fallback"
+    directory.mkdir(parents=True, exist_ok=True)
+    (directory / SOURCE_NAME).write_text(fallbacks.render(task, dtype, attrs), encoding="utf-8")
+    return {"kind": "registered_implementation", "reasons": ["outside_candidate_coverage"],
+            "implementation_id": fallbacks.implementation_id(task), "implementation_version": fallbacks.VERSION}
+
+
+# ---- dispatch and coverage check --------------------------------------------------------------
+
+
+def to_portfolio(parent: Parent) -> Portfolio:
+    """Exact dispatch over the parent's guards (``portfolio.Portfolio``): variant ``name`` is the
+    variant_key, the fallback's name its implementation id."""
+    variants = []
+    for v in parent.document["variants"]:
+        node = expr.guard(v["guard"]["expr"], where=f"guard of {v['variant_key']}")
+        variants.append(Variant(v["variant_key"], (lambda n, node=node: expr.evaluate(node, n))))
+    fb = parent.document["fallback"]
+    fallback = None
+    if fb["kind"] == "registered_implementation":
+        fallback = Fallback(fb["implementation_id"], handles=tuple(fb["reasons"]))
+    return Portfolio(tuple(variants), fallback)
+
+
+def selected_source(parent: Parent, record: Any) -> str:
+    """The source a dispatch record selects."""
+    if record.provider == "candidate":
+        return parent.source(f"variants/{record.selected}/{SOURCE_NAME}")
+    if record.provider == "fallback":
+        return parent.source(f"fallback/{SOURCE_NAME}")
+    raise PortfolioError(f"dispatch selected nothing: {record.outcome} ({record.detail})")
+
+
+@dataclass(frozen=True)
+class CheckRow:
+    instance_key: str
+    size: str
+    usage: str
+    provider: str  # candidate | fallback | none
+    variant_key: str | None
+
+
+@dataclass(frozen=True)
+class CheckReport:
+    ok: bool
+    problems: tuple[str, ...]
+    rows: tuple[CheckRow, ...]
+    domain_plan_digest: str
+
+    def document(self) -> dict[str, Any]:
+        return {"ok": self.ok, "problems": list(self.problems), "domain_plan_digest": self.domain_plan_digest,
+                "rows": [r.__dict__ for r in self.rows]}
+
+
+def check(parent: Parent, points: Sequence[Point]) -> CheckReport:
+    """Coverage of ``points`` by the parent's guards and the projection of every used source's
+    launch block onto the points it serves (CPU only; never raises on a failed check)."""
+    from .backend import CudaBackend, parse_launch_templates
+
+    digest = domain_digest(points)
+    problems: list[str] = []
+    if parent.document.get("domain_plan_digest") != digest:
+        problems.append("the parent was packed for another domain (pack and check need the same sizes)")
+    port = to_portfolio(parent)
+    rows: list[CheckRow] = []
+    hit: set[str] = set()
+    backend = CudaBackend()
+    for p in points:
+        rec = port.resolve(p.names)
+        if rec.outcome in ("candidate", "fallback"):
+            if rec.provider == "candidate":
+                hit.add(rec.selected)
+            try:
+                stages = [t.resolve(p.names) for t in parse_launch_templates(selected_source(parent, rec))]
+                problems.extend(f"{p.instance_key}: {msg}" for msg in backend.validate_launch(stages, {}))
+            except (ValueError, expr.ExprError) as exc:
+                problems.append(f"{p.instance_key}: launch of {rec.selected} does not resolve: {exc}")
+            rows.append(CheckRow(p.instance_key, p.size, p.usage, rec.provider, rec.selected if rec.provider == "candidate" else None))
+            continue
+        if rec.outcome == "dispatch_overlap":
+            problems.append(f"{p.instance_key}: more than one variant matches ({rec.detail})")
+        elif rec.outcome == "dispatch_unknown":
+            problems.append(f"{p.instance_key}: a guard cannot be evaluated ({rec.detail})")
+        else:
+            problems.append(f"{p.instance_key}: no variant matches and there is no implementation fallback")
+        rows.append(CheckRow(p.instance_key, p.size, p.usage, "none", None))
+    for v in parent.document["variants"]:
+        if v["variant_key"] not in hit:
+            problems.append(f"{v['variant_key']}: matches no point of the domain")
+    return CheckReport(not problems, tuple(problems), tuple(rows), digest)
+
+
+# ---- measurement (GPU) --------------------------------------------------------------------------
+
+
+@dataclass
+class ShardRun:
+    point: Point
+    provider: str
+    selected: str
+    candidate_us: float
+    baseline_us: float
+    correct: bool
+    detail: str = ""
+
+
+def _time_us(fn: Callable[[], Any], reps: int, warmup: int = 3) -> float:
+    """Median device time of ``fn`` over ``reps`` CUDA-event-timed calls on the current stream."""
+    import statistics
+
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return float(statistics.median(times))
+
+
+def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], *,
+            make_inputs: Callable[[Point], Mapping[str, Any]],
+            baseline: Callable[..., Any],
+            verify: Callable[[Point, Mapping[str, Any], Mapping[str, Any]], tuple[bool, str]],
+            reps: int = 20) -> list[ShardRun]:
+    """Dispatch, build, run, verify and time every benchmark point of ``points``.
+
+    ``make_inputs(point)`` gives the input tensors (CUDA, by ABI name); outputs are allocated from
+    the opspec's dims and dtypes; ``baseline(*inputs in ABI order)`` is the task's timing baseline;
+    ``verify(point, inputs, outputs)`` returns ``(ok, detail)``."""
+    import ctypes
+
+    import torch
+
+    from .track_factory import CudaTrackBuilder, CudaTrackEvaluator
+
+    port = to_portfolio(parent)
+    builder = CudaTrackBuilder()
+    builds: dict[str, Any] = {}
+    order = symbol_order(opspec)
+    torch_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32, "i32": torch.int32}
+    runs = []
+    for p in points:
+        if p.usage != "benchmark":
+            continue
+        rec = port.resolve(p.names)
+        source = selected_source(parent, rec)
+        key = hashlib.sha256(source.encode()).hexdigest()
+        if key not in builds:
+            builds[key] = builder.build(source)
+        launch = CudaTrackEvaluator.launcher(builds[key], [ctypes.c_longlong(p.names[s]) for s in order], names=p.names)
+        inputs = make_inputs(p)
+        dtype = p.instance_key.split("/")[0]
+        outputs = {}
+        for name, t in opspec["tensors"].items():
+            if t["role"] != "output":
+                continue
+            shape = tuple(int(expr.evaluate_term(d, p.names)) for d in t["dims"])
+            dt = dtype if t["dtype"] == "T" else t["dtype"]
+            outputs[name] = torch.empty(shape, dtype=torch_dtype[dt], device="cuda")
+        ptrs = [(inputs[n] if n in inputs else outputs[n]).data_ptr() for n in opspec["tensors"]]
+        launch(ptrs)
+        torch.cuda.synchronize()
+        ok, detail = verify(p, inputs, outputs)
+        ins = [inputs[n] for n, t in opspec["tensors"].items() if t["role"] == "input"]
+        cand_us = _time_us(lambda: launch(ptrs), reps)
+        base_us = _time_us(lambda: baseline(*ins), reps)
+        runs.append(ShardRun(p, rec.provider, rec.selected, cand_us, base_us, ok, detail))
+    return runs
+
+
+def performance(runs: Sequence[ShardRun]):
+    """The reference's two accounts over the measured shards (``portfolio.PerformanceReport``)."""
+    from .portfolio import PerformanceReport, ShardMeasurement
+
+    return PerformanceReport.evaluate([
+        ShardMeasurement(r.point.instance_key, r.point.usage, r.provider, r.candidate_us, r.baseline_us, correctness_ok=r.correct)
+        for r in runs
+    ])

@@ -110,10 +110,19 @@ class CudaBuild:
             "image_sha256": self.image_sha256,
             "image_bytes": len(self.image),
             "kernels": list(self.kernels),
-            "stages": [{"kernel": s.kernel, "grid": list(s.grid), "threads": list(s.threads), "smem": s.smem} for s in self.stages],
+            "stages": [_stage_document(s) for s in self.stages],
+            "symbolic_launch": any(s.symbolic for s in self.stages),
             "flags": list(self.flags),
             "target": "sm_100a",
         }
+
+
+def _stage_document(stage: Any) -> dict[str, Any]:
+    """A launch stage for the build record: integers when literal, the expressions otherwise."""
+    if not stage.symbolic:
+        r = stage.resolve({})
+        return {"kernel": r.kernel, "grid": list(r.grid), "threads": list(r.threads), "smem": r.smem}
+    return {"kernel": stage.kernel, "grid": list(stage.grid), "threads": list(stage.threads), "smem": stage.smem}
 
 
 class CudaTrackBuilder:
@@ -133,12 +142,15 @@ class CudaTrackBuilder:
         return candidate_text(cand)
 
     def check(self, source: str) -> tuple:
-        """Screen + launch block; return the parsed stages or raise :class:`TrackRefused`."""
+        """Screen + launch block; return the launch templates (values may be expressions over the
+        task's symbols, resolved per shape at launch) or raise :class:`TrackRefused`."""
+        from .backend import parse_launch_templates
+
         problems = self._backend.screen(source)
         if problems:
             raise TrackRefused("candidate refused before compilation: " + "; ".join(problems))
         try:
-            stages = self._backend.parse_launch(source)
+            stages = parse_launch_templates(source)
         except ValueError as exc:
             raise TrackRefused(f"launch block: {exc}") from exc
         if not stages:
@@ -195,6 +207,7 @@ class EvaluationRequest:
     scalars: Sequence[Any] = ()
     output_dtypes: Mapping[str, str] = field(default_factory=dict)
     time_reps: int = 0
+    names: Mapping[str, int] = field(default_factory=dict)  # the shape's symbols, for symbolic launch values
 
 
 class CudaTrackEvaluator:
@@ -204,17 +217,20 @@ class CudaTrackEvaluator:
         self.builder = builder or CudaTrackBuilder()
 
     @staticmethod
-    def launcher(build: CudaBuild, scalars: Sequence[Any] = (), stream: int | None = None) -> Callable[[list[int]], None]:
-        """``launch(pointers)`` running every stage of the build in order on the current stream."""
+    def launcher(build: CudaBuild, scalars: Sequence[Any] = (), stream: int | None = None,
+                 names: Mapping[str, int] | None = None) -> Callable[[list[int]], None]:
+        """``launch(pointers)`` running every stage of the build in order on the current stream;
+        ``names`` (the shape's symbols) resolve symbolic launch values once, here."""
         import torch
 
         from .candidates import Module
 
+        stages = [st.resolve(names) for st in build.stages]
         module = Module(build.image)
 
         def launch(ptrs: list[int]) -> None:
             s = torch.cuda.current_stream().cuda_stream if stream is None else stream
-            for st in build.stages:
+            for st in stages:
                 module.launch(st.kernel, st.grid, st.threads, list(ptrs) + list(scalars), smem=st.smem, stream=s)
 
         launch.module = module  # keep the image loaded as long as the launcher lives
@@ -232,7 +248,7 @@ class CudaTrackEvaluator:
             return dict(report, status="compile_error", detail=str(exc))
         report["build"] = build.document()
         try:
-            launch = self.launcher(build, request.scalars)
+            launch = self.launcher(build, request.scalars, names=request.names)
             from .runtime import CorrectnessRunner
 
             runner = CorrectnessRunner(request.specs, launch, output_dtypes=request.output_dtypes)

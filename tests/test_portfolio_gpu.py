@@ -1,0 +1,138 @@
+"""Shape portfolios on the B200: the registered fallback of every task is correct, and a packed
+portfolio dispatches, runs and is timed shard by shard with real fallback time in its accounts.
+
+Tolerances are the tasks' OpSpec ones (fp16 rtol 2e-3 / atol_rel 1e-3, bf16 rtol 1.6e-2 /
+atol_rel 8e-3; reduction_sum scales by sum |x| per row, lion by its error-scale hook).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as oref
+from shapeforge_b200 import cases, compare, fallbacks
+from shapeforge_b200 import portfolio_pack as pp
+from shapeforge_b200.track_factory import CudaTrackBuilder, CudaTrackEvaluator
+from tests.test_portfolio_pack import GEMV_OPSPEC, GEMV_VEC, WIDE_GUARD, make_tree
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp16": dict(rtol=2e-3, atol_rel=1e-3), "bf16": dict(rtol=1.6e-2, atol_rel=8e-3)}
+TD = {"fp16": torch.float16, "bf16": torch.bfloat16}
+L = cases.LION_DEFAULTS
+
+
+def _np(t):
+    return t.detach().cpu().to(torch.float64).numpy()
+
+
+def _case(task, case, seed, names, dtype):
+    """(inputs by ABI name, symbol order, outputs {name: shape}, oracle outputs, scales)."""
+    if task in ("relu", "sigmoid", "sigmoid_shift", "silu", "swiglu"):
+        inp = cases.membound_inputs(task, case, seed, (names["N"],), dtype)
+        f = {k: _np(v) for k, v in inp.items()}
+        ref = {"relu": lambda: oref.relu(f["x"]), "sigmoid": lambda: oref.sigmoid(f["x"]),
+               "sigmoid_shift": lambda: oref.sigmoid_shift(f["x"]), "silu": lambda: oref.silu(f["x"]),
+               "swiglu": lambda: oref.swiglu(f["gate"], f["up"])}[task]()
+        return inp, ("N",), {"y": (names["N"],)}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    if task in ("softmax", "reduction_sum"):
+        inp = cases.membound_inputs(task, case, seed, (names["M"], names["N"]), dtype)
+        x = _np(inp["x"])
+        if task == "softmax":
+            ref = oref.softmax(x)
+            return inp, ("M", "N"), {"y": x.shape}, {"y": ref}, {"y": compare.rms_scale(ref)}
+        ref = oref.reduction_sum(x)
+        return inp, ("M", "N"), {"y": (names["M"],)}, {"y": ref}, {"y": oref.reduction_sum_error_scale(x)}
+    if task == "rmsnorm":
+        inp = cases.rmsnorm_inputs(case, seed, names["M"], names["H"], dtype)
+        ref = oref.rmsnorm(_np(inp["x"]), _np(inp["w"]), 1e-6)
+        return inp, ("M", "H"), {"y": ref.shape}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    if task in ("gemm", "gemm_silu"):
+        m, n, k = names["M"], names["N"], names["K"]
+        inp = cases.gemm_inputs(case, seed, (m, k), (k, n), dtype)
+        fn = oref.gemm_nn if task == "gemm" else oref.gemm_silu
+        ref = fn(_np(inp["A"]), _np(inp["B"]))
+        return inp, ("M", "N", "K"), {"C": (m, n)}, {"C": ref}, {"C": compare.rms_scale(ref)}
+    if task == "gemv":
+        inp = cases.gemv_inputs(case, seed, names["M"], names["K"], dtype)
+        ref = oref.gemv(_np(inp["A"]), _np(inp["x"]))
+        return inp, ("M", "K"), {"y": (names["M"],)}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    if task == "lion":
+        inp = cases.lion_inputs(case, seed, names["N"], dtype)
+        f = [_np(inp[k]) for k in ("p", "g", "m")]
+        po, mo = oref.lion(*f, L["LR"], L["WD"], L["BETA1"], L["BETA2"])
+        sp, sm = oref.lion_error_scale(*f, po, mo, L["LR"], L["BETA1"], TOL[dtype]["atol_rel"])
+        return inp, ("N",), {"p_out": (names["N"],), "m_out": (names["N"],)}, {"p_out": po, "m_out": mo}, {"p_out": sp, "m_out": sm}
+    if task == "rope":
+        shape = (names["B"], names["H"], names["S"], names["D"])
+        inp = cases.membound_inputs("rope", case, seed, shape, dtype)
+        ref = oref.rope(_np(inp["x"]), 10000.0)
+        return inp, ("B", "H", "S", "D"), {"y": shape}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    raise KeyError(task)
+
+
+SHAPES = {
+    "relu": {"N": 65537}, "sigmoid": {"N": 65536}, "sigmoid_shift": {"N": 1001}, "silu": {"N": 65536}, "swiglu": {"N": 4099},
+    "lion": {"N": 65536}, "rmsnorm": {"M": 64, "H": 512}, "softmax": {"M": 64, "N": 515}, "reduction_sum": {"M": 64, "N": 1024},
+    "gemv": {"M": 256, "K": 513}, "gemm": {"M": 130, "N": 72, "K": 128}, "gemm_silu": {"M": 64, "N": 256, "K": 128},
+    "rope": {"B": 1, "H": 2, "S": 64, "D": 64},
+}
+CASES = {"reduction_sum": ("normal", "cancel", "ieee"), "softmax": ("normal", "large", "ieee")}
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("task", fallbacks.TASKS)
+def test_registered_fallback_matches_the_oracle(cuda_device, task, dtype):
+    names = SHAPES[task]
+    build = CudaTrackBuilder().build(fallbacks.render(task, dtype))
+    for ci, case in enumerate(CASES.get(task, ("normal", "large", "ieee"))):
+        inp, order, outs, refs, scales = _case(task, case, cases.case_seed(0, ci), names, dtype)
+        inp = {k: v.to(cuda_device) for k, v in inp.items()}
+        out = {k: torch.empty(shape, dtype=TD[dtype], device=cuda_device) for k, shape in outs.items()}
+        launch = CudaTrackEvaluator.launcher(build, [ctypes.c_longlong(names[s]) for s in order], names=names)
+        launch([t.data_ptr() for t in (*inp.values(), *out.values())])
+        torch.cuda.synchronize()
+        for k, ref in refs.items():
+            tol = dict(TOL[dtype], atol_rel=3e-6) if task == "reduction_sum" else TOL[dtype]
+            v = compare.check(_np(out[k]), ref, scales[k], dtype=dtype, **tol)
+            assert v.ok, (task, case, k, v.summary())
+
+
+def test_gemv_portfolio_dispatch_run_and_accounts(cuda_device, tmp_path):
+    """paper (4096 x 4096) dispatches to the vectorised variant, small (256 x 512) to the registered
+    fallback; both are verified against the oracle and timed against torch.mv, and the report's
+    shards carry both providers with their real times."""
+    points = pp.domain(GEMV_OPSPEC, "fp16")
+    parent = pp.pack(make_tree(tmp_path, {"wide": (WIDE_GUARD, GEMV_VEC)}), points)
+    assert pp.check(parent, points).ok
+
+    def make_inputs(p):
+        return {k: v.to(cuda_device) for k, v in cases.gemv_inputs("normal", 7, p.names["M"], p.names["K"], "fp16").items()}
+
+    def verify(p, inputs, outputs):
+        ref = oref.gemv(_np(inputs["A"]), _np(inputs["x"]))
+        v = compare.check(_np(outputs["y"]), ref, compare.rms_scale(ref), dtype="fp16", **TOL["fp16"])
+        return v.ok, v.summary()
+
+    runs = pp.measure(parent, GEMV_OPSPEC, points, make_inputs=make_inputs, baseline=torch.mv, verify=verify, reps=30)
+    by_key = {r.point.instance_key: r for r in runs}
+    assert set(by_key) == {"fp16/paper/benchmark", "fp16/small/benchmark"}
+    assert by_key["fp16/paper/benchmark"].provider == "candidate" and by_key["fp16/paper/benchmark"].selected == "wide"
+    assert by_key["fp16/small/benchmark"].provider == "fallback"
+    assert by_key["fp16/small/benchmark"].selected == "cuda-sm100.fallback.gemv"
+    for r in runs:
+        assert r.correct, (r.point.instance_key, r.detail)
+        assert r.candidate_us > 0 and r.baseline_us > 0
+    report = pp.performance(runs)
+    doc = report.document()
+    assert {s["provider"] for s in doc["shards"]} == {"candidate", "fallback"}
+    if report.publishable:
+        total = sum(r.candidate_us for r in runs)
+        assert report.fallback_time_fraction == pytest.approx(by_key["fp16/small/benchmark"].candidate_us / total)
+        assert report.fallback_count_fraction == pytest.approx(0.5)
+    print(json.dumps(doc, indent=1))

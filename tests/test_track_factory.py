@@ -85,11 +85,27 @@ def test_prepare_refuses_before_the_compiler():
     for src, why in ((SILU.replace("/* taic-launch", "/* no-launch"), "no taic-launch"),
                      (SILU.replace("kernel silu_candidate", "kernel other_name"), "is not an extern"),
                      (SILU + "\n__device__ void f() { __trap(); }\n", "trap"),
-                     (SILU.replace("grid=64,1,1", "grid=x"), "launch block")):
+                     (SILU.replace("grid=64,1,1", "grid=ceil_div(64)"), "launch block"),
+                     (SILU.replace("grid=64,1,1", "grid=eq(N,1)"), "launch block")):
         with pytest.raises(tf.TrackRefused, match=why):
             b.prepare(src)
     with pytest.raises(tf.TrackRefused, match="exactly one device_kernel"):
         b.prepare(SimpleNamespace(candidate=SimpleNamespace(entries=())))
+
+
+def test_symbolic_launch_values_resolve_per_shape():
+    """Launch values may be expressions over the task's symbols (the portfolio geometry
+    language); they are checked at prepare and resolved per shape at launch."""
+    from shapeforge_b200.backend import parse_launch_templates
+
+    src = SILU.replace("grid=64,1,1", "grid=ceil_div(N,256)")
+    tf.CudaTrackBuilder().prepare(src)
+    (tpl,) = parse_launch_templates(src)
+    assert tpl.symbolic
+    assert tpl.resolve({"N": 16384}).grid == (64, 1, 1)
+    assert tpl.resolve({"N": 16385}).grid == (65, 1, 1)
+    with pytest.raises(Exception, match="not declared"):
+        tpl.resolve({})
 
 
 def test_reference_candidate_artifact_is_read():
