@@ -76,6 +76,25 @@ class Module:
         _native.call("sf_launch_kernel", self.function(name), *[int(v) for v in g], *[int(v) for v in b], int(smem),
                      ctypes.c_void_p(stream), argv)
 
+    def bind(self, name: str, grid, block, args: Sequence[object], smem: int = 0, stream: int = 0):
+        """A zero-argument callable enqueueing this launch: the argument array is marshalled once,
+        so a call costs one C call (timing loops of short kernels stay device-bound)."""
+        holders = [a if isinstance(a, ctypes._SimpleCData) else ctypes.c_void_p(int(a)) for a in args]
+        argv = (ctypes.c_void_p * len(holders))(*[ctypes.cast(ctypes.pointer(h), ctypes.c_void_p) for h in holders])
+        g = [int(v) for v in tuple(grid) + (1,) * (3 - len(tuple(grid)))]
+        b = [int(v) for v in tuple(block) + (1,) * (3 - len(tuple(block)))]
+        fn, lib = self.function(name), _native.load()
+        err = ctypes.create_string_buffer(_native.ERR_CAP)
+        st = ctypes.c_void_p(stream)
+
+        def launch() -> None:
+            rc = lib.sf_launch_kernel(fn, *g, *b, int(smem), st, argv, err, _native.ERR_CAP)
+            if rc != _native.SF_OK:
+                raise _native.SfError(rc, err.value.decode(errors="replace"))
+
+        launch.keep = (holders, argv, self)  # the marshalled arguments live as long as the callable
+        return launch
+
     def close(self) -> None:
         if self.handle:
             _native.call("sf_module_unload", self.handle)

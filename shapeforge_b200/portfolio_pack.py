@@ -396,33 +396,26 @@ class ShardRun:
     baseline_us: float
     correct: bool
     detail: str = ""
+    timing_uncertain: bool = False
 
 
-def _time_us(fn: Callable[[], Any], reps: int, warmup: int = 3) -> float:
-    """Median device time of ``fn`` over ``reps`` CUDA-event-timed calls on the current stream."""
-    import statistics
+def _timed(candidate: Callable[[], Any], baseline: Callable[[], Any], reps: int) -> tuple[float, float, bool]:
+    """Per-launch device microseconds of candidate and baseline through the harness timing
+    protocol (``protocol.measure_interleaved``: batches sized to ~15 ms, interleaved repetitions,
+    up to three attempts); the flag is True when the kept attempt was noisy (CV > 5 %)."""
+    from . import protocol
 
-    import torch
-
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    times = []
-    for _ in range(reps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        b.synchronize()
-        times.append(a.elapsed_time(b) * 1e3)
-    return float(statistics.median(times))
+    runners = {"candidate": protocol.cuda_event_runner(lambda i: candidate()),
+               "baseline": protocol.cuda_event_runner(lambda i: baseline())}
+    noise, stats, _ = protocol.measure_interleaved(runners, reps=reps)
+    return stats["candidate"].median_s * 1e6, stats["baseline"].median_s * 1e6, noise > protocol.NOISY_CV
 
 
 def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], *,
             make_inputs: Callable[[Point], Mapping[str, Any]],
             baseline: Callable[..., Any],
             verify: Callable[[Point, Mapping[str, Any], Mapping[str, Any]], tuple[bool, str]],
-            reps: int = 20) -> list[ShardRun]:
+            reps: int = 15) -> list[ShardRun]:
     """Dispatch, build, run, verify and time every benchmark point of ``points``.
 
     ``make_inputs(point)`` gives the input tensors (CUDA, by ABI name); outputs are allocated from
@@ -432,7 +425,8 @@ def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], 
 
     import torch
 
-    from .track_factory import CudaTrackBuilder, CudaTrackEvaluator
+    from .candidates import Module
+    from .track_factory import CudaTrackBuilder
 
     port = to_portfolio(parent)
     builder = CudaTrackBuilder()
@@ -448,7 +442,6 @@ def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], 
         key = hashlib.sha256(source.encode()).hexdigest()
         if key not in builds:
             builds[key] = builder.build(source)
-        launch = CudaTrackEvaluator.launcher(builds[key], [ctypes.c_longlong(p.names[s]) for s in order], names=p.names)
         inputs = make_inputs(p)
         dtype = p.instance_key.split("/")[0]
         outputs = {}
@@ -459,13 +452,22 @@ def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], 
             dt = dtype if t["dtype"] == "T" else t["dtype"]
             outputs[name] = torch.empty(shape, dtype=torch_dtype[dt], device="cuda")
         ptrs = [(inputs[n] if n in inputs else outputs[n]).data_ptr() for n in opspec["tensors"]]
-        launch(ptrs)
+        stream = torch.cuda.current_stream().cuda_stream
+        module = Module(builds[key].image)
+        bound = [module.bind(st.kernel, st.grid, st.threads, ptrs + [ctypes.c_longlong(p.names[s]) for s in order],
+                             smem=st.smem, stream=stream)
+                 for st in (t.resolve(p.names) for t in builds[key].stages)]
+
+        def run(bound=bound) -> None:
+            for b in bound:
+                b()
+
+        run()
         torch.cuda.synchronize()
         ok, detail = verify(p, inputs, outputs)
         ins = [inputs[n] for n, t in opspec["tensors"].items() if t["role"] == "input"]
-        cand_us = _time_us(lambda: launch(ptrs), reps)
-        base_us = _time_us(lambda: baseline(*ins), reps)
-        runs.append(ShardRun(p, rec.provider, rec.selected, cand_us, base_us, ok, detail))
+        cand_us, base_us, noisy = _timed(run, lambda ins=ins: baseline(*ins), reps)
+        runs.append(ShardRun(p, rec.provider, rec.selected, cand_us, base_us, ok, detail, noisy))
     return runs
 
 
@@ -474,6 +476,7 @@ def performance(runs: Sequence[ShardRun]):
     from .portfolio import PerformanceReport, ShardMeasurement
 
     return PerformanceReport.evaluate([
-        ShardMeasurement(r.point.instance_key, r.point.usage, r.provider, r.candidate_us, r.baseline_us, correctness_ok=r.correct)
+        ShardMeasurement(r.point.instance_key, r.point.usage, r.provider, r.candidate_us, r.baseline_us,
+                         timing_uncertain=r.timing_uncertain, correctness_ok=r.correct)
         for r in runs
     ])

@@ -119,7 +119,7 @@ def test_gemv_portfolio_dispatch_run_and_accounts(cuda_device, tmp_path):
         v = compare.check(_np(outputs["y"]), ref, compare.rms_scale(ref), dtype="fp16", **TOL["fp16"])
         return v.ok, v.summary()
 
-    runs = pp.measure(parent, GEMV_OPSPEC, points, make_inputs=make_inputs, baseline=torch.mv, verify=verify, reps=30)
+    runs = pp.measure(parent, GEMV_OPSPEC, points, make_inputs=make_inputs, baseline=torch.mv, verify=verify, reps=15)
     by_key = {r.point.instance_key: r for r in runs}
     assert set(by_key) == {"fp16/paper/benchmark", "fp16/small/benchmark"}
     assert by_key["fp16/paper/benchmark"].provider == "candidate" and by_key["fp16/paper/benchmark"].selected == "wide"
