@@ -30,13 +30,24 @@ class CandidateCompileError(RuntimeError):
         self.log = log
 
 
-def compile_source(source: str, extra_flags: Sequence[str] = (), name: str = "candidate") -> bytes:
-    """Compile ``source`` to an sm_100a cubin (cached) and return the image bytes."""
-    flags = [*ARCH, "-O3", "-std=c++17", "-cubin", *extra_flags]
-    key = hashlib.sha256((source + "\0" + " ".join(flags)).encode()).hexdigest()[:24]
+def _flags(extra_flags: Sequence[str]) -> list[str]:
+    return [*ARCH, "-O3", "-std=c++17", "-cubin", *extra_flags]
+
+
+def cache_path(source: str, extra_flags: Sequence[str] = (), name: str = "candidate") -> Path:
+    """Where the cubin of ``source`` built with ``extra_flags`` is cached (hash of source + flags)."""
+    key = hashlib.sha256((source + "\0" + " ".join(_flags(extra_flags))).encode()).hexdigest()[:24]
+    return CACHE / f"{name}-{key}.cubin"
+
+
+def compile_source(source: str, extra_flags: Sequence[str] = (), name: str = "candidate", use_cache: bool = True) -> bytes:
+    """Compile ``source`` to an sm_100a cubin and return the image bytes.  Images are cached by the
+    hash of source + flags; ``use_cache=False`` always runs nvcc (a fresh build, as a confirmation
+    requires) and refreshes the cached copy."""
+    flags = _flags(extra_flags)
     CACHE.mkdir(parents=True, exist_ok=True)
-    out = CACHE / f"{name}-{key}.cubin"
-    if out.is_file():
+    out = cache_path(source, extra_flags, name)
+    if use_cache and out.is_file():
         return out.read_bytes()
     with tempfile.TemporaryDirectory() as d:
         src = Path(d) / f"{name}.cu"

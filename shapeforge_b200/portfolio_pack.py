@@ -397,30 +397,33 @@ class ShardRun:
     correct: bool
     detail: str = ""
     timing_uncertain: bool = False
+    candidate_cv: float = 0.0
+    baseline_cv: float = 0.0
+    attempts: int = 0
+    source_sha256: str = ""
+    cache_hit: bool = False
 
 
-def _timed(candidate: Callable[[], Any], baseline: Callable[[], Any], reps: int) -> tuple[float, float, bool]:
+def _timed(candidate: Callable[[], Any], baseline: Callable[[], Any], reps: int):
     """Per-launch device microseconds of candidate and baseline through the harness timing
     protocol (``protocol.measure_interleaved``: batches sized to ~15 ms, interleaved repetitions,
-    up to three attempts); the flag is True when the kept attempt was noisy (CV > 5 %)."""
+    up to three attempts).  Returns (candidate stats, baseline stats, noisy, attempts); noisy is
+    True when the kept attempt's CV is above 5 %."""
     from . import protocol
 
     runners = {"candidate": protocol.cuda_event_runner(lambda i: candidate()),
                "baseline": protocol.cuda_event_runner(lambda i: baseline())}
-    noise, stats, _ = protocol.measure_interleaved(runners, reps=reps)
-    return stats["candidate"].median_s * 1e6, stats["baseline"].median_s * 1e6, noise > protocol.NOISY_CV
+    noise, stats, attempts = protocol.measure_interleaved(runners, reps=reps)
+    return stats["candidate"], stats["baseline"], noise > protocol.NOISY_CV, attempts
 
 
-def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], *,
-            make_inputs: Callable[[Point], Mapping[str, Any]],
-            baseline: Callable[..., Any],
-            verify: Callable[[Point, Mapping[str, Any], Mapping[str, Any]], tuple[bool, str]],
-            reps: int = 15) -> list[ShardRun]:
-    """Dispatch, build, run, verify and time every benchmark point of ``points``.
-
-    ``make_inputs(point)`` gives the input tensors (CUDA, by ABI name); outputs are allocated from
-    the opspec's dims and dtypes; ``baseline(*inputs in ABI order)`` is the task's timing baseline;
-    ``verify(point, inputs, outputs)`` returns ``(ok, detail)``."""
+def run_point(parent: Parent, opspec: Mapping[str, Any], point: Point, inputs: Mapping[str, Any], *,
+              baseline: Callable[..., Any] | None,
+              verify: Callable[[Point, Mapping[str, Any], Mapping[str, Any]], tuple[bool, str]],
+              reps: int = 15, use_cache: bool = True, builds: dict[str, Any] | None = None) -> ShardRun:
+    """Dispatch ``point``, build the selected source (``use_cache=False``: a fresh nvcc build), run
+    it once on ``inputs`` (CUDA tensors by ABI name; outputs are allocated from the opspec), verify,
+    and — with a ``baseline`` — time candidate and baseline through the interleaved protocol."""
     import ctypes
 
     import torch
@@ -428,47 +431,57 @@ def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], 
     from .candidates import Module
     from .track_factory import CudaTrackBuilder
 
-    port = to_portfolio(parent)
-    builder = CudaTrackBuilder()
-    builds: dict[str, Any] = {}
-    order = symbol_order(opspec)
+    rec = to_portfolio(parent).resolve(point.names)
+    source = selected_source(parent, rec)
+    key = hashlib.sha256(source.encode()).hexdigest()
+    builds = {} if builds is None else builds
+    if key not in builds or not use_cache:
+        builds[key] = CudaTrackBuilder().build(source, use_cache=use_cache)
+    build = builds[key]
+    dtype = point.instance_key.split("/")[0]
     torch_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32, "i32": torch.int32}
-    runs = []
-    for p in points:
-        if p.usage != "benchmark":
+    outputs = {}
+    for name, t in opspec["tensors"].items():
+        if t["role"] != "output":
             continue
-        rec = port.resolve(p.names)
-        source = selected_source(parent, rec)
-        key = hashlib.sha256(source.encode()).hexdigest()
-        if key not in builds:
-            builds[key] = builder.build(source)
-        inputs = make_inputs(p)
-        dtype = p.instance_key.split("/")[0]
-        outputs = {}
-        for name, t in opspec["tensors"].items():
-            if t["role"] != "output":
-                continue
-            shape = tuple(int(expr.evaluate_term(d, p.names)) for d in t["dims"])
-            dt = dtype if t["dtype"] == "T" else t["dtype"]
-            outputs[name] = torch.empty(shape, dtype=torch_dtype[dt], device="cuda")
-        ptrs = [(inputs[n] if n in inputs else outputs[n]).data_ptr() for n in opspec["tensors"]]
-        stream = torch.cuda.current_stream().cuda_stream
-        module = Module(builds[key].image)
-        bound = [module.bind(st.kernel, st.grid, st.threads, ptrs + [ctypes.c_longlong(p.names[s]) for s in order],
-                             smem=st.smem, stream=stream)
-                 for st in (t.resolve(p.names) for t in builds[key].stages)]
+        shape = tuple(int(expr.evaluate_term(d, point.names)) for d in t["dims"])
+        outputs[name] = torch.empty(shape, dtype=torch_dtype[dtype if t["dtype"] == "T" else t["dtype"]], device="cuda")
+    ptrs = [(inputs[n] if n in inputs else outputs[n]).data_ptr() for n in opspec["tensors"]]
+    stream = torch.cuda.current_stream().cuda_stream
+    module = Module(build.image)
+    scalars = [ctypes.c_longlong(point.names[s]) for s in symbol_order(opspec)]
+    bound = [module.bind(st.kernel, st.grid, st.threads, ptrs + scalars, smem=st.smem, stream=stream)
+             for st in (t.resolve(point.names) for t in build.stages)]
 
-        def run(bound=bound) -> None:
-            for b in bound:
-                b()
+    def run() -> None:
+        for b in bound:
+            b()
 
-        run()
-        torch.cuda.synchronize()
-        ok, detail = verify(p, inputs, outputs)
+    run()
+    torch.cuda.synchronize()
+    ok, detail = verify(point, inputs, outputs)
+    shard = ShardRun(point, rec.provider, rec.selected, 0.0, 0.0, ok, detail, source_sha256=key, cache_hit=build.cache_hit)
+    if baseline is not None:
         ins = [inputs[n] for n, t in opspec["tensors"].items() if t["role"] == "input"]
-        cand_us, base_us, noisy = _timed(run, lambda ins=ins: baseline(*ins), reps)
-        runs.append(ShardRun(p, rec.provider, rec.selected, cand_us, base_us, ok, detail, noisy))
-    return runs
+        cand, base, noisy, attempts = _timed(run, lambda: baseline(*ins), reps)
+        shard.candidate_us, shard.baseline_us = cand.median_s * 1e6, base.median_s * 1e6
+        shard.candidate_cv, shard.baseline_cv = cand.cv, base.cv
+        shard.timing_uncertain, shard.attempts = noisy, attempts
+    return shard
+
+
+def measure(parent: Parent, opspec: Mapping[str, Any], points: Sequence[Point], *,
+            make_inputs: Callable[[Point], Mapping[str, Any]],
+            baseline: Callable[..., Any],
+            verify: Callable[[Point, Mapping[str, Any], Mapping[str, Any]], tuple[bool, str]],
+            reps: int = 15) -> list[ShardRun]:
+    """``run_point`` over every benchmark point of ``points`` (one build per distinct source).
+
+    ``make_inputs(point)`` gives the input tensors (CUDA, by ABI name); ``baseline(*inputs in ABI
+    order)`` is the task's timing baseline; ``verify(point, inputs, outputs)`` returns ``(ok, detail)``."""
+    builds: dict[str, Any] = {}
+    return [run_point(parent, opspec, p, make_inputs(p), baseline=baseline, verify=verify, reps=reps, builds=builds)
+            for p in points if p.usage == "benchmark"]
 
 
 def performance(runs: Sequence[ShardRun]):

@@ -103,6 +103,7 @@ class CudaBuild:
     kernels: tuple[str, ...]
     stages: tuple[Any, ...]
     flags: tuple[str, ...]
+    cache_hit: bool = False  # the image came from the cubin cache, not from this build
 
     def document(self) -> dict[str, Any]:
         return {
@@ -114,6 +115,7 @@ class CudaBuild:
             "symbolic_launch": any(s.symbolic for s in self.stages),
             "flags": list(self.flags),
             "target": "sm_100a",
+            "cache_hit": self.cache_hit,
         }
 
 
@@ -164,8 +166,9 @@ class CudaTrackBuilder:
         """Every check that needs no compiler and no device."""
         self.check(self._request_source(request))
 
-    def build(self, request: Any) -> CudaBuild:
-        """Compile once for sm_100a; a compiler failure raises ``CudaCompileError`` with the log."""
+    def build(self, request: Any, use_cache: bool = True) -> CudaBuild:
+        """Compile once for sm_100a; a compiler failure raises ``CudaCompileError`` with the log.
+        ``use_cache=False`` forces nvcc to run (``CudaBuild.cache_hit`` is then False)."""
         from .backend import CudaCompileError
         from .candidates import CandidateCompileError, compile_source
 
@@ -173,7 +176,10 @@ class CudaTrackBuilder:
         stages = self.check(source)
         flags = ("-lineinfo",) + self.extra_flags
         try:
-            image = compile_source(source, extra_flags=flags, name="track")
+            from .candidates import cache_path
+
+            cache_hit = use_cache and cache_path(source, flags, "track").is_file()
+            image = compile_source(source, extra_flags=flags, name="track", use_cache=use_cache)
         except CandidateCompileError as exc:
             raise CudaCompileError(f"{exc}\n{exc.log}") from exc
         kernels = tuple(dict.fromkeys(s.kernel for s in stages))
@@ -184,6 +190,7 @@ class CudaTrackBuilder:
             kernels=kernels,
             stages=stages,
             flags=flags,
+            cache_hit=cache_hit,
         )
 
 

@@ -136,3 +136,37 @@ def test_gemv_portfolio_dispatch_run_and_accounts(cuda_device, tmp_path):
         assert report.fallback_time_fraction == pytest.approx(by_key["fp16/small/benchmark"].candidate_us / total)
         assert report.fallback_count_fraction == pytest.approx(0.5)
     print(json.dumps(doc, indent=1))
+
+
+def test_gemv_portfolio_fresh_confirmation_and_publication(cuda_device, tmp_path):
+    """Each point runs twice from a fresh nvcc build: on the search seed and on its fresh seed.
+    Every subject is then correct on both runs, and a fully confirmed, publishable portfolio
+    lands in the catalog with subjects that re-verify.  Timing noise is a legitimate rejection
+    (the reference's rule); every other reason is a failure."""
+    from shapeforge_b200 import confirmation as cf
+
+    points = pp.domain(GEMV_OPSPEC, "fp16")
+    parent = pp.pack(make_tree(tmp_path / "src", {"wide": (WIDE_GUARD, GEMV_VEC)}), points)
+
+    def make_inputs(p, seed):
+        return {k: v.to(cuda_device) for k, v in cases.gemv_inputs("normal", seed, p.names["M"], p.names["K"], "fp16").items()}
+
+    def verify(p, inputs, outputs):
+        ref = oref.gemv(_np(inputs["A"]), _np(inputs["x"]))
+        v = compare.check(_np(outputs["y"]), ref, compare.rms_scale(ref), dtype="fp16", **TOL["fp16"])
+        return v.ok, v.summary()
+
+    runs, subjects = cf.confirm(parent, GEMV_OPSPEC, points, make_inputs=make_inputs, baseline=torch.mv, verify=verify,
+                                master_seed=20260101)
+    assert len(subjects) == 4 and len(runs) == 2
+    for s in subjects:
+        assert s["search_report"]["status"] == "ok" and s["confirmation_report"]["status"] == "ok", s["instance_key"]
+        assert s["search_report"]["cache_hit"] is False and s["confirmation_report"]["seed"] != cf.SEARCH_SEED
+        assert s["status"] == "confirmed" or s["reason"] == "timing_uncertain", (s["instance_key"], s["reason"])
+    if all(s["status"] == "confirmed" for s in subjects) and pp.performance(runs).publishable:
+        out = cf.publish(tmp_path / "kernels", "gemv", "fp16", parent, runs, subjects)
+        manifest = json.loads((out / "manifest.json").read_text())
+        assert len(manifest["subjects"]) == 4
+        for f in (out / "subjects").iterdir():
+            cf.verify_subject(json.loads(f.read_text()))
+        print(json.dumps(manifest, indent=1))
