@@ -16,7 +16,8 @@ Two sources, both produced by the reference itself:
   harness case seeds ``seed + 7919 * (i + 1)`` (``tcenv/backends/metal/v2_runtime.py:1602``), rounded
   to storage dtype, and the task's fp64 ``reference`` outputs, for bitdelta_gemm,
   flash_attention, rope, varlen_kda, mamba2_chunk_scan, relu, sigmoid, sigmoid_shift, lion, gemv,
-  gemm_silu and kda (fixed length, sizes single/small/tail).  Where the task module has an ``error_scale`` hook (lion) the recorded scales are
+  gemm_silu and kda (fixed length, sizes single/small/tail); varlen_kda also at its L2 capacity
+  size (capacity-sized inputs with the padding poison, the cu_seqlens sentinel tail).  Where the task module has an ``error_scale`` hook (lion) the recorded scales are
   the hook's, otherwise the RMS of the finite reference.
 
 ``python tests/golden/make_fixtures.py relu lion`` rewrites only the named tasks' fixtures.
@@ -355,6 +356,8 @@ def main(only=()) -> None:
             for dtype in ("fp16", "bf16"):
                 if task == "kda":
                     outs.extend(_kda_fixed(dtype))
+                elif task == "varlen_kda_capacity":
+                    outs.append(write(from_reference("varlen_kda", dtype, "capacity"), f"ref_varlen_kda_capacity_{dtype}"))
                 else:
                     outs.append(_new_task(task, dtype))
         for p in outs:
@@ -373,7 +376,7 @@ def main(only=()) -> None:
         outs.append(write(from_reference("flash_attention", dtype, "small", _fa_slice), f"ref_flash_attention_{dtype}"))
         outs.append(write(from_reference("rope", dtype, "small", _rope_slice), f"ref_rope_{dtype}"))
         outs.append(write(from_reference("mamba2_chunk_scan", dtype, "small", _mamba2_slice), f"ref_mamba2_chunk_scan_{dtype}"))
-        for size in ("mixed", "fixed", "uniform"):
+        for size in ("mixed", "fixed", "uniform", "capacity"):
             outs.append(write(from_reference("varlen_kda", dtype, size), f"ref_varlen_kda_{size}_{dtype}"))
         for task in NEW_TASKS:
             outs.append(_new_task(task, dtype))

@@ -268,3 +268,41 @@ def test_fixed_kda_against_oracle(cuda_device, dtype, shape):
             v2 = compare.check(_np(fin), ref_fin, compare.rms_scale(ref_fin), dtype="fp32", **FIXED_TOL[dtype])
             assert v1.ok, (shape, case, variant, "output", v1.summary())
             assert v2.ok, (shape, case, variant, "final_state", v2.summary())
+
+
+# ---- L2 capacity tier: continuous batching on one set of buffers ------------------------------------
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_capacity_tier_continuous_batching(cuda_device, dtype):
+    """The nine reference cases of the capacity size, in declared order, through ONE set of
+    capacity-sized buffers (a continuous-batching sequence of totals 16, 1, 9, 3, 16, ...): each
+    call's boundary is checked against the contract, its logical region matches the reference, and
+    every padding byte of both outputs still holds the poison after the call.  Then the timed
+    mixture covers every declared profile (``mixture_problems`` is empty)."""
+    from shapeforge_b200 import capacity as cap
+    from tests.test_capacity import CAPACITY_SIZE, CASES
+
+    doc = golden.load(f"ref_varlen_kda_capacity_{dtype}")
+    tdt = doc["tensor_dtypes"]
+    s = cap.CapacitySpec.from_size(CAPACITY_SIZE)
+    batch = cap.CapacityBatch(s, 2, 8, TD[dtype], cuda_device)
+    names = ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "scale")
+    per_case = {}
+    for rec in doc["records"]:
+        d = {k: _from_fixture(v, tdt[k], cuda_device) for k, v in rec["inputs"].items()}
+        cu = [int(v) for v in rec["inputs"]["cu_seqlens"]]
+        inputs = {k: d[k] for k in names}
+        per_case[rec["case"]] = (inputs, cu)
+        resolved = batch.run(inputs, cu=cu)
+        torch.cuda.synchronize()
+        assert batch.check_padding(resolved) == (), rec["case"]
+        ro = rec["refs"]["output"][resolved.logical("output")]
+        rf = rec["refs"]["final_state"][resolved.logical("final_state")]
+        v1 = _verdict(_np(batch.output[resolved.logical("output")]), ro, dtype, dtype)
+        v2 = _verdict(_np(batch.final_state[resolved.logical("final_state")]), rf, dtype, "fp32")
+        assert v1.ok, (rec["case"], "output", v1.summary())
+        assert v2.ok, (rec["case"], "final_state", v2.summary())
+    batches = cap.time_mixture(batch, s, CASES, lambda case: per_case[case], reps=5)
+    assert cap.mixture_problems(s, CASES, batches) == ()
+    assert all(b["device_us"] > 0 for b in batches)
