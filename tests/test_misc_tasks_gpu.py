@@ -170,7 +170,10 @@ def test_lion_cases_against_oracle(cuda_device, dtype):
             assert vm.ok, (n, case, "m_out", vm.summary())
 
 
-GEMV_SHAPES = [(4096, 4096), (256, 512), (1, 8), (7, 13), (300, 1000), (33, 2056), (2, 65536)]
+# Aligned K % 8 == 0 shapes take the vector kernel (including a ragged row count and K = 8 / 8192);
+# the rest take the scalar loop.
+GEMV_SHAPES = [(4096, 4096), (1501, 8192), (1024, 8), (2048, 2056), (256, 512), (1, 8), (7, 13), (300, 1000), (33, 2056),
+               (2, 65536)]
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
@@ -183,6 +186,20 @@ def test_gemv_cases_against_oracle(cuda_device, dtype):
             ref = oref.gemv(_np(inp["A"]), _np(inp["x"]))
             v = compare.check(_np(y), ref, compare.rms_scale(ref), dtype=dtype, **TOL[dtype])
             assert v.ok, ((m, k), case, v.summary())
+
+
+def test_gemv_kernels_agree(cuda_device):
+    """The vector kernel (variants 0 and 1) and the scalar loop (variant 2) meet the tolerance on
+    the same inputs (the ieee case: specials planted in A)."""
+    inp = {k: v.to(cuda_device) for k, v in cases.gemv_inputs("ieee", 31, 4096, 4096, "bf16").items()}
+    ref = oref.gemv(_np(inp["A"]), _np(inp["x"]))
+    for variant in (0, 1, 2):
+        y = ops.gemv(inp["A"], inp["x"], variant=variant)
+        torch.cuda.synchronize()
+        v = compare.check(_np(y), ref, compare.rms_scale(ref), dtype="bf16", **TOL["bf16"])
+        assert v.ok, (variant, v.summary())
+    code, where = ops.kernel_status()
+    assert code == 0, (code, where)
 
 
 def test_gemv_unaligned_and_k_zero(cuda_device):
