@@ -1,6 +1,6 @@
 """Fresh confirmation of a portfolio's shards, and publication into a ``kernels/b200`` catalog.
 
-A shard's search result (the candidate judged on the search seed's inputs) counts only after an
+A shard's search result (the candidate evaluated on the search seed's inputs) counts only after an
 independent confirmation: the same source rebuilt without the cubin cache, run on inputs from a
 fresh seed, verified again and timed again.  The verdict rules restate the subject confirmation
 of taic/portfolio_confirmation.py:66-116 (``_subject_verdict``):

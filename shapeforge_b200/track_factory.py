@@ -103,7 +103,7 @@ class CudaBuild:
     kernels: tuple[str, ...]
     stages: tuple[Any, ...]
     flags: tuple[str, ...]
-    cache_hit: bool = False  # the image came from the cubin cache, not from this build
+    cache_hit: bool = False  # the image came from the cubin cache rather than from an nvcc run
 
     def document(self) -> dict[str, Any]:
         return {
