@@ -493,3 +493,48 @@ def performance(runs: Sequence[ShardRun]):
                          timing_uncertain=r.timing_uncertain, correctness_ok=r.correct)
         for r in runs
     ])
+
+
+# ---- command line ---------------------------------------------------------------------------------
+
+
+def main(argv: Sequence[str] | None = None) -> int:
+    """``python -m shapeforge_b200.portfolio_pack pack|check`` (the reference's ``portfolio-pack`` /
+    ``portfolio-check`` commands for CUDA sources).
+
+    ``pack SRC --task-dir T --dtype D [--sizes a,b] --out PARENT.json`` validates the tree and writes
+    the parent; ``check PARENT.json --task-dir T --dtype D [--sizes a,b]`` prints the coverage report
+    as JSON and exits 1 when it has problems."""
+    import argparse
+    import sys
+
+    ap = argparse.ArgumentParser(prog="python -m shapeforge_b200.portfolio_pack")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    for name in ("pack", "check"):
+        p = sub.add_parser(name)
+        p.add_argument("path", help="source tree (pack) or parent JSON (check)")
+        p.add_argument("--task-dir", required=True, help="directory holding the task's opspec.json")
+        p.add_argument("--dtype", required=True, choices=("fp16", "bf16"))
+        p.add_argument("--sizes", default=None, help="comma-separated sizes (default: every declared size)")
+        if name == "pack":
+            p.add_argument("--out", required=True)
+    args = ap.parse_args(argv)
+    points = domain(load_opspec(args.task_dir), args.dtype, args.sizes.split(",") if args.sizes else None)
+    try:
+        if args.cmd == "pack":
+            parent = pack(args.path, points)
+            Path(args.out).write_text(parent.to_json() + "\n", encoding="utf-8")
+            print(json.dumps({"parent_sha256": parent.sha256, "domain_plan_digest": parent.document["domain_plan_digest"],
+                              "variants": [v["variant_key"] for v in parent.document["variants"]]}))
+            return 0
+        parent = Parent.from_json(Path(args.path).read_text(encoding="utf-8"))
+        report = check(parent, points)
+        print(json.dumps(report.document(), indent=1))
+        return 0 if report.ok else 1
+    except PortfolioError as exc:
+        print(f"portfolio: {exc}", file=sys.stderr)
+        return 2
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -285,3 +285,26 @@ def test_fallback_attributes_are_rendered():
     src = fallbacks.render("lion", "bf16", {"LR": 0.5})
     assert "#define ATTR_LR (0.5)" in src and "#define ATTR_BETA2 (0.99)" in src
     assert "typedef __nv_bfloat16 T;" in src
+
+
+def test_command_line_pack_and_check(tmp_path):
+    import subprocess
+    import sys
+
+    root = Path(__file__).resolve().parents[1]
+    (tmp_path / "task").mkdir()
+    (tmp_path / "task" / "opspec.json").write_text(json.dumps(GEMV_OPSPEC))
+    src = make_tree(tmp_path / "src", {"wide": (WIDE_GUARD, GEMV_VEC)})
+    run = lambda *a: subprocess.run([sys.executable, "-m", "shapeforge_b200.portfolio_pack", *a], capture_output=True,  # noqa: E731
+                                    text=True, cwd=root, timeout=120)
+    out = tmp_path / "parent.json"
+    r = run("pack", str(src), "--task-dir", str(tmp_path / "task"), "--dtype", "fp16", "--out", str(out))
+    assert r.returncode == 0, r.stderr
+    assert json.loads(r.stdout)["variants"] == ["wide"]
+    r = run("check", str(out), "--task-dir", str(tmp_path / "task"), "--dtype", "fp16")
+    assert r.returncode == 0 and json.loads(r.stdout)["ok"] is True
+    r = run("check", str(out), "--task-dir", str(tmp_path / "task"), "--dtype", "fp16", "--sizes", "paper")
+    assert r.returncode == 1 and "another domain" in r.stdout
+    (src / "variants" / "stray").mkdir()
+    r = run("pack", str(src), "--task-dir", str(tmp_path / "task"), "--dtype", "fp16", "--out", str(out))
+    assert r.returncode == 2 and "do not match" in r.stderr
