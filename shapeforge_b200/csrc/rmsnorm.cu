@@ -3,6 +3,9 @@
 // Semantics follow tasks/rmsnorm/reference.py:110-115 (fp64 oracle, one rounding at the output)
 // and opspec.json:5 (fp32 accumulation).  The op is HBM-bound: 2*R*H bytes of x and y plus
 // 2*H of w per call, ~1 flop/byte.  Design:
+//   * rows of at most 1024 elements (hidden % 8 == 0, aligned): one warp per row, shuffle-only
+//     reduction (rmsnorm_warp_kernel): a CTA and two barriers per 2 KB row made 4096 x 1024 run at
+//     half of HBM bandwidth;
 //   * fast path (hidden % 8 == 0, 16-byte aligned bases): one CTA per row, each thread keeps
 //     NV 128-bit vectors of the row in registers, so x is read from HBM exactly once; the
 //     sum of squares is a warp-shuffle + shared-memory reduction in fp32; w is read through
@@ -10,6 +13,8 @@
 //   * general path (any hidden, any alignment): one CTA per row, two strided passes (the
 //     second pass re-reads the row from L1/L2).
 #include "sf_common.cuh"
+
+#include <algorithm>
 
 namespace {
 
@@ -71,6 +76,67 @@ __global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const T* __restrict__
     }
 }
 
+// Rows of at most 1024 elements: one warp per row, NVW 16-byte vectors per lane held packed in
+// registers, the sum of squares reduced with shuffles only (no shared memory, no CTA barrier); a
+// row's x loads are issued before its w loads (w stays in L1/L2).  Rows are visited
+// grid-stride by the warps of a single wave of 8-warp CTAs.
+template <typename T, int NVW>
+__global__ void __launch_bounds__(256) rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                                                           int64_t rows, int64_t hidden, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nvec = hidden >> 3;
+    const int64_t wstride = (int64_t)gridDim.x * 8;
+    for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += wstride) {
+        const T* xr = x + row * hidden;
+        sf::Vec8<T> v[NVW], wv[NVW];
+        // x first (HBM), then w (L1/L2-resident): w's latency overlaps x's instead of preceding it.
+#pragma unroll
+        for (int i = 0; i < NVW; ++i) {
+            const int64_t idx = lane + 32 * i;
+            if (idx < nvec) v[i] = sf::ld_global_nc_v8<T>(xr + idx * 8);
+        }
+#pragma unroll
+        for (int i = 0; i < NVW; ++i) {
+            const int64_t idx = lane + 32 * i;
+            if (idx < nvec) wv[i] = *reinterpret_cast<const sf::Vec8<T>*>(w + idx * 8);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < NVW; ++i) {
+            const int64_t idx = lane + 32 * i;
+            if (idx < nvec) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float f = sf::Dt<T>::to_f(v[i].v[j]);
+                    ss = fmaf(f, f, ss);
+                }
+            }
+        }
+        const float r = rsqrtf(sf::warp_sum(ss) / (float)hidden + eps);
+        T* yr = y + row * hidden;
+#pragma unroll
+        for (int i = 0; i < NVW; ++i) {
+            const int64_t idx = lane + 32 * i;
+            if (idx < nvec) {
+                sf::Vec8<T> o;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    o.v[j] = sf::Dt<T>::from_f(sf::Dt<T>::to_f(v[i].v[j]) * r * sf::Dt<T>::to_f(wv[i].v[j]));
+                sf::st_global_v8<T>(yr + idx * 8, o);
+            }
+        }
+    }
+}
+
+template <typename T, int NVW>
+int launch_warp_rows(const T* x, const T* w, T* y, int64_t rows, int64_t hidden, float eps, cudaStream_t stream, char* err,
+                     uint64_t cap) {
+    static const int resident = sf::resident_ctas(rmsnorm_warp_kernel<T, NVW>, 256, 0);
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)sf::sm_count() * resident));
+    rmsnorm_warp_kernel<T, NVW><<<(unsigned)blocks, 256, 0, stream>>>(x, w, y, rows, hidden, eps);
+    return sf::check_launch("rmsnorm launch", err, cap);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_generic_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                               T* __restrict__ y, int64_t hidden, float eps) {
@@ -96,6 +162,14 @@ int launch_typed(const T* x, const T* w, T* y, int64_t rows, int64_t hidden, flo
     if (rows > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "rmsnorm: rows %lld exceeds the grid limit", (long long)rows);
     const bool vec_ok = (hidden % 8 == 0) && sf::aligned16(x) && sf::aligned16(w) && sf::aligned16(y);
     const int64_t nvec = hidden / 8;
+    // Rows of <= 1024 elements: a warp per row (variant 0; variant 1 keeps the CTA-per-row kernel).
+    // Longer rows stay on one CTA per row: eight vectors per lane take 124-158 registers, one CTA
+    // per SM, too few bytes in flight.
+    if (vec_ok && variant == 0 && nvec <= 128) {
+        if (nvec <= 32) return launch_warp_rows<T, 1>(x, w, y, rows, hidden, eps, stream, err, cap);
+        if (nvec <= 64) return launch_warp_rows<T, 2>(x, w, y, rows, hidden, eps, stream, err, cap);
+        return launch_warp_rows<T, 4>(x, w, y, rows, hidden, eps, stream, err, cap);
+    }
     // Choose NV (vectors per thread) so the CTA has between 32 and 1024 threads.
     int nv = 0;
     if (vec_ok && variant != 2) {

@@ -46,8 +46,10 @@ def test_golden_vectors(cuda_device, dtype):
 
 
 SHAPES = [
-    (64, 512),      # small tier
-    (4096, 1024),   # portfolio shards of the rmsnorm workload
+    (64, 512),      # small tier (a warp per row)
+    (4096, 1024),   # portfolio shards of the rmsnorm workload (a warp per row, four vectors per lane)
+    (1000, 8),      # one vector per row: 31 lanes of every warp masked
+    (33, 1016),     # 127 vectors: the last lane's fourth vector masked
     (4096, 4096),
     (4096, 8192),
     (4093, 4096),   # tail rows
