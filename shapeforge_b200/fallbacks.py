@@ -14,7 +14,10 @@ Each provider renders a single-source cuda-single candidate:
 * attributes (EPS, LR, BASE, ...) are compile-time constants rendered from the task's
   ``opspec.json`` defaults (or the caller's values);
 * arithmetic in fp32 (rope's angles in fp64), one rounding at the output, NaN/Inf propagating
-  the way the tasks' fp64 references do.
+  the way the tasks' fp64 references do;
+* the more involved tasks keep simple parallel forms: attention one warp per query row with an
+  online softmax, mamba2 one thread per output (masked terms still multiply x), the KDA
+  recurrences one warp per (sequence, head, state row) in fp32.
 
 Implementation ids are ``cuda-sm100.fallback.<task>``, version 1.
 """
@@ -160,13 +163,195 @@ _BODIES: dict[str, tuple[str, str]] = {
     }}
 }}
 """, "kernel {name} grid=min(ceil_div(B*H*S*trunc_div(D,2),256),2368) threads=256"),
+    "bitdelta_gemm": ("""extern "C" __global__ void {name}(const T* __restrict__ x, const unsigned int* __restrict__ bits, T* __restrict__ y,
+                                        long long M, long long N, long long K) {{
+    const long long n = (long long)blockIdx.x * 16 + threadIdx.x, m = (long long)blockIdx.y * 16 + threadIdx.y;
+    if (m >= M || n >= N) return;
+    float acc = 0.f;
+    for (long long k = 0; k < K; ++k) {{
+        const unsigned int word = bits[(k >> 5) * N + n];  /* bit j of word (kb, n) is row kb*32 + j: +1 set, -1 clear */
+        const float xv = ldf(x, m * K + k);
+        acc += ((word >> (k & 31)) & 1u) ? xv : -xv;
+    }}
+    y[m * N + n] = tof(acc * (float)ATTR_SCALE);
+}}
+""", "kernel {name} grid=ceil_div(N,16),ceil_div(M,16) threads=16,16"),
+    "flash_attention": ("""extern "C" __global__ void {name}(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, T* __restrict__ o,
+                                        long long B, long long H, long long S, long long D) {{
+    /* One warp per query row, online softmax; lane holds dims lane, lane + 32, ... (D <= 256). */
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= B * H * S) return;
+    const long long bh = row / S;
+    const T* qr = q + row * D;
+    const T* kb = k + bh * S * D;
+    const T* vb = v + bh * S * D;
+    float qv[8], acc[8];
+    for (int t = 0; t < 8; ++t) {{
+        const long long d = lane + 32 * t;
+        qv[t] = d < D ? ldf(qr, d) : 0.f;
+        acc[t] = 0.f;
+    }}
+    float m = -INFINITY, l = 0.f;
+    for (long long j = 0; j < S; ++j) {{
+        float part = 0.f;
+        for (int t = 0; t < 8; ++t) {{
+            const long long d = lane + 32 * t;
+            if (d < D) part = fmaf(qv[t], ldf(kb, j * D + d), part);
+        }}
+        for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+        const float s = part * (float)ATTR_SM_SCALE;
+        const float mn = fmaxf(m, s);  /* fmaxf drops a NaN s; p = exp(NaN) then poisons the row */
+        const float corr = (m == mn) ? 1.f : expf(m - mn);
+        const float p = (s == -INFINITY) ? 0.f : expf(s - mn);  /* a -inf score has weight 0 */
+        l = l * corr + p;
+        for (int t = 0; t < 8; ++t) {{
+            const long long d = lane + 32 * t;
+            if (d < D) acc[t] = acc[t] * corr + p * ldf(vb, j * D + d);
+        }}
+        m = mn;
+    }}
+    for (int t = 0; t < 8; ++t) {{
+        const long long d = lane + 32 * t;
+        if (d < D) o[row * D + d] = tof(acc[t] / l);
+    }}
+}}
+""", "kernel {name} grid=ceil_div(B*H*S,8) threads=256"),
+    "mamba2_chunk_scan": ("""extern "C" __global__ void {name}(const T* __restrict__ x, const T* __restrict__ dt, const T* __restrict__ cs,
+                                        const T* __restrict__ Bm, const T* __restrict__ Cm, const T* __restrict__ Dskip,
+                                        const T* __restrict__ states, T* __restrict__ y, long long BATCH, long long SEQLEN,
+                                        long long NHEADS, long long HEADDIM, long long DSTATE, long long CHUNK, long long NCHUNKS) {{
+    const long long total = BATCH * SEQLEN * NHEADS * HEADDIM;
+    for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (long long)gridDim.x * blockDim.x) {{
+        const long long p = o % HEADDIM, h = (o / HEADDIM) % NHEADS, t = (o / (HEADDIM * NHEADS)) % SEQLEN;
+        const long long b = o / (HEADDIM * NHEADS * SEQLEN);
+        const long long c = t / CHUNK, lpos = t % CHUNK, t0 = c * CHUNK;
+        const T* csr = cs + ((b * NHEADS + h) * NCHUNKS + c) * CHUNK;
+        const float csl = ldf(csr, lpos);
+        float acc = 0.f;
+        /* Every row of the chunk multiplies x, the masked ones by an exact 0 (a non-finite x
+           element makes its whole chunk non-finite, as in the fp64 reference). */
+        for (long long sp = 0; sp < CHUNK; ++sp) {{
+            const long long ts = t0 + sp;
+            float wgt = 0.f;
+            if (sp <= lpos) {{
+                float cb = 0.f;
+                for (long long n = 0; n < DSTATE; ++n) cb = fmaf(ldf(Cm, (b * SEQLEN + t) * DSTATE + n), ldf(Bm, (b * SEQLEN + ts) * DSTATE + n), cb);
+                wgt = cb * expf(csl - ldf(csr, sp)) * ldf(dt, (b * SEQLEN + ts) * NHEADS + h);
+            }}
+            acc = fmaf(wgt, ldf(x, ((b * SEQLEN + ts) * NHEADS + h) * HEADDIM + p), acc);
+        }}
+        float sc = 0.f;
+        for (long long n = 0; n < DSTATE; ++n)
+            sc = fmaf(ldf(Cm, (b * SEQLEN + t) * DSTATE + n), ldf(states, (((b * NCHUNKS + c) * NHEADS + h) * HEADDIM + p) * DSTATE + n), sc);
+        acc = fmaf(sc, expf(csl), acc);
+        acc = fmaf(ldf(Dskip, h), ldf(x, o), acc);
+        y[o] = tof(acc);
+    }}
+}}
+""", "kernel {name} grid=min(ceil_div(BATCH*SEQLEN*NHEADS*HEADDIM,256),2368) threads=256"),
 }
+
+# The KDA recurrence shared by the fixed-length and the varlen fallbacks: one warp per
+# (sequence, head, state row v), lane holding key columns lane, lane + 32, ... (D <= 128).
+_KDA_CHAIN = """__device__ void kda_chain(const T* q, const T* k, const T* v, const T* g, const T* beta, const float* A_log,
+                          const float* dt_bias, const float* s0, float* s_out, T* out, float scale, long long begin, long long end,
+                          long long H, long long D, long long h, long long row) {{
+    const int lane = threadIdx.x & 31;
+    float st[4];
+    for (int t = 0; t < 4; ++t) {{
+        const long long c = lane + 32 * t;
+        st[t] = c < D ? s0[row * D + c] : 0.f;
+    }}
+    const float da = expf(A_log[h]);
+    for (long long tok = begin; tok < end; ++tok) {{
+        const long long base = (tok * H + h) * D;
+        float qv[4], kv[4], nq = 0.f, nk = 0.f;
+        for (int t = 0; t < 4; ++t) {{
+            const long long c = lane + 32 * t;
+            qv[t] = c < D ? ldf(q, base + c) : 0.f;
+            kv[t] = c < D ? ldf(k, base + c) : 0.f;
+            nq = fmaf(qv[t], qv[t], nq);
+            nk = fmaf(kv[t], kv[t], nk);
+        }}
+        for (int off = 16; off > 0; off >>= 1) {{
+            nq += __shfl_xor_sync(0xffffffffu, nq, off);
+            nk += __shfl_xor_sync(0xffffffffu, nk, off);
+        }}
+        const float rq = rsqrtf(nq + 1e-6f) * scale, rk = rsqrtf(nk + 1e-6f);
+        float dot = 0.f;
+        for (int t = 0; t < 4; ++t) {{
+            const long long c = lane + 32 * t;
+            if (c < D) {{
+                const float ld = (float)ATTR_LOWER_BOUND * sigm(da * (ldf(g, base + c) + dt_bias[h * D + c]));
+                st[t] *= expf(ld);
+                dot = fmaf(st[t], kv[t] * rk, dot);
+            }}
+        }}
+        for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        const float r = (ldf(v, base + row) - dot) * sigm(ldf(beta, tok * H + h));
+        float o = 0.f;
+        for (int t = 0; t < 4; ++t) {{
+            const long long c = lane + 32 * t;
+            if (c < D) {{
+                st[t] = fmaf(r, kv[t] * rk, st[t]);
+                o = fmaf(st[t], qv[t] * rq, o);
+            }}
+        }}
+        for (int off = 16; off > 0; off >>= 1) o += __shfl_xor_sync(0xffffffffu, o, off);
+        if (lane == 0) out[base + row] = tof(o);
+    }}
+    for (int t = 0; t < 4; ++t) {{
+        const long long c = lane + 32 * t;
+        if (c < D) s_out[row * D + c] = st[t];
+    }}
+}}
+"""
+
+_BODIES["varlen_kda"] = (_KDA_CHAIN + """extern "C" __global__ void {name}(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+        const T* __restrict__ g, const T* __restrict__ beta, const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+        const float* __restrict__ initial_state, const int* __restrict__ cu_seqlens, const float* __restrict__ scale,
+        T* __restrict__ output, float* __restrict__ final_state, float* log_decay_tab, float* token_stats, unsigned int* work_items,
+        int* item_counts, int* handoff_flags, float* handoff_states, long long H, long long D) {{
+    /* Warps cover num_seqs * H * D rows exactly (D % 8 == 0); a sequence whose offsets hold the
+       negative capacity sentinel is left untouched. */
+    const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const long long row = w % D, h = (w / D) % H, s = w / (D * H);
+    const long long begin = cu_seqlens[s], end = cu_seqlens[s + 1];
+    if (begin < 0 || end < 0 || end < begin) return;
+    const long long off = (s * H + h) * D * D;
+    kda_chain(q, k, v, g, beta, A_log, dt_bias, initial_state + off, final_state + off, output, scale[0], begin, end, H, D, h, row);
+}}
+""", "kernel {name} grid=ceil_div(num_seqs*H*D,8) threads=256")
+
+_BODIES["kda"] = (_KDA_CHAIN + """extern "C" __global__ void {name}(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+        const T* __restrict__ g, const T* __restrict__ beta, const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+        const float* __restrict__ initial_state, const float* __restrict__ scale, T* __restrict__ output,
+        float* __restrict__ final_state, unsigned int* __restrict__ work_items, int* __restrict__ item_counts,
+        float* handoff_states, long long N, long long H, long long D) {{
+    const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (w == 0 && (threadIdx.x & 31) == 0) {{
+        /* The host program's work list: one piece [0, N), two empty ones. */
+        work_items[0] = 0u; work_items[1] = (unsigned int)N; work_items[2] = (unsigned int)N;
+        work_items[3] = 0u; work_items[4] = (unsigned int)N; work_items[5] = 0u;
+        item_counts[0] = 1;
+    }}
+    if (w >= H * D) return;
+    const long long row = w % D, h = w / D;
+    const long long off = h * D * D;
+    kda_chain(q, k, v, g, beta, A_log, dt_bias, initial_state + off, final_state + off, output, scale[0], 0, N, H, D, h, row);
+}}
+""", "kernel {name} grid=ceil_div(H*D,8) threads=256")
 
 # Attribute defaults of tasks/<task>/opspec.json (used when the caller passes none).
 ATTR_DEFAULTS: dict[str, dict[str, float]] = {
     "rmsnorm": {"EPS": 1e-6},
     "lion": {"LR": 0.001, "WD": 0.1, "BETA1": 0.9, "BETA2": 0.99},
     "rope": {"BASE": 10000.0},
+    "bitdelta_gemm": {"SCALE": 0.02},
+    "flash_attention": {"SM_SCALE": 0.125},
+    "kda": {"LOWER_BOUND": -5.0},
+    "varlen_kda": {"LOWER_BOUND": -5.0},
 }
 
 TASKS = tuple(sorted(_BODIES))

@@ -95,6 +95,14 @@ def domain(opspec: Mapping[str, Any], dtype: str, sizes: Sequence[str] | None = 
             raise PortfolioError(f"size {size!r} is not declared by the task (declared: {sorted(declared)})")
         entry = declared[size]
         names = {k: int(v) for k, v in entry.items() if k != "usage" and isinstance(v, int) and not isinstance(v, bool)}
+        # Varlen sizes declare their batch, not its symbols: total_tokens / num_seqs (and NSP1 =
+        # num_seqs + 1, the cu_seqlens length) come from seq_lens, or from the capacity of an L2 tier.
+        if isinstance(entry.get("capacity"), Mapping):
+            names.update(total_tokens=int(entry["capacity"]["total_tokens"]), num_seqs=int(entry["capacity"]["num_seqs"]))
+        elif isinstance(entry.get("seq_lens"), list):
+            names.update(total_tokens=sum(int(x) for x in entry["seq_lens"]), num_seqs=len(entry["seq_lens"]))
+        if "num_seqs" in names:
+            names["NSP1"] = names["num_seqs"] + 1
         for usage in entry.get("usage", ["benchmark"]):
             points.append(Point(f"{dtype}/{size}/{usage}", size, usage, names))
     return tuple(points)

@@ -73,6 +73,43 @@ def _case(task, case, seed, names, dtype):
         inp = cases.membound_inputs("rope", case, seed, shape, dtype)
         ref = oref.rope(_np(inp["x"]), 10000.0)
         return inp, ("B", "H", "S", "D"), {"y": shape}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    if task == "bitdelta_gemm":
+        m, n, k = names["M"], names["N"], names["K"]
+        inp = cases.bitdelta_inputs(case, seed, m, n, k, dtype)
+        ref = oref.bitdelta_gemm(_np(inp["x"]), inp["bits"].numpy(), 0.02)
+        return inp, ("M", "N", "K"), {"y": (m, n)}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    if task == "flash_attention":
+        shape = (names["B"], names["H"], names["S"], names["D"])
+        inp = cases.attention_inputs(case, seed, shape, dtype)
+        ref = oref.attention(_np(inp["q"]), _np(inp["k"]), _np(inp["v"]), 0.125)
+        return inp, ("B", "H", "S", "D"), {"o": shape}, {"o": ref}, {"o": compare.rms_scale(ref)}
+    if task == "mamba2_chunk_scan":
+        b, l, h, p, n, c = (names[k] for k in ("BATCH", "SEQLEN", "NHEADS", "HEADDIM", "DSTATE", "CHUNK"))
+        inp = cases.mamba2_inputs(case, seed, b, l, h, p, n, c, dtype)
+        ref = oref.mamba2_chunk_scan(*(_np(inp[k]) for k in ("x", "dt", "dA_cumsum", "Bmat", "Cmat", "Dskip", "states")))
+        order = ("BATCH", "SEQLEN", "NHEADS", "HEADDIM", "DSTATE", "CHUNK", "NCHUNKS")
+        return inp, order, {"y": (b, l, h, p)}, {"y": ref}, {"y": compare.rms_scale(ref)}
+    if task == "kda":
+        n, h, d = names["N"], names["H"], names["D"]
+        inp = cases.kda_fixed_inputs(case, seed, n, h, d, dtype)
+        f = [_np(inp[k]) for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state")]
+        ro, rf = oref.kda_fixed(*f, float(inp["scale"][0]), -5.0)
+        outs = {"output": (n, h, d), "final_state": ((h, d, d), torch.float32), "work_items": ((3, 2), torch.int32),
+                "item_counts": ((1,), torch.int32), "handoff_states": ((2, h, d, d), torch.float32)}
+        return inp, ("N", "H", "D"), outs, {"output": ro, "final_state": rf}, {"output": compare.rms_scale(ro),
+                                                                                 "final_state": compare.rms_scale(rf)}
+    if task == "varlen_kda":
+        lens, h, d = names["seq_lens"], names["H"], names["D"]
+        inp = cases.kda_task_inputs(lens, h, d, dtype, seed)
+        f = [_np(inp[k]) for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state")]
+        ro, rf = oref.varlen_kda(*f, inp["cu_seqlens"].numpy(), float(inp["scale"][0]), -5.0)
+        t, ns = sum(lens), len(lens)
+        outs = {"output": (t, h, d), "final_state": ((ns, h, d, d), torch.float32), "log_decay_tab": ((t, h, d), torch.float32),
+                "token_stats": ((t, h, 3), torch.float32), "work_items": ((ns * h * 3, 2), torch.int32),
+                "item_counts": ((ns * h * 3,), torch.int32), "handoff_flags": ((ns * h * 4,), torch.int32),
+                "handoff_states": ((ns * h * 2, d, d), torch.float32)}
+        return inp, ("H", "D"), outs, {"output": ro, "final_state": rf}, {"output": compare.rms_scale(ro),
+                                                                          "final_state": compare.rms_scale(rf)}
     raise KeyError(task)
 
 
@@ -81,8 +118,17 @@ SHAPES = {
     "lion": {"N": 65536}, "rmsnorm": {"M": 64, "H": 512}, "softmax": {"M": 64, "N": 515}, "reduction_sum": {"M": 64, "N": 1024},
     "gemv": {"M": 256, "K": 513}, "gemm": {"M": 130, "N": 72, "K": 128}, "gemm_silu": {"M": 64, "N": 256, "K": 128},
     "rope": {"B": 1, "H": 2, "S": 64, "D": 64},
+    "bitdelta_gemm": {"M": 33, "N": 72, "K": 256},
+    "flash_attention": {"B": 1, "H": 2, "S": 130, "D": 64},
+    "mamba2_chunk_scan": {"BATCH": 1, "SEQLEN": 128, "NHEADS": 2, "HEADDIM": 64, "DSTATE": 64, "CHUNK": 64, "NCHUNKS": 2},
+    "kda": {"N": 17, "H": 2, "D": 8},
+    "varlen_kda": {"H": 2, "D": 64, "seq_lens": [5, 0, 19, 1], "num_seqs": 4, "total_tokens": 25},
 }
-CASES = {"reduction_sum": ("normal", "cancel", "ieee"), "softmax": ("normal", "large", "ieee")}
+CASES = {"reduction_sum": ("normal", "cancel", "ieee"), "softmax": ("normal", "large", "ieee"),
+         "bitdelta_gemm": ("random", "edge_bits", "ieee"), "mamba2_chunk_scan": ("normal", "wide_range", "ieee"),
+         "kda": ("normal", "wide_range", "outlier"), "varlen_kda": ("normal",)}
+# The varlen_kda / kda tasks take the recurrence's looser opspec tolerance for varlen_kda.
+TASK_TOL = {"varlen_kda": {"fp16": dict(rtol=1e-2, atol_rel=5e-3), "bf16": dict(rtol=3e-2, atol_rel=1.5e-2)}}
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
@@ -93,14 +139,21 @@ def test_registered_fallback_matches_the_oracle(cuda_device, task, dtype):
     for ci, case in enumerate(CASES.get(task, ("normal", "large", "ieee"))):
         inp, order, outs, refs, scales = _case(task, case, cases.case_seed(0, ci), names, dtype)
         inp = {k: v.to(cuda_device) for k, v in inp.items()}
-        out = {k: torch.empty(shape, dtype=TD[dtype], device=cuda_device) for k, shape in outs.items()}
+        out = {}
+        for k, spec in outs.items():
+            shape, tdt = spec if isinstance(spec[0], tuple) else (spec, TD[dtype])
+            out[k] = torch.empty(shape, dtype=tdt, device=cuda_device)
         launch = CudaTrackEvaluator.launcher(build, [ctypes.c_longlong(names[s]) for s in order], names=names)
         launch([t.data_ptr() for t in (*inp.values(), *out.values())])
         torch.cuda.synchronize()
         for k, ref in refs.items():
-            tol = dict(TOL[dtype], atol_rel=3e-6) if task == "reduction_sum" else TOL[dtype]
-            v = compare.check(_np(out[k]), ref, scales[k], dtype=dtype, **tol)
+            tol = dict(TOL[dtype], atol_rel=3e-6) if task == "reduction_sum" else TASK_TOL.get(task, TOL)[dtype]
+            odt = "fp32" if out[k].dtype == torch.float32 else dtype
+            v = compare.check(_np(out[k]), ref, scales[k], dtype=odt, **tol)
             assert v.ok, (task, case, k, v.summary())
+        if task == "kda":
+            n = names["N"]
+            assert out["work_items"].cpu().tolist() == [[0, n], [n, 0], [n, 0]] and out["item_counts"].item() == 1
 
 
 def test_gemv_portfolio_dispatch_run_and_accounts(cuda_device, tmp_path):

@@ -259,6 +259,11 @@ FALLBACK_SHAPES = {
     "reduction_sum": [{"M": 4096, "N": 4096}], "gemv": [{"M": 4096, "K": 4096}, {"M": 1, "K": 3}],
     "gemm": [{"M": 2048, "N": 2048, "K": 2048}, {"M": 3, "N": 5, "K": 7}], "gemm_silu": [{"M": 256, "N": 256, "K": 128}],
     "rope": [{"B": 2, "H": 32, "S": 1024, "D": 128}, {"B": 1, "H": 1, "S": 1, "D": 2}],
+    "bitdelta_gemm": [{"M": 512, "N": 4096, "K": 4096}, {"M": 128, "N": 256, "K": 256}],
+    "flash_attention": [{"B": 2, "H": 8, "S": 1024, "D": 64}, {"B": 1, "H": 2, "S": 128, "D": 64}],
+    "mamba2_chunk_scan": [{"BATCH": 2, "SEQLEN": 2048, "NHEADS": 8, "HEADDIM": 64, "DSTATE": 64, "CHUNK": 64, "NCHUNKS": 32}],
+    "kda": [{"N": 256, "H": 8, "D": 64}, {"N": 1, "H": 2, "D": 8}],
+    "varlen_kda": [{"H": 64, "D": 128, "num_seqs": 6, "total_tokens": 8192}, {"H": 2, "D": 8, "num_seqs": 4, "total_tokens": 16}],
 }
 
 
@@ -279,6 +284,16 @@ def test_registered_fallbacks_render_check_and_resolve(task):
         fallbacks.render("no_such_task", "fp16")
     with pytest.raises(ValueError):
         fallbacks.render(task, "fp32")
+
+
+def test_varlen_sizes_get_their_batch_symbols():
+    opspec = {"sizes": {"mixed": {"H": 2, "D": 8, "seq_lens": [4, 8, 2], "usage": ["golden"]},
+                        "capacity": {"H": 2, "D": 8, "usage": ["benchmark"],
+                                     "capacity": {"total_tokens": 16, "num_seqs": 4, "cu_seqlens_sentinel": -1,
+                                                  "padding_poison_byte": 90}}}}
+    mixed, cap = pp.domain(opspec, "fp16")
+    assert mixed.names == {"H": 2, "D": 8, "total_tokens": 14, "num_seqs": 3, "NSP1": 4}
+    assert cap.names == {"H": 2, "D": 8, "total_tokens": 16, "num_seqs": 4, "NSP1": 5}
 
 
 def test_fallback_attributes_are_rendered():
