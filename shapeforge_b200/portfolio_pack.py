@@ -412,6 +412,28 @@ class ShardRun:
     cache_hit: bool = False
 
 
+def storage_dtype(name: str, task_dtype: str):
+    """The torch dtype holding an opspec tensor dtype (``T`` is the instance's dtype; ``u32`` is held
+    as int32, the same 4 bytes)."""
+    import torch
+
+    table = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32, "i32": torch.int32, "u32": torch.int32}
+    key = task_dtype if name == "T" else name
+    if key not in table:
+        raise PortfolioError(f"no storage dtype for {name!r}")
+    return table[key]
+
+
+def output_specs(opspec: Mapping[str, Any], point: Point) -> dict[str, tuple[tuple[int, ...], Any]]:
+    """Shape (dims evaluated on the point's symbols) and torch dtype of every output, in ABI order."""
+    dtype = point.instance_key.split("/")[0]
+    out = {}
+    for name, t in opspec["tensors"].items():
+        if t["role"] == "output":
+            out[name] = (tuple(int(expr.evaluate_term(d, point.names)) for d in t["dims"]), storage_dtype(t["dtype"], dtype))
+    return out
+
+
 def _timed(candidate: Callable[[], Any], baseline: Callable[[], Any], reps: int):
     """Per-launch device microseconds of candidate and baseline through the harness timing
     protocol (``protocol.measure_interleaved``: batches sized to ~15 ms, interleaved repetitions,
@@ -446,14 +468,7 @@ def run_point(parent: Parent, opspec: Mapping[str, Any], point: Point, inputs: M
     if key not in builds or not use_cache:
         builds[key] = CudaTrackBuilder().build(source, use_cache=use_cache)
     build = builds[key]
-    dtype = point.instance_key.split("/")[0]
-    torch_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32, "i32": torch.int32}
-    outputs = {}
-    for name, t in opspec["tensors"].items():
-        if t["role"] != "output":
-            continue
-        shape = tuple(int(expr.evaluate_term(d, point.names)) for d in t["dims"])
-        outputs[name] = torch.empty(shape, dtype=torch_dtype[dtype if t["dtype"] == "T" else t["dtype"]], device="cuda")
+    outputs = {name: torch.empty(shape, dtype=dt, device="cuda") for name, (shape, dt) in output_specs(opspec, point).items()}
     ptrs = [(inputs[n] if n in inputs else outputs[n]).data_ptr() for n in opspec["tensors"]]
     stream = torch.cuda.current_stream().cuda_stream
     module = Module(build.image)

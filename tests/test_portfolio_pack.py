@@ -323,3 +323,28 @@ def test_command_line_pack_and_check(tmp_path):
     (src / "variants" / "stray").mkdir()
     r = run("pack", str(src), "--task-dir", str(tmp_path / "task"), "--dtype", "fp16", "--out", str(out))
     assert r.returncode == 2 and "do not match" in r.stderr
+
+
+def test_output_specs_cover_every_task_dtype():
+    """Outputs are allocated from the opspec: derived dims evaluate on the point's symbols (the
+    varlen batch symbols included) and u32 is held as int32."""
+    import torch
+
+    opspec = {
+        "tensors": {
+            "q": {"role": "input", "dims": ["total_tokens", "H", "D"], "dtype": "T"},
+            "output": {"role": "output", "dims": ["total_tokens", "H", "D"], "dtype": "T"},
+            "final_state": {"role": "output", "dims": ["num_seqs", "H", "D", "D"], "dtype": "fp32"},
+            "work_items": {"role": "output", "dims": ["num_seqs*H*3", "2"], "dtype": "u32"},
+            "item_counts": {"role": "output", "dims": ["num_seqs*H*3"], "dtype": "i32"},
+        },
+        "sizes": {"mixed": {"H": 2, "D": 8, "seq_lens": [4, 8, 2], "usage": ["benchmark"]}},
+    }
+    (p,) = pp.domain(opspec, "bf16")
+    specs = pp.output_specs(opspec, p)
+    assert list(specs) == ["output", "final_state", "work_items", "item_counts"]
+    assert specs["output"] == ((14, 2, 8), torch.bfloat16)
+    assert specs["final_state"] == ((3, 2, 8, 8), torch.float32)
+    assert specs["work_items"] == ((18, 2), torch.int32) and specs["item_counts"] == ((18,), torch.int32)
+    with pytest.raises(pp.PortfolioError):
+        pp.storage_dtype("f8", "fp16")
