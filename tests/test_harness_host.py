@@ -36,7 +36,7 @@ def test_fill_plan_matches_reference_protocol():
 def test_fill_plan_agrees_with_reference_module():
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv.track import protocol as ref_protocol
 
     assert ref_protocol.GUARD_PATTERN == runtime.GUARD_PATTERN
@@ -64,7 +64,7 @@ def test_comparator_agrees_with_reference():
         pytest.skip("reference checkout not mounted")
     import torch
 
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     try:
         from tcenv.backends.metal.testing import scaled_error as ref_scaled_error  # imports Metal
     except Exception:
@@ -106,7 +106,7 @@ def test_interleaved_and_attempt_selection():
 def test_protocol_agrees_with_reference_bench():
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv import bench as ref_bench
 
     for per in (1e-7, 1e-5, 1e-3, 0.05, 0.3):
@@ -154,7 +154,7 @@ def test_accounts_specialized_and_effective():
 def test_accounts_agree_with_reference():
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv.portfolio_performance import performance as ref_perf
 
     spec = [("t/a/benchmark", "candidate", 10.0, 12.0), ("t/b/benchmark", "fallback", 5.0, 4.8), ("t/c/benchmark", "candidate", 3.0, 3.3)]
@@ -190,7 +190,7 @@ def test_plugin_loads_through_reference_registry_and_target():
     """The drop-in: the reference's own load_backend / load_target resolve cuda-sm100 / b200."""
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     import tcenv.backends.registry as registry
     import tcenv.target as target
 
@@ -215,7 +215,7 @@ def test_plugin_loads_through_reference_registry_and_target():
 def test_track_registry_file_loads_with_reference_loader():
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv.track.registry import load_track_registry
 
     reg = load_track_registry(ROOT / "backends" / "cuda-sm100" / "tracks.json")

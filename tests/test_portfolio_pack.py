@@ -118,7 +118,7 @@ def test_guard_digest_is_canonical():
 def test_expression_rules_match_the_reference_evaluator():
     import sys
 
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv.track import expr as rexpr
 
     rng = random.Random(3)

@@ -41,7 +41,7 @@ WRONG = SILU.replace("v / (1.0f + expf(-v))", "v")
 def _spec():
     doc = json.loads((ROOT / "backends" / "cuda-sm100" / "tracks.json").read_text())["tracks"][0]
     if REF.is_dir():
-        sys.path.insert(0, str(REF))
+        sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
         from tcenv.track.registry import load_track_registry
 
         reg = load_track_registry(ROOT / "backends" / "cuda-sm100" / "tracks.json")

@@ -69,7 +69,7 @@ def _cases(task):
 def test_task_directory_loads_with_reference_loader(task):
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
-    sys.path.insert(0, str(REF))
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv.taskcontract import load_task_contract
 
     contract = load_task_contract(ROOT / "tasks" / task)
