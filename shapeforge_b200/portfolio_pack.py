@@ -440,10 +440,12 @@ def _timed(candidate: Callable[[], Any], baseline: Callable[[], Any], reps: int)
     up to three attempts).  Returns (candidate stats, baseline stats, noisy, attempts); noisy is
     True when the kept attempt's CV is above 5 %."""
     from . import protocol
+    from .gpulock import gpu_lock
 
     runners = {"candidate": protocol.cuda_event_runner(lambda i: candidate()),
                "baseline": protocol.cuda_event_runner(lambda i: baseline())}
-    noise, stats, attempts = protocol.measure_interleaved(runners, reps=reps)
+    with gpu_lock("portfolio shard timing"):  # exclusive on this GPU for the whole measurement
+        noise, stats, attempts = protocol.measure_interleaved(runners, reps=reps)
     return stats["candidate"], stats["baseline"], noise > protocol.NOISY_CV, attempts
 
 

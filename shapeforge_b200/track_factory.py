@@ -258,13 +258,16 @@ class CudaTrackEvaluator:
             launch = self.launcher(build, request.scalars, names=request.names)
             from .runtime import CorrectnessRunner
 
+            from .gpulock import gpu_lock
+
             runner = CorrectnessRunner(request.specs, launch, output_dtypes=request.output_dtypes)
             results = []
-            for name, inputs, refs, scales in request.cases:
-                res = runner.run_case(name, inputs, refs, scales, request.rtol, request.atol_rel, request.exact)
-                results.append(res)
-                if not res.ok:
-                    break
+            with gpu_lock("correctness", exclusive=False):  # untimed: may overlap other untimed work, never a timing
+                for name, inputs, refs, scales in request.cases:
+                    res = runner.run_case(name, inputs, refs, scales, request.rtol, request.atol_rel, request.exact)
+                    results.append(res)
+                    if not res.ok:
+                        break
         except Exception as exc:  # noqa: BLE001 - a device error is the candidate's runtime_error
             return dict(report, status="runtime_error", detail=str(exc))
         report["cases"] = [r.summary() for r in results]
@@ -282,9 +285,12 @@ class CudaTrackEvaluator:
         """The reference's interleaved protocol (median of ``reps`` batches, CV gate, attempts)."""
         from . import protocol
 
+        from .gpulock import gpu_lock
+
         ptrs = runner.pointers()
         run_k = protocol.cuda_event_runner(lambda i: launch(ptrs))
-        noise, stats, attempts = protocol.measure_interleaved({"candidate": run_k}, reps=reps)
+        with gpu_lock("candidate timing"):  # exclusive on this GPU for the whole measurement
+            noise, stats, attempts = protocol.measure_interleaved({"candidate": run_k}, reps=reps)
         return {"protocol": "interleaved", "noise_cv": noise, "attempts": attempts, "candidate": stats["candidate"].to_dict()}
 
 
