@@ -1,0 +1,54 @@
+"""Supervised evaluation on the host (tcenv/evaluate.py supervise, tcenv/v2_worker.py run_bounded_v2):
+deadlines per heartbeat stage, lock waits excluded from the timeout, typed failures, and the kernel
+releasing a killed worker's GPU lock.  The failures are host-made (fake workers), none on a GPU.
+"""
+
+from __future__ import annotations
+
+import time
+
+from shapeforge_b200 import gpulock
+from shapeforge_b200.supervise import run_bounded
+
+F = "tests.supervise_fakes"
+
+
+def test_a_finished_worker_returns_its_report():
+    assert run_bounded(f"{F}:ok", {"value": 7}, timeout=60) == {"status": "ok", "value": 7}
+
+
+def test_a_hung_launch_is_killed_at_the_launch_deadline():
+    t0 = time.monotonic()
+    rep = run_bounded(f"{F}:hang_in_launch", timeout=120, launch_deadline_s=1.0)
+    assert rep["status"] == "timeout" and rep["reason"] == "launch"
+    assert time.monotonic() - t0 < 30
+
+
+def test_a_slow_compile_is_killed_at_the_compile_deadline():
+    rep = run_bounded(f"{F}:slow_compile", timeout=120, compile_deadline_s=1.0)
+    assert rep["status"] == "timeout" and rep["reason"] == "compile"
+
+
+def test_the_whole_evaluation_has_a_timeout():
+    rep = run_bounded(f"{F}:busy", timeout=1.0)
+    assert rep["status"] == "timeout" and rep["reason"] == "timeout"
+
+
+def test_time_queued_for_the_gpu_lock_does_not_count():
+    rep = run_bounded(f"{F}:queued_then_done", {"queued": 2.0, "work": 0.1}, timeout=1.0)
+    assert rep == {"status": "ok"}
+
+
+def test_crashes_and_exceptions_are_typed():
+    rep = run_bounded(f"{F}:exits_without_report", timeout=60)
+    assert rep["status"] == "crash" and rep["returncode"] == 3
+    rep = run_bounded(f"{F}:raises", timeout=60)
+    assert rep["status"] == "runtime_error" and "candidate blew up" in rep["detail"]
+
+
+def test_a_killed_workers_gpu_lock_is_released(tmp_path, monkeypatch):
+    monkeypatch.setenv("SF_GPU_LOCK_DIR", str(tmp_path))
+    rep = run_bounded(f"{F}:holds_lock_then_hangs", {"lock_dir": str(tmp_path)}, timeout=120, launch_deadline_s=1.0)
+    assert rep["status"] == "timeout" and rep["reason"] == "launch"
+    with gpulock.gpu_lock("timing", device=7, max_wait_s=5.0):
+        pass
