@@ -52,6 +52,16 @@ class Heartbeat:
         os.replace(tmp, self.path)  # readers never see a half-written line
 
 
+_current: Heartbeat | None = None
+
+
+def mark(stage: str) -> None:
+    """Mark this process's heartbeat (a no-op outside a supervised worker).  The track builder marks
+    ``C`` around nvcc, the evaluator ``B`` around each correctness run and ``E`` after."""
+    if _current is not None:
+        _current.mark(stage)
+
+
 def read_heartbeat(path: str | Path) -> tuple[str, float] | None:
     try:
         stage, t = Path(path).read_text(encoding="ascii").split()
@@ -135,6 +145,9 @@ def run_bounded(target: str, args: Mapping[str, Any] | None = None, *, timeout: 
 def _worker_main(request_path: str) -> int:
     req = json.loads(Path(request_path).read_text(encoding="utf-8"))
     hb = Heartbeat(req["heartbeat"])
+    # Run as ``-m``, this file is ``__main__``: install the heartbeat on the package module, the one
+    # the builder and the evaluator import ``mark`` from.
+    importlib.import_module("shapeforge_b200.supervise")._current = hb
     hb.mark("E")
     # Lock waits are marked W (excluded from the timeout), compiles C, launches B.
     from . import gpulock

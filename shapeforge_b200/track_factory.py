@@ -177,9 +177,14 @@ class CudaTrackBuilder:
         flags = ("-lineinfo",) + self.extra_flags
         try:
             from .candidates import cache_path
+            from .supervise import mark
 
             cache_hit = use_cache and cache_path(source, flags, "track").is_file()
-            image = compile_source(source, extra_flags=flags, name="track", use_cache=use_cache)
+            mark("C")  # a supervised worker's compile deadline runs from here
+            try:
+                image = compile_source(source, extra_flags=flags, name="track", use_cache=use_cache)
+            finally:
+                mark("E")
         except CandidateCompileError as exc:
             raise CudaCompileError(f"{exc}\n{exc.log}") from exc
         kernels = tuple(dict.fromkeys(s.kernel for s in stages))
@@ -262,9 +267,15 @@ class CudaTrackEvaluator:
 
             runner = CorrectnessRunner(request.specs, launch, output_dtypes=request.output_dtypes)
             results = []
+            from .supervise import mark
+
             with gpu_lock("correctness", exclusive=False):  # untimed: may overlap other untimed work, never a timing
                 for name, inputs, refs, scales in request.cases:
-                    res = runner.run_case(name, inputs, refs, scales, request.rtol, request.atol_rel, request.exact)
+                    mark("B")  # a supervised worker's launch deadline covers each case's trials
+                    try:
+                        res = runner.run_case(name, inputs, refs, scales, request.rtol, request.atol_rel, request.exact)
+                    finally:
+                        mark("E")
                     results.append(res)
                     if not res.ok:
                         break

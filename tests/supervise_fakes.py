@@ -55,3 +55,11 @@ def holds_lock_then_hangs(heartbeat, lock_dir, device=7):
         heartbeat.mark("B")
         time.sleep(60.0)
     return {"status": "ok"}
+
+
+def builds_a_candidate(heartbeat, source):
+    """Compile a candidate with the track builder (fresh nvcc run): it marks C around nvcc."""
+    from shapeforge_b200.track_factory import CudaTrackBuilder
+
+    build = CudaTrackBuilder().build(source, use_cache=False)
+    return {"status": "ok", "kernels": list(build.kernels), "cache_hit": build.cache_hit}

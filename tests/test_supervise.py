@@ -52,3 +52,20 @@ def test_a_killed_workers_gpu_lock_is_released(tmp_path, monkeypatch):
     assert rep["status"] == "timeout" and rep["reason"] == "launch"
     with gpulock.gpu_lock("timing", device=7, max_wait_s=5.0):
         pass
+
+
+SRC = """extern "C" __global__ void k(const float* x, float* y) { y[threadIdx.x] = x[threadIdx.x]; }
+/* taic-launch
+kernel k grid=1 threads=32
+*/
+"""
+
+
+def test_the_track_builder_runs_under_the_compile_deadline():
+    """A real nvcc build inside a supervised worker: finishes under a generous compile deadline, and
+    is killed under one shorter than nvcc's own start-up (the builder marks C around nvcc)."""
+    rep = run_bounded(f"{F}:builds_a_candidate", {"source": SRC}, timeout=300, compile_deadline_s=240)
+    assert rep == {"status": "ok", "kernels": ["k"], "cache_hit": False}
+    rep = run_bounded(f"{F}:builds_a_candidate", {"source": SRC.replace("threadIdx.x]", "threadIdx.x] ")}, timeout=300,
+                      compile_deadline_s=0.05)
+    assert rep["status"] == "timeout" and rep["reason"] == "compile"
