@@ -175,9 +175,6 @@ class CudaBackend:
     runtime_headers = "#include <cuda_fp16.h>\n#include <cuda_bf16.h>\n"
     capabilities = Capabilities()
 
-    def __init__(self) -> None:
-        self._hooks: dict[str, Any] = {}
-
     # ---- parent-process, text-only hooks -------------------------------------------------------
 
     def track_adapter(self, track):
@@ -320,7 +317,15 @@ class CudaBackend:
     # ---- child-process hooks (device) ----------------------------------------------------------
 
     def set_heartbeat_hooks(self, *, on_compile=None, on_launch=None) -> None:
-        self._hooks = {"compile": on_compile, "launch": on_launch}
+        """Install ``(begin, end)`` pairs run around every nvcc build and every synchronised launch
+        (a correctness case, a k-launch timing batch); an omitted pair is left as it is
+        (tcenv/backends/base.py:194 contract)."""
+        from . import heartbeat
+
+        if on_compile is not None:
+            heartbeat.set_compile_hooks(*on_compile)
+        if on_launch is not None:
+            heartbeat.set_launch_hooks(*on_launch)
 
     def context(self):
         import torch
@@ -362,10 +367,13 @@ class CudaBackend:
         """Run every case (``(name, inputs, refs, scales)``) through the three guarded trials."""
         from .runtime import CorrectnessRunner
 
+        from .heartbeat import launching
+
         runner = CorrectnessRunner(specs, launch, ctx, output_dtypes=output_dtypes)
         results = []
         for name, inputs, refs, scales in cases:
-            results.append(runner.run_case(name, inputs, refs, scales, rtol, atol_rel, exact))
+            with launching():
+                results.append(runner.run_case(name, inputs, refs, scales, rtol, atol_rel, exact))
             if not results[-1].ok:
                 break  # the reference stops at the first failing case
         return results
@@ -379,7 +387,10 @@ class CudaBackend:
 
         stream = torch.cuda.current_stream().cuda_stream
 
+        from .heartbeat import launching
+
         def run_k(k: int) -> float:
-            return _native.run_batch(desc, pointer_sets, k, stream, use_graph=use_graph)
+            with launching():
+                return _native.run_batch(desc, pointer_sets, k, stream, use_graph=use_graph)
 
         return run_k

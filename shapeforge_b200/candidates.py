@@ -16,7 +16,7 @@ import tempfile
 from pathlib import Path
 from typing import Sequence
 
-from . import _native
+from . import _native, heartbeat
 from .build import ARCH, nvcc
 
 CACHE = Path(os.environ.get("SF_CANDIDATE_CACHE", Path(tempfile.gettempdir()) / "shapeforge_b200_candidates"))
@@ -53,7 +53,8 @@ def compile_source(source: str, extra_flags: Sequence[str] = (), name: str = "ca
         src = Path(d) / f"{name}.cu"
         src.write_text(source)
         tmp = Path(d) / "out.cubin"
-        proc = subprocess.run([nvcc(), *flags, str(src), "-o", str(tmp)], capture_output=True, text=True)
+        with heartbeat.compiling():  # an evaluation worker's compile deadline covers nvcc only
+            proc = subprocess.run([nvcc(), *flags, str(src), "-o", str(tmp)], capture_output=True, text=True)
         if proc.returncode != 0:
             raise CandidateCompileError(f"nvcc failed for {name}", proc.stdout + proc.stderr)
         data = tmp.read_bytes()

@@ -441,9 +441,18 @@ def _timed(candidate: Callable[[], Any], baseline: Callable[[], Any], reps: int)
     True when the kept attempt's CV is above 5 %."""
     from . import protocol
     from .gpulock import gpu_lock
+    from .heartbeat import launching
 
-    runners = {"candidate": protocol.cuda_event_runner(lambda i: candidate()),
-               "baseline": protocol.cuda_event_runner(lambda i: baseline())}
+    def batch(fn: Callable[[], Any]) -> Callable[[int], float]:
+        run_k = protocol.cuda_event_runner(lambda i: fn())
+
+        def bracketed(k: int) -> float:
+            with launching():  # one synchronised k-launch batch
+                return run_k(k)
+
+        return bracketed
+
+    runners = {"candidate": batch(candidate), "baseline": batch(baseline)}
     with gpu_lock("portfolio shard timing"):  # exclusive on this GPU for the whole measurement
         noise, stats, attempts = protocol.measure_interleaved(runners, reps=reps)
     return stats["candidate"], stats["baseline"], noise > protocol.NOISY_CV, attempts
@@ -482,8 +491,11 @@ def run_point(parent: Parent, opspec: Mapping[str, Any], point: Point, inputs: M
         for b in bound:
             b()
 
-    run()
-    torch.cuda.synchronize()
+    from .heartbeat import launching
+
+    with launching():  # an evaluation worker's launch deadline covers the verified run
+        run()
+        torch.cuda.synchronize()
     ok, detail = verify(point, inputs, outputs)
     shard = ShardRun(point, rec.provider, rec.selected, 0.0, 0.0, ok, detail, source_sha256=key, cache_hit=build.cache_hit)
     if baseline is not None:

@@ -1,8 +1,9 @@
 """Supervised evaluation: one worker process per candidate evaluation, heartbeats, deadlines.
 
 Restates the supervision of tcenv/evaluate.py ``supervise`` (:1143) and tcenv/v2_worker.py
-``run_bounded_v2`` (:450): the parent owns every deadline, the worker only writes a heartbeat file
-``"<stage> <unix time>"``:
+``run_bounded_v2`` (:450): the parent owns every deadline, the worker only overwrites one
+heartbeat record (the reference's fixed 22-byte form, :mod:`shapeforge_b200.heartbeat`) through the
+backend's compile / launch hooks and the GPU lock's wait hooks:
 
 * ``C`` — compiling: the worker is killed when one compile is older than ``compile_deadline_s``;
 * ``B`` — inside a GPU launch (or a synchronising call): killed when older than ``launch_deadline_s``;
@@ -33,41 +34,15 @@ import traceback
 from pathlib import Path
 from typing import Any, Mapping
 
+from .heartbeat import HeartbeatFile, read
+
 COMPILE_DEADLINE_S = 600.0
 LAUNCH_DEADLINE_S = 10.0
 KILL_WAIT_S = 10.0
 
 
-class Heartbeat:
-    """The worker side: ``mark("B")`` before a launch, ``mark("E")`` after it, and so on."""
-
-    def __init__(self, path: str | Path | None) -> None:
-        self.path = Path(path) if path else None
-
-    def mark(self, stage: str) -> None:
-        if self.path is None:
-            return
-        tmp = self.path.with_suffix(".tmp")
-        tmp.write_text(f"{stage} {time.time():.6f}", encoding="ascii")
-        os.replace(tmp, self.path)  # readers never see a half-written line
-
-
-_current: Heartbeat | None = None
-
-
-def mark(stage: str) -> None:
-    """Mark this process's heartbeat (a no-op outside a supervised worker).  The track builder marks
-    ``C`` around nvcc, the evaluator ``B`` around each correctness run and ``E`` after."""
-    if _current is not None:
-        _current.mark(stage)
-
-
-def read_heartbeat(path: str | Path) -> tuple[str, float] | None:
-    try:
-        stage, t = Path(path).read_text(encoding="ascii").split()
-        return stage, float(t)
-    except (OSError, ValueError):
-        return None
+Heartbeat = HeartbeatFile
+read_heartbeat = read
 
 
 def popen_group(cmd: list[str], **kw: Any) -> subprocess.Popen:
@@ -144,15 +119,9 @@ def run_bounded(target: str, args: Mapping[str, Any] | None = None, *, timeout: 
 
 def _worker_main(request_path: str) -> int:
     req = json.loads(Path(request_path).read_text(encoding="utf-8"))
-    hb = Heartbeat(req["heartbeat"])
-    # Run as ``-m``, this file is ``__main__``: install the heartbeat on the package module, the one
-    # the builder and the evaluator import ``mark`` from.
-    importlib.import_module("shapeforge_b200.supervise")._current = hb
+    hb = HeartbeatFile(req["heartbeat"])
     hb.mark("E")
-    # Lock waits are marked W (excluded from the timeout), compiles C, launches B.
-    from . import gpulock
-
-    gpulock.set_wait_hooks(lambda: hb.mark("W"), lambda: hb.mark("E"))
+    hb.install()  # compiles C, launches B, lock waits W (excluded from the timeout)
     module, func = req["target"].split(":")
     try:
         report = getattr(importlib.import_module(module), func)(heartbeat=hb, **req["args"])

@@ -177,14 +177,9 @@ class CudaTrackBuilder:
         flags = ("-lineinfo",) + self.extra_flags
         try:
             from .candidates import cache_path
-            from .supervise import mark
 
             cache_hit = use_cache and cache_path(source, flags, "track").is_file()
-            mark("C")  # a supervised worker's compile deadline runs from here
-            try:
-                image = compile_source(source, extra_flags=flags, name="track", use_cache=use_cache)
-            finally:
-                mark("E")
+            image = compile_source(source, extra_flags=flags, name="track", use_cache=use_cache)
         except CandidateCompileError as exc:
             raise CudaCompileError(f"{exc}\n{exc.log}") from exc
         kernels = tuple(dict.fromkeys(s.kernel for s in stages))
@@ -267,15 +262,12 @@ class CudaTrackEvaluator:
 
             runner = CorrectnessRunner(request.specs, launch, output_dtypes=request.output_dtypes)
             results = []
-            from .supervise import mark
+            from .heartbeat import launching
 
             with gpu_lock("correctness", exclusive=False):  # untimed: may overlap other untimed work, never a timing
                 for name, inputs, refs, scales in request.cases:
-                    mark("B")  # a supervised worker's launch deadline covers each case's trials
-                    try:
+                    with launching():  # the launch deadline covers each case's three trials
                         res = runner.run_case(name, inputs, refs, scales, request.rtol, request.atol_rel, request.exact)
-                    finally:
-                        mark("E")
                     results.append(res)
                     if not res.ok:
                         break
@@ -298,8 +290,15 @@ class CudaTrackEvaluator:
 
         from .gpulock import gpu_lock
 
+        from .heartbeat import launching
+
         ptrs = runner.pointers()
-        run_k = protocol.cuda_event_runner(lambda i: launch(ptrs))
+        batch = protocol.cuda_event_runner(lambda i: launch(ptrs))
+
+        def run_k(k: int) -> float:
+            with launching():  # one synchronised k-launch batch
+                return batch(k)
+
         with gpu_lock("candidate timing"):  # exclusive on this GPU for the whole measurement
             noise, stats, attempts = protocol.measure_interleaved({"candidate": run_k}, reps=reps)
         return {"protocol": "interleaved", "noise_cv": noise, "attempts": attempts, "candidate": stats["candidate"].to_dict()}

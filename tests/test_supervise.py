@@ -7,6 +7,8 @@ from __future__ import annotations
 
 import time
 
+import pytest
+
 from shapeforge_b200 import gpulock
 from shapeforge_b200.supervise import run_bounded
 
@@ -69,3 +71,70 @@ def test_the_track_builder_runs_under_the_compile_deadline():
     rep = run_bounded(f"{F}:builds_a_candidate", {"source": SRC.replace("threadIdx.x]", "threadIdx.x] ")}, timeout=300,
                       compile_deadline_s=0.05)
     assert rep["status"] == "timeout" and rep["reason"] == "compile"
+
+
+def test_heartbeat_record_is_the_fixed_width_interchange_form(tmp_path):
+    from shapeforge_b200 import heartbeat
+
+    rec = heartbeat.record("B", 1767225600.25)
+    assert rec == b"B" + b"%020.6f\n" % 1767225600.25 and len(rec) == 22
+    assert heartbeat.parse(rec) == ("B", 1767225600.25)
+    assert heartbeat.parse(rec[:15]) is None  # half-written: no beat
+    assert heartbeat.parse(b"\x00" * 22) is None
+    hb = heartbeat.HeartbeatFile(tmp_path / "hb")
+    hb.mark("C")
+    hb.mark("E")  # overwritten in place, same width
+    assert (tmp_path / "hb").stat().st_size == 22 and heartbeat.read(tmp_path / "hb")[0] == "E"
+    hb.close()
+
+
+def test_the_reference_parent_reads_our_worker_record(tmp_path):
+    """A reference parent process supervising this backend's worker reads the same record."""
+    import os
+    import sys
+    from pathlib import Path
+
+    ref = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+    if not (ref / "tcenv").is_dir():
+        pytest.skip("reference checkout not mounted")
+    if str(ref) not in sys.path:
+        sys.path.append(str(ref))
+    from tcenv.evaluate import _read_heartbeat
+
+    from shapeforge_b200 import heartbeat
+
+    hb = heartbeat.HeartbeatFile(tmp_path / "hb")
+    hb.mark("W")
+    stage, at = _read_heartbeat(tmp_path / "hb")
+    assert stage == "W" and abs(at - heartbeat.read(tmp_path / "hb")[1]) < 1e-6
+    hb.close()
+
+
+def test_backend_hooks_bracket_nvcc_and_launches():
+    """The reference's workers install (begin, end) pairs through Backend.set_heartbeat_hooks; the
+    CUDA backend runs the compile pair around nvcc (not around a cache hit) and the launch pair
+    around each synchronised launch."""
+    from shapeforge_b200 import heartbeat
+    from shapeforge_b200.backend import CudaBackend
+    from shapeforge_b200.candidates import compile_source
+
+    calls = []
+    CudaBackend().set_heartbeat_hooks(on_compile=(lambda: calls.append("C"), lambda: calls.append("c")),
+                                      on_launch=(lambda: calls.append("B"), lambda: calls.append("b")))
+    try:
+        src = 'extern "C" __global__ void hb_probe(int* x) { x[0] = 1; }\n'
+        compile_source(src, name="hbprobe", use_cache=False)
+        assert calls == ["C", "c"]
+        compile_source(src, name="hbprobe", use_cache=True)  # served from the cache: no compiler run
+        assert calls == ["C", "c"]
+        with pytest.raises(RuntimeError):
+            with heartbeat.launching():
+                raise RuntimeError("device error")
+        assert calls == ["C", "c", "B", "b"]  # the end hook runs on an error too
+        CudaBackend().set_heartbeat_hooks(on_compile=None)  # an omitted pair stays installed
+        with heartbeat.launching():
+            pass
+        assert calls[-2:] == ["B", "b"]
+    finally:
+        heartbeat.set_compile_hooks(None, None)
+        heartbeat.set_launch_hooks(None, None)
