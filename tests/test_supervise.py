@@ -138,3 +138,40 @@ def test_backend_hooks_bracket_nvcc_and_launches():
     finally:
         heartbeat.set_compile_hooks(None, None)
         heartbeat.set_launch_hooks(None, None)
+
+
+def test_timing_batches_are_bracketed_as_launches(monkeypatch, tmp_path):
+    """The portfolio shard timing and the track evaluator's timing run each synchronised k-launch
+    batch inside the launch pair (a fake CUDA-event runner on the host; the real protocol)."""
+    from shapeforge_b200 import heartbeat, portfolio_pack, protocol
+    from shapeforge_b200.track_factory import CudaTrackEvaluator
+
+    monkeypatch.setenv("SF_GPU_LOCK_DIR", str(tmp_path))
+    inside = []
+    depth = [0]
+    heartbeat.set_launch_hooks(lambda: depth.__setitem__(0, depth[0] + 1), lambda: depth.__setitem__(0, depth[0] - 1))
+
+    def fake_runner(launch, stream=None):
+        def run_k(k):
+            inside.append(depth[0])
+            for i in range(k):
+                launch(i)
+            return 1e-5 * k
+        return run_k
+
+    monkeypatch.setattr(protocol, "cuda_event_runner", fake_runner)
+    try:
+        cand, base, noisy, attempts = portfolio_pack._timed(lambda: None, lambda: None, reps=3)
+        assert inside and all(d == 1 for d in inside) and depth[0] == 0
+        assert not noisy and attempts == 1 and abs(cand.median_s - 1e-5) < 1e-12
+
+        class Runner:
+            def pointers(self):
+                return [0]
+
+        inside.clear()
+        doc = CudaTrackEvaluator._time(lambda ptrs: None, Runner(), 3)
+        assert inside and all(d == 1 for d in inside) and depth[0] == 0
+        assert doc["protocol"] == "interleaved" and doc["attempts"] == 1
+    finally:
+        heartbeat.set_launch_hooks(None, None)
