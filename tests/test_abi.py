@@ -2,7 +2,6 @@
 
 from __future__ import annotations
 
-import ctypes
 import re
 from pathlib import Path
 

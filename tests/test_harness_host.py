@@ -3,7 +3,6 @@ Backend protocol's text hooks, and the drop-in through the reference's own loade
 
 from __future__ import annotations
 
-import math
 import os
 import sys
 from pathlib import Path
