@@ -314,6 +314,95 @@ class CudaBackend:
     def compiler_baseline(self, task_name, dtype, size, baseline_us, candidate_us) -> dict:
         return {}
 
+    def assemble(self, contract: Any, source: str) -> tuple[str, int]:
+        """The compilation unit: the runtime headers, then the candidate (tcenv/backends/base.py:236)."""
+        return self.runtime_headers + source, self.runtime_headers.count("\n")
+
+    def rewrite_compiler_lines(self, contract: Any, message: str, header_lines: int) -> str:
+        """Map nvcc's ``file(LINE)`` / ``file:LINE:`` positions back to candidate lines (base.py:245);
+        a position inside the header is reported as such."""
+
+        def fix(open_: str, close: str):
+            def repl(m: re.Match) -> str:
+                line = int(m.group(2)) - header_lines
+                return f"{m.group(1)}{open_}{line}{close}" if line >= 1 else f"{m.group(1)}{open_}<runtime header>{close}"
+            return repl
+
+        message = re.sub(r"(\S+?\.cu)\((\d+)\)", fix("(", ")"), message)
+        return re.sub(r"(\S+?\.cu):(\d+):", fix(":", ":"), message)
+
+    # Validation pass (base.py:98-118).  CUDA builds are not instrumented, so the shared-memory
+    # figure a validation build reports is the real one; the only filter is the reference's.
+    def is_instrumented_size_only(self, violations: list[str]) -> bool:
+        from . import kernel_stats
+
+        return kernel_stats.only_static_smem_limit(violations)
+
+    def validation_problems(self, violations: list[str], static_bytes: list[int], max_tg_memory: int) -> list[str]:
+        """Drop the static shared-memory message when every entry's static bytes fit the limit."""
+        from . import kernel_stats
+
+        if all(int(b) <= int(max_tg_memory) for b in static_bytes):
+            return [v for v in violations if kernel_stats.STATIC_SMEM_LIMIT not in v]
+        return list(violations)
+
+    def validation_summary(self, *, size_only: bool, target: Any) -> str:
+        if not size_only:
+            return "clean"
+        limits = target.limits if hasattr(target, "limits") else target["limits"]
+        limit = limits.max_threadgroup_memory_bytes if hasattr(limits, "max_threadgroup_memory_bytes") else limits["max_threadgroup_memory_bytes"]
+        return f"skipped: only the static shared-memory figure was over the {limit} B limit"
+
+    def coverage(self, task: Any, results: list, source: str, toolchain: dict) -> dict:
+        """Sampled cases (the task's generated cases and seeds), not a domain sweep (base.py:207)."""
+        return {"kind": "sampling", "scope": ""}
+
+    def artifact_builder(self, *, kernel_contract: Any = None, math: str = "fast", kernel_names: Any = None,
+                         diagnostic_profile: str | None = None, specialization: Any = None):
+        """The one builder of this backend (base.py:271): the cuda-single nvcc build."""
+        from .track_factory import CudaTrackBuilder
+
+        if diagnostic_profile is not None:
+            raise ValueError(f"no diagnostic build profile {diagnostic_profile!r} is registered for cuda-sm100")
+        if math not in ("fast", "safe"):
+            raise ValueError(f"math mode must be fast or safe, got {math!r}")
+        return CudaTrackBuilder(extra_flags=("--use_fast_math",) if math == "fast" else ())
+
+    def check_abi(self, contract: Any, kernels: list[Any], *, target: Any = None, device_info: Mapping[str, Any] | None = None,
+                  spec: Any = None, validation: bool = False) -> list[str]:
+        """Compiled entries (``kernel_stats.KernelResources``) against the launch stages ``spec``
+        and the target's limits (base.py:293): every stage's entry compiled, threads, shared memory
+        and registers within one SM."""
+        from . import kernel_stats
+
+        limits = getattr(target, "limits", None) if target is not None else None
+        max_threads = int(getattr(limits, "max_threads_per_threadgroup", kernel_stats.MAX_THREADS_PER_CTA))
+        max_smem = int(getattr(limits, "max_threadgroup_memory_bytes", kernel_stats.MAX_SMEM_PER_CTA))
+        live = int((device_info or {}).get("max_smem_per_block_optin") or 0)
+        if live:
+            max_smem = min(max_smem, live)
+        by_name = {k.name: k for k in kernels}
+        stages = list(spec or [])
+        if stages:
+            problems = kernel_stats.check_stages(by_name, stages, max_threads=max_threads, max_smem=max_smem)
+        else:
+            problems = [f"entry `{k.name}`: {kernel_stats.STATIC_SMEM_LIMIT} ({k.static_smem} > {max_smem} bytes)"
+                        for k in kernels if k.static_smem > max_smem]
+        if validation:
+            problems = self.validation_problems(problems, [k.static_smem for k in kernels], max_smem)
+        return problems
+
+    def pipeline_stats(self, kernel: Any, contract: Any, device_info: Mapping[str, Any], *, kernel_source: str | None = None) -> dict:
+        """One compiled entry under one launch stage ``contract`` (base.py:305)."""
+        from . import kernel_stats
+
+        return kernel_stats.stats(kernel, contract, device_info)
+
+    def pipeline_stats_many(self, pairs: list, device_info: Mapping[str, Any], *, kernel_source: str | None = None) -> dict:
+        from . import kernel_stats
+
+        return kernel_stats.stats_many(pairs, device_info)
+
     # ---- child-process hooks (device) ----------------------------------------------------------
 
     def set_heartbeat_hooks(self, *, on_compile=None, on_launch=None) -> None:

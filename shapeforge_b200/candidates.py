@@ -10,13 +10,14 @@ from __future__ import annotations
 
 import ctypes
 import hashlib
+import json
 import os
 import subprocess
 import tempfile
 from pathlib import Path
 from typing import Sequence
 
-from . import _native, heartbeat
+from . import _native, heartbeat, kernel_stats
 from .build import ARCH, nvcc
 
 CACHE = Path(os.environ.get("SF_CANDIDATE_CACHE", Path(tempfile.gettempdir()) / "shapeforge_b200_candidates"))
@@ -54,12 +55,32 @@ def compile_source(source: str, extra_flags: Sequence[str] = (), name: str = "ca
         src.write_text(source)
         tmp = Path(d) / "out.cubin"
         with heartbeat.compiling():  # an evaluation worker's compile deadline covers nvcc only
-            proc = subprocess.run([nvcc(), *flags, str(src), "-o", str(tmp)], capture_output=True, text=True)
+            # -Xptxas -v only prints each entry's resources; the image is the same, so it is not
+            # part of the cache key.
+            proc = subprocess.run([nvcc(), *flags, "-Xptxas", "-v", str(src), "-o", str(tmp)], capture_output=True,
+                                  text=True)
         if proc.returncode != 0:
             raise CandidateCompileError(f"nvcc failed for {name}", proc.stdout + proc.stderr)
         data = tmp.read_bytes()
+    res = kernel_stats.parse_ptxas(proc.stdout + proc.stderr)
+    _resources_path(out).write_text(json.dumps({k: v.to_dict() for k, v in res.items()}, sort_keys=True))
     out.write_bytes(data)
     return data
+
+
+def _resources_path(cubin: Path) -> Path:
+    return cubin.with_suffix(".resources.json")
+
+
+def kernel_resources(source: str, extra_flags: Sequence[str] = (), name: str = "candidate",
+                     use_cache: bool = True) -> dict[str, "kernel_stats.KernelResources"]:
+    """Per-entry resources (registers, static shared memory, spills, ...) that ptxas assigned when
+    ``source`` was built with ``extra_flags``; builds it when the record is missing."""
+    path = _resources_path(cache_path(source, extra_flags, name))
+    if not (use_cache and path.is_file() and cache_path(source, extra_flags, name).is_file()):
+        compile_source(source, extra_flags, name, use_cache=False)
+    doc = json.loads(path.read_text())
+    return {k: kernel_stats.KernelResources(**v) for k, v in doc.items()}
 
 
 class Module:

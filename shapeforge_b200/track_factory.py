@@ -104,6 +104,7 @@ class CudaBuild:
     stages: tuple[Any, ...]
     flags: tuple[str, ...]
     cache_hit: bool = False  # the image came from the cubin cache rather than from an nvcc run
+    resources: Mapping[str, Any] = field(default_factory=dict)  # entry -> kernel_stats.KernelResources
 
     def document(self) -> dict[str, Any]:
         return {
@@ -176,10 +177,11 @@ class CudaTrackBuilder:
         stages = self.check(source)
         flags = ("-lineinfo",) + self.extra_flags
         try:
-            from .candidates import cache_path
+            from .candidates import cache_path, kernel_resources
 
             cache_hit = use_cache and cache_path(source, flags, "track").is_file()
             image = compile_source(source, extra_flags=flags, name="track", use_cache=use_cache)
+            resources = kernel_resources(source, flags, "track")
         except CandidateCompileError as exc:
             raise CudaCompileError(f"{exc}\n{exc.log}") from exc
         kernels = tuple(dict.fromkeys(s.kernel for s in stages))
@@ -191,6 +193,7 @@ class CudaTrackBuilder:
             stages=stages,
             flags=flags,
             cache_hit=cache_hit,
+            resources=resources,
         )
 
 
@@ -254,6 +257,19 @@ class CudaTrackEvaluator:
         except CudaCompileError as exc:
             return dict(report, status="compile_error", detail=str(exc))
         report["build"] = build.document()
+        if build.resources:
+            # Compiled resources against the launch, before anything launches (Backend.check_abi).
+            from . import kernel_stats
+
+            try:
+                stages = [st.resolve(request.names) for st in build.stages]
+            except Exception:  # noqa: BLE001 - the launcher below reports an unresolvable launch
+                stages = []
+            problems = kernel_stats.check_stages(build.resources, stages)
+            if problems:
+                return dict(report, status="abi_error", detail="; ".join(problems))
+            if stages:
+                report["pipeline"] = kernel_stats.stats_many([(build.resources[s.kernel], s) for s in stages])
         try:
             launch = self.launcher(build, request.scalars, names=request.names)
             from .runtime import CorrectnessRunner
