@@ -265,6 +265,11 @@ class CudaBackend:
                                      "bf16": float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))},
                 "source": "MEASURED_PEAKS.json",
             }
+        from .calibrate import cache_file
+
+        cached = cache_file(target_id)
+        if cached.is_file():
+            return json.loads(cached.read_text())
         return json.loads((ROOT / "targets" / target_id / "calibration.json").read_text())
 
     def roofline(self, task: Any, time_s: float, calibration: dict) -> dict:
@@ -275,7 +280,15 @@ class CudaBackend:
         min_bytes = float(get("min_bytes", 0) or 0)
         flops = float(get("flops", 0) or 0)
         dtype = get("dtype", "fp16")
-        peak_bw = float(calibration.get("copy_gbs")) * 1e9
+        # With the task's read/write split, the achievable bandwidth follows its mix
+        # (profile.py:233-248); without it, the copy figure.
+        rd, wr = get("read_bytes"), get("write_bytes")
+        if rd is not None and wr is not None:
+            from .calibrate import effective_peak_gbps
+
+            peak_bw = effective_peak_gbps(rd, wr, calibration) * 1e9
+        else:
+            peak_bw = float(calibration.get("copy_gbs")) * 1e9
         peak_fl = float(calibration["peak_tflops"].get(dtype, calibration["peak_tflops"]["fp16"])) * 1e12
         t_mem = min_bytes / peak_bw if min_bytes else 0.0
         t_cmp = flops / peak_fl if flops else 0.0
