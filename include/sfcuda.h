@@ -247,13 +247,16 @@ SF_API int sf_gemm_silu(const void* A, const void* B, void* C, int64_t M, int64_
 /*
  * gemm_nn without any device allocation (no counterpart in the reference).  Same result as
  * sf_gemm_nn with a workspace, for callers that cannot allocate device memory at call time:
- * code running inside a host callback (where CUDA API calls are forbidden), hosts whose device
- * memory is fully reserved by another allocator, and certified/real-time hosts that forbid
- * allocation after start-up.  The transpose scratch is a fixed file-scope device array of
- * SF_GEMM_NN_NOALLOC_MAX_SCRATCH_BYTES, held on every GPU that loads the library until exit;
- * problems with K*N*2 bytes above it are rejected with SF_EINVAL.  The first call on a device
- * resolves the array's address (cudaGetSymbolAddress) — make it before any stream capture.
- * All calls share the array: calls that overlap on the GPU race; serialise them on one stream.
+ * hosts whose device memory is fully reserved by another allocator they give no access to, and
+ * certified/real-time hosts that forbid allocation after start-up.  Shapes sf_gemm_nn runs
+ * without a workspace (N % 8 == 0 with aligned tensors, the general kernel, K == 0) run the same
+ * way here and have no size limit.  Shapes that need B transposed use a fixed file-scope device
+ * array of SF_GEMM_NN_NOALLOC_MAX_SCRATCH_BYTES, held on every GPU that loads the library until
+ * exit; those with K*N*2 bytes above it are rejected with SF_EINVAL.  The first such call in a
+ * CUDA context resolves the array's address (cudaGetSymbolAddress) — make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race; serialise them on
+ * one stream.  Like every entry point here it makes CUDA API calls, so it must not be called
+ * from a host function or stream callback.
  */
 #define SF_GEMM_NN_NOALLOC_MAX_SCRATCH_BYTES (32ull * 1024ull * 1024ull)
 SF_API int sf_gemm_nn_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int32_t dtype,
