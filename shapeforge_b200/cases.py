@@ -369,9 +369,11 @@ def kda_gated_lengths(seed: int = SEARCH_SEED, num_seqs: int = 8, lo: int = 256,
     return [int(x) for x in torch.randint(lo, hi + 1, (num_seqs,), generator=g)]
 
 
-def kda_gated_inputs(lengths, heads: int, dim: int, dtype: str, seed: int = SEARCH_SEED) -> dict[str, torch.Tensor]:
+def kda_gated_inputs(lengths, heads: int, dim: int, dtype: str, seed: int = SEARCH_SEED, logit_shift: float = 0.0,
+                     g_const: float | None = None) -> dict[str, torch.Tensor]:
     """The gated KDA workload: q, k ~ N(0,1) then L2-normalised per head (in fp32, then rounded),
-    v ~ N(0,1), beta = sigmoid(N(0,1)) fp32 [T,H], g = logsigmoid(N(0,1)) fp32 [T,H,D]."""
+    v ~ N(0,1), beta = sigmoid(N(0,1)) fp32 [T,H], g = logsigmoid(N(0,1) + logit_shift) fp32
+    [T,H,D], or g = g_const everywhere when given (strong-decay variants of the workload)."""
     g = generator(seed + 1)
     t = int(sum(lengths))
     q = torch.randn((t, heads, dim), generator=g)
@@ -380,7 +382,9 @@ def kda_gated_inputs(lengths, heads: int, dim: int, dtype: str, seed: int = SEAR
     q = q / q.norm(dim=-1, keepdim=True).clamp_min(1e-12)
     k = k / k.norm(dim=-1, keepdim=True).clamp_min(1e-12)
     beta = torch.sigmoid(torch.randn((t, heads), generator=g))
-    gl = torch.nn.functional.logsigmoid(torch.randn((t, heads, dim), generator=g))
+    gl = torch.nn.functional.logsigmoid(torch.randn((t, heads, dim), generator=g) + logit_shift)
+    if g_const is not None:
+        gl = torch.full_like(gl, float(g_const))
     return {"q": round_to(q, dtype), "k": round_to(k, dtype), "v": round_to(v, dtype), "g": gl.float(), "beta": beta.float(),
             "cu_seqlens": cu_from_lengths(lengths)}
 

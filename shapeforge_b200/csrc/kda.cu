@@ -216,8 +216,8 @@ int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, co
     if (N == 0) return SF_OK;
     if (!q || !k || !v || !g || !beta || !a_log || !dt_bias || !initial_state || !cu_seqlens || !scale || !out || !final_state)
         return sf::fail(SF_EINVAL, err, cap, "kda: null tensor pointer");
-    // Variant 0: the chunked tensor-core kernel when it applies (D = 128, aligned rows,
-    // LOWER_BOUND >= -5.4), else the recurrent one; 1 forces the chunked kernel, 2 the recurrent one.
+    // Variant 0: the chunked tensor-core kernel when it applies (D = 128, aligned rows), else the
+    // recurrent one; 1 forces the chunked kernel, 2 the recurrent one.
     if (variant != 2) {
         rc = sf_kda_task_chunk_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, out, final_state, N, H, D,
                                       lower_bound, dtype, st, variant == 1 ? err : nullptr, variant == 1 ? cap : 0);

@@ -9,9 +9,12 @@
 // and the outputs are
 //   o_t = S0 (q~_t * e^{b_t}) + sum_{i<=t} M[t,i] w_i,               M[t,i] = <q~_t e^{b_t}, k_i e^{-b_i}>
 // (q~ = q * scale); the chunk ends with S = S0 diag(e^{b_15}) + W^T Kend, Kend_i = k_i e^{b_15 - b_i}.
-// The factor e^{-b_i} stays finite while the log-decay summed over 16 tokens stays above -87 per
-// channel (always true for decays bounded by -5 per token; for N(0,1) logits it would take 16
-// successive values below -5.4).
+// Every exponential the kernel takes is finite for any log-decay: A and M are products of factors
+// e^{+-(b_t - r)} measured from a per-channel reference r at the midpoint of that channel's b range
+// over the chunk (no factor above e^80 while the range stays within 160, i.e. decays above about
+// -10 per token on average), and a chunk with a wider range forms A and M pair by pair from
+// e^{b_t - b_i} <= 1; Kp, Qp and Kend are exponentials of b_t, b_15 - b_t <= 0.  Per-token decays
+// are floored at -200 (e^-200 is 0 in fp32 either way).
 //
 // Writing B = diag(beta) and T = (I + B A)^-1 B (16 x 16, lower triangular, state-independent),
 // the rows of a chunk are
@@ -39,8 +42,7 @@
 // The task op (tasks/varlen_kda/reference.py:323-374) runs the same kernel with TASK = true: g and beta
 // arrive as 16-bit tensors, each chunk's q and k rows are L2-normalised (rsqrt(sum x^2 + 1e-6), q times
 // the scale tensor) from the staged registers, the log-decay is LOWER_BOUND * sigmoid(exp(A_log[h]) *
-// (g + dt_bias[h, c])) (>= LOWER_BOUND per token, so e^{-b} stays finite over 16 tokens for
-// LOWER_BOUND >= -5.4) and beta is sigmoid(beta).
+// (g + dt_bias[h, c])) (in [LOWER_BOUND, 0] per token) and beta is sigmoid(beta).
 // Every mbarrier wait is bounded; a timeout is reported through sf_kernel_status.
 #include "sf_common.cuh"
 #include "sm100.cuh"
@@ -59,6 +61,13 @@ constexpr int NT = 384;      // threads: a state warpgroup and two prep warpgrou
 constexpr int WG = 128;      // threads per warpgroup
 constexpr int KP = D + 4;    // fp32 staging row stride: 16-byte rows, rows r and r+8 in distinct bank groups
 constexpr uint32_t TMEM_COLS = 256;  // S [0,128), [W'|O'] [128,160)
+// A and M are formed from per-token factors e^{+-(b_t - r)}, r the midpoint of a channel's b range
+// over the chunk; a channel whose half-range exceeds this could overflow them (e^88 is fp32's
+// limit), and the chunk then takes the pairwise path.
+constexpr float FACTOR_LIMIT = 80.f;
+// Per-token log-decays are floored here: e^-200 is 0 in fp32 either way, and the floor keeps the
+// cumulative sums, and the differences of them that the kernel exponentiates, precise.
+constexpr float DECAY_FLOOR = -200.f;
 
 struct Layout {
     static constexpr int WH = 0;                   // W^T high [128 v x 64 (t < 16 used)], 16-bit K-major
@@ -87,7 +96,8 @@ struct Layout {
     static constexpr int TMT = TT + C * C * 4;
     static constexpr int NQ = TMT + C * C * 4;     // task: inverse L2 norms of q and k per token
     static constexpr int NK = NQ + C * 4;
-    static constexpr int PREP_BYTES = NK + C * 4;
+    static constexpr int WIDE = NK + C * 4;        // per-warp votes: a channel's decay range is too wide to factor
+    static constexpr int PREP_BYTES = WIDE + 16;
     static constexpr int BARS = PREP + 2 * PREP_BYTES;
     static constexpr int BYTES = BARS + 64;
 };
@@ -303,38 +313,59 @@ __global__ void __launch_bounds__(NT, 1)
             if (ci + 2 < nchunks) load_chunk<T, TASK>(pf, q, k, v, g, beta, t0 + 2 * C, min(C, end - t0 - 2 * C), H, h, wtid);
 
             // ---- factors in fp32 (thread = key channel c) ----
+            // b_t = the cumulative log-decay from the chunk start.  A and M need e^{b_t - b_i}
+            // (i <= t); they are products of per-token factors e^{+-(b_t - r)} measured from this
+            // channel's reference r, the midpoint of its b range over the chunk, so no factor is
+            // larger than e^{half-range}.  When any channel's half-range exceeds FACTOR_LIMIT the
+            // chunk forms A and M pair by pair instead (exact for any decay).  Kp, Qp (measured
+            // from the chunk start) and Kend (to the chunk end) are exponentials of differences
+            // that are <= 0 for decays <= 0, and stay finite for every input.
             float kp[C], qp[C];
             float elast;
+            bool exact;
             {
-                const float* gs = reinterpret_cast<const float*>(prep + Layout::GS);
+                float* gs = reinterpret_cast<float*>(prep + Layout::GS);
                 const uint16_t* ks = reinterpret_cast<const uint16_t*>(prep + Layout::KS);
                 const uint16_t* qs = reinterpret_cast<const uint16_t*>(prep + Layout::QS);
                 float bcum[C];
-                float bacc = 0.f;
+                float bacc = 0.f, blo = 0.f, bhi = 0.f;
 #pragma unroll
                 for (int t = 0; t < C; ++t) {
                     float gl = gs[t * D + c];
                     if (TASK) gl = task_lb * (1.0f / (1.0f + __expf(-task_ea * (gl + task_dtb))));
+                    gl = gl < DECAY_FLOOR ? DECAY_FLOOR : gl;  // NaN passes through
                     bacc += t < nt_chunk ? gl : 0.f;
                     bcum[t] = bacc;
+                    blo = t == 0 ? bacc : fminf(blo, bacc);
+                    bhi = t == 0 ? bacc : fmaxf(bhi, bacc);
+                    gs[t * D + c] = bacc;  // b, for the pairwise path and Kend (own column only)
                 }
                 elast = __expf(bacc);
+                const float ref = 0.5f * (blo + bhi);
+                const bool wide = !(0.5f * (bhi - blo) <= FACTOR_LIMIT);  // NaN counts as wide
+                const bool warp_wide = __any_sync(0xffffffffu, wide);
+                if ((wtid & 31) == 0) reinterpret_cast<uint32_t*>(prep + Layout::WIDE)[wtid >> 5] = warp_wide ? 1u : 0u;
                 const float* nq = reinterpret_cast<const float*>(prep + Layout::NQ);
                 const float* nk = reinterpret_cast<const float*>(prep + Layout::NK);
 #pragma unroll
                 for (int t = 0; t < C; ++t) {
                     const float kv = from16<T>(ks[t * D + c]) * (TASK ? nk[t] : 1.0f);
                     const float qv = from16<T>(qs[t * D + c]) * (TASK ? nq[t] * qscale : qscale);
-                    const float e = __expf(bcum[t]), en = __expf(-bcum[t]);
-                    kp[t] = kv * e;
-                    qp[t] = qv * e;
-                    kp32[t * KP + c] = kp[t];
+                    const float x = bcum[t] - ref;
+                    const float e = __expf(x), en = __expf(-x), e0 = __expf(bcum[t]);
+                    kp[t] = kv * e0;
+                    qp[t] = qv * e0;
+                    kp32[t * KP + c] = kv * e;
                     kn32[t * KP + c] = kv * en;
-                    qp32[t * KP + c] = qp[t];
+                    qp32[t * KP + c] = qv * e;
                 }
             }
             sm100::named_barrier_sync(bar_id, WG);
             {
+                const uint32_t* votes = reinterpret_cast<const uint32_t*>(prep + Layout::WIDE);
+                exact = (votes[0] | votes[1] | votes[2] | votes[3]) != 0u;
+            }
+            if (!exact) {
                 // A[t][i] (i < t) and M[t][i] (i <= t): thread -> rows t of Kp and Qp, columns i and
                 // i + 8; even and odd channels accumulate in the two halves of packed pairs.
                 const int t = wtid >> 3, i0c = wtid & 7;
@@ -359,8 +390,46 @@ __global__ void __launch_bounds__(NT, 1)
                 ta[t * C + i0c + 8] = i0c + 8 < t ? a1.x + a1.y : 0.f;
                 tm[t * C + i0c] = i0c <= t ? m0.x + m0.y : 0.f;
                 tm[t * C + i0c + 8] = i0c + 8 <= t ? m1.x + m1.y : 0.f;
+            } else {
+                // Pairwise: A[t][i] = sum_c k_t k_i e^{b_t - b_i}, M[t][i] = sum_c q~_t k_i e^{b_t - b_i},
+                // one exponential per (pair, channel).  Columns are visited from a per-thread offset
+                // so the eight rows i of a warp fall in distinct banks.
+                const int t = wtid >> 3, i0c = wtid & 7;
+                const float* bs32 = reinterpret_cast<const float*>(prep + Layout::GS);
+                const uint16_t* ks = reinterpret_cast<const uint16_t*>(prep + Layout::KS);
+                const uint16_t* qs = reinterpret_cast<const uint16_t*>(prep + Layout::QS);
+                const float* nq = reinterpret_cast<const float*>(prep + Layout::NQ);
+                const float* nk = reinterpret_cast<const float*>(prep + Layout::NK);
+                const float nkt = TASK ? nk[t] : 1.0f, nqt = TASK ? nq[t] * qscale : qscale;
+#pragma unroll 1
+                for (int half = 0; half < 2; ++half) {
+                    const int i = i0c + 8 * half;
+                    float a = 0.f, m = 0.f;
+                    if (i <= t) {
+#pragma unroll 4
+                        for (int cc = 0; cc < D; ++cc) {
+                            const int col = (cc + 4 * i0c) & (D - 1);
+                            const float ki = from16<T>(ks[i * D + col]) * __expf(bs32[t * D + col] - bs32[i * D + col]);
+                            a = fmaf(from16<T>(ks[t * D + col]), ki, a);
+                            m = fmaf(from16<T>(qs[t * D + col]), ki, m);
+                        }
+                    }
+                    const float nki = TASK ? nk[i] : 1.0f;
+                    ta[t * C + i] = i < t ? a * nkt * nki : 0.f;
+                    tm[t * C + i] = i <= t ? m * nqt * nki : 0.f;
+                }
             }
             sm100::named_barrier_sync(bar_id, WG);
+            {
+                // Kend_t = k_t e^{b_15 - b_t} into this channel's column of Kn (A and M are done with it).
+                const float* bs32 = reinterpret_cast<const float*>(prep + Layout::GS);
+                const uint16_t* ks = reinterpret_cast<const uint16_t*>(prep + Layout::KS);
+                const float* nk = reinterpret_cast<const float*>(prep + Layout::NK);
+                const float blast = bs32[(C - 1) * D + c];
+#pragma unroll
+                for (int t = 0; t < C; ++t)
+                    kn32[t * KP + c] = from16<T>(ks[t * D + c]) * (TASK ? nk[t] : 1.0f) * __expf(blast - bs32[t * D + c]);
+            }
             if (wtid < C) {
                 // T = (I + B A)^-1 B, column j by forward substitution: x_t = [t == j] - beta_t sum_{i<t} A[t][i] x_i.
                 const int j = wtid;
@@ -412,7 +481,7 @@ __global__ void __launch_bounds__(NT, 1)
                     }
                     *reinterpret_cast<float*>(b1 + kmaj32(t, c)) = k2;
                     *reinterpret_cast<float*>(b1 + kmaj32(C + t, c)) = q2;
-                    *reinterpret_cast<uint16_t*>(keb + kmaj(t, c, 2048)) = to16<T>(kn32[t * KP + c] * elast);  // Kend = k e^{b_15 - b_t}
+                    *reinterpret_cast<uint16_t*>(keb + kmaj(t, c, 2048)) = to16<T>(kn32[t * KP + c]);  // Kend = k e^{b_15 - b_t}
                 }
                 // T, M T and v for the state warpgroup's Vt = T v, Ov = (M T) v.
                 float* tb = reinterpret_cast<float*>(smem + Layout::TB) + b * 2 * C * C;
@@ -631,7 +700,6 @@ int sf_kda_task_chunk_launch(const void* q, const void* k, const void* v, const 
                              const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* out,
                              void* final_state, int64_t N, int64_t H, int64_t Dd, float lower_bound, int32_t dtype, cudaStream_t st,
                              char* err, uint64_t cap) {
-    if (!(lower_bound >= -5.4f)) return sf::fail(SF_EINVAL, err, cap, "kda: the chunked kernel needs LOWER_BOUND >= -5.4");
     return chunk_launch<true>(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, Dd, 0.f,
                               TaskArgs{(const float*)a_log, (const float*)dt_bias, (const float*)scale, lower_bound}, dtype, st, err, cap);
 }

@@ -7,14 +7,17 @@ Per sequence s and head h, with an fp64 state S [D_v, D_k] starting at zero:
 q and k arrive L2-normalised, g is the per-channel log-decay used as given and beta the gate
 used as given.  Values: q, k, v ~ N(0,1) with q, k normalised per token and head,
 beta = sigmoid(N(0,1)), g = logsigmoid(N(0,1)) (the workload distribution); strong_decay shifts
-the decay logits by -3 and wide_v scales v by 100.
+the decay logits by -3, decay_shift8 by -8, constant_decay6 sets every log-decay to -6,
+extreme_decay draws them around -30 with a few exact zeros of the decay (g = -inf), and wide_v
+scales v by 100.  The decay cases span the range a chunked kernel has to survive: cumulative
+log-decays of -100 to -500 over 16 tokens, and infinite ones.
 
 Segmentation: every case keeps the tier's total token count and sequence count (the packed
 shapes are fixed) and re-cuts the batch: canonical (the declared lengths), permuted, skewed (one
 long sequence, the rest of length 1), all_unaligned_primes (prime lengths, the last one takes the
 remainder), max_handoff_stress (lengths 16k +- 1 so sequences straddle 16-token chunk edges),
 chunk_boundary (multiples of 16), zero_length (every other sequence empty), single_sequence (one
-sequence holds every token) and fresh_distribution (seeded random cut points).  strong_decay and
+sequence holds every token) and fresh_distribution (seeded random cut points).  The decay cases and
 wide_v use the canonical cut.
 """
 
@@ -59,7 +62,7 @@ def _fit(lengths, total):
 def _cut(case, canonical, seed):
     n, total = len(canonical), sum(canonical)
     g = _generator(seed + 4099)
-    if case in ("canonical", "strong_decay", "wide_v"):
+    if case in ("canonical", "wide_v") or case in DECAY_CASES:
         return list(canonical)
     if case == "permuted":
         return [canonical[i] for i in torch.randperm(n, generator=g).tolist()]
@@ -94,6 +97,9 @@ def _cut(case, canonical, seed):
     raise ValueError(f"unknown case {case!r}")
 
 
+DECAY_CASES = ("strong_decay", "decay_shift8", "constant_decay6", "extreme_decay")
+
+
 def gen_inputs(case, seed, instance):
     lengths = _cut(case, [int(x) for x in instance.canonical_seq_lens], seed)
     heads, dim = int(instance.symbols["H"]), int(instance.symbols["D"])
@@ -109,9 +115,18 @@ def gen_inputs(case, seed, instance):
     logits = torch.randn((total, heads, dim), generator=g, dtype=f64)
     if case == "strong_decay":
         logits = logits - 3.0
+    elif case == "decay_shift8":
+        logits = logits - 8.0
     elif case == "wide_v":
         v = v * 100.0
-    return {"q": q, "k": k, "v": v, "g": torch.nn.functional.logsigmoid(logits), "beta": beta,
+    decay = torch.nn.functional.logsigmoid(logits)
+    if case == "constant_decay6":
+        decay = torch.full_like(decay, -6.0)
+    elif case == "extreme_decay":
+        decay = -30.0 + 5.0 * torch.randn(decay.shape, generator=g, dtype=f64)
+        zero = torch.rand(decay.shape, generator=g, dtype=f64) < 0.01
+        decay = torch.where(zero, torch.full_like(decay, -math.inf), decay)
+    return {"q": q, "k": k, "v": v, "g": decay, "beta": beta,
             "cu_seqlens": torch.tensor(_offsets(lengths), dtype=torch.int32)}
 
 

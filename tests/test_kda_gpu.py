@@ -60,14 +60,35 @@ def test_reference_vectors(cuda_device, tier, dtype):
         assert v2.ok, (tier, rec["case"], "final_state", v2.summary())
 
 
-def _oracle_task(inp, heads):
+def _oracle_task(inp, heads, lower_bound=-5.0):
     f = lambda n: _np(inp[n])  # noqa: E731
     sel = lambda a: a[:, heads]  # noqa: E731
     out, fin = oref.varlen_kda(
         sel(f("q")), sel(f("k")), sel(f("v")), sel(f("g")), sel(f("beta")), f("A_log")[heads],
         f("dt_bias").reshape(-1, inp["q"].shape[2])[heads].reshape(-1), f("initial_state")[:, heads],
-        inp["cu_seqlens"].cpu().numpy(), float(f("scale")[0]), -5.0)
+        inp["cu_seqlens"].cpu().numpy(), float(f("scale")[0]), lower_bound)
     return out, fin
+
+
+@pytest.mark.parametrize("lower_bound", [-12.0, -60.0])
+def test_task_op_chunked_strong_lower_bound(cuda_device, lower_bound):
+    """LOWER_BOUND beyond what 16-token factors can hold (cumulative decays down to -190 and -960
+    per chunk): the chunked kernel (variant 1) forms those chunks pair by pair and still matches
+    the fp64 oracle."""
+    lengths = [300, 0, 45, 16]
+    heads = 2
+    inp = cases.kda_task_inputs(lengths, heads, 128, "bf16", seed=cases.case_seed(12, 4))
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    out, fin = ops.varlen_kda(d["q"], d["k"], d["v"], d["g"], d["beta"], d["A_log"], d["dt_bias"], d["initial_state"],
+                              d["cu_seqlens"], d["scale"], lower_bound=lower_bound, variant=1)
+    torch.cuda.synchronize()
+    code, where = ops.kernel_status()
+    assert code == 0, (code, where)
+    ro, rf = _oracle_task(d, [0, 1], lower_bound)
+    v1 = _verdict(_np(out), ro, "bf16", "bf16")
+    v2 = _verdict(_np(fin), rf, "bf16", "fp32")
+    assert v1.ok, ("output", lower_bound, v1.summary())
+    assert v2.ok, ("final_state", lower_bound, v2.summary())
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
@@ -159,6 +180,64 @@ def test_gated_workload(cuda_device, dtype):
     assert v1.ok, ("output", v1.summary())
     assert v2.ok, ("final_state", v2.summary())
     assert not torch.isnan(out).any()
+
+
+@pytest.mark.parametrize("decay", [("shift", -8.0), ("const", -6.0), ("const", -30.0)])
+def test_gated_workload_strong_decay(cuda_device, decay):
+    """The workload's lengths and shapes with strong decays, on the default (chunked) kernel:
+    logits shifted by -8 (about -8 per token, cumulative -130 over a 16-token chunk), a constant
+    -6 (-96), and a constant -30 (-480, past what per-token factors can hold, so every chunk takes
+    the pairwise path).  Checked on three heads against the fp64 recurrence."""
+    kind, val = decay
+    lengths = cases.kda_gated_lengths()
+    heads, dim = 16, 128
+    kw = {"logit_shift": val} if kind == "shift" else {"g_const": val}
+    inp = cases.kda_gated_inputs(lengths, heads, dim, "bf16", **kw)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    scale = 1.0 / math.sqrt(dim)
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], scale)
+    torch.cuda.synchronize()
+    code, where = ops.kernel_status()
+    assert code == 0, (code, where)
+    assert torch.isfinite(out.float()).all() and torch.isfinite(fin).all()
+    hs = [0, 7, 15]
+    ro, rf = _oracle_gated(d, hs, scale)
+    v1 = _verdict(_np(out)[:, hs], ro, "bf16", "bf16")
+    v2 = _verdict(_np(fin)[:, hs], rf, "bf16", "fp32")
+    assert v1.ok, ("output", decay, v1.summary())
+    assert v2.ok, ("final_state", decay, v2.summary())
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_gated_chunked_mixed_decay_with_state(cuda_device, dtype):
+    """Chunks of ordinary, strong and infinite decay in one sequence, from a non-zero initial state
+    (variant 1, the chunked kernel): each 16-token chunk of a channel takes the factored or the
+    pairwise path on its own."""
+    lengths = [7, 48, 130, 0, 65]
+    heads = 2
+    inp = cases.kda_gated_inputs(lengths, heads, 128, dtype, seed=21)
+    gen = torch.Generator().manual_seed(5)
+    g = inp["g"].clone()
+    t = g.shape[0]
+    band = (torch.arange(t) // 16) % 3  # chunk bands: 0 ordinary, 1 strong, 2 extreme
+    strong = -6.0 + torch.randn(g.shape, generator=gen)
+    extreme = -40.0 + 10.0 * torch.randn(g.shape, generator=gen)
+    g = torch.where((band == 1)[:, None, None], strong, g)
+    g = torch.where((band == 2)[:, None, None], extreme, g)
+    g[torch.rand(g.shape, generator=gen) < 0.005] = -math.inf
+    inp["g"] = g.float()
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    s0 = (0.1 * torch.randn((len(lengths), heads, 128, 128), generator=gen)).to(cuda_device)
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, initial_state=s0, variant=1)
+    torch.cuda.synchronize()
+    code, where = ops.kernel_status()
+    assert code == 0, (code, where)
+    f = lambda n: _np(d[n])  # noqa: E731
+    ro, rf = oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), inp["cu_seqlens"].numpy(), 0.125, state0=_np(s0))
+    v1 = _verdict(_np(out), ro, dtype, dtype)
+    v2 = _verdict(_np(fin), rf, dtype, "fp32")
+    assert v1.ok, ("output", v1.summary())
+    assert v2.ok, ("final_state", v2.summary())
 
 
 def test_gated_small_ragged(cuda_device):
