@@ -58,21 +58,75 @@ def test_scaled_error_specials_and_floor():
     assert compare.floor_for("fp16") == pytest.approx(0.51 * 2.0**-24)
 
 
+def _reference_comparator():
+    """``scaled_error`` and ``_floor`` from the reference's tcenv/backends/metal/testing.py:140-177.
+
+    That module imports the Metal runtime at the top, so the two functions are taken out of its
+    source with ``ast`` and run as written, with torch and the reference's own subnormal table
+    (tcenv/dtypes.py) as their globals."""
+    import ast
+
+    import torch
+
+    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
+    from tcenv.dtypes import FLOAT_TINY_SUBNORMAL
+
+    path = REF / "tcenv" / "backends" / "metal" / "testing.py"
+    tree = ast.parse(path.read_text())
+    funcs = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in ("scaled_error", "_floor")]
+    assert len(funcs) == 2
+    ns = {"torch": torch, "FLOAT_TINY_SUBNORMAL": FLOAT_TINY_SUBNORMAL}
+    exec(compile(ast.Module(body=funcs, type_ignores=[]), str(path), "exec"), ns)
+    return ns["scaled_error"], ns["_floor"]
+
+
 def test_comparator_agrees_with_reference():
+    """compare.scaled_error / floor_for against the reference's own functions: random values,
+    per-element and scalar scales, every dtype floor, planted specials (matching and mismatching
+    NaN / +-inf), non-finite scales and exact mode; errors and pass/fail verdicts must agree."""
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
     import torch
 
-    sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
-    try:
-        from tcenv.backends.metal.testing import scaled_error as ref_scaled_error  # imports Metal
-    except Exception:
-        pytest.skip("the reference comparator module needs Metal (objc) to import")
+    ref_scaled_error, ref_floor = _reference_comparator()
+    for dt in ("fp16", "bf16", "fp32", "fp64", "i32"):
+        assert compare.floor_for(dt) == ref_floor(dt), dt
     rng = np.random.default_rng(0)
-    o, r = rng.normal(size=100), rng.normal(size=100)
-    ours = compare.scaled_error(o, r, 0.7, 2e-3, 1e-3, False, 1e-8)
-    theirs = ref_scaled_error(torch.tensor(o), torch.tensor(r), 0.7, 2e-3, 1e-3, False, 1e-8).numpy()
-    np.testing.assert_allclose(ours, theirs)
+    specials = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-8, 6e-8])
+
+    def agree(o, r, scale, rtol, atol_rel, exact, floor):
+        ours = compare.scaled_error(o, r, scale, rtol, atol_rel, exact, floor)
+        sc = torch.tensor(scale) if isinstance(scale, np.ndarray) else scale
+        theirs = ref_scaled_error(torch.tensor(o), torch.tensor(r), sc, rtol, atol_rel, exact, floor).numpy()
+        assert ours.shape == theirs.shape
+        assert np.array_equal(np.isinf(ours), np.isinf(theirs))
+        assert np.array_equal(np.isnan(ours), np.isnan(theirs))
+        fin = np.isfinite(ours)
+        np.testing.assert_allclose(ours[fin], theirs[fin], rtol=1e-12, atol=0)
+        assert np.array_equal(ours > 1.0, theirs > 1.0)
+
+    for trial in range(40):
+        n = int(rng.integers(1, 300))
+        r = rng.normal(size=n) * 10.0 ** rng.integers(-6, 4)
+        o = r + rng.normal(size=n) * 10.0 ** rng.integers(-8, 0)
+        if trial % 2:
+            idx = rng.integers(0, n, size=max(1, n // 10))
+            r[idx] = rng.choice(specials, size=idx.size)
+            o[idx] = np.where(rng.random(idx.size) < 0.6, r[idx], rng.choice(specials, size=idx.size))
+        scale = np.abs(rng.normal(size=n)) if trial % 3 == 0 else float(abs(rng.normal()))
+        dtype = ("fp16", "bf16", "fp32")[trial % 3]
+        rtol, atol_rel = [(2e-3, 1e-3), (1.6e-2, 8e-3), (1e-5, 1e-6)][trial % 3]
+        agree(o, r, scale, rtol, atol_rel, False, compare.floor_for(dtype))
+        agree(o, r, scale, rtol, atol_rel, True, 0.0)
+    # Non-finite scales fail everything, scalar or per element.
+    o = rng.normal(size=16)
+    for bad in (np.nan, np.inf):
+        agree(o, o.copy(), bad, 2e-3, 1e-3, False, 0.0)
+        sc = np.ones(16)
+        sc[3] = bad
+        agree(o, o.copy(), sc, 2e-3, 1e-3, False, 0.0)
+    # Zero scale and zero reference: only the floor is left.
+    agree(np.array([0.0, 1e-8, 3e-8, -1e-7]), np.zeros(4), 0.0, 2e-3, 1e-3, False, compare.floor_for("fp16"))
 
 
 # ---- timing protocol (tcenv/bench.py) ----------------------------------------------------------------

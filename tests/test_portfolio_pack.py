@@ -8,6 +8,7 @@ The expression rules are cross-checked against the reference's own evaluator
 from __future__ import annotations
 
 import json
+import os
 import random
 from pathlib import Path
 
@@ -17,7 +18,7 @@ from shapeforge_b200 import expr, fallbacks
 from shapeforge_b200 import portfolio_pack as pp
 from shapeforge_b200.backend import CudaBackend, parse_launch_templates
 
-REF = Path("/root/reference")
+REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
 
 # tasks/gemv/opspec.json: tensors, spec_params and sizes (paper is golden + benchmark, small too).
 GEMV_OPSPEC = {

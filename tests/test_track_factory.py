@@ -10,6 +10,7 @@ is mounted, else built from the same document.
 from __future__ import annotations
 
 import json
+import os
 import sys
 from pathlib import Path
 from types import SimpleNamespace
@@ -21,7 +22,7 @@ from shapeforge_b200 import track_factory as tf
 from shapeforge_b200.backend import CudaBackend, CudaCompileError
 
 ROOT = Path(__file__).resolve().parents[1]
-REF = Path("/root/reference")
+REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
 
 SILU = r'''
 #include <cuda_fp16.h>

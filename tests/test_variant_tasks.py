@@ -12,6 +12,7 @@ from __future__ import annotations
 import importlib.util
 import json
 import math
+import os
 import sys
 from pathlib import Path
 from types import SimpleNamespace
@@ -24,7 +25,7 @@ from oracle import ops as oref
 from shapeforge_b200 import compare
 
 ROOT = Path(__file__).resolve().parents[1]
-REF = Path("/root/reference")
+REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
 TASKS = ("gemm_nt", "bitdelta_gemm_base", "flash_attention_causal", "varlen_kda_gated")
 STORAGE = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32, "i32": torch.int32, "u32": torch.int32}
 
