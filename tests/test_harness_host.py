@@ -131,41 +131,72 @@ def test_comparator_agrees_with_reference():
 
 # ---- timing protocol (tcenv/bench.py) ----------------------------------------------------------------
 
-def test_choose_iters_targets_batch_duration():
+def test_device_batch_size_targets_batch_duration():
     per = 1e-5
-    k = protocol.choose_iters(lambda k: k * per, target_s=0.015, kmin=4)
+    k = protocol.batch_size(lambda k: k * per, target_s=0.015, kmin=4)
     assert k in (1499, 1500)  # 0.015 / 1e-5 in floating point
-    assert protocol.choose_iters(lambda k: k * 0.5, target_s=0.015, kmin=4) == 3  # slow: bounded by the watchdog budget
-    assert protocol.choose_iters(lambda k: k * 1e-9, target_s=0.015, kmin=4, kmax=4000) == 4000
+    assert protocol.batch_size(lambda k: k * 0.5, target_s=0.015, kmin=4) == 3  # slow: bounded by the watchdog share
+    assert protocol.batch_size(lambda k: k * 1e-9, target_s=0.015, kmin=4, kmax=4000) == 4000
+    assert protocol.batch_size(lambda k: k * 0.01, target_s=0.015, kmin=4) == 4  # at least the rotating sets
+    # The doubling search never runs a batch near the watchdog share.
+    sizes = []
+    protocol.batch_size(lambda k: sizes.append(k) or k * 0.2, target_s=0.015, kmin=4)
+    assert max(sizes) == 1
 
 
-def test_interleaved_and_attempt_selection():
-    calls = []
+def test_device_protocol_rotation_and_attempts():
+    firsts = []
 
-    def runner(name, per):
+    def runner(name, per, jitter=()):
+        calls = []
+
         def run_k(k):
-            calls.append(name)
-            return per * k
+            calls.append(k)
+            firsts.append(name)
+            j = jitter[len(calls) % len(jitter)] if jitter else 0.0
+            return per * k * (1.0 + j)
         return run_k
 
-    noise, stats, attempts = protocol.measure_interleaved({"candidate": runner("c", 2e-6), "torch": runner("t", 3e-6)}, reps=5)
+    noise, stats, attempts = protocol.measure_interleaved({"candidate": runner("c", 2e-6), "torch": runner("t", 3e-6)}, reps=6,
+                                                          provider="device")
     assert attempts == 1 and noise == 0.0
     assert stats["candidate"].median_s == pytest.approx(2e-6)
-    assert stats["torch"].reps == 5
-    assert protocol.select_attempt([(0.2, "a"), (0.04, "b"), (0.01, "c")]) == (0.04, "b")
-    assert protocol.select_attempt([(0.2, "a"), (0.1, "b")]) == (0.1, "b")
+    assert stats["torch"].reps == 6
+    # Rotated order: after batch sizing, repetition r starts with runner r mod 2.
+    timed = firsts[-16:]
+    assert timed[0::2] == ["c", "t"] * 4
+    # A runner that is always noisy: three attempts, the least noisy kept and reported.
+    noisy = runner("n", 1e-5, jitter=(0.0, 0.5, -0.3))
+    noise, stats, attempts = protocol.measure_interleaved({"candidate": noisy}, reps=5, provider="device")
+    assert attempts == protocol.BENCH_ATTEMPTS and noise > protocol.NOISY_CV
+    # candidate_serial never decides quietness.
+    noise, stats, attempts = protocol.measure_interleaved({"candidate": runner("c", 2e-6), "candidate_serial": noisy}, reps=5,
+                                                          provider="device")
+    assert attempts == 1 and noise == 0.0
 
 
-def test_protocol_agrees_with_reference_bench():
+def test_harness_provider_is_the_reference_protocol():
     if not REF.is_dir():
         pytest.skip("reference checkout not mounted")
     sys.path.append(str(REF))  # after this repository: the reference also has a `tests` package
     from tcenv import bench as ref_bench
 
-    for per in (1e-7, 1e-5, 1e-3, 0.05, 0.3):
-        run = lambda k, per=per: k * per  # noqa: E731
-        assert protocol.choose_iters(run) == ref_bench.choose_iters(run)
-    assert ref_bench.QUIET_CV == protocol.QUIET_CV and ref_bench.BENCH_ATTEMPTS == protocol.BENCH_ATTEMPTS
+    assert protocol.harness_bench() is ref_bench
+    assert (ref_bench.QUIET_CV, ref_bench.BENCH_ATTEMPTS, ref_bench.BATCH_WALL_BUDGET_S) == (
+        protocol.QUIET_CV, protocol.BENCH_ATTEMPTS, protocol.BATCH_WALL_BUDGET_S)
+    seen = []
+
+    def run_k(k):
+        seen.append(k)
+        return 1e-5 * k
+
+    noise, stats, attempts = protocol.measure_interleaved({"candidate": run_k}, reps=4, provider="harness")
+    # The harness sizes the batch from its own probe (1, 1, then a probe batch): 0.015 / 1e-5.
+    assert seen[:2] == [1, 1] and stats["candidate"].iters == ref_bench.choose_iters(lambda k: 1e-5 * k)
+    assert stats["candidate"].median_s == pytest.approx(1e-5) and attempts == 1
+    # The two providers agree on a deterministic runner.
+    _, dev, _ = protocol.measure_interleaved({"candidate": run_k}, reps=4, provider="device")
+    assert dev["candidate"].median_s == pytest.approx(stats["candidate"].median_s)
 
 
 # ---- exact dispatch and accounts -----------------------------------------------------------------------
