@@ -403,8 +403,9 @@ def _bitdelta_base_workload(m: int, n: int = 4096, k: int = 4096, dtype: str = "
 
 
 def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", world: int = 1, rank: int = 0) -> Workload:
-    """With world > 1 the heads are split into contiguous ranges (every rank runs all sequences
-    for its heads); the job's units are the full problem's bytes."""
+    """With world > 1 the 8 x H (sequence, head) chains are dealt to ranks by a token balance
+    (``shard.chain_assign``) and each rank runs its chains repacked as a single-head packed batch;
+    the job's units are the full problem's bytes."""
     import math
 
     import torch
@@ -414,40 +415,54 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
     lengths = cases.kda_gated_lengths()
     total = int(sum(lengths))
     n = len(lengths)
-    per_head = lambda hh: (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * hh * total + 4.0 * n * hh * dim * dim  # noqa: E731
-    total_bytes = per_head(heads)
-    full_heads = heads
-    if world > 1:
-        h0, h1 = shard.head_ranges(heads, world)[rank]
-        heads = h1 - h0
-    nbytes = per_head(heads)
+    per_token = 3 * 2 * dim + 4 * dim + 4 + 2 * dim  # q, k, v, g, beta in; out
+    total_bytes = per_token * heads * total + 4.0 * n * heads * dim * dim
+    cu = [0]
+    for x in lengths:
+        cu.append(cu[-1] + x)
+    chains = shard.chain_assign(lengths, heads, world)[rank] if world > 1 else None
 
-    def make_inputs(seed):
-        return cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed + 1000 * rank)
+    if chains is None:
+        def make_inputs(seed):
+            return cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed)
+
+        dims, out_specs = (n, heads, dim), [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)]
+        nbytes = total_bytes
+    else:
+        cu_r = shard.chain_offsets(cu, chains)
+        t_r = cu_r[-1]
+
+        def make_inputs(seed):
+            full = cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed)
+            packed = {k: shard.pack_chains(full[k], cu, chains) for k in ("q", "k", "v", "g", "beta")}
+            packed["cu_seqlens"] = torch.tensor(cu_r, dtype=torch.int32)
+            return packed
+
+        dims, out_specs = (len(chains), 1, dim), [((t_r, 1, dim), cases.TORCH_DTYPE[dtype]), ((len(chains), 1, dim, dim), torch.float32)]
+        nbytes = per_token * t_r + 4.0 * len(chains) * dim * dim
 
     def cpu_rows(rows):
         # The delta-rule recurrence (tasks/varlen_kda/reference.py:352-368, gate supplied) through
         # the oracle port on the first `rows` tokens of one (sequence, head) chain.
         from oracle import ops as oref
 
-        inp = make_inputs(cases.SEARCH_SEED)
+        inp = cases.kda_gated_inputs(lengths, 1, dim, dtype, seed=cases.SEARCH_SEED)
         t = min(rows, lengths[0])
         f = lambda name: inp[name][:t, :1].double().numpy()  # noqa: E731
-        cu = [0, t]
-        return ((lambda: oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), cu, 1.0 / math.sqrt(dim))),
-                (3 * 2 * dim + 4 * dim + 4 + 2 * dim) * float(t), f"fp64 recurrence over {t} tokens of one chain")
+        return ((lambda: oref.varlen_kda_gated(f("q"), f("k"), f("v"), f("g"), f("beta"), [0, t], 1.0 / math.sqrt(dim))),
+                per_token * float(t), f"fp64 recurrence over {t} tokens of one chain")
 
     wl = _op_workload(
         "kda_gated", "GB/s", "hbm", dtype, nbytes,
         {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
                      "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
          "total_tokens": total},
-        "kda_chunk_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"],
-        [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim),
+        "kda_chunk_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
         (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,))
-    if world > 1:
+    if chains is not None:
         wl.sharded, wl.total_units = True, total_bytes
-        wl.shard_note = f"H={full_heads} heads split into {world} contiguous ranges (rank {rank}: {heads} heads, all sequences)"
+        wl.shard_note = (f"{n}x{heads} (sequence, head) chains dealt to {world} ranks by token count (rank {rank}: "
+                         f"{len(chains)} chains, {t_r} token-heads), repacked as single-head batches")
     return wl
 
 
@@ -895,11 +910,105 @@ def run_reference(args, wl: Workload) -> dict:
         "vs_baseline": None,
         "dtype": wl.dtype,
         "data": "synthetic",
-        "config": wl.config,
+        "config": _config(wl, args.gpus),
         "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                          "sample": f"{desc} per step (oracle/ restatement of the task reference.py)"},
         "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+# The naturally sharded paths, measured beside the default (replicated) workload so that a run at
+# --gpus N also reports them: attention split by (b, h), varlen KDA by (sequence, head) chains.
+SHARDED_WORKLOADS = ("attention_causal_4x32x2048x128", "kda_gated")
+
+
+def _peak(wl: Workload, clock_summary: dict | None) -> tuple[float, str]:
+    peaks, peak_src = measured_peaks()
+    if wl.bound == "tensor":
+        # The burst GEMM peak for a kernel that ran at full clock; the sustained one (measured
+        # under the power cap) when the timed region itself was power-capped or clocked down.
+        capped = bool(clock_summary) and ("sw_power_cap" in clock_summary["reasons"] or
+                                          clock_summary["sm_mhz"] < 0.97 * float(clock_summary["sm_max_mhz"] or 0))
+        kind = "bf16_tflops_sustained" if capped else "bf16_tflops"
+    else:
+        kind = "hbm_gbs"
+    return float(peaks.get(kind, FALLBACK_PEAKS[kind])), f"{peak_src} ({kind})"
+
+
+def _device_timed(args, wl: Workload, world: int, local: int, steps: int):
+    """W warm-up then exactly ``steps`` launches of ``wl`` (one CUDA graph), bracketed by barriers
+    and synchronisation; returns (this rank's seconds, the max over ranks, clock summary)."""
+    import torch
+    import torch.distributed as dist
+
+    from shapeforge_b200 import _native
+
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    sets = wl.make_sets(dev, wl.nsets)
+    ptr_sets = [p for _, p in sets]
+    desc = wl.desc()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    _native.run_batch(desc, ptr_sets, args.warmup, sptr)
+    torch.cuda.synchronize(dev)
+    # Timed: sf_run_batch captures the launches (set i % nsets for launch i) into one CUDA graph
+    # before the timed region, launches it between two CUDA events on this stream and
+    # synchronises; it returns the events' elapsed device time.  (--no-graph enqueues the
+    # launches one by one from C instead.)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        el_s = _native.run_batch(desc, ptr_sets, steps, sptr, use_graph=not args.no_graph)
+        torch.cuda.synchronize(dev)
+    barrier()
+    code, where = _native.kernel_status(sptr)
+    if code:
+        raise RuntimeError(f"tensor-core kernel status {code} (wait {where}) during the timed region")
+    t = torch.tensor([el_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return el_s, float(t.item()), clocks.summary(), sets
+
+
+def run_sharded(args, world: int, rank: int, local: int) -> dict:
+    """Device-timed lines of the sharded workloads at this world size (strong scaling: the job is
+    the full problem, value = its units / the slowest rank's time)."""
+    import torch
+
+    out = {}
+    steps = max(1, min(args.steps, 100))
+    for name in SHARDED_WORKLOADS:
+        wl = WORKLOADS[name](world, rank)
+        el_s, max_s, clock_summary, sets = _device_timed(args, wl, world, local, steps)
+        del sets
+        torch.cuda.empty_cache()
+        scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+        job = wl.total_units if wl.sharded else wl.units_per_step
+        achieved = wl.units_per_step / (el_s / steps) / scale
+        peak, peak_src = _peak(wl, clock_summary)
+        out[name] = {
+            "value": job * steps / max_s / scale,
+            "unit": wl.unit,
+            "ms_per_step": max_s / steps * 1e3,
+            "steps": steps,
+            "scaling": "strong",
+            "n_gpus": world,
+            "parallelism": wl.shard_note if world > 1 else "1 GPU",
+            "roofline": {"bound": wl.bound, "achieved_rank0": achieved, "peak": peak, "frac_rank0": achieved / peak,
+                         "peak_source": peak_src, "kernel": wl.kernel},
+            "gpu_launches": steps * wl.launches_per_step,
+            "clocks": clock_summary,
+        }
+    return out
+
+
+def _config(wl: Workload, world: int) -> dict:
+    return dict(wl.config, parallelism=(wl.shard_note if wl.sharded else f"replicas x{world}") if world > 1 else "1 GPU")
 
 
 def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | None:
@@ -912,36 +1021,14 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
     torch.cuda.set_device(dev)
     _native.load()
     stream = torch.cuda.current_stream(dev)
-    sptr = stream.cuda_stream
-    sets = wl.make_sets(dev, wl.nsets)
-    ptr_sets = [p for _, p in sets]
-    desc = wl.desc()
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # Warm-up (untimed): W steps.
-    _native.run_batch(desc, ptr_sets, args.warmup, sptr)
-    torch.cuda.synchronize(dev)
-
-    # Timed: exactly K steps.  sf_run_batch captures the K launches (set i % nsets for launch i)
-    # into one CUDA graph before the timed region, launches it between two CUDA events on this
-    # stream and synchronises; it returns the events' elapsed device time.  (--no-graph enqueues
-    # the launches one by one from C instead.)
-    barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
-        el_s = _native.run_batch(desc, ptr_sets, args.steps, sptr, use_graph=not args.no_graph)
-        torch.cuda.synchronize(dev)
-    barrier()
-    code, where = _native.kernel_status(sptr)
-    if code:
-        raise RuntimeError(f"tensor-core kernel status {code} (wait {where}) during the timed region")
-    t = torch.tensor([el_s], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_s = float(t.item())
+    # W untimed warm-up steps, then exactly K timed steps (one CUDA graph between two events).
+    el_s, max_s, clock_summary, sets = _device_timed(args, wl, world, local, args.steps)
+    del sets
 
     # End to end through the C ABI with host buffers (pinned): every step copies its inputs from
     # host to device, runs the operator and copies its outputs back, all inside the timed region.
@@ -1011,18 +1098,7 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
     # Algorithmic units of one step over the step's device time (one launch of the dominant kernel).
     per_step_s = el_s / args.steps
     achieved = wl.units_per_step / per_step_s / scale
-    peaks, peak_src = measured_peaks()
-    clock_summary = clocks.summary()
-    peak_kind = "hbm_gbs"
-    if wl.bound == "tensor":
-        # The burst GEMM peak for a kernel that ran at full clock; the sustained one (measured
-        # under the power cap) when the timed region itself was power-capped or clocked down.
-        capped = bool(clock_summary) and ("sw_power_cap" in clock_summary["reasons"] or
-                                          clock_summary["sm_mhz"] < 0.97 * float(clock_summary["sm_max_mhz"] or 0))
-        peak_kind = "bf16_tflops_sustained" if capped else "bf16_tflops"
-        peak = float(peaks.get(peak_kind, FALLBACK_PEAKS[peak_kind]))
-    else:
-        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    peak, peak_src = _peak(wl, clock_summary)
     e2e_value = job_units * e2e_steps / e2e_time / scale
     h2d = sum(h.numel() * h.element_size() for h in h_in)
     d2h = sum(h.numel() * h.element_size() for h in h_out)
@@ -1039,14 +1115,14 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
         "vs_baseline": None,
         "dtype": wl.dtype,
         "data": "synthetic",
-        "config": dict(wl.config, parallelism=(wl.shard_note if wl.sharded else f"replicas x{world}") if world > 1 else "1 GPU"),
+        "config": _config(wl, world),
         "roofline": {
             "bound": wl.bound,
             "achieved": achieved,
             "peak": peak,
             "unit": wl.unit,
             "frac": achieved / peak,
-            "peak_source": f"{peak_src} ({peak_kind})",
+            "peak_source": peak_src,
             "traffic": _traffic(wl.kernel, wl.name),
             "kernel": wl.kernel,
         },
@@ -1062,6 +1138,16 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
     return line
 
 
+def _finish(args, line: dict | None, world: int, rank: int, local: int) -> dict | None:
+    """Add the sharded paths' lines to the default workload's line (every rank takes part)."""
+    if args.workload == DEFAULT_WORKLOAD and not args.no_sharded:
+        sharded = run_sharded(args, world, rank, local)
+        if line is not None:
+            line["sharded"] = sharded
+            line["gpu_launches"] += sum(v["gpu_launches"] for v in sharded.values())
+    return line
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1070,6 +1156,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded attention / KDA lines added to the default workload's line")
     ap.add_argument("--no-graph", action="store_true",
                     help="enqueue the K timed launches one by one instead of as one captured CUDA graph")
     args = ap.parse_args()
@@ -1086,15 +1174,18 @@ def main() -> None:
     if world > 1:
         import datetime
 
-        # Keep stdout to the one JSON line (NCCL's version banner goes to stdout at INFO/VERSION).
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        # Communicator set-up lines (ranks, transports, NVLS) go to stderr; stdout keeps the one
+        # JSON line.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         import torch
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     try:
-        line = run_ours(args, wl, world, rank, local)
+        line = _finish(args, run_ours(args, wl, world, rank, local), world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

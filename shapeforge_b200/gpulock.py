@@ -13,7 +13,9 @@ keyed by device index: timing on GPU 3 excludes other work on GPU 3 only.  Same 
   returns to shared;
 * the lock is ``flock`` on ``<dir>/gpu<index>.lock``, so the kernel releases it when the holder
   exits, killed or not; an exclusive holder writes its pid and purpose into the file
-  (``holder(device)``);
+  (``holder(device)``); ``<index>`` is the physical GPU: a process restricted by
+  ``CUDA_VISIBLE_DEVICES`` (a per-GPU worker sees its GPU as device 0) locks the GPU the mask
+  names, so workers on different GPUs never share a lock;
 * waiting longer than ``max_wait_s`` raises ``GpuLockTimeout``; ``set_wait_hooks`` lets a worker
   mark its heartbeat while it queues.
 
@@ -45,7 +47,7 @@ class _State:
         self.writable = True
 
 
-_states: dict[int, _State] = {}
+_states: dict[int | str, _State] = {}
 _wait_hooks: tuple[Callable[[], None], Callable[[], None]] | None = None
 
 
@@ -53,8 +55,23 @@ def lock_dir() -> Path:
     return Path(os.environ.get("SF_GPU_LOCK_DIR") or Path.home() / ".cache" / "shapeforge_b200")
 
 
-def lock_file(device: int) -> Path:
-    return lock_dir() / f"gpu{int(device)}.lock"
+def lock_file(device: int | str) -> Path:
+    return lock_dir() / f"gpu{device}.lock"
+
+
+def physical_device(logical: int) -> int | str:
+    """The GPU behind this process's device ``logical``: its entry of ``CUDA_VISIBLE_DEVICES``
+    (an index, or a UUID / MIG name made file-name safe) when the mask is set, else ``logical``."""
+    mask = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if mask is None or not mask.strip():
+        return int(logical)
+    entries = [e.strip() for e in mask.split(",") if e.strip()]
+    if not 0 <= logical < len(entries):
+        return int(logical)
+    entry = entries[logical]
+    if entry.isdigit():
+        return int(entry)
+    return "".join(ch if ch.isalnum() or ch in "-_" else "_" for ch in entry)
 
 
 def set_wait_hooks(on_wait: Callable[[], None], on_acquired: Callable[[], None]) -> None:
@@ -63,7 +80,7 @@ def set_wait_hooks(on_wait: Callable[[], None], on_acquired: Callable[[], None])
     _wait_hooks = (on_wait, on_acquired)
 
 
-def holder(device: int) -> str:
+def holder(device: int | str) -> str:
     """The exclusive holder's note (``pid N: what``), or "" when none was written."""
     try:
         return lock_file(device).read_text(encoding="utf-8", errors="replace").strip()
@@ -104,8 +121,9 @@ def _acquire(fd: int, flag: int, max_wait_s: float) -> float:
 @contextmanager
 def gpu_lock(what: str, *, exclusive: bool = True, device: int | None = None,
              max_wait_s: float = DEFAULT_MAX_WAIT_S) -> Iterator[float]:
-    """Hold the lock of ``device`` (default: the current CUDA device) for the block."""
-    dev = _current_device() if device is None else int(device)
+    """Hold the lock of ``device`` (this process's device index; default: the current CUDA
+    device) for the block; the lock is the physical GPU's (``physical_device``)."""
+    dev = physical_device(_current_device() if device is None else int(device))
     st = _states.setdefault(dev, _State())
     want = "ex" if exclusive else "sh"
     outer, outer_what = st.mode, st.what

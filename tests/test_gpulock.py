@@ -110,3 +110,41 @@ def test_wait_hooks_fire_when_queued(lock_dir):
         gpulock._wait_hooks = None
         release.set()
         p.join(30)
+
+
+def _hold_masked(lock_dir, mask, ready, release, seconds):
+    import os
+
+    os.environ["SF_GPU_LOCK_DIR"] = lock_dir
+    os.environ["CUDA_VISIBLE_DEVICES"] = mask
+    from shapeforge_b200 import gpulock as gl
+
+    with gl.gpu_lock("masked child", device=0):
+        ready.set()
+        release.wait(seconds)
+
+
+def test_lock_is_the_physical_gpu_behind_a_device_mask(lock_dir, monkeypatch):
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3,5")
+    assert gpulock.physical_device(0) == 3 and gpulock.physical_device(1) == 5
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "GPU-1a2b/x")
+    assert gpulock.physical_device(0) == "GPU-1a2b_x"
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert gpulock.physical_device(2) == 2
+    # A worker that sees only GPU 3 (as its device 0) holds GPU 3's lock: device 3 here is
+    # blocked, device 0 here is free.
+    ctx = mp.get_context("spawn")
+    ready, release = ctx.Event(), ctx.Event()
+    p = ctx.Process(target=_hold_masked, args=(lock_dir, "3", ready, release, 10.0))
+    p.start()
+    try:
+        assert ready.wait(60)
+        assert gpulock.holder(3).endswith(": masked child")
+        with pytest.raises(gpulock.GpuLockTimeout):
+            with gpulock.gpu_lock("timing", device=3, max_wait_s=0.3):
+                pass
+        with gpulock.gpu_lock("timing", device=0, max_wait_s=0.3) as waited:
+            assert waited < 0.3
+    finally:
+        release.set()
+        p.join(30)

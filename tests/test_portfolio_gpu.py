@@ -191,6 +191,41 @@ def test_gemv_portfolio_dispatch_run_and_accounts(cuda_device, tmp_path):
     print(json.dumps(doc, indent=1))
 
 
+def gemv_recipe(seed: int = 7) -> dict:
+    """What a portfolio worker needs for the gemv portfolio (called inside the worker, on its GPU)."""
+    dev = torch.device("cuda", 0)
+
+    def make_inputs(p):
+        return {k: v.to(dev) for k, v in cases.gemv_inputs("normal", seed, p.names["M"], p.names["K"], "fp16").items()}
+
+    def verify(p, inputs, outputs):
+        ref = oref.gemv(_np(inputs["A"]), _np(inputs["x"]))
+        v = compare.check(_np(outputs["y"]), ref, compare.rms_scale(ref), dtype="fp16", **TOL["fp16"])
+        return v.ok, v.summary()
+
+    return {"make_inputs": make_inputs, "baseline": torch.mv, "verify": verify}
+
+
+def test_gemv_portfolio_one_gpu_per_shard(cuda_device, tmp_path):
+    """The same portfolio with its shards dealt to every GPU of the machine, one worker process
+    per GPU: every shard verified and timed, both providers in one report."""
+    from shapeforge_b200 import fanout
+
+    points = pp.domain(GEMV_OPSPEC, "fp16")
+    parent = pp.pack(make_tree(tmp_path, {"wide": (WIDE_GUARD, GEMV_VEC)}), points)
+    runs = fanout.measure_on_gpus(parent, GEMV_OPSPEC, points, recipe="tests.test_portfolio_gpu:gemv_recipe", reps=15,
+                                  timeout_s=900)
+    by_key = {r.point.instance_key: r for r in runs}
+    assert set(by_key) == {"fp16/paper/benchmark", "fp16/small/benchmark"}
+    assert by_key["fp16/paper/benchmark"].selected == "wide" and by_key["fp16/small/benchmark"].provider == "fallback"
+    for r in runs:
+        assert r.correct, (r.point.instance_key, r.detail)
+        assert r.candidate_us > 0 and r.baseline_us > 0
+    doc = pp.performance(runs).document()
+    assert {s["provider"] for s in doc["shards"]} == {"candidate", "fallback"}
+    print(json.dumps(doc, indent=1))
+
+
 def test_gemv_portfolio_fresh_confirmation_and_publication(cuda_device, tmp_path):
     """Each point runs twice from a fresh nvcc build: on the search seed and on its fresh seed.
     Every subject is then correct on both runs, and a fully confirmed, publishable portfolio
