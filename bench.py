@@ -1174,11 +1174,11 @@ def main() -> None:
     if world > 1:
         import datetime
 
-        # Communicator set-up lines (ranks, transports, NVLS) go to stderr; stdout keeps the one
-        # JSON line.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        # Communicator set-up lines (ranks, transports, NVLS) go to stderr, whatever the
+        # environment asked for; stdout keeps the one JSON line.
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+        os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
         import torch
         import torch.distributed as dist
 
