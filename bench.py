@@ -144,6 +144,8 @@ class Workload:
     sharded: bool = False
     total_units: float | None = None
     shard_note: str = ""
+    # CPU tensors of the workload at the search seed (for the registered-baseline timing).
+    cpu_inputs: Callable | None = None
 
 
 def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
@@ -207,6 +209,7 @@ def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
         cpu_rows=cpu_rows,
         total_rows=m,
         nsets=nsets,
+        cpu_inputs=lambda: cases.gemm_bench_inputs(m, n, k, dtype, seed=cases.SEARCH_SEED),
     )
 
 
@@ -268,6 +271,7 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
         cpu_rows=cpu_rows,
         total_rows=rows,
         nsets=nsets,
+        cpu_inputs=lambda: cases.rmsnorm_bench_inputs(rows, hidden, dtype),
     )
 
 
@@ -316,7 +320,7 @@ def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_input
     return Workload(name=name, unit=unit, bound=bound, dtype=dtype, units_per_step=units,
                     config=dict(config, l2=f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB"),
                     kernel=kernel, make_sets=make_sets, desc=desc, host_inputs=host_inputs, e2e_launch=e2e_launch,
-                    cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets)
+                    cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets, cpu_inputs=lambda: make_inputs(cases_seed()))
 
 
 def cases_seed() -> int:
@@ -858,6 +862,40 @@ def cpu_baseline(wl: Workload, budget_s: float = 15.0) -> dict:
             "sample": f"{desc} x{reps} in {el:.1f} s"}
 
 
+# Sample of each configuration's registered-baseline timing (rows / heads / tokens), sized so a
+# call takes tens of milliseconds on the host cores.
+REGISTERED_SAMPLE = {"rmsnorm": 4096, "gemm_nt": 512, "bitdelta_base": 4096, "attention": 4, "kda_gated": 512}
+
+
+def registered_baseline(wl: Workload, reps: int = 7) -> dict | None:
+    """The task's registered library baseline (``oracle/baselines.py``: the torch calls of
+    tasks/<t>/baselines.py on CPU tensors) on a sample of the workload, timed with this
+    library's timing protocol (interleaved repetitions, median) on all host threads."""
+    import torch
+
+    from oracle import baselines
+    from shapeforge_b200 import protocol
+
+    key = next((k for k in REGISTERED_SAMPLE if wl.name.startswith(k)), None)
+    if key is None or wl.cpu_inputs is None:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    fn, units, desc = baselines.registered(wl.name, wl.cpu_inputs(), REGISTERED_SAMPLE[key])
+
+    def run_k(k: int) -> float:
+        t0 = time.perf_counter()
+        for _ in range(k):
+            fn()
+        return time.perf_counter() - t0
+
+    noise, stats, attempts = protocol.measure_interleaved({"registered": run_k}, reps=reps, kmin=1, target_s=0.05)
+    per = stats["registered"].median_s
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    return {"value": units / per / scale, "unit": wl.unit, "cores": threads, "kind": "registered baseline (torch CPU)",
+            "sample": f"{desc}: median of {stats['registered'].reps} repetitions, {per * 1e3:.2f} ms per call, CV {noise:.3f}"}
+
+
 def _traffic(kernel: str, workload: str) -> float | None:
     """Per-launch DRAM traffic recorded from an ncu capture in profiles/ (``traffic_bytes: N``)."""
     for p in sorted((ROOT / "profiles").glob("*.md")):
@@ -1135,6 +1173,9 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
+        reg = registered_baseline(wl)
+        if reg is not None:
+            line["registered_baseline"] = reg
     return line
 
 
