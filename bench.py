@@ -461,7 +461,7 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
         {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
                      "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
          "total_tokens": total},
-        "kda_chunk_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
+        "kda_c32_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
         (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,))
     if chains is not None:
         wl.sharded, wl.total_units = True, total_bytes

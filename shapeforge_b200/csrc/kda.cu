@@ -240,11 +240,15 @@ int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void*
     if (N == 0) return SF_OK;
     if (!q || !k || !v || !g || !beta || !cu_seqlens || !out || !final_state)
         return sf::fail(SF_EINVAL, err, cap, "kda_gated: null tensor pointer");
-    // Variant 0: the chunked tensor-core kernel when it applies (D = 128, aligned rows), else the
-    // recurrent one; 1 forces the chunked kernel, 2 the recurrent kernel.
+    // Variant 0: the 32-token chunked tensor-core kernel when it applies (D = 128, aligned rows),
+    // else the recurrent one; 1 forces the 32-token kernel, 3 the 16-token kernel, 2 the
+    // recurrent kernel.
+    if (variant == 3)
+        return sf_kda_gated_chunk_launch(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, D, scale, dtype, st, err,
+                                         cap);
     if (variant != 2) {
-        rc = sf_kda_gated_chunk_launch(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, D, scale, dtype, st,
-                                       variant == 1 ? err : nullptr, variant == 1 ? cap : 0);
+        rc = sf_kda_gated_c32_launch(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, D, scale, dtype, st,
+                                     variant == 1 ? err : nullptr, variant == 1 ? cap : 0);
         if (rc == SF_OK || variant == 1 || rc != SF_EINVAL) return rc;
     }
     if (dtype == SF_DTYPE_F16)

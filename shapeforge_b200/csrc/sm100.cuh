@@ -108,6 +108,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Kernel
     }
 }
 
+// ---- per-thread asynchronous copies (cp.async) ----------------------------------------------
+// Copy 16 bytes from global memory to shared memory asynchronously; only `src_bytes` (0 or 16)
+// are read and the rest of the 16 bytes is zero-filled.  `src` must be 16-byte aligned.
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes) : "memory");
+}
+
+// Copy 4 bytes (src_bytes 0 or 4; zero-filled when 0) from global to shared memory asynchronously.
+__device__ __forceinline__ void cp_async_4(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed; the arrival counts
+// toward the barrier's expected count (.noinc), so a barrier fed by n threads is initialised with n.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // ---- TMA ------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -186,6 +204,19 @@ __device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, ui
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n"
         "}\n" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T for kind::tf32: both operands fp32 in shared memory (read as
+// tf32), described by shared-memory descriptors.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -345,6 +376,13 @@ __host__ __device__ constexpr uint32_t idesc_f16_bmn(uint32_t m, uint32_t n, boo
 //   [15] A major  [16] B major (0 = K)  [17,23) N >> 3  [24,29) M >> 4
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t m, uint32_t n, bool bf16) {
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Instruction descriptor of kind::f16 with an fp32 accumulator and the major-ness of each operand
+// chosen: a_mn / b_mn set bit 15 / 16 (the operand is MN-major in shared memory).
+__host__ __device__ constexpr uint32_t idesc_f16_major(uint32_t m, uint32_t n, bool bf16, bool a_mn, bool b_mn) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+           ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 // Instruction descriptor of kind::tf32 with an fp32 accumulator, both operands K-major (A and B

@@ -119,6 +119,39 @@ int tmap_3d(CUtensorMap* out, const void* base, int64_t d0, int64_t d1, int64_t 
     return SF_OK;
 }
 
+int tmap_3d_f32(CUtensorMap* out, const void* base, int64_t d0, int64_t d1, int64_t d2, int64_t stride1_bytes, int64_t stride2_bytes,
+                int box0, int box1, int box2, char* err, uint64_t cap) {
+    // Cached under a key of its own (dtype field = 2, swizzle field = -4).
+    const Key key{reinterpret_cast<uintptr_t>(base), d1 * 1000003 + d2, d0, stride1_bytes ^ (stride2_bytes << 20), box0,
+                  box1 * 4096 + box2, 2, -4};
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto it = g_cache.find(key);
+        if (it != g_cache.end()) {
+            *out = it->second;
+            return SF_OK;
+        }
+    }
+    auto fn = encode_fn();
+    if (!fn) return fail(SF_EDEVICE, err, cap, "cuTensorMapEncodeTiled is unavailable from the driver");
+    cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+    cuuint64_t strides[2] = {(cuuint64_t)stride1_bytes, (cuuint64_t)stride2_bytes};
+    cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, (cuuint32_t)box2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMap map;
+    CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SF_EINVAL, err, cap, "cuTensorMapEncodeTiled (3-D fp32) failed (%d)", (int)r);
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (g_cache.size() > 4096) g_cache.clear();
+        g_cache.emplace(key, map);
+    }
+    *out = map;
+    return SF_OK;
+}
+
 int tmap_kmajor(CUtensorMap* out, const void* base, int64_t rows, int64_t K, int box_rows, bool bf16, char* err, uint64_t cap) {
     return tmap_2d(out, base, rows, K, K * 2, 64, box_rows, 2, bf16, err, cap);
 }
