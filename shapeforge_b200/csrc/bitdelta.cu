@@ -19,6 +19,9 @@
 //      through distributed shared memory (each CTA sums a slice of the M rows of y from every
 //      peer's partial and writes it).  No workspace.
 //
+// One to four rows of x take a streaming kernel instead (bitdelta_base_stream_kernel, below): a
+// matrix-vector stream over W_base and the sign words, no tensor cores.
+//
 // Sign expansion uses a 256-entry shared-memory table: one 16-byte lookup per 8 signs.  The
 // base kernel keeps 8 interleaved copies of the table (entry e of copy k at 16-byte slot
 // 8e + k) and lane L reads copy L % 8, so the 8 lanes of each 128-bit shared-memory phase hit 8
@@ -513,6 +516,73 @@ __global__ void bitdelta_base_fallback(const T* __restrict__ x, const T* __restr
     y[idx] = sf::Dt<T>::from_f(a1 + sf::Dt<T>::to_f(alpha[n]) * a2);
 }
 
+// ---- few-row streaming kernel (M <= 4) -----------------------------------------------------------
+// For one to four rows of x the product is a matrix-vector stream over W_base (2NK bytes) and the
+// packed signs (NK/8 bytes): one warp per output column n (a row of W_base), lanes streaming
+// 16-byte vectors of that row with four in flight before the first multiply-add, the 8 signs of a
+// vector taken from one byte of its 32-bit sign word (bit j of S_words[n, k/32] is S[n, k], k = 8v
+// + j for vector v), x read through L1 (every warp reads the same x).  fp32 accumulators of
+// x.W_base^T and x.S^T per row, a shuffle reduction, y = acc_w + alpha[n] acc_s: the same two
+// products and the same combination as the tensor-core kernel.
+constexpr int STREAM_WARPS = 4;
+constexpr int STREAM_UNROLL = 4;
+
+template <typename T, int MR>
+__global__ void __launch_bounds__(STREAM_WARPS * 32, MR == 1 ? 8 : 4)
+    bitdelta_base_stream_kernel(const T* __restrict__ x, const T* __restrict__ wb, const uint32_t* __restrict__ sw,
+                                const T* __restrict__ alpha, T* __restrict__ y, int64_t N, int64_t K) {
+    const int lane = threadIdx.x & 31;
+    const int64_t kv = K >> 3, kw = K >> 5;
+    const int64_t wstride = (int64_t)gridDim.x * STREAM_WARPS;
+    for (int64_t n = (int64_t)blockIdx.x * STREAM_WARPS + (threadIdx.x >> 5); n < N; n += wstride) {
+        const T* row = wb + n * K;
+        const uint32_t* srow = sw + n * kw;
+        float aw[MR], as[MR];
+#pragma unroll
+        for (int m = 0; m < MR; ++m) aw[m] = as[m] = 0.f;
+        for (int64_t v0 = lane; v0 < kv; v0 += 32 * STREAM_UNROLL) {
+            sf::Vec8<T> w[STREAM_UNROLL];
+            uint32_t bits[STREAM_UNROLL];
+#pragma unroll
+            for (int u = 0; u < STREAM_UNROLL; ++u) {
+                const int64_t v = v0 + 32 * u;
+                if (v < kv) {
+                    w[u] = sf::ld_global_nc_v8<T>(row + v * 8);
+                    bits[u] = __ldg(srow + (v >> 2)) >> (8 * (v & 3));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < STREAM_UNROLL; ++u) {
+                const int64_t v = v0 + 32 * u;
+                if (v < kv) {
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        sf::Vec8<T> xv;
+                        *reinterpret_cast<uint4*>(&xv) = __ldg(reinterpret_cast<const uint4*>(x + m * K + v * 8));
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float xf = sf::Dt<T>::to_f(xv.v[j]);
+                            aw[m] = fmaf(sf::Dt<T>::to_f(w[u].v[j]), xf, aw[m]);
+                            as[m] += ((bits[u] >> j) & 1u) ? xf : -xf;
+                        }
+                    }
+                }
+            }
+        }
+        const float al = sf::Dt<T>::to_f(alpha[n]);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            float a = aw[m], b = as[m];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                a += __shfl_xor_sync(0xffffffffu, a, off);
+                b += __shfl_xor_sync(0xffffffffu, b, off);
+            }
+            if (lane == 0) y[m * N + n] = sf::Dt<T>::from_f(a + al * b);
+        }
+    }
+}
+
 // ---- host ----------------------------------------------------------------------------------------
 
 sm100::KernelStatus* status_ptr() {
@@ -613,6 +683,36 @@ int sf_bitdelta_base_launch(const void* x, const void* w_base, const void* s_wor
     if (M == 0 || N == 0) return SF_OK;
     if (!x || !w_base || !s_words || !alpha || !y) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: null tensor pointer");
     const bool tc = tc_ok(x, M, N, K) && sf::aligned16(w_base);
+    // Variant 0: the streaming kernel for M <= 4 (aligned bases), else the tensor-core kernel, else
+    // the general kernel; 1 forces the tensor-core kernel, 2 the general one, 3 the streaming one.
+    const bool stream = M <= 4 && sf::aligned16(x) && sf::aligned16(w_base) && K > 0;
+    if (variant == 3 && !stream) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: the streaming variant needs M <= 4 and aligned bases");
+    if (stream && (variant == 0 || variant == 3)) {
+        int64_t blocks = (N + STREAM_WARPS - 1) / STREAM_WARPS;
+        const int64_t cap_blocks = (int64_t)sf::sm_count() * (M == 1 ? 8 : 4);
+        if (blocks > cap_blocks) blocks = cap_blocks;
+#define SF_BITDELTA_STREAM(TT, MRV)                                                                                             \
+    bitdelta_base_stream_kernel<TT, MRV><<<(unsigned)blocks, STREAM_WARPS * 32, 0, st>>>((const TT*)x, (const TT*)w_base,        \
+                                                                                         (const uint32_t*)s_words,             \
+                                                                                         (const TT*)alpha, (TT*)y, N, K)
+        if (dtype == SF_DTYPE_F16) {
+            switch (M) {
+                case 1: SF_BITDELTA_STREAM(__half, 1); break;
+                case 2: SF_BITDELTA_STREAM(__half, 2); break;
+                case 3: SF_BITDELTA_STREAM(__half, 3); break;
+                default: SF_BITDELTA_STREAM(__half, 4); break;
+            }
+        } else {
+            switch (M) {
+                case 1: SF_BITDELTA_STREAM(__nv_bfloat16, 1); break;
+                case 2: SF_BITDELTA_STREAM(__nv_bfloat16, 2); break;
+                case 3: SF_BITDELTA_STREAM(__nv_bfloat16, 3); break;
+                default: SF_BITDELTA_STREAM(__nv_bfloat16, 4); break;
+            }
+        }
+#undef SF_BITDELTA_STREAM
+        return sf::check_launch("bitdelta_base stream launch", err, cap);
+    }
     if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "bitdelta_base: the tensor-core variant needs aligned bases");
     if (tc && variant != 2) {
         return dtype == SF_DTYPE_F16 ? launch_base_tc<__half>(x, w_base, s_words, alpha, y, M, N, K, st, err, cap)

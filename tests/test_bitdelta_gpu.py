@@ -92,3 +92,23 @@ def test_base_fallback_matches(cuda_device):
     torch.cuda.synchronize()
     ref = oref.bitdelta_gemm_base(_np(d["x"]), _np(d["w_base"]), inp["s_words"].numpy(), _np(d["alpha"]))
     assert compare.check(_np(y), ref, compare.rms_scale(ref), dtype="fp16", **TOL["fp16"]).ok
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("shape,variant", [((1, 4096, 4096), 3), ((1, 4096, 4096), 1), ((2, 300, 256), 3), ((3, 200, 96), 3),
+                                           ((4, 1024, 4096), 3), ((1, 77, 32), 3)])
+def test_base_streaming_and_tensor_core_variants(cuda_device, dtype, shape, variant):
+    """The few-row streaming kernel (variant 3: M <= 4, a matrix-vector stream over W_base and the
+    sign words) and, at M = 1, the tensor-core kernel it replaces by default (variant 1), on every
+    case including planted specials, against the oracle."""
+    m, n, k = shape
+    for ci, case in enumerate(cases.BITDELTA_BASE_CASES):
+        inp = cases.bitdelta_base_inputs(case, cases.case_seed(1, ci), m, n, k, dtype)
+        d = {kk: v.to(cuda_device) for kk, v in inp.items()}
+        y = torch.full((m, n), float("nan"), dtype=TD[dtype], device=cuda_device)
+        ops.bitdelta_gemm_base(d["x"], d["w_base"], d["s_words"], d["alpha"], out=y, variant=variant)
+        torch.cuda.synchronize()
+        _status_ok()
+        ref = oref.bitdelta_gemm_base(_np(d["x"]), _np(d["w_base"]), inp["s_words"].numpy(), _np(d["alpha"]))
+        v = compare.check(_np(y), ref, compare.rms_scale(ref), dtype=dtype, **TOL[dtype])
+        assert v.ok, (case, shape, variant, v.summary())
