@@ -402,7 +402,7 @@ def _bitdelta_base_workload(m: int, n: int = 4096, k: int = 4096, dtype: str = "
         f"bitdelta_base_m{m}", "GB/s", "hbm", dtype, nbytes,
         {"workload": f"bitdelta y = x.(W_base + diag(alpha) S)^T, x {dtype} [{m},{k}] ~ N(0,1), W_base {dtype} [{n},{k}] ~ N(0,0.02), "
                      f"S Bernoulli(0.5) packed u32 [{n},{k // 32}], alpha {dtype} U(1e-3,1e-2)", "shape": [m, n, k]},
-        "bitdelta_base_kernel", "bitdelta_gemm_base", make_inputs, ["x", "w_base", "s_words", "alpha"],
+        "bitdelta_base_stream_kernel" if m <= 4 else "bitdelta_base_kernel", "bitdelta_gemm_base", make_inputs, ["x", "w_base", "s_words", "alpha"],
         [((m, n), cases.TORCH_DTYPE[dtype])], (m, n, k), cpu_rows=cpu_rows, total_rows=n)
 
 
