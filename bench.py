@@ -276,10 +276,11 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
 
 
 def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_inputs, in_names, out_specs, dims, attrs=(), flags=0,
-                 cpu_rows=None, total_rows=1, null_args=()) -> Workload:
+                 cpu_rows=None, total_rows=1, null_args=(), scratch_bytes=0, launches_per_step=1) -> Workload:
     """A workload over one C-ABI operator: ``make_inputs(seed)`` gives CPU tensors named
     ``in_names`` (ABI order, followed by the outputs ``out_specs`` = [(shape, dtype)]);
-    ``null_args`` are ABI positions passed as NULL (optional tensors)."""
+    ``null_args`` are ABI positions passed as NULL (optional tensors); ``scratch_bytes`` > 0
+    appends a device workspace of that size (one per device, launches are stream-ordered)."""
     import numpy as np
     import torch
 
@@ -289,19 +290,27 @@ def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_input
     per_set = sum(t.numel() * t.element_size() for t in sample.values()) + sum(
         int(np.prod(s)) * torch.tensor([], dtype=dt).element_size() for s, dt in out_specs)
     nsets = max(2, int(np.ceil(2 * L2_BYTES / per_set)))
+    scratch = {}
 
-    def ptr_list(ins, outs):
+    def scratch_ptr(dev):
+        if not scratch_bytes:
+            return []
+        if dev not in scratch:
+            scratch[dev] = torch.empty(scratch_bytes, dtype=torch.uint8, device=dev)
+        return [scratch[dev].data_ptr()]
+
+    def ptr_list(ins, outs, dev):
         ptrs = [ins[n].data_ptr() for n in in_names] + [o.data_ptr() for o in outs]
         for pos in null_args:
             ptrs.insert(pos, 0)
-        return ptrs
+        return ptrs + scratch_ptr(dev)
 
     def make_sets(dev, count):
         out = []
         for s in range(count):
             ins = {k: v.to(dev) for k, v in make_inputs(cases_seed() + s).items()}
             outs = [torch.empty(shape, dtype=dt, device=dev) for shape, dt in out_specs]
-            out.append(((ins, outs), ptr_list(ins, outs)))
+            out.append(((ins, outs), ptr_list(ins, outs, dev)))
         return out
 
     def desc():
@@ -315,12 +324,13 @@ def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_input
         ptrs = [t.data_ptr() for t in d_in] + [o.data_ptr() for o in d_out]
         for pos in null_args:
             ptrs.insert(pos, 0)
-        _native.run_op(desc(), ptrs, stream)
+        _native.run_op(desc(), ptrs + scratch_ptr(d_in[0].device), stream)
 
     return Workload(name=name, unit=unit, bound=bound, dtype=dtype, units_per_step=units,
                     config=dict(config, l2=f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB"),
                     kernel=kernel, make_sets=make_sets, desc=desc, host_inputs=host_inputs, e2e_launch=e2e_launch,
-                    cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets, cpu_inputs=lambda: make_inputs(cases_seed()))
+                    cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets, launches_per_step=launches_per_step,
+                    cpu_inputs=lambda: make_inputs(cases_seed()))
 
 
 def cases_seed() -> int:
@@ -414,7 +424,7 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
 
     import torch
 
-    from shapeforge_b200 import cases, shard
+    from shapeforge_b200 import cases, ops, shard
 
     lengths = cases.kda_gated_lengths()
     total = int(sum(lengths))
@@ -430,7 +440,8 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
         def make_inputs(seed):
             return cases.kda_gated_inputs(lengths, heads, dim, dtype, seed=seed)
 
-        dims, out_specs = (n, heads, dim), [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)]
+        ws = ops.varlen_kda_gated_workspace_bytes(total, n, heads, dim)
+        dims, out_specs = (n, heads, dim, total, ws), [((total, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)]
         nbytes = total_bytes
     else:
         cu_r = shard.chain_offsets(cu, chains)
@@ -442,7 +453,8 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
             packed["cu_seqlens"] = torch.tensor(cu_r, dtype=torch.int32)
             return packed
 
-        dims, out_specs = (len(chains), 1, dim), [((t_r, 1, dim), cases.TORCH_DTYPE[dtype]), ((len(chains), 1, dim, dim), torch.float32)]
+        ws = ops.varlen_kda_gated_workspace_bytes(t_r, len(chains), 1, dim)
+        dims, out_specs = (len(chains), 1, dim, t_r, ws), [((t_r, 1, dim), cases.TORCH_DTYPE[dtype]), ((len(chains), 1, dim, dim), torch.float32)]
         nbytes = per_token * t_r + 4.0 * len(chains) * dim * dim
 
     def cpu_rows(rows):
@@ -461,8 +473,8 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
         {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
                      "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
          "total_tokens": total},
-        "kda_c32_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
-        (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,))
+        "kda_chain_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
+        (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,), scratch_bytes=ws, launches_per_step=3)
     if chains is not None:
         wl.sharded, wl.total_units = True, total_bytes
         wl.shard_note = (f"{n}x{heads} (sequence, head) chains dealt to {world} ranks by token count (rank {rank}: "

@@ -204,6 +204,20 @@ SF_API int sf_varlen_kda_gated(const void* q, const void* k, const void* v, cons
                int64_t H, int64_t D, float scale, int32_t dtype, void* stream, char* err, uint64_t cap);
 
 /*
+ * varlen_kda_gated with a caller workspace: the two-pass kernels (every 32-token chunk's operands
+ * formed in parallel into `workspace`, then one state chain per (sequence, head)) when D = 128 and
+ * `workspace` holds sf_varlen_kda_gated_workspace_bytes(total_tokens, num_seqs, H, D) bytes at a
+ * 256-byte-aligned address; otherwise as sf_varlen_kda_gated.  total_tokens = cu_seqlens[num_seqs]
+ * (the rows of q); the workspace needs no initialisation and may be reused once the call's work on
+ * `stream` is done.  No reference counterpart: the reference's varlen_kda ABI has no workspace.
+ */
+SF_API uint64_t sf_varlen_kda_gated_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int64_t H, int64_t D);
+SF_API int sf_varlen_kda_gated_ws(const void* q, const void* k, const void* v, const void* g, const void* beta,
+               const void* cu_seqlens, const void* initial_state, void* output, void* final_state, int64_t num_seqs,
+               int64_t total_tokens, int64_t H, int64_t D, float scale, int32_t dtype, void* workspace,
+               uint64_t workspace_bytes, void* stream, char* err, uint64_t cap);
+
+/*
  * mamba2_chunk_scan (tasks/mamba2_chunk_scan/reference.py:106-127): the Mamba-2 SSD chunk scan of
  * one B/C group.  x [B,L,H,P], dt [B,L,H], dA_cumsum [B,H,NC,chunk] (NC = L / chunk),
  * Bmat/Cmat [B,L,N], Dskip [H], states [B,NC,H,P,N] in, y [B,L,H,P] out, all in dtype, fp32
@@ -339,8 +353,10 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_ATTENTION dims = {B, H, S, D}  attrs = {scale}  flags bit 0 = causal  args = {q, k, v, o}
  *   SF_OP_KDA       dims = {num_seqs, H, D}  attrs = {lower_bound}
  *                   args = {q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state}
- *   SF_OP_KDA_GATED dims = {num_seqs, H, D}  attrs = {scale}
- *                   args = {q, k, v, g, beta, cu_seqlens, initial_state (may be NULL), output, final_state}
+ *   SF_OP_KDA_GATED dims = {num_seqs, H, D, total_tokens, ws_bytes}  attrs = {scale}
+ *                   args = {q, k, v, g, beta, cu_seqlens, initial_state (may be NULL), output, final_state,
+ *                           workspace (may be NULL: single-pass kernels)}
+ *                   variant 4 forces the two-pass kernels, 1 the single-pass 32-token kernel
  *   SF_OP_MAMBA2    dims = {B, L, H, P, N, chunk}
  *                   args = {x, dt, dA_cumsum, Bmat, Cmat, Dskip, states, y}
  *   SF_OP_RELU / SF_OP_SIGMOID / SF_OP_SIGMOID_SHIFT  dims = {n}       args = {x, y}

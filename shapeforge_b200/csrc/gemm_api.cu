@@ -235,17 +235,18 @@ extern "C" int sf_kernel_status(uint32_t* code, uint32_t* where, void* stream, c
     if (!code || !where) return sf::fail(SF_EINVAL, err, cap, "sf_kernel_status: null output");
     // Each tensor-core module keeps its own status word; the first failure found is reported
     // (the wait ids are unique across modules) and every word is cleared.
-    uint32_t c[6] = {0, 0, 0, 0, 0, 0}, w[6] = {0, 0, 0, 0, 0, 0};
+    uint32_t c[7] = {0, 0, 0, 0, 0, 0, 0}, w[7] = {0, 0, 0, 0, 0, 0, 0};
     if (sf_gemm_status_read(&c[0], &w[0], (cudaStream_t)stream) != SF_OK ||
         sf_bitdelta_status_read(&c[1], &w[1], (cudaStream_t)stream) != SF_OK ||
         sf_attention_status_read(&c[2], &w[2], (cudaStream_t)stream) != SF_OK ||
         sf_mamba2_status_read(&c[3], &w[3], (cudaStream_t)stream) != SF_OK ||
         sf_kda_status_read(&c[4], &w[4], (cudaStream_t)stream) != SF_OK ||
-        sf_kda32_status_read(&c[5], &w[5], (cudaStream_t)stream) != SF_OK)
+        sf_kda32_status_read(&c[5], &w[5], (cudaStream_t)stream) != SF_OK ||
+        sf_kda_split_status_read(&c[6], &w[6], (cudaStream_t)stream) != SF_OK)
         return sf::fail(SF_EDEVICE, err, cap, "sf_kernel_status: reading the status word failed");
     *code = 0;
     *where = 0;
-    for (int i = 0; i < 6; ++i) {
+    for (int i = 0; i < 7; ++i) {
         if (c[i] && !*code) {
             *code = c[i];
             *where = w[i];

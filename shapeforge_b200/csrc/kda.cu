@@ -234,15 +234,22 @@ int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, co
 
 int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                         const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
-                        int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+                        int32_t dtype, int32_t variant, int64_t total_tokens, void* workspace, uint64_t workspace_bytes,
+                        cudaStream_t st, char* err, uint64_t cap) {
     int rc = check(N, H, D, dtype, err, cap);
     if (rc) return rc;
     if (N == 0) return SF_OK;
     if (!q || !k || !v || !g || !beta || !cu_seqlens || !out || !final_state)
         return sf::fail(SF_EINVAL, err, cap, "kda_gated: null tensor pointer");
-    // Variant 0: the 32-token chunked tensor-core kernel when it applies (D = 128, aligned rows),
-    // else the recurrent one; 1 forces the 32-token kernel, 3 the 16-token kernel, 2 the
-    // recurrent kernel.
+    // Variant 0: the two-pass kernels (all chunks prepared in parallel, then the chains) when
+    // they apply (D = 128, aligned rows, a workspace of sf_varlen_kda_gated_workspace_bytes),
+    // else the single-pass 32-token kernel, else the recurrent one.  4 forces the two-pass
+    // kernels, 1 the single-pass 32-token kernel, 3 the 16-token kernel, 2 the recurrent kernel.
+    if (variant == 4 || (variant == 0 && workspace)) {
+        rc = sf_kda_gated_split_launch(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, total_tokens, H, D, scale, dtype,
+                                       workspace, workspace_bytes, st, variant == 4 ? err : nullptr, variant == 4 ? cap : 0);
+        if (rc == SF_OK || variant == 4 || rc != SF_EINVAL) return rc;
+    }
     if (variant == 3)
         return sf_kda_gated_chunk_launch(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, H, D, scale, dtype, st, err,
                                          cap);
@@ -322,6 +329,18 @@ extern "C" int sf_varlen_kda(const void* q, const void* k, const void* v, const 
 extern "C" int sf_varlen_kda_gated(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                                    const void* initial_state, void* output, void* final_state, int64_t num_seqs, int64_t H, int64_t D,
                                    float scale, int32_t dtype, void* stream, char* err, uint64_t cap) {
+    return sf_kda_gated_launch(q, k, v, g, beta, cu_seqlens, initial_state, output, final_state, num_seqs, H, D, scale, dtype, 0, 0,
+                               nullptr, 0, (cudaStream_t)stream, err, cap);
+}
+
+extern "C" uint64_t sf_varlen_kda_gated_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int64_t H, int64_t D) {
+    return sf_kda_gated_split_workspace(total_tokens, num_seqs, H, D);
+}
+
+extern "C" int sf_varlen_kda_gated_ws(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                                      const void* cu_seqlens, const void* initial_state, void* output, void* final_state,
+                                      int64_t num_seqs, int64_t total_tokens, int64_t H, int64_t D, float scale, int32_t dtype,
+                                      void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap) {
     return sf_kda_gated_launch(q, k, v, g, beta, cu_seqlens, initial_state, output, final_state, num_seqs, H, D, scale, dtype, 0,
-                               (cudaStream_t)stream, err, cap);
+                               total_tokens, workspace, workspace_bytes, (cudaStream_t)stream, err, cap);
 }

@@ -30,6 +30,7 @@
 // start-address field; shared-memory addresses stay below 2^18, so the field never carries).
 // Every mbarrier wait is bounded and reports through sf_kernel_status; a role whose wait gave up
 // keeps executing the same barrier sequence without work, so the CTA always runs to its end.
+#include "kda_layout.cuh"
 #include "sf_common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -93,37 +94,12 @@ struct __align__(8) Bars {
     uint32_t tmem_base;
 };
 
-template <typename T>
-__device__ __forceinline__ uint16_t to16(float x) {
-    const T h = sf::Dt<T>::from_f(x);
-    return *reinterpret_cast<const uint16_t*>(&h);
-}
-template <typename T>
-__device__ __forceinline__ float from16(uint16_t u) {
-    return sf::Dt<T>::to_f(*reinterpret_cast<const T*>(&u));
-}
-
-// Byte offset of fp32 element (row r, column c) of a K-major operand with the 128-byte swizzle,
-// K-blocks of 32 columns `blk` bytes apart.
-__device__ __forceinline__ int kmaj32(int r, int c, int blk) {
-    return (c >> 5) * blk + r * 128 + ((((c & 31) >> 2) ^ (r & 7)) << 4) + ((c & 3) << 2);
-}
-// Byte offset of 16-bit element (row r = K index, column c = MN index) of an MN-major operand with
-// the 128-byte swizzle, 64-column blocks `blk` bytes apart.
-__device__ __forceinline__ int mnmaj16(int r, int c, int blk) {
-    return (c >> 6) * blk + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1);
-}
-// Byte offset of the 16-byte chunk j (0..7) of row r in a 128-byte-swizzled row-major tile.
-__device__ __forceinline__ int chunk128(int r, int j) { return r * 128 + (((j & 7) ^ (r & 7)) << 4); }
-
-template <typename T>
-__device__ __forceinline__ uint32_t pack_hi_lo(float x0, float x1, uint32_t& lo) {
-    const uint16_t h0 = to16<T>(x0), h1 = to16<T>(x1);
-    const float f0 = from16<T>(h0), f1 = from16<T>(h1);
-    const float r0 = isfinite(f0) ? x0 - f0 : 0.f, r1 = isfinite(f1) ? x1 - f1 : 0.f;
-    lo = (uint32_t)to16<T>(r0) | ((uint32_t)to16<T>(r1) << 16);
-    return (uint32_t)h0 | ((uint32_t)h1 << 16);
-}
+using kdal::chunk128;
+using kdal::from16;
+using kdal::kmaj32;
+using kdal::mnmaj16;
+using kdal::pack_hi_lo;
+using kdal::to16;
 
 // Stage one chunk's q, k (16-bit), g and beta (fp32) into shared memory with cp.async: tokens past
 // the chain's end are zero-filled (nothing is read for them).  Every prep thread copies its share

@@ -227,7 +227,8 @@ int sf_kda_task_chunk_launch(const void* q, const void* k, const void* v, const 
                              char* err, uint64_t cap);
 int sf_kda_gated_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                         const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
-                        int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);
+                        int32_t dtype, int32_t variant, int64_t total_tokens, void* workspace, uint64_t workspace_bytes,
+                        cudaStream_t st, char* err, uint64_t cap);
 int sf_kda_gated_chunk_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
                               const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
                               int32_t dtype, cudaStream_t st, char* err, uint64_t cap);
@@ -236,6 +237,12 @@ int sf_kda_gated_c32_launch(const void* q, const void* k, const void* v, const v
                             const void* initial_state, void* out, void* final_state, int64_t N, int64_t H, int64_t D, float scale,
                             int32_t dtype, cudaStream_t st, char* err, uint64_t cap);
 int sf_kda32_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
+uint64_t sf_kda_gated_split_workspace(int64_t total_tokens, int64_t nseq, int64_t H, int64_t D);
+int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                              const void* initial_state, void* out, void* final_state, int64_t N, int64_t total_tokens, int64_t H,
+                              int64_t D, float scale, int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st,
+                              char* err, uint64_t cap);
+int sf_kda_split_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
 int sf_mamba2_launch(const void* x, const void* dt, const void* cs, const void* bm, const void* cm, const void* dskip, const void* states,
                      void* y, int64_t B, int64_t L, int64_t H, int64_t P, int64_t N, int64_t C, int32_t dtype, int32_t variant,
                      cudaStream_t st, char* err, uint64_t cap);

@@ -108,6 +108,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Kernel
     }
 }
 
+// Non-blocking probe of the phase with parity `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred P;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, P;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for latency-critical waits: the thread polls instead of being suspended, so it
+// resumes within a few cycles of the phase completing.  Same time limit and status report.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, KernelStatus* st, uint32_t where,
+                                               uint64_t limit_ns = 2000000000ull) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t polls = 0;
+    while (true) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((++polls & 1023u) == 0) {
+            if (st && *reinterpret_cast<volatile unsigned int*>(&st->code) != 0) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                if (st) {
+                    if (atomicCAS(&st->code, 0u, 1u) == 0u) st->where = where;
+                }
+                return false;
+            }
+        }
+    }
+}
+
 // ---- per-thread asynchronous copies (cp.async) ----------------------------------------------
 // Copy 16 bytes from global memory to shared memory asynchronously; only `src_bytes` (0 or 16)
 // are read and the rest of the 16 bytes is zero-filled.  `src` must be 16-byte aligned.
@@ -125,6 +161,26 @@ __device__ __forceinline__ void cp_async_4(uint32_t dst_smem, const void* src, u
 __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+
+// ---- bulk copies ----------------------------------------------------------------------------
+// Contiguous copy of `bytes` from global memory into this CTA's shared memory by the bulk-copy
+// engine; completion decrements the transaction count of `bar` by `bytes`.  Both addresses must
+// be 16-byte aligned and `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Contiguous copy of `bytes` from this CTA's shared memory to global memory by the bulk-copy
+// engine, tracked by the issuing thread's bulk groups (bulk_commit / bulk_wait_all).  Shared
+// memory written by generic stores must be fenced to the async proxy first.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- TMA ------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -362,6 +418,20 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t 
     d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
     d |= (uint64_t)1 << 46;
     d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Shared-memory descriptor for an MN-major 32-bit (tf32) operand in the 128-byte swizzle with
+// 32-byte granules (layout type 1, SWIZZLE_128B_BASE32B): rows of 32 MN elements (128 B) per K
+// index, 4 K rows per 512-byte atom with the row's 32-byte granules XOR-ed by (K index & 3), atoms
+// (4-K groups) `sbo` bytes apart and 32-element MN blocks `lbo` bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_b32(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)1 << 61;
     return d;
 }
 

@@ -347,9 +347,14 @@ def kda(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound: flo
 
 
 def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: torch.Tensor | None = None,
-                     output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0):
+                     output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0,
+                     workspace: torch.Tensor | None = None):
     """Gated KDA workload: q, k pre-normalised, ``g`` fp32 log-decay used directly, ``beta`` fp32
-    gate used directly, state from zero (or ``initial_state``)."""
+    gate used directly, state from zero (or ``initial_state``).
+
+    At D = 128 the default (and ``variant=4``) runs the two-pass kernels over ``workspace`` (uint8,
+    at least ``varlen_kda_gated_workspace_bytes``; allocated here when not given); ``variant=1``
+    forces the single-pass 32-token kernel, 2 the recurrent kernel, 3 the 16-token kernel."""
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check(t, name, q.dtype)
     _check(g, "g", torch.float32)
@@ -363,10 +368,20 @@ def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: 
     if initial_state is not None:
         _check(initial_state, "initial_state", torch.float32)
         s0 = initial_state.data_ptr()
+    need = varlen_kda_gated_workspace_bytes(t_, n, h, d) if variant in (0, 4) else 0
+    if workspace is None and need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if workspace is not None else 0
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     ptrs = [q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), cu_seqlens.data_ptr(), s0,
-            output.data_ptr(), final_state.data_ptr()]
-    _run("varlen_kda_gated", q, ptrs, dims=(n, h, d), attrs=(scale,), variant=variant)
+            output.data_ptr(), final_state.data_ptr(), ws_ptr]
+    _run("varlen_kda_gated", q, ptrs, dims=(n, h, d, t_, ws_bytes), attrs=(scale,), variant=variant)
     return output, final_state
+
+
+def varlen_kda_gated_workspace_bytes(total_tokens: int, num_seqs: int, heads: int, dim: int) -> int:
+    """Workspace bytes of the two-pass gated KDA kernels (0 when they do not apply)."""
+    return int(_native.load().sf_varlen_kda_gated_workspace_bytes(total_tokens, num_seqs, heads, dim))
 
 
 def mamba2_chunk_scan(x, dt, dA_cumsum, b_mat, c_mat, d_skip, states, out: torch.Tensor | None = None,

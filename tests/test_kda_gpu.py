@@ -208,11 +208,12 @@ def test_gated_workload_strong_decay(cuda_device, decay):
     assert v2.ok, ("final_state", decay, v2.summary())
 
 
+@pytest.mark.parametrize("variant", [1, 4])
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
-def test_gated_chunked_mixed_decay_with_state(cuda_device, dtype):
-    """Chunks of ordinary, strong and infinite decay in one sequence, from a non-zero initial state
-    (variant 1, the chunked kernel): each 16-token chunk of a channel takes the factored or the
-    pairwise path on its own."""
+def test_gated_chunked_mixed_decay_with_state(cuda_device, dtype, variant):
+    """Chunks of ordinary, strong and infinite decay in one sequence, from a non-zero initial state,
+    on the single-pass (variant 1) and two-pass (variant 4) chunked kernels: each chunk takes the
+    factored or the pairwise path on its own."""
     lengths = [7, 48, 130, 0, 65]
     heads = 2
     inp = cases.kda_gated_inputs(lengths, heads, 128, dtype, seed=21)
@@ -228,7 +229,8 @@ def test_gated_chunked_mixed_decay_with_state(cuda_device, dtype):
     inp["g"] = g.float()
     d = {k: v.to(cuda_device) for k, v in inp.items()}
     s0 = (0.1 * torch.randn((len(lengths), heads, 128, 128), generator=gen)).to(cuda_device)
-    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, initial_state=s0, variant=1)
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, initial_state=s0,
+                                    variant=variant)
     torch.cuda.synchronize()
     code, where = ops.kernel_status()
     assert code == 0, (code, where)
@@ -238,6 +240,44 @@ def test_gated_chunked_mixed_decay_with_state(cuda_device, dtype):
     v2 = _verdict(_np(fin), rf, dtype, "fp32")
     assert v1.ok, ("output", v1.summary())
     assert v2.ok, ("final_state", v2.summary())
+
+
+def test_gated_two_pass_matches_single_pass(cuda_device):
+    """The two-pass kernels (the default at D = 128) against the single-pass 32-token kernel on the
+    workload: the same chunk algebra, so the outputs agree to a few 16-bit ulps."""
+    lengths = cases.kda_gated_lengths()
+    inp = cases.kda_gated_inputs(lengths, 16, 128, "bf16")
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    args = (d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 1.0 / math.sqrt(128))
+    o4, f4 = ops.varlen_kda_gated(*args, variant=4)
+    o1, f1 = ops.varlen_kda_gated(*args, variant=1)
+    torch.cuda.synchronize()
+    assert ops.kernel_status()[0] == 0
+    assert (o4.float() - o1.float()).abs().max().item() <= 0.02 * o1.float().abs().max().item()
+    assert (f4 - f1).abs().max().item() <= 1e-3 * f1.abs().max().item()
+
+
+def test_gated_two_pass_rejects_understated_token_count(cuda_device):
+    """A total token count below cu_seqlens[-1] (which also sizes the workspace too small): the
+    kernels skip all work and report it through the status word (code 2, where 96); no row past the
+    stated count is read and the workspace bounds are never crossed."""
+    from shapeforge_b200 import _native
+
+    lengths = [100, 300]
+    inp = cases.kda_gated_inputs(lengths, 2, 128, "bf16", seed=4)
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    t_small = 40
+    ws_bytes = ops.varlen_kda_gated_workspace_bytes(t_small, 2, 2, 128)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=cuda_device)
+    out = torch.full_like(d["v"], 3.0)
+    fin = torch.full((2, 2, 128, 128), 3.0, device=cuda_device)
+    ptrs = [d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["g"].data_ptr(), d["beta"].data_ptr(), d["cu_seqlens"].data_ptr(),
+            0, out.data_ptr(), fin.data_ptr(), ws.data_ptr()]
+    desc = _native.op_desc("varlen_kda_gated", "bf16", dims=(2, 2, 128, t_small, ws_bytes), attrs=(0.125,), variant=4)
+    _native.run_op(desc, ptrs, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert ops.kernel_status() == (2, 96)
+    assert torch.all(out == 3.0) and torch.all(fin == 3.0)
 
 
 def test_gated_small_ragged(cuda_device):
@@ -251,17 +291,20 @@ def test_gated_small_ragged(cuda_device):
     assert _verdict(_np(fin), rf, "bf16", "fp32").ok
 
 
+@pytest.mark.parametrize("variant", [1, 4])
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
-def test_gated_chunked_ragged_with_state(cuda_device, dtype):
-    """The chunked tensor-core kernel (variant 1): lengths around the 16-token chunk edges, an
-    empty sequence, and a non-zero initial state, against the fp64 recurrence."""
-    lengths = [1, 0, 15, 16, 17, 33, 200]
+def test_gated_chunked_ragged_with_state(cuda_device, dtype, variant):
+    """The chunked tensor-core kernels (variant 1 single-pass, 4 two-pass): lengths around the
+    16- and 32-token chunk edges, an empty sequence, more chunks than ring stages, and a non-zero
+    initial state, against the fp64 recurrence."""
+    lengths = [1, 0, 15, 16, 17, 31, 32, 33, 64, 200]
     heads = 2
     inp = cases.kda_gated_inputs(lengths, heads, 128, dtype, seed=5)
     d = {k: v.to(cuda_device) for k, v in inp.items()}
     g = torch.Generator().manual_seed(11)
     s0 = (0.1 * torch.randn((len(lengths), heads, 128, 128), generator=g)).to(cuda_device)
-    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, initial_state=s0, variant=1)
+    out, fin = ops.varlen_kda_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["cu_seqlens"], 0.125, initial_state=s0,
+                                    variant=variant)
     torch.cuda.synchronize()
     code, where = ops.kernel_status()
     assert code == 0, (code, where)
