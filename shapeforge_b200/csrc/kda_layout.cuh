@@ -32,6 +32,16 @@ __device__ __forceinline__ int mnmaj16(int r, int c, int blk) {
 // Byte offset of the 16-byte chunk j (0..7) of row r in a 128-byte-swizzled row-major tile.
 __device__ __forceinline__ int chunk128(int r, int j) { return r * 128 + (((j & 7) ^ (r & 7)) << 4); }
 
+// e^x as one ex2.approx.ftz of x log2(e): the relative error is that of ex2.approx (about 2^-22)
+// plus |x| times the rounding of x log2(e) (about 1e-5 at |x| = 80, the largest factor exponent);
+// results below the fp32 normal range flush to zero, negligible against the other terms of the
+// sums they enter.
+__device__ __forceinline__ float fexp(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+    return y;
+}
+
 // Two fp32 values as packed 16-bit high parts (returned) and the 16-bit rounding of their
 // residuals (`lo`); a non-finite high part gets a zero residual.
 template <typename T>

@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(P_NT, 3)
         info[1] = hh;
         info[2] = t0;
         info[3] = nt;
+        info[4] = 0;  // a bounded wait of thread 0 gave up
     }
     __syncthreads();
     if (!info[0]) return;
@@ -225,7 +226,10 @@ __global__ void __launch_bounds__(P_NT, 3)
     }
     float* bs = reinterpret_cast<float*>(smem + PL::BS);
     if (p < C) bs[p] = p < nt ? beta[(size_t)(t0 + p) * H + hh] : 0.f;
-    bool ok = sm100::mbar_wait(bar_ld, 0, status, 90);
+    // Thread 0 alone waits for the staged inputs (and below, for each MMA); the other warps sleep
+    // at the CTA barrier instead of polling.
+    if (p == 0 && !sm100::mbar_wait(bar_ld, 0, status, 90)) info[4] = 1;
+    __syncthreads();
 
     // ---- the thread's 16 tokens of channel c: log-decay, k, q~ (zero past the chain's end) ----
     // Channel c's element of token t = 16 * half + jj in a staged tile sits at the row base +
@@ -287,7 +291,7 @@ __global__ void __launch_bounds__(P_NT, 3)
     __syncthreads();
     const float blo = fminf(xlo[c], xlo[128 + c]), bhi = fmaxf(xhi[c], xhi[128 + c]);
     const float blast = xlast[c];
-    const float elast_c = __expf(blast);
+    const float elast_c = kdal::fexp(blast);
     const float ref = 0.5f * (blo + bhi);
     const bool wide = !(0.5f * (bhi - blo) <= FACTOR_LIMIT);  // NaN counts as wide
     {
@@ -300,43 +304,49 @@ __global__ void __launch_bounds__(P_NT, 3)
         // fp32 vectors for a narrow channel; -Kp (high | low, a K-major row per channel) for the
         // K2 | M T Kp MMA; Kend into the slot; Qp seeds the M T Kp columns of that MMA's
         // accumulator (which then holds Q2), whose K2 columns start at zero.
-        const float er = __expf(ref), elr = __expf(blast - ref);
+        const float er = kdal::fexp(ref), elr = kdal::fexp(blast - ref);
         uint32_t qp[16], zero[16], kh[8], kl[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            float kf[4], qf[4], kn[4], kp[4];
+        for (int jj = 0; jj < 16; ++jj) zero[jj] = 0u;
+        // The two paths are separate loops so that neither executes the other's exponentials.
+        if (!wide) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int jj = 4 * u + e, t = 16 * half + jj;
-                float kend;
-                if (!wide) {
+            for (int u = 0; u < 4; ++u) {
+                float kf[4], qf[4], kn[4], kp[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int jj = 4 * u + e;
                     const float x = bl[jj] - ref;
-                    const float ex = __expf(x), en = __expf(-x);
+                    const float ex = kdal::fexp(x), en = kdal::fexp(-x);
                     kf[e] = kv[jj] * ex;
                     qf[e] = qv[jj] * ex;
                     kn[e] = kv[jj] * en;
                     kp[e] = kf[e] * er;
                     qp[jj] = __float_as_uint(qf[e] * er);
-                    kend = kn[e] * elr;
-                } else {
-                    const float e0 = __expf(bl[jj]);
-                    kf[e] = qf[e] = kn[e] = 0.f;
-                    kp[e] = kv[jj] * e0;
-                    qp[jj] = __float_as_uint(qv[jj] * e0);
-                    kend = kv[jj] * __expf(blast - bl[jj]);
+                    kend16[jj] = to16<T>(kn[e] * elr);
                 }
-                zero[jj] = 0u;
-                kend16[jj] = to16<T>(kend);
-                (void)t;
-            }
-            if (!wide) {
                 const int m = 16 * half + 4 * u;
                 *reinterpret_cast<float4*>(smem + PL::PA + mnmaj32(m, c, 16384)) = make_float4(kf[0], kf[1], kf[2], kf[3]);
                 *reinterpret_cast<float4*>(smem + PL::PA + mnmaj32(C + m, c, 16384)) = make_float4(qf[0], qf[1], qf[2], qf[3]);
                 *reinterpret_cast<float4*>(smem + PL::PB + mnmaj32(m, c, 16384)) = make_float4(kn[0], kn[1], kn[2], kn[3]);
+                kh[2 * u] = kdal::pack_hi_lo2<T>(-kp[0], -kp[1], kl[2 * u]);
+                kh[2 * u + 1] = kdal::pack_hi_lo2<T>(-kp[2], -kp[3], kl[2 * u + 1]);
             }
-            kh[2 * u] = kdal::pack_hi_lo2<T>(-kp[0], -kp[1], kl[2 * u]);
-            kh[2 * u + 1] = kdal::pack_hi_lo2<T>(-kp[2], -kp[3], kl[2 * u + 1]);
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float kp[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int jj = 4 * u + e;
+                    const float e0 = kdal::fexp(bl[jj]);
+                    kp[e] = kv[jj] * e0;
+                    qp[jj] = __float_as_uint(qv[jj] * e0);
+                    kend16[jj] = to16<T>(kv[jj] * kdal::fexp(blast - bl[jj]));
+                }
+                kh[2 * u] = kdal::pack_hi_lo2<T>(-kp[0], -kp[1], kl[2 * u]);
+                kh[2 * u + 1] = kdal::pack_hi_lo2<T>(-kp[2], -kp[3], kl[2 * u + 1]);
+            }
         }
         uint8_t* kprow = smem + PL::KP;
         *reinterpret_cast<uint4*>(kprow + chunk128(c, 2 * half)) = make_uint4(kh[0], kh[1], kh[2], kh[3]);
@@ -369,9 +379,10 @@ __global__ void __launch_bounds__(P_NT, 3)
                 sm100::mma_tf32(tmem + P_TM_D1, ad0 + (uint64_t)((kk * 1024) >> 4), bd0 + (uint64_t)((kk * 1024) >> 4), idesc,
                                 kk > 0 ? 1u : 0u);
             sm100::mma_commit(bar_p1);
+            if (!sm100::mbar_wait(bar_p1, 0, status, 91)) info[4] = 1;
+            sm100::tc_fence_before();
         }
-        __syncwarp();
-        if (!sm100::mbar_wait(bar_p1, 0, status, 91)) ok = false;
+        __syncthreads();
         sm100::tc_fence_after();
         {
             // M=64 layout: rows 16*i + r sit in TMEM lane 32*i + r (r < 16).  Quadrants 0/1: A rows
@@ -521,11 +532,12 @@ __global__ void __launch_bounds__(P_NT, 3)
                                idesc, 1u);
         }
         sm100::mma_commit(bar_p4);
+        if (!sm100::mbar_wait(bar_p4, 0, status, 92)) info[4] = 1;
+        sm100::tc_fence_before();
     }
-    __syncwarp();
-    if (!sm100::mbar_wait(bar_p4, 0, status, 92)) ok = false;
+    __syncthreads();
     sm100::tc_fence_after();
-    if (ok) {
+    if (!info[4]) {
         uint32_t k2r[16], q2r[16];
         sm100::tmem_ld_32x32b_x16(tmem + lane_q + P_TM_D4 + (uint32_t)(16 * half), k2r);
         sm100::tmem_ld_32x32b_x16(tmem + lane_q + P_TM_D4 + (uint32_t)(C + 16 * half), q2r);
@@ -544,14 +556,15 @@ __global__ void __launch_bounds__(P_NT, 3)
                 make_uint4(q2r[8 * gq + 4], q2r[8 * gq + 5], q2r[8 * gq + 6], q2r[8 * gq + 7]);
         }
     }
-    // The slot: B1 (32 KB) and KE | TMB | EL (16.5 KB) by two bulk copies, complete before exit.
+    // The slot: B1 (32 KB) and KE | TMB | EL (16.5 KB) by two bulk copies; the CTA leaves once
+    // they have read shared memory (the chain kernel is a later launch on the same stream).
     sm100::fence_proxy_async_smem();
     __syncthreads();
     if (p == 0) {
         sm100::bulk_store(slot + SL_B1, sm100::smem_u32(smem + P_B1), 32768);
         sm100::bulk_store(slot + SL_KE, sm100::smem_u32(smem + P_KE), SLOT_BYTES - SL_KE);
         sm100::bulk_commit();
-        sm100::bulk_wait_all();
+        sm100::bulk_wait_read();
     }
     sm100::tc_fence_before();
     __syncthreads();
@@ -708,8 +721,13 @@ __global__ void __launch_bounds__(K_NT, 1)
                 sm100::mma_commit(&bars->m1);
             }
             __syncwarp();
-            if (!sm100::mbar_wait(&bars->full[st], n & 1, status, 105)) ok = false;  // e^{b_31} of the chunk landed
-            if (!sm100::mbar_wait_spin(&bars->m1, ci & 1, status, 102)) ok = false;
+            // Thread 0 (which saw the chunk's slot land before its MMAs) waits for the accumulator;
+            // the other seven warps sleep at the barrier instead of polling next to the MMA issue.
+            if (tid == 0) {
+                if (!sm100::mbar_wait_spin(&bars->m1, ci & 1, status, 102)) ok = false;
+                sm100::tc_fence_before();
+            }
+            sm100::named_barrier_sync(1, 256);
             sm100::tc_fence_after();
             // Epilogue, split so both halves finish together: warps 0-3 write W^T (high | low)
             // and decay S columns 0-31; warps 4-7 decay S columns 32-127, then store o (after the
@@ -789,8 +807,12 @@ __global__ void __launch_bounds__(K_NT, 1)
             }
         }
         // ---- final state ----
-        if (nch > 0 && !sm100::mbar_wait(&bars->empty[(nch - 1) % NSTAGE], ((nch - 1) / NSTAGE) & 1, status, 106)) ok = false;
+        if (tid == 0 && nch > 0 && !sm100::mbar_wait(&bars->empty[(nch - 1) % NSTAGE], ((nch - 1) / NSTAGE) & 1, status, 106))
+            ok = false;
+        sm100::tc_fence_before();
+        sm100::named_barrier_sync(1, 256);
         sm100::tc_fence_after();
+        ok = ok && *reinterpret_cast<volatile unsigned int*>(&status->code) == 0;
         if (ok) {
 #pragma unroll 1
             for (int cb = 0; cb < 2; ++cb) {
