@@ -35,6 +35,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "per-shard latency and % roofline (HBM GB/s or TC TFLOPS) per OpSpec task"
+# Forced kernel variant of the operator workloads (--variant; 0 = the default dispatch).
+VARIANT = 0
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -314,7 +316,7 @@ def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_input
         return out
 
     def desc():
-        return _native.op_desc(op, dtype, dims=dims, attrs=attrs, flags=flags)
+        return _native.op_desc(op, dtype, dims=dims, attrs=attrs, flags=flags, variant=VARIANT)
 
     def host_inputs():
         ins = make_inputs(cases_seed())
@@ -1209,11 +1211,15 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--variant", type=int, default=0,
+                    help="forced kernel variant of an operator workload (sf_op_desc.variant; 0 = default dispatch)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the sharded attention / KDA lines added to the default workload's line")
     ap.add_argument("--no-graph", action="store_true",
                     help="enqueue the K timed launches one by one instead of as one captured CUDA graph")
     args = ap.parse_args()
+    global VARIANT
+    VARIANT = args.variant
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = _dist()
