@@ -595,6 +595,8 @@ struct __align__(8) ChainBars {
     uint64_t wready;         // W^T written and S decayed (256 arrivals)
     uint32_t tmem_base;
 };
+// TMEM: the state, then the w | o accumulator in two buffers (chunk parity), so the o warps can read
+// a chunk's o after the hand-off while the next chunk's MMAs fill the other buffer.
 constexpr uint32_t TM_S = 0, TM_ACC = 128, K_TMEM_COLS = 256;
 
 // r[j] *= e[j] for 32 state columns (e: 16-byte aligned shared memory).
@@ -698,6 +700,7 @@ __global__ void __launch_bounds__(K_NT, 1)
             const int st = ci % NSTAGE, n = ci / NSTAGE;
             const int t0 = begin + ci * C, nt = min(C, end - t0);
             uint8_t* stg = smem + st * STAGE_BYTES;
+            const uint32_t acc_t = tmem + TM_ACC + (uint32_t)(64 * (ci & 1));
             if (tid == 0) {
                 if (!sm100::mbar_wait_spin(&bars->full[st], n & 1, status, 101)) ok = false;
                 sm100::tc_fence_after();
@@ -709,14 +712,14 @@ __global__ void __launch_bounds__(K_NT, 1)
                     for (int part = 0; part < 2; ++part) {
 #pragma unroll
                         for (int kk = 0; kk < 2; ++kk)
-                            sm100::mma_f16(tmem + TM_ACC, vd0 + (uint64_t)((kk * 2048) >> 4), td0 + (uint64_t)((part * 64 + kk * 32) >> 4),
+                            sm100::mma_f16(acc_t, vd0 + (uint64_t)((kk * 2048) >> 4), td0 + (uint64_t)((part * 64 + kk * 32) >> 4),
                                            idv, (part | kk) != 0 ? 1u : 0u);
                     }
                     constexpr uint32_t idt = sm100::idesc_tf32(128, 64) | (1u << 16);  // B MN-major
                     const uint64_t b1d = sm100::smem_desc_mn_b32(sm100::smem_u32(stg + SL_B1), 16384, 512);
 #pragma unroll
                     for (int kk = 0; kk < D / 8; ++kk)
-                        sm100::mma_tf32_ta(tmem + TM_ACC, tmem + TM_S + (uint32_t)(kk * 8), b1d + (uint64_t)((kk * 1024) >> 4), idt, 1u);
+                        sm100::mma_tf32_ta(acc_t, tmem + TM_S + (uint32_t)(kk * 8), b1d + (uint64_t)((kk * 1024) >> 4), idt, 1u);
                 }
                 sm100::mma_commit(&bars->m1);
             }
@@ -729,44 +732,33 @@ __global__ void __launch_bounds__(K_NT, 1)
             }
             sm100::named_barrier_sync(1, 256);
             sm100::tc_fence_after();
-            // Epilogue, split so both halves finish together: warps 0-3 write W^T (high | low)
-            // and decay S columns 0-31; warps 4-7 decay S columns 32-127, then store o (after the
-            // hand-off, off the critical path).
-            const float* el = reinterpret_cast<const float*>(stg + SL_EL);
-            uint32_t a[32];
-            sm100::tmem_ld_32x32b_x32(tmem + lane_q + TM_ACC + (uint32_t)(C * role), a);
-            if (role == 0) {
-                uint32_t r[32];
-                sm100::tmem_ld_32x32b_x32(tmem + lane_q + TM_S, r);
-                sm100::tmem_ld_wait();
-                uint32_t hi[16], lo[16];
+            // Epilogue, split evenly: warp group r (r = 0, 1) packs W^T's tokens 16r .. 16r+15 (high |
+            // low) and decays S columns 64r .. 64r+63; group 1 also takes o, which it stores after
+            // the hand-off, off the critical path.
+            const float* el = reinterpret_cast<const float*>(stg + SL_EL) + 64 * role;
+            const uint32_t scol = tmem + lane_q + TM_S + (uint32_t)(64 * role);
+            uint32_t wv[16], r0[32], r1[32];
+            sm100::tmem_ld_32x32b_x16(acc_t + lane_q + (uint32_t)(16 * role), wv);
+            sm100::tmem_ld_32x32b_x32(scol, r0);
+            sm100::tmem_ld_32x32b_x32(scol + 32u, r1);
+            sm100::tmem_ld_wait();
+            {
+                uint32_t hi[8], lo[8];
 #pragma unroll
-                for (int u = 0; u < 16; ++u) hi[u] = kdal::pack_hi_lo2<T>(__uint_as_float(a[2 * u]), __uint_as_float(a[2 * u + 1]), lo[u]);
+                for (int u = 0; u < 8; ++u) hi[u] = kdal::pack_hi_lo2<T>(__uint_as_float(wv[2 * u]), __uint_as_float(wv[2 * u + 1]), lo[u]);
                 uint8_t* row = smem + KL::WT;
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    *reinterpret_cast<uint4*>(row + chunk128(vr, jj)) = make_uint4(hi[4 * jj], hi[4 * jj + 1], hi[4 * jj + 2], hi[4 * jj + 3]);
-                    *reinterpret_cast<uint4*>(row + chunk128(vr, 4 + jj)) =
+                for (int jj = 0; jj < 2; ++jj) {
+                    *reinterpret_cast<uint4*>(row + chunk128(vr, 2 * role + jj)) =
+                        make_uint4(hi[4 * jj], hi[4 * jj + 1], hi[4 * jj + 2], hi[4 * jj + 3]);
+                    *reinterpret_cast<uint4*>(row + chunk128(vr, 4 + 2 * role + jj)) =
                         make_uint4(lo[4 * jj], lo[4 * jj + 1], lo[4 * jj + 2], lo[4 * jj + 3]);
                 }
-                decay32(r, el);
-                sm100::tmem_st_32x32b_x32(tmem + lane_q + TM_S, r);
-            } else {
-                uint32_t r0[32], r1[32];
-                sm100::tmem_ld_32x32b_x32(tmem + lane_q + TM_S + 32u, r0);
-                sm100::tmem_ld_32x32b_x32(tmem + lane_q + TM_S + 64u, r1);
-                sm100::tmem_ld_wait();
-#pragma unroll
-                for (int u = 0; u < 16; ++u) a[u] = (uint32_t)to16<T>(__uint_as_float(a[2 * u])) | ((uint32_t)to16<T>(__uint_as_float(a[2 * u + 1])) << 16);
-                decay32(r0, el + 32);
-                decay32(r1, el + 64);
-                sm100::tmem_st_32x32b_x32(tmem + lane_q + TM_S + 32u, r0);
-                sm100::tmem_st_32x32b_x32(tmem + lane_q + TM_S + 64u, r1);
-                sm100::tmem_ld_32x32b_x32(tmem + lane_q + TM_S + 96u, r0);
-                sm100::tmem_ld_wait();
-                decay32(r0, el + 96);
-                sm100::tmem_st_32x32b_x32(tmem + lane_q + TM_S + 96u, r0);
             }
+            decay32(r0, el);
+            decay32(r1, el + 32);
+            sm100::tmem_st_32x32b_x32(scol, r0);
+            sm100::tmem_st_32x32b_x32(scol + 32u, r1);
             sm100::tmem_st_wait();
             sm100::fence_proxy_async_smem();
             sm100::tc_fence_before();
@@ -790,11 +782,15 @@ __global__ void __launch_bounds__(K_NT, 1)
             }
             __syncwarp();
             if (role == 1) {
-                // o^T row v -> o [t][v] in shared memory, then whole 256-byte token rows to global
+                // o^T row v (this chunk's accumulator buffer, which the next chunk's MMAs do not
+                // touch) -> o [t][v] in shared memory, then whole 256-byte token rows to global
                 // with 16-byte stores (rows past the chain's end are not stored).
+                uint32_t a[32];
+                sm100::tmem_ld_32x32b_x32(acc_t + lane_q + (uint32_t)C, a);
+                sm100::tmem_ld_wait();
                 uint16_t* os = reinterpret_cast<uint16_t*>(smem + KL::OS);
 #pragma unroll
-                for (int t = 0; t < C; ++t) os[t * D + vr] = (uint16_t)(a[t >> 1] >> (16 * (t & 1)));
+                for (int t = 0; t < C; ++t) os[t * D + vr] = to16<T>(__uint_as_float(a[t]));
                 sm100::named_barrier_sync(2, 128);
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
