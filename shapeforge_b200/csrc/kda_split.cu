@@ -592,7 +592,6 @@ struct __align__(8) ChainBars {
     uint64_t full[NSTAGE];   // slot (transaction bytes) and V (32 cp.async arrivals) of a chunk landed
     uint64_t empty[NSTAGE];  // the chunk's state update done (commit): the stage may be refilled
     uint64_t m1;             // w | o accumulator ready (commit)
-    uint64_t wready;         // W^T written and S decayed (256 arrivals)
     uint32_t tmem_base;
 };
 // TMEM: the state, then the w | o accumulator in two buffers (chunk parity), so the o warps can read
@@ -640,7 +639,6 @@ __global__ void __launch_bounds__(K_NT, 1)
             sm100::mbar_init(&bars->empty[i], 1);
         }
         sm100::mbar_init(&bars->m1, 1);
-        sm100::mbar_init(&bars->wready, 256);
         sm100::fence_mbar_init();
     }
     if (warp == 0) {
@@ -762,9 +760,8 @@ __global__ void __launch_bounds__(K_NT, 1)
             sm100::tmem_st_wait();
             sm100::fence_proxy_async_smem();
             sm100::tc_fence_before();
-            sm100::mbar_arrive(&bars->wready);
+            sm100::named_barrier_sync(1, 256);  // W^T written and S decayed by all eight warps
             if (tid == 0) {
-                if (!sm100::mbar_wait_spin(&bars->wready, ci & 1, status, 103)) ok = false;
                 sm100::tc_fence_after();
                 if (ok) {
                     constexpr uint32_t idu = sm100::idesc_f16_bmn(128, D, BF16);
