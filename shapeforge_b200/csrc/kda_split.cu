@@ -20,9 +20,11 @@
 //       EL  e^{b_31} fp32 [128]                                             512 B
 //  3. kda_chain_kernel: one CTA per (sequence, head) chain, the fp32 state [Dv, Dk] in TMEM.  A
 //     producer warp streams the chain's slots (one bulk copy each) and V (cp.async, zero-filled past
-//     the chain's end) through a 3-stage ring.  Per chunk, thread 0 issues
-//     ACC = V^T [T ; MT]^T + S [-K2 ; Q2]^T (so ACC holds w^T | o^T); eight warps store o, write
-//     W^T as 16-bit high | low parts and decay S; thread 0 issues S += W^T Kend.
+//     the chain's end) through a 3-stage ring.  An MMA warp issues, per chunk,
+//     ACC += S [-K2 ; Q2]^T into the chunk's accumulator (already holding V^T [T ; MT]^T, so it ends
+//     as w^T | o^T), then the next chunk's V^T [T ; MT]^T into the other accumulator buffer while
+//     eight state warps write W^T as 16-bit high | low parts and decay S, then S += W^T Kend; the
+//     state warps store o after handing W^T over.
 //
 // Numerics match kda_c32.cu: the A and M factors e^{+-(b_t - r)} use the midpoint r of each channel's
 // b range over the chunk, a chunk whose range exceeds 160 in some channel forms A and M pair by pair,
@@ -575,7 +577,7 @@ __global__ void __launch_bounds__(P_NT, 3)
 // ---------------------------------------------------------------------------------------------
 // 3. chain: one (sequence, head) per CTA
 // ---------------------------------------------------------------------------------------------
-constexpr int K_NT = 288;  // warps 0-7 state, warp 8 producer
+constexpr int K_NT = 320;  // warps 0-7 state, warp 8 producer, warp 9 MMA issue
 constexpr int NSTAGE = 3;
 constexpr int STAGE_V = 50176;  // V of the chunk, 16-bit MN-major 2 x (32 x 128 B), after the slot image
 constexpr int STAGE_BYTES = STAGE_V + 8192;
@@ -592,6 +594,10 @@ struct __align__(8) ChainBars {
     uint64_t full[NSTAGE];   // slot (transaction bytes) and V (32 cp.async arrivals) of a chunk landed
     uint64_t empty[NSTAGE];  // the chunk's state update done (commit): the stage may be refilled
     uint64_t m1;             // w | o accumulator ready (commit)
+    uint64_t wready;         // W^T written and S decayed (one arrival per state warp)
+    uint64_t oread[2];       // o read out of accumulator buffer b (one arrival per o warp); one
+                             // barrier per buffer, so a wait can never alias a later chunk's phase
+    uint64_t sinit;          // initial state in TMEM (one arrival per state warp)
     uint32_t tmem_base;
 };
 // TMEM: the state, then the w | o accumulator in two buffers (chunk parity), so the o warps can read
@@ -639,6 +645,10 @@ __global__ void __launch_bounds__(K_NT, 1)
             sm100::mbar_init(&bars->empty[i], 1);
         }
         sm100::mbar_init(&bars->m1, 1);
+        sm100::mbar_init(&bars->wready, 8);
+        sm100::mbar_init(&bars->oread[0], 4);
+        sm100::mbar_init(&bars->oread[1], 4);
+        sm100::mbar_init(&bars->sinit, 8);
         sm100::fence_mbar_init();
     }
     if (warp == 0) {
@@ -676,6 +686,70 @@ __global__ void __launch_bounds__(K_NT, 1)
         // The copies of the last chunks have landed before the CTA can exit.
         for (int ci = max(0, nch - NSTAGE); ci < nch; ++ci)
             if (!sm100::mbar_wait(&bars->full[ci % NSTAGE], (ci / NSTAGE) & 1, status, 104)) ok = false;
+    } else if (warp == 9) {
+        // ======================= MMA issue (lane 0) =======================
+        // Per chunk: S [-K2 ; Q2]^T into the chunk's accumulator (which already holds
+        // V^T [T ; MT]^T), then -- while the state warps run the chunk's epilogue -- the next
+        // chunk's V^T [T ; MT]^T into the other accumulator buffer, then S += W^T Kend once the
+        // epilogue hands W^T over.  The tensor pipe executes one thread's MMAs in issue order.
+        if (lane == 0 && nch > 0) {
+            constexpr uint32_t idv = sm100::idesc_f16_major(128, 64, BF16, true, false);
+            constexpr uint32_t idt = sm100::idesc_tf32(128, 64) | (1u << 16);  // B MN-major
+            constexpr uint32_t idu = sm100::idesc_f16_bmn(128, D, BF16);
+            auto issue_v = [&](int ci) {
+                uint8_t* stg = smem + (ci % NSTAGE) * STAGE_BYTES;
+                const uint32_t acc_t = tmem + TM_ACC + (uint32_t)(64 * (ci & 1));
+                const uint64_t vd0 = sm100::smem_desc_mn_sw128(sm100::smem_u32(stg + STAGE_V), 4096, 1024);
+                const uint64_t td0 = sm100::smem_desc_k_sw128(sm100::smem_u32(stg + SL_TMB));
+#pragma unroll
+                for (int part = 0; part < 2; ++part) {
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk)
+                        sm100::mma_f16(acc_t, vd0 + (uint64_t)((kk * 2048) >> 4), td0 + (uint64_t)((part * 64 + kk * 32) >> 4), idv,
+                                       (part | kk) != 0 ? 1u : 0u);
+                }
+            };
+            if (!sm100::mbar_wait_spin(&bars->full[0], 0, status, 101)) ok = false;
+            sm100::tc_fence_after();
+            if (ok) issue_v(0);
+            if (!sm100::mbar_wait_spin(&bars->sinit, 0, status, 107)) ok = false;
+            sm100::tc_fence_after();
+            for (int ci = 0; ci < nch; ++ci) {
+                const int st = ci % NSTAGE;
+                uint8_t* stg = smem + st * STAGE_BYTES;
+                if (ok) {
+                    const uint32_t acc_t = tmem + TM_ACC + (uint32_t)(64 * (ci & 1));
+                    const uint64_t b1d = sm100::smem_desc_mn_b32(sm100::smem_u32(stg + SL_B1), 16384, 512);
+#pragma unroll
+                    for (int kk = 0; kk < D / 8; ++kk)
+                        sm100::mma_tf32_ta(acc_t, tmem + TM_S + (uint32_t)(kk * 8), b1d + (uint64_t)((kk * 1024) >> 4), idt, 1u);
+                }
+                sm100::mma_commit(&bars->m1);
+                if (ci + 1 < nch) {
+                    const int cn = ci + 1;
+                    if (!sm100::mbar_wait_spin(&bars->full[cn % NSTAGE], (cn / NSTAGE) & 1, status, 101)) ok = false;
+                    // The buffer's previous chunk (cn - 2, its ((cn - 2) / 2)-th use) has had its o read out.
+                    if (cn >= 2 && !sm100::mbar_wait_spin(&bars->oread[cn & 1], ((cn - 2) >> 1) & 1, status, 108)) ok = false;
+                    sm100::tc_fence_after();
+                    if (ok) issue_v(cn);
+                }
+                if (!sm100::mbar_wait_spin(&bars->wready, ci & 1, status, 103)) ok = false;
+                sm100::tc_fence_after();
+                if (ok) {
+                    const uint64_t wd0 = sm100::smem_desc_k_sw128(sm100::smem_u32(smem + KL::WT));
+                    const uint64_t kd0 = sm100::smem_desc_mn_sw128(sm100::smem_u32(stg + SL_KE), 4096, 1024);
+#pragma unroll
+                    for (int part = 0; part < 2; ++part) {
+#pragma unroll
+                        for (int kk = 0; kk < 2; ++kk)
+                            sm100::mma_f16(tmem + TM_S, wd0 + (uint64_t)((part * 64 + kk * 32) >> 4), kd0 + (uint64_t)((kk * 2048) >> 4), idu,
+                                           1u);
+                    }
+                }
+                sm100::mma_commit(&bars->empty[st]);
+            }
+        }
+        __syncwarp();
     } else {
         // ======================= state: value row v, S columns [64 * role, 64 * role + 64) =======================
         const int qd = warp & 3, role = warp >> 2;  // role 0: w, role 1: o
@@ -692,39 +766,17 @@ __global__ void __launch_bounds__(K_NT, 1)
         }
         sm100::tmem_st_wait();
         sm100::tc_fence_before();
-        sm100::named_barrier_sync(1, 256);
-        sm100::tc_fence_after();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&bars->sinit);
         for (int ci = 0; ci < nch; ++ci) {
             const int st = ci % NSTAGE, n = ci / NSTAGE;
             const int t0 = begin + ci * C, nt = min(C, end - t0);
             uint8_t* stg = smem + st * STAGE_BYTES;
             const uint32_t acc_t = tmem + TM_ACC + (uint32_t)(64 * (ci & 1));
+            // Thread 0 waits for the chunk's slot (its e^{b_31}) and accumulator; the other seven
+            // warps sleep at the barrier instead of polling.
             if (tid == 0) {
-                if (!sm100::mbar_wait_spin(&bars->full[st], n & 1, status, 101)) ok = false;
-                sm100::tc_fence_after();
-                if (ok) {
-                    constexpr uint32_t idv = sm100::idesc_f16_major(128, 64, BF16, true, false);
-                    const uint64_t vd0 = sm100::smem_desc_mn_sw128(sm100::smem_u32(stg + STAGE_V), 4096, 1024);
-                    const uint64_t td0 = sm100::smem_desc_k_sw128(sm100::smem_u32(stg + SL_TMB));
-#pragma unroll
-                    for (int part = 0; part < 2; ++part) {
-#pragma unroll
-                        for (int kk = 0; kk < 2; ++kk)
-                            sm100::mma_f16(acc_t, vd0 + (uint64_t)((kk * 2048) >> 4), td0 + (uint64_t)((part * 64 + kk * 32) >> 4),
-                                           idv, (part | kk) != 0 ? 1u : 0u);
-                    }
-                    constexpr uint32_t idt = sm100::idesc_tf32(128, 64) | (1u << 16);  // B MN-major
-                    const uint64_t b1d = sm100::smem_desc_mn_b32(sm100::smem_u32(stg + SL_B1), 16384, 512);
-#pragma unroll
-                    for (int kk = 0; kk < D / 8; ++kk)
-                        sm100::mma_tf32_ta(acc_t, tmem + TM_S + (uint32_t)(kk * 8), b1d + (uint64_t)((kk * 1024) >> 4), idt, 1u);
-                }
-                sm100::mma_commit(&bars->m1);
-            }
-            __syncwarp();
-            // Thread 0 (which saw the chunk's slot land before its MMAs) waits for the accumulator;
-            // the other seven warps sleep at the barrier instead of polling next to the MMA issue.
-            if (tid == 0) {
+                if (!sm100::mbar_wait(&bars->full[st], n & 1, status, 105)) ok = false;
                 if (!sm100::mbar_wait_spin(&bars->m1, ci & 1, status, 102)) ok = false;
                 sm100::tc_fence_before();
             }
@@ -760,24 +812,8 @@ __global__ void __launch_bounds__(K_NT, 1)
             sm100::tmem_st_wait();
             sm100::fence_proxy_async_smem();
             sm100::tc_fence_before();
-            sm100::named_barrier_sync(1, 256);  // W^T written and S decayed by all eight warps
-            if (tid == 0) {
-                sm100::tc_fence_after();
-                if (ok) {
-                    constexpr uint32_t idu = sm100::idesc_f16_bmn(128, D, BF16);
-                    const uint64_t wd0 = sm100::smem_desc_k_sw128(sm100::smem_u32(smem + KL::WT));
-                    const uint64_t kd0 = sm100::smem_desc_mn_sw128(sm100::smem_u32(stg + SL_KE), 4096, 1024);
-#pragma unroll
-                    for (int part = 0; part < 2; ++part) {
-#pragma unroll
-                        for (int kk = 0; kk < 2; ++kk)
-                            sm100::mma_f16(tmem + TM_S, wd0 + (uint64_t)((part * 64 + kk * 32) >> 4), kd0 + (uint64_t)((kk * 2048) >> 4), idu,
-                                           1u);
-                    }
-                }
-                sm100::mma_commit(&bars->empty[st]);
-            }
             __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&bars->wready);  // W^T written and S decayed (this warp's rows)
             if (role == 1) {
                 // o^T row v (this chunk's accumulator buffer, which the next chunk's MMAs do not
                 // touch) -> o [t][v] in shared memory, then whole 256-byte token rows to global
@@ -785,6 +821,9 @@ __global__ void __launch_bounds__(K_NT, 1)
                 uint32_t a[32];
                 sm100::tmem_ld_32x32b_x32(acc_t + lane_q + (uint32_t)C, a);
                 sm100::tmem_ld_wait();
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&bars->oread[ci & 1]);  // the buffer may take chunk ci + 2
                 uint16_t* os = reinterpret_cast<uint16_t*>(smem + KL::OS);
 #pragma unroll
                 for (int t = 0; t < C; ++t) os[t * D + vr] = to16<T>(__uint_as_float(a[t]));
