@@ -780,14 +780,17 @@ def _kda_task_workload(heads: int = 64, dim: int = 128, lengths=(2048, 1024, 102
                 float(inp["scale"][0]), -5.0)
         return (lambda: oref.varlen_kda(*args)), 5.0 * 2 * tt * dim + 2.0 * 4 * dim * dim, f"fp64 recurrence over {tt} tokens of one chain"
 
+    from shapeforge_b200 import ops
+
+    ws = ops.varlen_kda_workspace_bytes(t, n, heads, dim)
     return _op_workload(
         f"varlen_kda_h{heads}_mixed", "GB/s", "hbm", dtype, nbytes,
         {"workload": f"task varlen_kda v6_h64_mixed: {n} sequences {lengths}, H={heads}, D={dim}, {dtype}, the task's input "
                      "stream (0.5 N(0,1) q/k/v/g/beta, A_log = log U(1,16), dt_bias, non-zero initial state)", "total_tokens": t},
-        "kda_chunk_kernel", "varlen_kda", make_inputs,
+        "kda_chain_kernel", "varlen_kda", make_inputs,
         ["q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "cu_seqlens", "scale"],
-        [((t, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim), (-5.0,),
-        cpu_rows=cpu_rows, total_rows=lengths[0])
+        [((t, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim, t, ws), (-5.0,),
+        cpu_rows=cpu_rows, total_rows=lengths[0], scratch_bytes=ws, launches_per_step=3)
 
 
 WORKLOADS = {

@@ -180,6 +180,22 @@ SF_API int sf_varlen_kda(const void* q, const void* k, const void* v, const void
                char* err, uint64_t cap);
 
 /*
+ * varlen_kda with a caller workspace: the two-pass kernels (every 32-token chunk's operands,
+ * norms and gates included, formed in parallel into `workspace`, then one state chain per
+ * (sequence, head)) when D = 128 and `workspace` holds sf_varlen_kda_workspace_bytes(total_tokens,
+ * num_seqs, H, D) bytes at a 256-byte-aligned address; otherwise as sf_varlen_kda.  total_tokens =
+ * the rows of q (a sequence ending past it is reported through sf_kernel_status, code 2 where 96,
+ * with no work done); the workspace needs no initialisation and may be reused once the call's work
+ * on `stream` is done.  Replaces the same call as sf_varlen_kda (the task's kernel entry,
+ * tasks/varlen_kda/reference.py:323-374); the reference's ABI has no workspace.
+ */
+SF_API uint64_t sf_varlen_kda_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int64_t H, int64_t D);
+SF_API int sf_varlen_kda_ws(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+               const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* output,
+               void* final_state, int64_t num_seqs, int64_t total_tokens, int64_t H, int64_t D, float lower_bound,
+               int32_t dtype, void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap);
+
+/*
  * kda: fixed-length Kimi Delta Attention forward (tasks/kda/reference.py reference(); opspec.json
  * formula): the varlen_kda recurrence over ONE sequence of N tokens, without cu_seqlens.
  * q, k, v, g [N, H, D] and beta [N, H] in dtype; A_log [H], dt_bias [H*D], scale [1] fp32;
@@ -351,8 +367,10 @@ SF_API int32_t sf_op_nargs(int32_t op);
  *   SF_OP_BITDELTA  dims = {M, N, K}               attrs = {scale}     args = {x, bits, y}
  *   SF_OP_BITDELTA_BASE dims = {M, N, K}                               args = {x, w_base, s_words, alpha, y}
  *   SF_OP_ATTENTION dims = {B, H, S, D}  attrs = {scale}  flags bit 0 = causal  args = {q, k, v, o}
- *   SF_OP_KDA       dims = {num_seqs, H, D}  attrs = {lower_bound}
- *                   args = {q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state}
+ *   SF_OP_KDA       dims = {num_seqs, H, D, total_tokens, ws_bytes}  attrs = {lower_bound}
+ *                   args = {q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state,
+ *                           workspace (may be NULL: the 16-token chunked kernel)}
+ *                   variant 4 forces the two-pass kernels, 1 the 16-token chunked kernel, 2 the recurrent one
  *   SF_OP_KDA_GATED dims = {num_seqs, H, D, total_tokens, ws_bytes}  attrs = {scale}
  *                   args = {q, k, v, g, beta, cu_seqlens, initial_state (may be NULL), output, final_state,
  *                           workspace (may be NULL: single-pass kernels)}

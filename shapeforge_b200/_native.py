@@ -120,6 +120,8 @@ SIGNATURES: dict[str, tuple[object, tuple]] = {
     "sf_varlen_kda": (ctypes.c_int, (_P,) * 12 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_kda": (ctypes.c_int, (_P,) * 14 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
     "sf_varlen_kda_gated": (ctypes.c_int, (_P,) * 9 + (_I64, _I64, _I64, _F32, _I32, _P, *_ERR)),
+    "sf_varlen_kda_workspace_bytes": (_U64, (_I64, _I64, _I64, _I64)),
+    "sf_varlen_kda_ws": (ctypes.c_int, (_P,) * 12 + (_I64, _I64, _I64, _I64, _F32, _I32, _P, _U64, _P, *_ERR)),
     "sf_varlen_kda_gated_workspace_bytes": (_U64, (_I64, _I64, _I64, _I64)),
     "sf_varlen_kda_gated_ws": (ctypes.c_int, (_P,) * 9 + (_I64, _I64, _I64, _I64, _F32, _I32, _P, _U64, _P, *_ERR)),
     "sf_mamba2_chunk_scan": (ctypes.c_int, (_P,) * 8 + (_I64,) * 6 + (_I32, _P, *_ERR)),

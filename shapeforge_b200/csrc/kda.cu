@@ -210,14 +210,23 @@ int check(int64_t N, int64_t H, int64_t D, int32_t dtype, char* err, uint64_t ca
 
 int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log, const void* dt_bias,
                   const void* initial_state, const void* cu_seqlens, const void* scale, void* out, void* final_state, int64_t N,
-                  int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
+                  int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, int64_t total_tokens, void* workspace,
+                  uint64_t workspace_bytes, cudaStream_t st, char* err, uint64_t cap) {
     int rc = check(N, H, D, dtype, err, cap);
     if (rc) return rc;
     if (N == 0) return SF_OK;
     if (!q || !k || !v || !g || !beta || !a_log || !dt_bias || !initial_state || !cu_seqlens || !scale || !out || !final_state)
         return sf::fail(SF_EINVAL, err, cap, "kda: null tensor pointer");
-    // Variant 0: the chunked tensor-core kernel when it applies (D = 128, aligned rows), else the
-    // recurrent one; 1 forces the chunked kernel, 2 the recurrent one.
+    // Variant 0: the two-pass kernels (all 32-token chunks prepared in parallel, then the chains)
+    // when they apply (D = 128, aligned rows, a workspace of sf_varlen_kda_workspace_bytes), else
+    // the 16-token chunked kernel (D = 128, aligned rows), else the recurrent one.  4 forces the
+    // two-pass kernels, 1 the 16-token chunked kernel, 2 the recurrent one.
+    if (variant == 4 || (variant == 0 && workspace)) {
+        rc = sf_kda_task_split_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, out, final_state, N,
+                                      total_tokens, H, D, lower_bound, dtype, workspace, workspace_bytes, st,
+                                      variant == 4 ? err : nullptr, variant == 4 ? cap : 0);
+        if (rc == SF_OK || variant == 4 || rc != SF_EINVAL) return rc;
+    }
     if (variant != 2) {
         rc = sf_kda_task_chunk_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, out, final_state, N, H, D,
                                       lower_bound, dtype, st, variant == 1 ? err : nullptr, variant == 1 ? cap : 0);
@@ -306,7 +315,7 @@ int sf_kda_fixed_launch(const void* q, const void* k, const void* v, const void*
     // 1e-3): at D = 128 one output in 76,800 of the wide_range case landed at 1.15x the bound.
     // variant 1 still forces the chunked kernel.
     return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, work_items, scale, out, final_state, 1, H, D, lower_bound,
-                         dtype, variant == 1 ? 1 : 2, st, err, cap);
+                         dtype, variant == 1 ? 1 : 2, 0, nullptr, 0, st, err, cap);
 }
 
 extern "C" int sf_kda(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
@@ -323,7 +332,19 @@ extern "C" int sf_varlen_kda(const void* q, const void* k, const void* v, const 
                              void* final_state, int64_t num_seqs, int64_t H, int64_t D, float lower_bound, int32_t dtype, void* stream,
                              char* err, uint64_t cap) {
     return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state, num_seqs, H, D,
-                         lower_bound, dtype, 0, (cudaStream_t)stream, err, cap);
+                         lower_bound, dtype, 0, 0, nullptr, 0, (cudaStream_t)stream, err, cap);
+}
+
+extern "C" uint64_t sf_varlen_kda_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int64_t H, int64_t D) {
+    return sf_kda_gated_split_workspace(total_tokens, num_seqs, H, D);
+}
+
+extern "C" int sf_varlen_kda_ws(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                                const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* output,
+                                void* final_state, int64_t num_seqs, int64_t total_tokens, int64_t H, int64_t D, float lower_bound,
+                                int32_t dtype, void* workspace, uint64_t workspace_bytes, void* stream, char* err, uint64_t cap) {
+    return sf_kda_launch(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state, num_seqs, H, D,
+                         lower_bound, dtype, 0, total_tokens, workspace, workspace_bytes, (cudaStream_t)stream, err, cap);
 }
 
 extern "C" int sf_varlen_kda_gated(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,

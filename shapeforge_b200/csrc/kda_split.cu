@@ -137,7 +137,8 @@ struct PL {
     static constexpr int VOTE = XHI + 1024;  // 8 words
     static constexpr int INFO = VOTE + 32;   // valid, head, first token, token count
     static constexpr int BARS = INFO + 32;   // staged, p1, p4, TMEM base
-    static constexpr int BYTES = BARS + 32;
+    static constexpr int NRM = BARS + 32;    // task op: 1 / |q_t| [32], then 1 / |k_t| [32]
+    static constexpr int BYTES = NRM + 256;
 };
 constexpr int P_SQ = PL::PA, P_SK = PL::PA + 8192, P_SG = PL::PA + 16384;  // staged inputs inside PA
 constexpr int TTS = 36;  // row stride of L^-1 / T (16-byte aligned rows for float4 reads)
@@ -145,7 +146,7 @@ constexpr int P_TA = PL::PB, P_TMM = P_TA + 4224, P_TT = P_TMM + 4224, P_TMT = P
 static_assert(P_TP + 16 * 17 * 4 <= PL::KP, "T matrices fit the Kn space");
 static_assert(PL::PB % 1024 == 0 && PL::KP % 1024 == 0, "operand tiles are 1024-byte aligned");
 constexpr uint32_t P_TM_D1 = 0, P_TM_D4 = 64, P_TMEM_COLS = 128;
-constexpr uint32_t STAGED_BYTES = 32768;
+constexpr uint32_t STAGED_BYTES = 32768, STAGED_BYTES_TASK = 24576;
 constexpr int P_KE = PL::PA, P_TMB = PL::PA + 8192, P_EL = PL::PA + 16384, P_B1 = PL::PB;
 static_assert(P_B1 + 32768 <= PL::BS, "B1 image fits PB and KP");
 
@@ -156,17 +157,29 @@ __device__ __forceinline__ int mnmaj32(int m, int r, int blk) {
     return (m >> 5) * blk + r * 128 + ((((m & 31) >> 3) ^ (r & 3)) << 5) + ((m & 7) << 2);
 }
 
+// The task op's in-op transforms (tasks/varlen_kda/reference.py:323-374): q and k rows
+// L2-normalised (rsqrt(sum x^2 + 1e-6), q times *scale), log-decay lower_bound *
+// sigmoid(exp(A_log[h]) * (g + dt_bias[h, c])) from 16-bit g, beta = sigmoid(beta).
+struct TaskGate {
+    const float* a_log;    // [H]
+    const float* dt_bias;  // [H * D]
+    const float* scale;    // [1]
+    float lower_bound;
+};
+
 // kind::tf32 instruction descriptor with both operands MN-major.
 __host__ __device__ constexpr uint32_t idesc_tf32_mn(uint32_t m, uint32_t n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) | (1u << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
-template <typename T>
+// TASK: g and beta are 16-bit raw gates and the TaskGate transforms apply; otherwise g is the fp32
+// log-decay, beta fp32 and q is multiplied by `scale`.
+template <typename T, bool TASK>
 __global__ void __launch_bounds__(P_NT, 3)
     kda_prep_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tg,
-                    const T* __restrict__ q, const T* __restrict__ k, const float* __restrict__ beta, const int32_t* __restrict__ cu,
-                    const int32_t* __restrict__ base, int nseq, int64_t max_slots, float scale, int H, uint8_t* __restrict__ slots,
-                    sm100::KernelStatus* status) {
+                    const T* __restrict__ q, const T* __restrict__ k, const void* __restrict__ beta, const int32_t* __restrict__ cu,
+                    const int32_t* __restrict__ base, int nseq, int64_t max_slots, float scale, TaskGate task, int H,
+                    uint8_t* __restrict__ slots, sm100::KernelStatus* status) {
     constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -203,14 +216,15 @@ __global__ void __launch_bounds__(P_NT, 3)
             sm100::mbar_init(bar_p1, 1);
             sm100::mbar_init(bar_p4, 1);
             sm100::fence_mbar_init();
-            sm100::mbar_arrive_expect_tx(bar_ld, STAGED_BYTES);
+            sm100::mbar_arrive_expect_tx(bar_ld, TASK ? STAGED_BYTES_TASK : STAGED_BYTES);
 #pragma unroll
             for (int b = 0; b < 2; ++b) {
                 sm100::tma_load_3d(smem + P_SQ + 4096 * b, &tq, bar_ld, 64 * b, hh, t0);
                 sm100::tma_load_3d(smem + P_SK + 4096 * b, &tk, bar_ld, 64 * b, hh, t0);
             }
+            // g: 16-bit boxes of 64 channels (task) or fp32 boxes of 32 channels.
 #pragma unroll
-            for (int b = 0; b < 4; ++b) sm100::tma_load_3d(smem + P_SG + 4096 * b, &tg, bar_ld, 32 * b, hh, t0);
+            for (int b = 0; b < (TASK ? 2 : 4); ++b) sm100::tma_load_3d(smem + P_SG + 4096 * b, &tg, bar_ld, (TASK ? 64 : 32) * b, hh, t0);
         }
         info[0] = valid;
         info[1] = hh;
@@ -227,30 +241,80 @@ __global__ void __launch_bounds__(P_NT, 3)
         sm100::tmem_relinquish();
     }
     float* bs = reinterpret_cast<float*>(smem + PL::BS);
-    if (p < C) bs[p] = p < nt ? beta[(size_t)(t0 + p) * H + hh] : 0.f;
+    if (p < C) {
+        float b = 0.f;
+        if (p < nt) {
+            if (TASK) b = 1.0f / (1.0f + __expf(-sf::Dt<T>::to_f(static_cast<const T*>(beta)[(size_t)(t0 + p) * H + hh])));
+            else b = static_cast<const float*>(beta)[(size_t)(t0 + p) * H + hh];
+        }
+        bs[p] = b;
+    }
+    const float qscale = TASK ? *task.scale : scale;
     // Thread 0 alone waits for the staged inputs (and below, for each MMA); the other warps sleep
     // at the CTA barrier instead of polling.
     if (p == 0 && !sm100::mbar_wait(bar_ld, 0, status, 90)) info[4] = 1;
     __syncthreads();
+    float* nrm = reinterpret_cast<float*>(smem + PL::NRM);
+    if (TASK) {
+        // 1 / |q_t| and 1 / |k_t|: thread -> token p / 8, channels 16 (p & 7) .. + 15 (two 16-byte
+        // chunks of one 64-channel box row), the 8 threads of a token reduce by shuffles.
+        const int tt = p >> 3, part = p & 7;
+        const int roff = (part >> 2) * 4096 + tt * 128;
+        float sq = 0.f, sk = 0.f;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int co = ((2 * (part & 3) + u) ^ (tt & 7)) << 4;
+            const uint4 qw = *reinterpret_cast<const uint4*>(smem + P_SQ + roff + co);
+            const uint4 kw = *reinterpret_cast<const uint4*>(smem + P_SK + roff + co);
+            const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ka[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float q0 = from16<T>((uint16_t)(qa[e] & 0xFFFFu)), q1 = from16<T>((uint16_t)(qa[e] >> 16));
+                const float k0 = from16<T>((uint16_t)(ka[e] & 0xFFFFu)), k1 = from16<T>((uint16_t)(ka[e] >> 16));
+                sq = fmaf(q0, q0, fmaf(q1, q1, sq));
+                sk = fmaf(k0, k0, fmaf(k1, k1, sk));
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        if (part == 0) {
+            nrm[tt] = rsqrtf(sq + 1e-6f);
+            nrm[C + tt] = rsqrtf(sk + 1e-6f);
+        }
+        __syncthreads();
+    }
 
     // ---- the thread's 16 tokens of channel c: log-decay, k, q~ (zero past the chain's end) ----
     // Channel c's element of token t = 16 * half + jj in a staged tile sits at the row base +
     // jj * 128 + (its 16-byte chunk XOR (jj & 7) * 16): t & 7 == jj & 7, so only the XOR varies.
     const int gch = ((c & 31) >> 2) << 4, hch = ((c & 63) >> 3) << 4;
-    const uint8_t* sg0 = smem + P_SG + (c >> 5) * 4096 + half * 2048 + ((c & 3) << 2);
+    const uint8_t* sg0 = TASK ? smem + P_SG + (c >> 6) * 4096 + half * 2048 + ((c & 7) << 1)
+                              : smem + P_SG + (c >> 5) * 4096 + half * 2048 + ((c & 3) << 2);
     const uint8_t* sk0 = smem + P_SK + (c >> 6) * 4096 + half * 2048 + ((c & 7) << 1);
     const uint8_t* sq0 = sk0 - P_SK + P_SQ;
+    const float task_ea = TASK ? __expf(task.a_log[hh]) : 0.f;
+    const float task_dtb = TASK ? task.dt_bias[(size_t)hh * D + c] : 0.f;
     float bl[16], kv[16], qv[16];
 #pragma unroll
     for (int jj = 0; jj < 16; ++jj) {
         const bool live = 16 * half + jj < nt;
         const int rw = jj * 128;
-        const float gl = *reinterpret_cast<const float*>(sg0 + rw + (gch ^ ((jj & 7) << 4)));
-        const float kx = from16<T>(*reinterpret_cast<const uint16_t*>(sk0 + rw + (hch ^ ((jj & 7) << 4))));
-        const float qx = from16<T>(*reinterpret_cast<const uint16_t*>(sq0 + rw + (hch ^ ((jj & 7) << 4))));
+        float gl, kx = from16<T>(*reinterpret_cast<const uint16_t*>(sk0 + rw + (hch ^ ((jj & 7) << 4))));
+        float qx = from16<T>(*reinterpret_cast<const uint16_t*>(sq0 + rw + (hch ^ ((jj & 7) << 4)))) * qscale;
+        if (TASK) {
+            const float gx = from16<T>(*reinterpret_cast<const uint16_t*>(sg0 + rw + (hch ^ ((jj & 7) << 4))));
+            gl = task.lower_bound * (1.0f / (1.0f + __expf(-task_ea * (gx + task_dtb))));
+            kx *= nrm[C + 16 * half + jj];
+            qx *= nrm[16 * half + jj];
+        } else {
+            gl = *reinterpret_cast<const float*>(sg0 + rw + (gch ^ ((jj & 7) << 4)));
+        }
         bl[jj] = live ? gl : 0.f;
         kv[jj] = live ? kx : 0.f;
-        qv[jj] = live ? qx * scale : 0.f;
+        qv[jj] = live ? qx : 0.f;
     }
     sm100::tc_fence_before();
     __syncthreads();  // the staged inputs are consumed: PA is free for the factors
@@ -432,12 +496,15 @@ __global__ void __launch_bounds__(P_NT, 3)
                 }
             }
         }
+        // The raw q, k rows read above take the task op's norms here (and q its scale).
+        const float nkt = TASK ? nrm[C + t] : 1.f, nqt = TASK ? nrm[t] * qscale : qscale;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int i = i0 + 8 * u;
             const bool live = t < nt && i < nt;
-            ta[t * 33 + i] = (live && i < t) ? a[u] : 0.f;
-            tmm[t * 33 + i] = (live && i <= t) ? m[u] * scale : 0.f;
+            const float nki = TASK ? nrm[C + i] : 1.f;
+            ta[t * 33 + i] = (live && i < t) ? a[u] * nkt * nki : 0.f;
+            tmm[t * 33 + i] = (live && i <= t) ? m[u] * nqt * nki : 0.f;
         }
     }
     __syncthreads();  // A and M are written; PA (factors or b) is consumed
@@ -886,12 +953,13 @@ uint64_t sf_kda_gated_split_workspace(int64_t total_tokens, int64_t nseq, int64_
     return (uint64_t)(header_bytes(nseq) + slot_bound(total_tokens, nseq, H) * SLOT_BYTES);
 }
 
-// The two-pass kernels; SF_EINVAL (without launching) when the shape, alignment or workspace does
-// not qualify.
-int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
-                              const void* initial_state, void* out, void* final_state, int64_t N, int64_t total_tokens, int64_t H,
-                              int64_t Dd, float scale, int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st,
-                              char* err, uint64_t cap) {
+namespace {
+
+template <bool TASK>
+int split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                 const void* initial_state, void* out, void* final_state, int64_t N, int64_t total_tokens, int64_t H, int64_t Dd,
+                 float scale, TaskGate task, int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st, char* err,
+                 uint64_t cap) {
     if (Dd != D || !sf::aligned16(q) || !sf::aligned16(k) || !sf::aligned16(v) || !sf::aligned16(g) || !sf::aligned16(out) ||
         !sf::aligned16(final_state) || (initial_state && !sf::aligned16(initial_state)))
         return sf::fail(SF_EINVAL, err, cap, "kda: the two-pass kernels need D = 128 and 16-byte-aligned tensors");
@@ -908,10 +976,12 @@ int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const
     static std::atomic<uint64_t> attr_done{0};
     if (sf::once_per_device(attr_done)) {
         // Three prep CTAs share an SM only with the whole unified L1 / shared array as shared memory.
-        cudaFuncSetAttribute(kda_prep_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
-        cudaFuncSetAttribute(kda_prep_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
-        cudaFuncSetAttribute(kda_prep_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-        cudaFuncSetAttribute(kda_prep_kernel<__nv_bfloat16>, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+        cudaFuncSetAttribute(kda_prep_kernel<__half, TASK>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
+        cudaFuncSetAttribute(kda_prep_kernel<__nv_bfloat16, TASK>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
+        cudaFuncSetAttribute(kda_prep_kernel<__half, TASK>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+        cudaFuncSetAttribute(kda_prep_kernel<__nv_bfloat16, TASK>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
         cudaFuncSetAttribute(kda_chain_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, CHAIN_SMEM);
         cudaFuncSetAttribute(kda_chain_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, CHAIN_SMEM);
     }
@@ -920,20 +990,22 @@ int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const
     const int32_t* cu = static_cast<const int32_t*>(cu_seqlens);
     kda_slots_kernel<<<1, 1024, 0, st>>>(cu, (int)N, total_tokens, base, status);
     if (nslots > 0) {
-        // [T, H, D] views of q, k (boxes of 64 channels) and g (32 channels) x one head x 32 tokens.
+        // [T, H, D] views of q, k (boxes of 64 channels) and g (64 channels of 16-bit gates for the
+        // task op, else 32 channels of fp32 log-decay) x one head x 32 tokens.
         const bool bf16 = dtype == SF_DTYPE_BF16;
         CUtensorMap tq, tk, tg;
         int rc = sf::tmap_3d(&tq, q, D, H, total_tokens, D * 2, H * D * 2, 64, 1, C, bf16, err, cap);
         if (rc == SF_OK) rc = sf::tmap_3d(&tk, k, D, H, total_tokens, D * 2, H * D * 2, 64, 1, C, bf16, err, cap);
-        if (rc == SF_OK) rc = sf::tmap_3d_f32(&tg, g, D, H, total_tokens, D * 4, H * D * 4, 32, 1, C, err, cap);
+        if (rc == SF_OK)
+            rc = TASK ? sf::tmap_3d(&tg, g, D, H, total_tokens, D * 2, H * D * 2, 64, 1, C, bf16, err, cap)
+                      : sf::tmap_3d_f32(&tg, g, D, H, total_tokens, D * 4, H * D * 4, 32, 1, C, err, cap);
         if (rc != SF_OK) return rc;
         if (dtype == SF_DTYPE_F16)
-            kda_prep_kernel<__half><<<(unsigned)nslots, P_NT, PREP_SMEM, st>>>(tq, tk, tg, (const __half*)q, (const __half*)k,
-                                                                               (const float*)beta, cu, base, (int)N, nslots, scale,
-                                                                               (int)H, slots, status);
+            kda_prep_kernel<__half, TASK><<<(unsigned)nslots, P_NT, PREP_SMEM, st>>>(
+                tq, tk, tg, (const __half*)q, (const __half*)k, beta, cu, base, (int)N, nslots, scale, task, (int)H, slots, status);
         else
-            kda_prep_kernel<__nv_bfloat16><<<(unsigned)nslots, P_NT, PREP_SMEM, st>>>(
-                tq, tk, tg, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const float*)beta, cu, base, (int)N, nslots, scale, (int)H,
+            kda_prep_kernel<__nv_bfloat16, TASK><<<(unsigned)nslots, P_NT, PREP_SMEM, st>>>(
+                tq, tk, tg, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, beta, cu, base, (int)N, nslots, scale, task, (int)H,
                 slots, status);
     }
     if (dtype == SF_DTYPE_F16)
@@ -944,7 +1016,31 @@ int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const
         kda_chain_kernel<__nv_bfloat16><<<(unsigned)(N * H), K_NT, CHAIN_SMEM, st>>>(
             (const __nv_bfloat16*)v, cu, base, (int)N, nslots, (const float*)initial_state, (int)H, slots, (__nv_bfloat16*)out,
             (float*)final_state, status);
-    return sf::check_launch("kda_gated two-pass launch", err, cap);
+    return sf::check_launch(TASK ? "kda two-pass launch" : "kda_gated two-pass launch", err, cap);
+}
+
+}  // namespace
+
+// The two-pass kernels; SF_EINVAL (without launching) when the shape, alignment or workspace does
+// not qualify.
+int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* cu_seqlens,
+                              const void* initial_state, void* out, void* final_state, int64_t N, int64_t total_tokens, int64_t H,
+                              int64_t Dd, float scale, int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st,
+                              char* err, uint64_t cap) {
+    return split_launch<false>(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, total_tokens, H, Dd, scale,
+                               TaskGate{nullptr, nullptr, nullptr, 0.f}, dtype, workspace, workspace_bytes, st, err, cap);
+}
+
+// The task op (in-op q/k norms, gates from A_log / dt_bias, sigmoid beta, an initial state) on the
+// two-pass kernels; same qualification rules and workspace.
+int sf_kda_task_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                             const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* out,
+                             void* final_state, int64_t N, int64_t total_tokens, int64_t H, int64_t Dd, float lower_bound,
+                             int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st, char* err, uint64_t cap) {
+    if (!a_log || !dt_bias || !scale || !initial_state) return sf::fail(SF_EINVAL, err, cap, "kda: null gate / scale / state pointer");
+    return split_launch<true>(q, k, v, g, beta, cu_seqlens, initial_state, out, final_state, N, total_tokens, H, Dd, 0.f,
+                              TaskGate{(const float*)a_log, (const float*)dt_bias, (const float*)scale, lower_bound}, dtype, workspace,
+                              workspace_bytes, st, err, cap);
 }
 
 int sf_kda_split_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream) {

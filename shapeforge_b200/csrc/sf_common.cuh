@@ -216,7 +216,8 @@ int sf_attention_launch(const void* q, const void* k, const void* v, void* o, in
 int sf_attention_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
 int sf_kda_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log, const void* dt_bias,
                   const void* initial_state, const void* cu_seqlens, const void* scale, void* out, void* final_state, int64_t N,
-                  int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, cudaStream_t st, char* err, uint64_t cap);
+                  int64_t H, int64_t D, float lower_bound, int32_t dtype, int32_t variant, int64_t total_tokens, void* workspace,
+                  uint64_t workspace_bytes, cudaStream_t st, char* err, uint64_t cap);
 int sf_kda_fixed_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
                         const void* dt_bias, const void* initial_state, const void* scale, void* out, void* final_state,
                         void* work_items, void* item_counts, int64_t N, int64_t H, int64_t D, float lower_bound, int32_t dtype,
@@ -242,6 +243,10 @@ int sf_kda_gated_split_launch(const void* q, const void* k, const void* v, const
                               const void* initial_state, void* out, void* final_state, int64_t N, int64_t total_tokens, int64_t H,
                               int64_t D, float scale, int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st,
                               char* err, uint64_t cap);
+int sf_kda_task_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta, const void* a_log,
+                             const void* dt_bias, const void* initial_state, const void* cu_seqlens, const void* scale, void* out,
+                             void* final_state, int64_t N, int64_t total_tokens, int64_t H, int64_t D, float lower_bound,
+                             int32_t dtype, void* workspace, uint64_t workspace_bytes, cudaStream_t st, char* err, uint64_t cap);
 int sf_kda_split_status_read(uint32_t* code, uint32_t* where, cudaStream_t stream);
 int sf_mamba2_launch(const void* x, const void* dt, const void* cs, const void* bm, const void* cm, const void* dskip, const void* states,
                      void* y, int64_t B, int64_t L, int64_t H, int64_t P, int64_t N, int64_t C, int32_t dtype, int32_t variant,

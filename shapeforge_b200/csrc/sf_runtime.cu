@@ -117,7 +117,7 @@ extern "C" int32_t sf_op_nargs(int32_t op) {
         case SF_OP_BITDELTA: return 3;
         case SF_OP_BITDELTA_BASE: return 5;
         case SF_OP_ATTENTION: return 4;
-        case SF_OP_KDA: return 12;
+        case SF_OP_KDA: return 13;
         case SF_OP_KDA_GATED: return 10;
         case SF_OP_MAMBA2: return 8;
         case SF_OP_RELU: return 2;
@@ -163,7 +163,8 @@ static int dispatch(const sf_op_desc* d, const void* const* a, cudaStream_t s, c
                                        d->flags & 1, d->dtype, d->variant, s, err, cap);
         case SF_OP_KDA:
             return sf_kda_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], a[8], a[9], (void*)a[10], (void*)a[11], d->dims[0],
-                                 d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype, d->variant, s, err, cap);
+                                 d->dims[1], d->dims[2], (float)d->attrs[0], d->dtype, d->variant, d->dims[3], (void*)a[12],
+                                 (uint64_t)d->dims[4], s, err, cap);
         case SF_OP_KDA_GATED:
             return sf_kda_gated_launch(a[0], a[1], a[2], a[3], a[4], a[5], a[6], (void*)a[7], (void*)a[8], d->dims[0], d->dims[1],
                                        d->dims[2], (float)d->attrs[0], d->dtype, d->variant, d->dims[3], (void*)a[9],

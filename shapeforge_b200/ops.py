@@ -298,11 +298,14 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
 
 
 def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, lower_bound: float = -5.0,
-               output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0):
+               output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0,
+               workspace: torch.Tensor | None = None):
     """Packed-varlen KDA forward (tasks/varlen_kda/reference.py:323-374).  ``scale`` is the
     task's one-element fp32 tensor; returns ``(output [T,H,D], final_state [N,H,D,D])``.
-    ``variant``: 0 = the chunked tensor-core kernel where it applies (D = 128), else the
-    recurrent one; 1 = chunked only; 2 = recurrent only."""
+    ``variant``: 0 = the two-pass kernels over ``workspace`` (uint8, at least
+    ``varlen_kda_workspace_bytes``; allocated here when not given) where they apply (D = 128),
+    else the 16-token chunked kernel (D = 128), else the recurrent one; 4 = two-pass only;
+    1 = 16-token chunked only; 2 = recurrent only."""
     for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
         _check(t, name, q.dtype)
     for name, t in (("A_log", a_log), ("dt_bias", dt_bias), ("initial_state", initial_state), ("scale", scale)):
@@ -312,9 +315,19 @@ def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scal
     n = cu_seqlens.numel() - 1
     output = torch.empty_like(v) if output is None else output
     final_state = torch.empty((n, h, d, d), dtype=torch.float32, device=q.device) if final_state is None else final_state
+    need = varlen_kda_workspace_bytes(t_, n, h, d) if variant in (0, 4) and n > 0 else 0
+    if workspace is None and need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if workspace is not None else 0
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     ptrs = [x.data_ptr() for x in (q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, output, final_state)]
-    _run("varlen_kda", q, ptrs, dims=(n, h, d), attrs=(lower_bound,), variant=variant)
+    _run("varlen_kda", q, ptrs + [ws_ptr], dims=(n, h, d, t_, ws_bytes), attrs=(lower_bound,), variant=variant)
     return output, final_state
+
+
+def varlen_kda_workspace_bytes(total_tokens: int, num_seqs: int, heads: int, dim: int) -> int:
+    """Workspace bytes of the two-pass varlen KDA kernels (0 when they do not apply)."""
+    return int(_native.load().sf_varlen_kda_workspace_bytes(total_tokens, num_seqs, heads, dim))
 
 
 def kda(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound: float = -5.0,

@@ -70,17 +70,18 @@ def _oracle_task(inp, heads, lower_bound=-5.0):
     return out, fin
 
 
+@pytest.mark.parametrize("variant", [1, 4])
 @pytest.mark.parametrize("lower_bound", [-12.0, -60.0])
-def test_task_op_chunked_strong_lower_bound(cuda_device, lower_bound):
-    """LOWER_BOUND beyond what 16-token factors can hold (cumulative decays down to -190 and -960
-    per chunk): the chunked kernel (variant 1) forms those chunks pair by pair and still matches
-    the fp64 oracle."""
+def test_task_op_chunked_strong_lower_bound(cuda_device, lower_bound, variant):
+    """LOWER_BOUND beyond what the chunk factors can hold (cumulative decays down to -190 and -960
+    per 16-token chunk): the 16-token chunked kernel (variant 1) and the two-pass 32-token kernels
+    (variant 4) form those chunks pair by pair and still match the fp64 oracle."""
     lengths = [300, 0, 45, 16]
     heads = 2
     inp = cases.kda_task_inputs(lengths, heads, 128, "bf16", seed=cases.case_seed(12, 4))
     d = {k: v.to(cuda_device) for k, v in inp.items()}
     out, fin = ops.varlen_kda(d["q"], d["k"], d["v"], d["g"], d["beta"], d["A_log"], d["dt_bias"], d["initial_state"],
-                              d["cu_seqlens"], d["scale"], lower_bound=lower_bound, variant=1)
+                              d["cu_seqlens"], d["scale"], lower_bound=lower_bound, variant=variant)
     torch.cuda.synchronize()
     code, where = ops.kernel_status()
     assert code == 0, (code, where)
@@ -92,12 +93,13 @@ def test_task_op_chunked_strong_lower_bound(cuda_device, lower_bound):
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 4])
 def test_task_op_chunked_and_recurrent(cuda_device, dtype, variant):
-    """The task op at D = 128 through the chunked tensor-core kernel (variant 1: in-op q/k norms,
-    gates from A_log / dt_bias, sigmoid beta, initial state) and the recurrent kernel (variant 2),
-    both against the fp64 oracle; a 700-token sequence carries the state through 44 chunks, a
-    zero-length one is skipped."""
+    """The task op at D = 128 through the 16-token chunked tensor-core kernel (variant 1: in-op q/k
+    norms, gates from A_log / dt_bias, sigmoid beta, initial state), the recurrent kernel (variant
+    2) and the two-pass kernels (variant 4: every 32-token chunk prepared into a workspace, then
+    the chains), all against the fp64 oracle; a 700-token sequence carries the state through 44
+    chunks, a zero-length one is skipped."""
     lengths = [700, 0, 33, 16, 129]
     heads = 3
     inp = cases.kda_task_inputs(lengths, heads, 128, dtype, seed=cases.case_seed(11, 2))
@@ -156,6 +158,48 @@ def test_capacity_sentinel_leaves_padding(cuda_device):
     ro, rf = _oracle_task(d, [0, 1])
     assert _verdict(_np(out[:9]), ro, "fp16", "fp16").ok
     assert _verdict(_np(fin[:3]), rf, "fp16", "fp32").ok
+
+
+def test_task_op_two_pass_capacity_sentinel(cuda_device):
+    """The two-pass kernels at D = 128 under the capacity contract: entries of -1 after the resolved
+    total end the batch, padding rows of the output and unused final-state rows keep their bytes,
+    and the live sequences match the oracle."""
+    lengths = [70, 33, 1]
+    heads, dim = 2, 128
+    inp = cases.kda_task_inputs(lengths, heads, dim, "bf16", seed=cases.case_seed(5, 9))
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    cap_seqs, cap_tokens = 5, 160
+    cu = torch.tensor([0, 70, 103, 104, -1, -1], dtype=torch.int32, device=cuda_device)
+    pad = lambda t, n: torch.cat([t, torch.zeros((n - t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)])  # noqa: E731
+    q, k, v, g, beta = (pad(d[n], cap_tokens) for n in ("q", "k", "v", "g", "beta"))
+    s0 = pad(d["initial_state"], cap_seqs)
+    out = torch.full((cap_tokens, heads, dim), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    fin = torch.full((cap_seqs, heads, dim, dim), 7.0, dtype=torch.float32, device=cuda_device)
+    ops.varlen_kda(q, k, v, g, beta, d["A_log"], d["dt_bias"], s0, cu, d["scale"], output=out, final_state=fin, variant=4)
+    torch.cuda.synchronize()
+    code, where = ops.kernel_status()
+    assert code == 0, (code, where)
+    assert torch.all(out[104:] == 7.0)
+    assert torch.all(fin[3:] == 7.0)
+    ro, rf = _oracle_task(d, [0, 1])
+    assert _verdict(_np(out[:104]), ro, "bf16", "bf16").ok
+    assert _verdict(_np(fin[:3]), rf, "bf16", "fp32").ok
+
+
+def test_task_op_two_pass_matches_chunked(cuda_device):
+    """The two-pass kernels and the 16-token chunked kernel agree on a batch of many heads (all
+    heads compared, each to the other's RMS scale at the task tolerance)."""
+    lengths = [257, 96, 31, 512]
+    inp = cases.kda_task_inputs(lengths, 8, 128, "bf16", seed=cases.case_seed(3, 7))
+    d = {k: v.to(cuda_device) for k, v in inp.items()}
+    args = [d[n] for n in ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "cu_seqlens", "scale")]
+    o4, f4 = ops.varlen_kda(*args, variant=4)
+    o1, f1 = ops.varlen_kda(*args, variant=1)
+    torch.cuda.synchronize()
+    v1 = _verdict(_np(o4), _np(o1), "bf16", "bf16")
+    v2 = _verdict(_np(f4), _np(f1), "bf16", "fp32")
+    assert v1.ok, v1.summary()
+    assert v2.ok, v2.summary()
 
 
 def _oracle_gated(inp, heads, scale):
