@@ -138,7 +138,8 @@ struct PL {
     static constexpr int INFO = VOTE + 32;   // valid, head, first token, token count
     static constexpr int BARS = INFO + 32;   // staged, p1, p4, TMEM base
     static constexpr int NRM = BARS + 32;    // task op: 1 / |q_t| [32], then 1 / |k_t| [32]
-    static constexpr int BYTES = NRM + 256;
+    static constexpr int DTB = NRM + 256;    // task op: dt_bias[h, 0..127]
+    static constexpr int BYTES = DTB + 512;
 };
 constexpr int P_SQ = PL::PA, P_SK = PL::PA + 8192, P_SG = PL::PA + 16384;  // staged inputs inside PA
 constexpr int TTS = 36;  // row stride of L^-1 / T (16-byte aligned rows for float4 reads)
@@ -192,24 +193,34 @@ __global__ void __launch_bounds__(P_NT, 3)
     const int p = threadIdx.x, lane = p & 31, pw = p >> 5;
     const int c = p & 127, half = p >> 7;
     const int64_t j = blockIdx.x;
-    if (p == 0) {
+    if (pw == 0) {
+        // The slot's sequence: the last s with base[s] * H <= j, found by warp 0 in a 32-way search
+        // (one round of loads for up to 32 sequences; base[0] = 0 keeps lane 0's probe true).
         const int64_t total = (int64_t)base[nseq] * H;
         int valid = 0, hh = 0, t0 = 0, nt = 0;
         if (total > max_slots) {
-            if (j == 0) report_bad_workspace(status);
+            if (j == 0 && lane == 0) report_bad_workspace(status);
         } else if (j < total) {
-            int lo = 0, hi = nseq - 1;  // the last sequence whose slots start at or before j
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if ((int64_t)base[mid] * H <= j) lo = mid;
-                else hi = mid - 1;
+            int lo = 0, n = nseq;
+            while (n > 1) {
+                const int step = (n + 31) >> 5;
+                const bool le = lane * step < n && (int64_t)base[lo + lane * step] * H <= j;
+                const int last = 31 - __clz(__ballot_sync(0xffffffffu, le) | 1u);
+                lo += last * step;
+                n = min(step, n - last * step);
             }
-            const int64_t r = j - (int64_t)base[lo] * H;
-            const int nch = base[lo + 1] - base[lo];
+            // base[lo], base[lo + 1], cu[lo], cu[lo + 1] in one round.
+            const int x = lane < 2 ? base[lo + lane] : (lane < 4 ? cu[lo + lane - 2] : 0);
+            const int b0 = __shfl_sync(0xffffffffu, x, 0), b1 = __shfl_sync(0xffffffffu, x, 1);
+            const int c0 = __shfl_sync(0xffffffffu, x, 2), c1 = __shfl_sync(0xffffffffu, x, 3);
+            const int64_t r = j - (int64_t)b0 * H;
+            const int nch = b1 - b0;
             hh = (int)(r / nch);
-            t0 = cu[lo] + C * (int)(r % nch);
-            nt = min(C, cu[lo + 1] - t0);
+            t0 = c0 + C * (int)(r % nch);
+            nt = min(C, c1 - t0);
             valid = 1;
+        }
+        if (lane == 0 && valid) {
             // q, k, g of the chunk's 32 token rows (rows past the chain's end are read and then
             // ignored; rows past the tensor are zero-filled).
             sm100::mbar_init(bar_ld, 1);
@@ -226,11 +237,13 @@ __global__ void __launch_bounds__(P_NT, 3)
 #pragma unroll
             for (int b = 0; b < (TASK ? 2 : 4); ++b) sm100::tma_load_3d(smem + P_SG + 4096 * b, &tg, bar_ld, (TASK ? 64 : 32) * b, hh, t0);
         }
-        info[0] = valid;
-        info[1] = hh;
-        info[2] = t0;
-        info[3] = nt;
-        info[4] = 0;  // a bounded wait of thread 0 gave up
+        if (lane == 0) {
+            info[0] = valid;
+            info[1] = hh;
+            info[2] = t0;
+            info[3] = nt;
+            info[4] = 0;  // a bounded wait of thread 0 gave up
+        }
     }
     __syncthreads();
     if (!info[0]) return;
@@ -249,6 +262,8 @@ __global__ void __launch_bounds__(P_NT, 3)
         }
         bs[p] = b;
     }
+    float* dtb = reinterpret_cast<float*>(smem + PL::DTB);
+    if (TASK && p < D) dtb[p] = task.dt_bias[(size_t)hh * D + p];
     const float qscale = TASK ? *task.scale : scale;
     // Thread 0 alone waits for the staged inputs (and below, for each MMA); the other warps sleep
     // at the CTA barrier instead of polling.
@@ -257,22 +272,40 @@ __global__ void __launch_bounds__(P_NT, 3)
     float* nrm = reinterpret_cast<float*>(smem + PL::NRM);
     if (TASK) {
         // 1 / |q_t| and 1 / |k_t|: thread -> token p / 8, channels 16 (p & 7) .. + 15 (two 16-byte
-        // chunks of one 64-channel box row), the 8 threads of a token reduce by shuffles.
+        // chunks of one 64-channel box row), the 8 threads of a token reduce by shuffles.  The same
+        // thread turns its 16 gates into log-decays, written as fp32 into PB in the layout the fp32
+        // g boxes of the gated workload have (box of 32 channels x 32 tokens, 128-byte swizzle),
+        // where the factor pass reads them; PB is free until that pass writes Kn.
         const int tt = p >> 3, part = p & 7;
         const int roff = (part >> 2) * 4096 + tt * 128;
+        const float ea = __expf(task.a_log[hh]);
         float sq = 0.f, sk = 0.f;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int co = ((2 * (part & 3) + u) ^ (tt & 7)) << 4;
             const uint4 qw = *reinterpret_cast<const uint4*>(smem + P_SQ + roff + co);
             const uint4 kw = *reinterpret_cast<const uint4*>(smem + P_SK + roff + co);
-            const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ka[4] = {kw.x, kw.y, kw.z, kw.w};
+            const uint4 gw = *reinterpret_cast<const uint4*>(smem + P_SG + roff + co);
+            const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ka[4] = {kw.x, kw.y, kw.z, kw.w}, ga[4] = {gw.x, gw.y, gw.z, gw.w};
+            float ld[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float q0 = from16<T>((uint16_t)(qa[e] & 0xFFFFu)), q1 = from16<T>((uint16_t)(qa[e] >> 16));
                 const float k0 = from16<T>((uint16_t)(ka[e] & 0xFFFFu)), k1 = from16<T>((uint16_t)(ka[e] >> 16));
                 sq = fmaf(q0, q0, fmaf(q1, q1, sq));
                 sk = fmaf(k0, k0, fmaf(k1, k1, sk));
+                const int ch = 16 * part + 8 * u + 2 * e;
+                const float g0 = from16<T>((uint16_t)(ga[e] & 0xFFFFu)), g1 = from16<T>((uint16_t)(ga[e] >> 16));
+                ld[2 * e] = task.lower_bound * __fdividef(1.0f, 1.0f + __expf(-ea * (g0 + dtb[ch])));
+                ld[2 * e + 1] = task.lower_bound * __fdividef(1.0f, 1.0f + __expf(-ea * (g1 + dtb[ch + 1])));
+            }
+            // Channels 16 part + 8 u .. + 7: two 16-byte chunks of box (part >> 1), row tt.
+            uint8_t* gd = smem + PL::PB + (part >> 1) * 4096 + tt * 128;
+#pragma unroll
+            for (int v2 = 0; v2 < 2; ++v2) {
+                const int chunk = 4 * (part & 1) + 2 * u + v2;
+                *reinterpret_cast<float4*>(gd + ((chunk ^ (tt & 7)) << 4)) =
+                    make_float4(ld[4 * v2], ld[4 * v2 + 1], ld[4 * v2 + 2], ld[4 * v2 + 3]);
             }
         }
 #pragma unroll
@@ -291,26 +324,21 @@ __global__ void __launch_bounds__(P_NT, 3)
     // Channel c's element of token t = 16 * half + jj in a staged tile sits at the row base +
     // jj * 128 + (its 16-byte chunk XOR (jj & 7) * 16): t & 7 == jj & 7, so only the XOR varies.
     const int gch = ((c & 31) >> 2) << 4, hch = ((c & 63) >> 3) << 4;
-    const uint8_t* sg0 = TASK ? smem + P_SG + (c >> 6) * 4096 + half * 2048 + ((c & 7) << 1)
-                              : smem + P_SG + (c >> 5) * 4096 + half * 2048 + ((c & 3) << 2);
+    // fp32 log-decays: the staged g boxes, or (task op) the decays formed above in PB.
+    const uint8_t* sg0 = smem + (TASK ? PL::PB : P_SG) + (c >> 5) * 4096 + half * 2048 + ((c & 3) << 2);
     const uint8_t* sk0 = smem + P_SK + (c >> 6) * 4096 + half * 2048 + ((c & 7) << 1);
     const uint8_t* sq0 = sk0 - P_SK + P_SQ;
-    const float task_ea = TASK ? __expf(task.a_log[hh]) : 0.f;
-    const float task_dtb = TASK ? task.dt_bias[(size_t)hh * D + c] : 0.f;
     float bl[16], kv[16], qv[16];
 #pragma unroll
     for (int jj = 0; jj < 16; ++jj) {
         const bool live = 16 * half + jj < nt;
         const int rw = jj * 128;
-        float gl, kx = from16<T>(*reinterpret_cast<const uint16_t*>(sk0 + rw + (hch ^ ((jj & 7) << 4))));
+        const float gl = *reinterpret_cast<const float*>(sg0 + rw + (gch ^ ((jj & 7) << 4)));
+        float kx = from16<T>(*reinterpret_cast<const uint16_t*>(sk0 + rw + (hch ^ ((jj & 7) << 4))));
         float qx = from16<T>(*reinterpret_cast<const uint16_t*>(sq0 + rw + (hch ^ ((jj & 7) << 4)))) * qscale;
         if (TASK) {
-            const float gx = from16<T>(*reinterpret_cast<const uint16_t*>(sg0 + rw + (hch ^ ((jj & 7) << 4))));
-            gl = task.lower_bound * (1.0f / (1.0f + __expf(-task_ea * (gx + task_dtb))));
             kx *= nrm[C + 16 * half + jj];
             qx *= nrm[16 * half + jj];
-        } else {
-            gl = *reinterpret_cast<const float*>(sg0 + rw + (gch ^ ((jj & 7) << 4)));
         }
         bl[jj] = live ? gl : 0.f;
         kv[jj] = live ? kx : 0.f;
@@ -587,6 +615,9 @@ __global__ void __launch_bounds__(P_NT, 3)
 
     // ---- [-K2 | Q2] = [0 | Qp] + (-Kp)^T . [T ; MT]^T: M = 128 (channels), N = 64, K = 32, bf16 x3, both K-major ----
     if (p == 0) {
+        // The KE | TMB | EL part of the slot is final: its bulk store overlaps the MMA below.
+        sm100::bulk_store(slot + SL_KE, sm100::smem_u32(smem + P_KE), SLOT_BYTES - SL_KE);
+        sm100::bulk_commit();
         sm100::tc_fence_after();
         constexpr uint32_t idesc = sm100::idesc_f16(128, 64, BF16);
         const uint64_t ad0 = sm100::smem_desc_k_sw128(sm100::smem_u32(smem + PL::KP));
@@ -625,13 +656,12 @@ __global__ void __launch_bounds__(P_NT, 3)
                 make_uint4(q2r[8 * gq + 4], q2r[8 * gq + 5], q2r[8 * gq + 6], q2r[8 * gq + 7]);
         }
     }
-    // The slot: B1 (32 KB) and KE | TMB | EL (16.5 KB) by two bulk copies; the CTA leaves once
-    // they have read shared memory (the chain kernel is a later launch on the same stream).
+    // B1 (32 KB) by a second bulk copy; the CTA leaves once both copies have read shared memory
+    // (the chain kernel is a later launch on the same stream).
     sm100::fence_proxy_async_smem();
     __syncthreads();
     if (p == 0) {
         sm100::bulk_store(slot + SL_B1, sm100::smem_u32(smem + P_B1), 32768);
-        sm100::bulk_store(slot + SL_KE, sm100::smem_u32(smem + P_KE), SLOT_BYTES - SL_KE);
         sm100::bulk_commit();
         sm100::bulk_wait_read();
     }
