@@ -23,6 +23,11 @@
 // into two 128-column halves (N=128 MMAs), so the last round takes half a tile instead of a whole
 // one (4096^3: 3.5 instead of 4 tile times per CTA).  Every mbarrier wait is bounded (sm100::mbar_wait):
 // a wait that gives up records a status word and the CTA drains to its teardown.
+//
+// Small problems (K-major B, at most one SM's worth of 128 x 64 tiles) take gemm_nt_small_kernel
+// instead: one CTA per 128 x 64 tile, an 8-stage ring of 64-deep K-blocks (24 KB each), so up to
+// K = 512 every load of the CTA is in flight at once and the tile costs one memory round trip; the
+// persistent kernel would leave most SMs idle and stream its K-blocks through two ring rounds.
 #include "sf_common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -295,6 +300,132 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 1) sm100::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ---- small problems: one 128 x 64 tile per CTA, all K-blocks in flight ---------------------------
+constexpr int SBN = 64;
+constexpr int S_STAGES = 8;
+constexpr int S_B_BYTES = SBN * BK * 2;  // 8 KB
+constexpr int S_STAGE_BYTES = A_BYTES + S_B_BYTES;
+constexpr int S_TMEM_COLS = SBN;
+constexpr int S_SMEM_BYTES = S_STAGES * S_STAGE_BYTES + 1024 + 256;
+
+struct __align__(8) SmallBarriers {
+    uint64_t full[S_STAGES];
+    uint64_t empty[S_STAGES];
+    uint64_t acc_full;
+    uint32_t tmem_base;
+};
+
+template <typename T, bool SILU>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_nt_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M,
+                         int N, int K, sm100::KernelStatus* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    SmallBarriers* bars = reinterpret_cast<SmallBarriers*>(smem + S_STAGES * S_STAGE_BYTES);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tiles_n = (N + SBN - 1) / SBN;
+    const int tm = blockIdx.x / tiles_n, tn = blockIdx.x - tm * tiles_n;  // neighbouring CTAs share A rows
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_STAGES; ++s) {
+            sm100::mbar_init(&bars->full[s], 1);
+            sm100::mbar_init(&bars->empty[s], 1);
+        }
+        sm100::mbar_init(&bars->acc_full, 1);
+        sm100::fence_mbar_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&bars->tmem_base, S_TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int stage = kb % S_STAGES;
+                // Reuse of a stage (K > 512) waits for the MMAs that read it; the first round passes.
+                if (!sm100::mbar_wait(&bars->empty[stage], ((uint32_t)(kb / S_STAGES) & 1u) ^ 1u, status, 11)) break;
+                uint8_t* sa = smem + stage * S_STAGE_BYTES;
+                sm100::mbar_arrive_expect_tx(&bars->full[stage], S_STAGE_BYTES);
+                sm100::tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * BK, tm * BM);
+                sm100::tma_load_2d(sa + A_BYTES, &tmap_b, &bars->full[stage], kb * BK, tn * SBN);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+            constexpr uint32_t idesc = sm100::idesc_f16(BM, SBN, BF);
+            bool ok = true;
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int stage = kb % S_STAGES;
+                if (!sm100::mbar_wait(&bars->full[stage], (uint32_t)(kb / S_STAGES) & 1u, status, 12)) {
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t sa = sm100::smem_u32(smem + stage * S_STAGE_BYTES);
+                const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    sm100::mma_f16(tmem_base, sm100::smem_desc_k_sw128(sa + k * 32), sm100::smem_desc_k_sw128(sb + k * 32), idesc,
+                                   (kb > 0 || k > 0) ? 1u : 0u);
+                sm100::mma_commit(&bars->empty[stage]);
+            }
+            if (ok) sm100::mma_commit(&bars->acc_full);
+        }
+    } else {
+        const int quad = warp & 3;
+        const int row = tm * BM + quad * 32 + lane;
+        const bool vec_ok = (N % 8) == 0;
+        if (sm100::mbar_wait(&bars->acc_full, 0, status, 13)) {
+            sm100::tc_fence_after();
+            const uint32_t t_base = tmem_base + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < SBN; c += 32) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(t_base + (uint32_t)c, r);
+                sm100::tmem_ld_wait();
+                if (SILU) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float2 v = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        const float2 o = sf::f2_mul(v, sf::sigmoid2_nr(v));
+                        r[j] = __float_as_uint(o.x);
+                        r[j + 1] = __float_as_uint(o.y);
+                    }
+                }
+                const int col0 = tn * SBN + c;
+                if (row < M) {
+                    T* dst = C + (size_t)row * (size_t)N + col0;
+                    if (vec_ok && col0 + 32 <= N) {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) p[j] = pack2<T>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) d4[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j < N) dst[j] = sf::Dt<T>::from_f(__uint_as_float(r[j]));
+                        }
+                    }
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem_base, S_TMEM_COLS);
+}
+
 // ---- host side ----------------------------------------------------------------------------------
 
 template <typename T, bool BMN, bool SILU>
@@ -318,11 +449,24 @@ int launch_tc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     sm100::KernelStatus* st = nullptr;
     if (cudaGetSymbolAddress((void**)&st, g_gemm_status) != cudaSuccess || !st)
         return sf::fail(SF_EDEVICE, err, cap, "gemm: cannot resolve the status word");
+    const int64_t sms = std::max(1, sf::sm_count());
+    const int64_t small_ctas = ((M + BM - 1) / BM) * ((N + SBN - 1) / SBN);
+    if (!BMN && small_ctas <= sms) {
+        // At most one 128 x 64 tile per SM: the small-problem kernel.
+        CUtensorMap mb64;
+        rc = sf::tmap_kmajor(&mb64, B, N, K, SBN, bf16, err, cap);
+        if (rc) return rc;
+        static std::atomic<uint64_t> small_attr_done{0};
+        if (sf::once_per_device(small_attr_done))
+            cudaFuncSetAttribute(gemm_nt_small_kernel<T, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM_BYTES);
+        gemm_nt_small_kernel<T, SILU><<<(unsigned)small_ctas, NUM_THREADS, S_SMEM_BYTES, stream>>>(ma, mb64, (T*)C, (int)M, (int)N,
+                                                                                               (int)K, st);
+        return sf::check_launch("gemm_nt small tcgen05 launch", err, cap);
+    }
     static std::atomic<uint64_t> attr_done{0};
     if (sf::once_per_device(attr_done))
         cudaFuncSetAttribute(gemm_nt_tc_kernel<T, BMN, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const int64_t sms = std::max(1, sf::sm_count());
     // Tiles left over after the last full round of the persistent CTAs are split into halves when
     // the halves still fit in one round.
     const int64_t rounds = tiles / sms, tail = tiles - rounds * sms;

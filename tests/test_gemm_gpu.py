@@ -71,6 +71,9 @@ NT_SHAPES = [
     (300, 200, 72),        # ragged M/N, K tail inside a block
     (1, 256, 64),          # single row
     (129, 257, 136),       # N % 8 != 0: scalar epilogue stores
+    (256, 320, 1000),      # small-problem kernel: 16 K-blocks through its 8-stage ring, K tail
+    (1024, 1152, 256),     # small-problem kernel at 144 CTAs (one 128 x 64 tile per SM)
+    (1024, 1216, 128),     # 152 tiles of 128 x 64: the persistent kernel again
     (4096, 4096, 4096),    # the workload
     (4095, 4096, 4096),    # tail shard
 ]
