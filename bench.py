@@ -203,7 +203,8 @@ def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
             "inputs": "U(-1,1), seed 7",
             "l2": f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB",
         },
-        kernel="gemm_nt_tc_kernel",
+        # One 128 x 64 tile per SM or fewer: the small-problem kernel (B200: 148 SMs).
+        kernel="gemm_nt_small_kernel" if -(-m // 128) * -(-n // 64) <= 148 else "gemm_nt_tc_kernel",
         make_sets=make_sets,
         desc=desc,
         host_inputs=host_inputs,
