@@ -148,6 +148,8 @@ class Workload:
     shard_note: str = ""
     # CPU tensors of the workload at the search seed (for the registered-baseline timing).
     cpu_inputs: Callable | None = None
+    # Steps of several launches: what `achieved` and `traffic` cover.
+    roofline_note: str = ""
 
 
 def _gemm_nt_workload(m: int, n: int, k: int, dtype: str = "fp16") -> Workload:
@@ -279,7 +281,7 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
 
 
 def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_inputs, in_names, out_specs, dims, attrs=(), flags=0,
-                 cpu_rows=None, total_rows=1, null_args=(), scratch_bytes=0, launches_per_step=1) -> Workload:
+                 cpu_rows=None, total_rows=1, null_args=(), scratch_bytes=0, launches_per_step=1, roofline_note="") -> Workload:
     """A workload over one C-ABI operator: ``make_inputs(seed)`` gives CPU tensors named
     ``in_names`` (ABI order, followed by the outputs ``out_specs`` = [(shape, dtype)]);
     ``null_args`` are ABI positions passed as NULL (optional tensors); ``scratch_bytes`` > 0
@@ -333,6 +335,7 @@ def _op_workload(name, unit, bound, dtype, units, config, kernel, op, make_input
                     config=dict(config, l2=f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB"),
                     kernel=kernel, make_sets=make_sets, desc=desc, host_inputs=host_inputs, e2e_launch=e2e_launch,
                     cpu_rows=cpu_rows, total_rows=total_rows, nsets=nsets, launches_per_step=launches_per_step,
+                    roofline_note=roofline_note,
                     cpu_inputs=lambda: make_inputs(cases_seed()))
 
 
@@ -419,6 +422,11 @@ def _bitdelta_base_workload(m: int, n: int = 4096, k: int = 4096, dtype: str = "
         [((m, n), cases.TORCH_DTYPE[dtype])], (m, n, k), cpu_rows=cpu_rows, total_rows=n)
 
 
+# The two-pass KDA step is three launches (chunk prefix, parallel chunk preparation, state chains).
+KDA_ROOFLINE_NOTE = ("step of 3 launches (kda_slots_kernel, kda_prep_kernel, kda_chain_kernel): achieved = algorithmic bytes "
+                     "/ step time; traffic = the named (longest) kernel's DRAM bytes per launch")
+
+
 def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", world: int = 1, rank: int = 0) -> Workload:
     """With world > 1 the 8 x H (sequence, head) chains are dealt to ranks by a token balance
     (``shard.chain_assign``) and each rank runs its chains repacked as a single-head packed batch;
@@ -476,8 +484,9 @@ def _kda_gated_workload(heads: int = 16, dim: int = 128, dtype: str = "bf16", wo
         {"workload": f"varlen gated KDA, {n} packed sequences {lengths} (seeded U(256,4096)), H={heads}, D={dim}, q/k {dtype} "
                      "L2-normalised, v {dtype}, beta=sigmoid(N) fp32, g=logsigmoid(N) fp32, zero initial state".replace("{dtype}", dtype),
          "total_tokens": total},
-        "kda_chain_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
+        "kda_prep_kernel", "varlen_kda_gated", make_inputs, ["q", "k", "v", "g", "beta", "cu_seqlens"], out_specs, dims,
         (1.0 / math.sqrt(dim),), cpu_rows=cpu_rows, total_rows=lengths[0], null_args=(6,), scratch_bytes=ws, launches_per_step=3)
+    wl.roofline_note = KDA_ROOFLINE_NOTE
     if chains is not None:
         wl.sharded, wl.total_units = True, total_bytes
         wl.shard_note = (f"{n}x{heads} (sequence, head) chains dealt to {world} ranks by token count (rank {rank}: "
@@ -788,10 +797,10 @@ def _kda_task_workload(heads: int = 64, dim: int = 128, lengths=(2048, 1024, 102
         f"varlen_kda_h{heads}_mixed", "GB/s", "hbm", dtype, nbytes,
         {"workload": f"task varlen_kda v6_h64_mixed: {n} sequences {lengths}, H={heads}, D={dim}, {dtype}, the task's input "
                      "stream (0.5 N(0,1) q/k/v/g/beta, A_log = log U(1,16), dt_bias, non-zero initial state)", "total_tokens": t},
-        "kda_chain_kernel", "varlen_kda", make_inputs,
+        "kda_prep_kernel", "varlen_kda", make_inputs,
         ["q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "cu_seqlens", "scale"],
         [((t, heads, dim), cases.TORCH_DTYPE[dtype]), ((n, heads, dim, dim), torch.float32)], (n, heads, dim, t, ws), (-5.0,),
-        cpu_rows=cpu_rows, total_rows=lengths[0], scratch_bytes=ws, launches_per_step=3)
+        cpu_rows=cpu_rows, total_rows=lengths[0], scratch_bytes=ws, launches_per_step=3, roofline_note=KDA_ROOFLINE_NOTE)
 
 
 WORKLOADS = {
@@ -1181,6 +1190,7 @@ def run_ours(args, wl: Workload, world: int, rank: int, local: int) -> dict | No
             "peak_source": peak_src,
             "traffic": _traffic(wl.kernel, wl.name),
             "kernel": wl.kernel,
+            **({"note": wl.roofline_note} if wl.roofline_note else {}),
         },
         "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps,
