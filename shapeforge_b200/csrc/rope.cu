@@ -5,9 +5,9 @@
 //   y[..., i + half] = x[..., i] * sin(angle) + x[..., i+half] * cos(angle)
 //
 // HBM-bound (2 x 16-bit per element in + out).  The angle depends only on (s, i), so a CTA owns a
-// block of 32 positions and a share of the B*H heads: each thread computes the cos/sin of its 8
-// frequencies at its position once and then streams its 16-byte x1/x2 vectors through every head of
-// its share, two heads per step.  inv_freq[i] = r^i with r = BASE^(-1/half) computed once on the
+// block of 32 positions and a share of the B*H heads: each thread issues the 16-byte x1/x2 loads of
+// up to 8 heads of its share at once, computes the cos/sin of its 8 frequencies at its position
+// while they are in flight (once per thread), then rotates and stores them.  inv_freq[i] = r^i with r = BASE^(-1/half) computed once on the
 // host in double precision (a thread's first frequency by repeated squaring, the next ones by
 // repeated multiplication: relative error below 2^-46); the angle s * inv_freq is formed and
 // reduced modulo 2 pi in double precision, so positions in the thousands keep full accuracy, and
@@ -15,13 +15,20 @@
 #include "sf_common.cuh"
 
 #include <cmath>
+#include <type_traits>
 
 namespace {
 
 constexpr int POS_PER_CTA = 32;
 
+// Heads a thread handles per step: all their 16-byte loads are issued before the angles are
+// computed, so the DRAM latency overlaps the double-precision angle reduction (4 for bf16, whose
+// conversions need more registers, so that two CTAs still fit on an SM without spills).
 template <typename T>
-__global__ void __launch_bounds__(256) rope_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t bh, int64_t S,
+__host__ __device__ constexpr int heads_per_step() { return std::is_same<T, __half>::value ? 8 : 4; }
+
+template <typename T>
+__global__ void __launch_bounds__(256, 2) rope_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t bh, int64_t S,
                                                        int64_t D, double ratio, int64_t bh_per_cta) {
     const int64_t half = D / 2;
     const int64_t vec_per_pos = half / 8;
@@ -30,49 +37,50 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const T* __restrict__ x, 
     const int64_t iv = local % vec_per_pos;
     const int64_t s = (int64_t)blockIdx.x * POS_PER_CTA + p;
     if (p >= POS_PER_CTA || s >= S) return;
-    float c[8], sn[8];
-    {
-        double f = 1.0, sq = ratio;
-        for (int64_t e = iv * 8; e > 0; e >>= 1) {  // ratio^(8 iv)
-            if (e & 1) f *= sq;
-            sq *= sq;
-        }
-        constexpr double TWO_PI = 6.283185307179586476925286766559;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const double ang = (double)s * f;
-            const double red = ang - rint(ang * (1.0 / TWO_PI)) * TWO_PI;
-            __sincosf((float)red, &sn[j], &c[j]);
-            f *= ratio;
-        }
-    }
     const int64_t h0 = (int64_t)blockIdx.y * bh_per_cta;
     const int64_t h1 = min(bh, h0 + bh_per_cta);
-    auto rotate = [&](const sf::Vec8<T>& a, const sf::Vec8<T>& b, T* yr) {
-        sf::Vec8<T> o1, o2;
+    constexpr int HG = heads_per_step<T>();
+    float c[8], sn[8];
+    for (int64_t hb = h0; hb < h1; hb += HG) {
+        sf::Vec8<T> a[HG], b[HG];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float x1 = sf::Dt<T>::to_f(a.v[j]), x2 = sf::Dt<T>::to_f(b.v[j]);
-            o1.v[j] = sf::Dt<T>::from_f(x1 * c[j] - x2 * sn[j]);
-            o2.v[j] = sf::Dt<T>::from_f(x1 * sn[j] + x2 * c[j]);
+        for (int u = 0; u < HG; ++u) {
+            if (hb + u < h1) {
+                const T* xr = x + ((hb + u) * S + s) * D + iv * 8;
+                a[u] = sf::ld_global_nc_v8<T>(xr);
+                b[u] = sf::ld_global_nc_v8<T>(xr + half);
+            }
         }
-        sf::st_global_v8<T>(yr + iv * 8, o1);
-        sf::st_global_v8<T>(yr + half + iv * 8, o2);
-    };
-    int64_t h = h0;
-    for (; h + 1 < h1; h += 2) {
-        const T* xa = x + (h * S + s) * D;
-        const T* xb = x + ((h + 1) * S + s) * D;
-        const sf::Vec8<T> a0 = sf::ld_global_nc_v8<T>(xa + iv * 8);
-        const sf::Vec8<T> b0 = sf::ld_global_nc_v8<T>(xa + half + iv * 8);
-        const sf::Vec8<T> a1 = sf::ld_global_nc_v8<T>(xb + iv * 8);
-        const sf::Vec8<T> b1 = sf::ld_global_nc_v8<T>(xb + half + iv * 8);
-        rotate(a0, b0, y + (h * S + s) * D);
-        rotate(a1, b1, y + ((h + 1) * S + s) * D);
-    }
-    if (h < h1) {
-        const T* xr = x + (h * S + s) * D;
-        rotate(sf::ld_global_nc_v8<T>(xr + iv * 8), sf::ld_global_nc_v8<T>(xr + half + iv * 8), y + (h * S + s) * D);
+        if (hb == h0) {
+            double f = 1.0, sq = ratio;
+            for (int64_t e = iv * 8; e > 0; e >>= 1) {  // ratio^(8 iv)
+                if (e & 1) f *= sq;
+                sq *= sq;
+            }
+            constexpr double TWO_PI = 6.283185307179586476925286766559;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const double ang = (double)s * f;
+                const double red = ang - rint(ang * (1.0 / TWO_PI)) * TWO_PI;
+                __sincosf((float)red, &sn[j], &c[j]);
+                f *= ratio;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < HG; ++u) {
+            if (hb + u < h1) {
+                sf::Vec8<T> o1, o2;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float x1 = sf::Dt<T>::to_f(a[u].v[j]), x2 = sf::Dt<T>::to_f(b[u].v[j]);
+                    o1.v[j] = sf::Dt<T>::from_f(x1 * c[j] - x2 * sn[j]);
+                    o2.v[j] = sf::Dt<T>::from_f(x1 * sn[j] + x2 * c[j]);
+                }
+                T* yr = y + ((hb + u) * S + s) * D + iv * 8;
+                sf::st_global_v8<T>(yr, o1);
+                sf::st_global_v8<T>(yr + half, o2);
+            }
+        }
     }
 }
 
@@ -102,8 +110,8 @@ int launch_t(const void* x, void* y, int64_t B, int64_t H, int64_t S, int64_t D,
     const bool vec = variant != 2 && half % 8 == 0 && sf::aligned16(x) && sf::aligned16(y) && (half / 8) * POS_PER_CTA <= 256;
     if (vec) {
         const int64_t pos_blocks = (S + POS_PER_CTA - 1) / POS_PER_CTA;
-        // Enough CTAs to fill the GPU several times over; each walks a share of the heads.
-        int64_t splits = (int64_t)sf::sm_count() * 8 / (pos_blocks > 0 ? pos_blocks : 1);
+        // About two CTAs per SM in one wave; each walks a share of the heads, HG at a time.
+        int64_t splits = (int64_t)sf::sm_count() * 2 / (pos_blocks > 0 ? pos_blocks : 1);
         if (splits < 1) splits = 1;
         if (splits > bh) splits = bh;
         if (splits > 65535) splits = 65535;
