@@ -97,7 +97,7 @@ def test_rope_reference_vectors(cuda_device, dtype):
 
 
 SHAPES = {
-    "softmax": [(8192, 2048), (64, 512), (5, 3), (3, 1000), (2, 8200)],
+    "softmax": [(8192, 2048), (64, 512), (5, 3), (3, 1000), (2, 8200), (33, 64), (9, 2040)],
     "reduction_sum": [(4096, 4096), (64, 1024), (256, 4096), (7, 13), (3, 70000)],
     "silu": [(16777216,), (65536,), (1,), (1001,)],
     "swiglu": [(16777216,), (65536,), (13,)],
