@@ -163,8 +163,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         sm100::mbar_init(&bars->acc_full, 1);
         sm100::fence_mbar_init();
     }
-    // The first ring of W_base / x tiles is requested before anything else (the slots start
-    // empty), so DRAM latency overlaps the table build and TMEM allocation.
+    // Sign words of the first 16 K-blocks are requested first, then (after a CTA barrier, so the
+    // memory system sees them ahead of every CTA's burst of W_base tiles) the first ring of W_base /
+    // x tiles; both latencies overlap the table build and TMEM allocation.
     const int pre = min(stages, max(kb_end - kb_begin, 0));
     auto issue = [&](int kb, int s) {
         uint8_t* st = smem + s * stage_bytes;
@@ -172,12 +173,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         sm100::tma_load_2d(st, &tmap_w, &bars->full_w[s], kb * BK, n0);
         sm100::tma_load_2d(st + ROW_TILE_BYTES, &tmap_x, &bars->full_w[s], kb * BK, 0);
     };
-    if (threadIdx.x == 0) {
-        sm100::tma_prefetch_desc(&tmap_w);
-        sm100::tma_prefetch_desc(&tmap_x);
-        for (int i = 0; i < pre; ++i) issue(kb_begin + i, i);
-    }
-    // Sign words of the first 16 K-blocks: requested before the set-up barrier as well.
     const int t = threadIdx.x - 64;
     const int n = n0 + t;
     const bool row_live = warp >= 2 && t < tile_n && n < N;
@@ -200,6 +195,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     };
     if (warp >= 2 && kb_end > kb_begin) load_words(kb_begin);
+    __syncthreads();  // barrier initialisation visible; the sign-word loads issued
+    if (threadIdx.x == 0) {
+        sm100::tma_prefetch_desc(&tmap_w);
+        sm100::tma_prefetch_desc(&tmap_x);
+        for (int i = 0; i < pre; ++i) issue(kb_begin + i, i);
+    }
     build_sign_lut8<T>(lut);
     if (warp == 1) {
         sm100::tmem_alloc(&bars->tmem_base, tmem_cols);
