@@ -268,7 +268,7 @@ def _rmsnorm_workload(rows: int, hidden: int, dtype: str = "fp16") -> Workload:
             "shape": [rows, hidden],
             "l2": f"inputs rotate over {nsets} sets ({nsets * per_set / 2**20:.0f} MiB) > L2 126 MB",
         },
-        kernel="rmsnorm_vec_kernel",
+        kernel="rmsnorm_warp_kernel" if hidden <= 1024 else "rmsnorm_vec_kernel",  # a warp per row up to 1024 elements
         make_sets=make_sets,
         desc=desc,
         host_inputs=host_inputs,
