@@ -385,7 +385,9 @@ def _attention_workload(b: int, h: int, s: int, d: int, causal: bool = True, dty
         f"attention_{'causal' if causal else 'full'}_{b}x{h}x{s}x{d}", "TFLOP/s", "tensor", dtype, flops,
         {"workload": f"flash attention forward {'causal' if causal else 'non-causal'}, q/k/v {dtype} [{b},{h},{s},{d}] ~ N(0,1), "
                      f"scale 1/sqrt({d}), fp32 softmax statistics", "shape": [b, h, s, d]},
-        "fa_fwd_kernel", "flash_attention", make_inputs, ["q", "k", "v"], [(shape, cases.TORCH_DTYPE[dtype])],
+        # At most one (b*h, 128-row query tile) CTA per SM (B200: 148): the S-double-buffered kernel.
+        "fa_fwd_db_kernel" if shape[0] * shape[1] * -(-s // 128) <= 148 else "fa_fwd_kernel",
+        "flash_attention", make_inputs, ["q", "k", "v"], [(shape, cases.TORCH_DTYPE[dtype])],
         shape, (scale,), 1 if causal else 0, cpu_rows=cpu_rows, total_rows=s)
     if world > 1:
         wl.sharded, wl.total_units = True, total_flops

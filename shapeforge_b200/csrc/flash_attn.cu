@@ -132,10 +132,13 @@ struct Layout {
 
 // One score tile of one query row (the calling thread's TMEM lane): row max, lazy rescale of O,
 // exponentials, P_j (high + residual) over the score columns, published a half at a time on
-// p_full[0] / p_full[1].  MASK: keys past `lim` (tile-relative) score -inf.
+// p_full[0] / p_full[1].  MASK: keys past `lim` (tile-relative) score -inf.  `o_ready` (when not
+// null) completes a phase per P.V: a warp that must rescale O first waits for P_{j-1}.V_{j-1}
+// (the kernel that double-buffers S issues S_{j+1} before P_j.V_j, so S_j does not imply it).
 template <typename T, int D, bool MASK>
 __device__ __forceinline__ void softmax_tile(uint32_t tmem, uint32_t tmem_o, uint32_t lane_off, int lim, int j, float scale_log2,
-                                             float& m, float& l, uint64_t* p_full) {
+                                             float& m, float& l, uint64_t* p_full, uint64_t* o_ready = nullptr,
+                                             sm100::KernelStatus* status = nullptr) {
     constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
     // Pass 1: row max of the raw scores (scale > 0 commutes with max); NaN propagates.
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -163,10 +166,15 @@ __device__ __forceinline__ void softmax_tile(uint32_t tmem, uint32_t tmem_o, uin
     const bool need = !(m_new <= m + 8.0f);
     const float m_old = m;
     if (need) m = m_new;
-    // P.V_{j-1} has completed: the commit that published S_j was issued after it.
+    // P.V_{j-1} has completed: the commit that published S_j was issued after it (or, with
+    // o_ready, once that barrier's phase j - 1 is complete).
     if (j > 0) {
         const float alpha = need ? ex2_approx(m_old - m_new) : 1.0f;
         if (__any_sync(0xffffffffu, need)) {
+            if (o_ready) {
+                sm100::mbar_wait(o_ready, (uint32_t)(j - 1) & 1u, status, 40);
+                sm100::tc_fence_after();
+            }
 #pragma unroll 1
             for (int c = 0; c < D / 32; ++c) {
                 uint32_t r[32];
@@ -405,6 +413,219 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     if (warp == 1) sm100::tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ---- small grids: one CTA per SM, S double-buffered -----------------------------------------------
+// When the (b*h, query tile) grid is at most one CTA per SM, no second CTA shares an SM to run its
+// MMAs under this CTA's softmax, so this kernel overlaps them inside the CTA: 512 TMEM columns,
+// S_j in [128 (j & 1), 128 (j & 1) + 128), O in [256, 256 + D).  The MMA warp issues S_0, S_1,
+// P_0.V_0, S_2, P_1.V_1, ...: S_{j+1} runs on the tensor pipe while the softmax works on S_j, and
+// S_{j+2} is issued after P_j.V_j, which read the same columns (the pipe runs one CTA's MMAs in
+// issue order).  K and V have NST slots each.  (On full grids two CTAs per SM of fa_fwd_kernel are
+// faster: 693 against 619 TF/s at causal B4 H32 S2048 D128.)
+constexpr uint32_t DB_TMEM_COLS = 512;
+constexpr uint32_t DB_O_COL = 256;
+
+template <int D>
+struct LayoutDB {
+    static constexpr int DB = D / 64;
+    static constexpr int NST = D == 64 ? 4 : 2;
+    static constexpr int TILE = DB * BOX_BYTES;
+    static constexpr int Q = 0;
+    static constexpr int K = Q + TILE;
+    static constexpr int V = K + NST * TILE;
+    static constexpr int BARS = V + NST * TILE;
+    static constexpr int BYTES = BARS + 512;
+};
+
+struct __align__(8) BarsDB {
+    uint64_t q_full;
+    uint64_t k_full[4], k_empty[4];
+    uint64_t v_full[4], v_empty[4];
+    uint64_t s_full[2];      // S buffer b holds S_j (j & 1 == b); one phase per use
+    uint64_t p_full[2][2];   // P_j of buffer b, keys [0,64) and [64,128)
+    uint64_t o_ready;        // one phase per P_j.V_j
+    uint64_t o_done;
+    uint32_t tmem_base;
+};
+
+template <typename T, int D, bool CAUSAL>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fa_fwd_db_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                     T* __restrict__ o, int S, int BH, int nq, int group, float scale_log2, sm100::KernelStatus* status) {
+    using L = LayoutDB<D>;
+    constexpr int DB = L::DB;
+    constexpr int NST = L::NST;
+    constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    BarsDB* bars = reinterpret_cast<BarsDB*>(smem + L::BARS);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t per_group = (int64_t)group * nq;
+    const int g = (int)((int64_t)blockIdx.x / per_group);
+    const int hbase = g * group;
+    const int gsize = min(group, BH - hbase);
+    const int rem = (int)((int64_t)blockIdx.x - (int64_t)g * per_group);
+    const int bh = hbase + rem % gsize;
+    const int qt = CAUSAL ? (nq - 1 - rem / gsize) : rem / gsize;
+    const int nkv_all = (S + BN - 1) / BN;
+    const int nkv = CAUSAL ? min(qt + 1, nkv_all) : nkv_all;
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bars->q_full, 1);
+        for (int i = 0; i < NST; ++i) {
+            sm100::mbar_init(&bars->k_full[i], 1);
+            sm100::mbar_init(&bars->k_empty[i], 1);
+            sm100::mbar_init(&bars->v_full[i], 1);
+            sm100::mbar_init(&bars->v_empty[i], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            sm100::mbar_init(&bars->s_full[b], 1);
+            sm100::mbar_init(&bars->p_full[b][0], 128);
+            sm100::mbar_init(&bars->p_full[b][1], 128);
+        }
+        sm100::mbar_init(&bars->o_ready, 1);
+        sm100::mbar_init(&bars->o_done, 1);
+        sm100::fence_mbar_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&bars->tmem_base, DB_TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const uint32_t tmem_o = tmem + DB_O_COL;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            sm100::tma_prefetch_desc(&tq);
+            sm100::tma_prefetch_desc(&tk);
+            sm100::tma_prefetch_desc(&tv);
+            sm100::mbar_arrive_expect_tx(&bars->q_full, L::TILE);
+            for (int b = 0; b < DB; ++b) sm100::tma_load_3d(smem + L::Q + b * BOX_BYTES, &tq, &bars->q_full, b * 64, qt * BM, bh);
+            for (int j = 0; j < nkv; ++j) {
+                const int st = j % NST;
+                const uint32_t ph = (uint32_t)(j / NST) & 1u;
+                if (!sm100::mbar_wait(&bars->k_empty[st], ph ^ 1u, status, 41)) break;
+                sm100::mbar_arrive_expect_tx(&bars->k_full[st], L::TILE);
+                for (int b = 0; b < DB; ++b)
+                    sm100::tma_load_3d(smem + L::K + st * L::TILE + b * BOX_BYTES, &tk, &bars->k_full[st], b * 64, j * BN, bh);
+                if (!sm100::mbar_wait(&bars->v_empty[st], ph ^ 1u, status, 42)) break;
+                sm100::mbar_arrive_expect_tx(&bars->v_full[st], L::TILE);
+                for (int b = 0; b < DB; ++b)
+                    sm100::tma_load_3d(smem + L::V + st * L::TILE + b * BOX_BYTES, &tv, &bars->v_full[st], b * 64, j * BN, bh);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = sm100::idesc_f16(BM, BN, BF16);
+            constexpr uint32_t idesc_o = sm100::idesc_f16_bmn(BM, D, BF16);
+            const uint32_t sq = sm100::smem_u32(smem + L::Q);
+            bool ok = sm100::mbar_wait(&bars->q_full, 0, status, 43);
+            // S_j = Q . K_j^T into buffer j & 1.
+            auto issue_s = [&](int j) -> bool {
+                const int st = j % NST;
+                if (!sm100::mbar_wait(&bars->k_full[st], (uint32_t)(j / NST) & 1u, status, 44)) return false;
+                sm100::tc_fence_after();
+                const uint32_t sk = sm100::smem_u32(smem + L::K + st * L::TILE);
+                const uint32_t dst = tmem + 128u * (uint32_t)(j & 1);
+#pragma unroll
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint32_t off = (uint32_t)((k >> 2) * BOX_BYTES + (k & 3) * 32);
+                    sm100::mma_f16(dst, sm100::smem_desc_k_sw128(sq + off), sm100::smem_desc_k_sw128(sk + off), idesc_s, k > 0 ? 1u : 0u);
+                }
+                sm100::mma_commit(&bars->s_full[j & 1]);
+                sm100::mma_commit(&bars->k_empty[st]);
+                return true;
+            };
+            if (ok && nkv > 0) ok = issue_s(0);
+            for (int j = 0; j < nkv && ok; ++j) {
+                if (j + 1 < nkv && !issue_s(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                // O += P_j . V_j, each half of the keys as soon as the softmax has written its P.
+                const int st = j % NST;
+                if (!sm100::mbar_wait(&bars->v_full[st], (uint32_t)(j / NST) & 1u, status, 46)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t sv = sm100::smem_u32(smem + L::V + st * L::TILE);
+                const uint32_t pb = tmem + 128u * (uint32_t)(j & 1);
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    if (!sm100::mbar_wait(&bars->p_full[j & 1][half], (uint32_t)(j >> 1) & 1u, status, 45)) {
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+#pragma unroll
+                    for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
+                        const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
+                        sm100::mma_f16_ta(tmem_o, pb + p_hi_col(kk), bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    }
+#pragma unroll
+                    for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
+                        const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
+                        sm100::mma_f16_ta(tmem_o, pb + p_lo_col(kk), bd, idesc_o, 1u);
+                    }
+                }
+                if (!ok) break;
+                sm100::mma_commit(&bars->v_empty[st]);
+                sm100::mma_commit(&bars->o_ready);
+            }
+            if (ok) sm100::mma_commit(&bars->o_done);
+        }
+    } else {
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const int q = qt * BM + row;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            if (!sm100::mbar_wait(&bars->s_full[j & 1], (uint32_t)(j >> 1) & 1u, status, 47)) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+            const int key0 = j * BN;
+            const bool masked = (CAUSAL && j == qt) || key0 + BN > S;
+            const int lim = masked ? min(CAUSAL && j == qt ? row : BN - 1, S - 1 - key0) : BN - 1;
+            const uint32_t sb = tmem + 128u * (uint32_t)(j & 1);
+            if (masked)
+                softmax_tile<T, D, true>(sb, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[j & 1][0], &bars->o_ready, status);
+            else
+                softmax_tile<T, D, false>(sb, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[j & 1][0], &bars->o_ready, status);
+        }
+        if (ok && nkv > 0 && sm100::mbar_wait(&bars->o_done, 0, status, 49)) {
+            sm100::tc_fence_after();
+            const float inv = 1.0f / l;
+            T* orow = o + ((int64_t)bh * S + q) * D;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+                sm100::tmem_ld_wait();
+                if (q < S) {
+                    uint4* d4 = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        d4[i] = make_uint4(pack2<T>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
+                                           pack2<T>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
+                                           pack2<T>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
+                                           pack2<T>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, DB_TMEM_COLS);
+}
+
 // ---- general fallback: one warp per query row, fp32, any D <= 256 / alignment ------------------
 template <typename T>
 __global__ void __launch_bounds__(128) fa_fallback_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
@@ -453,6 +674,32 @@ sm100::KernelStatus* status_ptr() {
 int tmap_bhsd(CUtensorMap* out, const void* base, int64_t BH, int64_t S, int64_t D, bool bf16, char* err, uint64_t cap);
 
 template <typename T, int D, bool CAUSAL>
+int launch_db_t(const void* q, const void* k, const void* v, void* o, int64_t BH, int64_t S, float scale, cudaStream_t st, char* err,
+                uint64_t cap) {
+    const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+    CUtensorMap mq, mk, mv;
+    int rc = tmap_bhsd(&mq, q, BH, S, D, bf16, err, cap);
+    if (!rc) rc = tmap_bhsd(&mk, k, BH, S, D, bf16, err, cap);
+    if (!rc) rc = tmap_bhsd(&mv, v, BH, S, D, bf16, err, cap);
+    if (rc) return rc;
+    sm100::KernelStatus* status = status_ptr();
+    if (!status) return sf::fail(SF_EDEVICE, err, cap, "attention: cannot resolve the status word");
+    // One CTA per SM: all 512 TMEM columns, and more than half the shared memory so that a second
+    // CTA (which would wait for TMEM) is never co-resident.
+    const int smem = std::max(LayoutDB<D>::BYTES + 1024, 120 * 1024);
+    static std::atomic<uint64_t> attr_done{0};
+    if (sf::once_per_device(attr_done))
+        cudaFuncSetAttribute(fa_fwd_db_kernel<T, D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const int64_t nq = (S + BM - 1) / BM;
+    if (BH > 0x7fffffffLL || nq > 0x7fffffffLL || BH * nq > 0x7fffffffLL) return sf::fail(SF_EINVAL, err, cap, "attention: grid too large");
+    const int64_t kv_head = 4 * S * D;
+    const int group = (int)std::max<int64_t>(1, std::min<int64_t>({16, BH, (32LL << 20) / std::max<int64_t>(kv_head, 1)}));
+    fa_fwd_db_kernel<T, D, CAUSAL><<<(unsigned)(BH * nq), NUM_THREADS, smem, st>>>(mq, mk, mv, (T*)o, (int)S, (int)BH, (int)nq, group,
+                                                                                  scale * 1.4426950408889634f, status);
+    return sf::check_launch("attention launch", err, cap);
+}
+
+template <typename T, int D, bool CAUSAL>
 int launch_tc_t(const void* q, const void* k, const void* v, void* o, int64_t BH, int64_t S, float scale, cudaStream_t st, char* err,
                 uint64_t cap) {
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -484,7 +731,17 @@ int launch_t(const void* q, const void* k, const void* v, void* o, int64_t BH, i
              int32_t variant, cudaStream_t st, char* err, uint64_t cap) {
     const bool tc = (D == 64 || D == 128) && sf::aligned16(q) && sf::aligned16(k) && sf::aligned16(v) && sf::aligned16(o) &&
                     S < (1LL << 31) && BH < (1LL << 31);
-    if (variant == 1 && !tc) return sf::fail(SF_EINVAL, err, cap, "attention: the tensor-core variant needs D in {64,128} and aligned tensors");
+    if ((variant == 1 || variant == 3) && !tc) return sf::fail(SF_EINVAL, err, cap, "attention: the tensor-core variant needs D in {64,128} and aligned tensors");
+    // Variant 3, or by default a grid of at most one (b*h, query tile) CTA per SM: the kernel that
+    // overlaps Q.K with the softmax inside the CTA.
+    const int64_t ctas = BH * ((S + BM - 1) / BM);
+    if (tc && (variant == 3 || (variant == 0 && ctas <= (int64_t)sf::sm_count()))) {
+        if (D == 64)
+            return causal ? launch_db_t<T, 64, true>(q, k, v, o, BH, S, scale, st, err, cap)
+                          : launch_db_t<T, 64, false>(q, k, v, o, BH, S, scale, st, err, cap);
+        return causal ? launch_db_t<T, 128, true>(q, k, v, o, BH, S, scale, st, err, cap)
+                      : launch_db_t<T, 128, false>(q, k, v, o, BH, S, scale, st, err, cap);
+    }
     if (tc && variant != 2) {
         if (D == 64)
             return causal ? launch_tc_t<T, 64, true>(q, k, v, o, BH, S, scale, st, err, cap)

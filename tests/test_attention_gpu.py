@@ -69,14 +69,18 @@ def test_reference_vectors(cuda_device, dtype):
 TASK_SHAPES = [(1, 2, 128, 64), (2, 8, 1024, 64), (1, 2, 200, 64), (1, 1, 77, 128)]
 
 
+# Variants: 0 = default dispatch (a grid of at most one CTA per SM takes the kernel with S
+# double-buffered in TMEM, larger grids two CTAs per SM), 1 = the two-CTA kernel, 3 = the
+# double-buffered kernel at any grid.
+@pytest.mark.parametrize("variant", [0, 1, 3])
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
 @pytest.mark.parametrize("shape", TASK_SHAPES, ids=["x".join(map(str, s)) for s in TASK_SHAPES])
-def test_task_cases_noncausal(cuda_device, dtype, shape):
+def test_task_cases_noncausal(cuda_device, dtype, shape, variant):
     for ci, case in enumerate(cases.ATTENTION_CASES):
         inp = cases.attention_inputs(case, cases.case_seed(0, ci), shape, dtype)
         q, k, v = (inp[n].to(cuda_device) for n in ("q", "k", "v"))
         o = torch.full_like(q, float("nan"))
-        ops.flash_attention(q, k, v, 0.125, causal=False, out=o)
+        ops.flash_attention(q, k, v, 0.125, causal=False, out=o, variant=variant)
         torch.cuda.synchronize()
         _status_ok()
         heads = [0, shape[1] - 1] if shape[1] > 2 else None
@@ -87,15 +91,16 @@ def test_task_cases_noncausal(cuda_device, dtype, shape):
 CAUSAL_SHAPES = [(4, 32, 2048, 128), (4, 32, 512, 128), (4, 32, 2048, 64), (1, 2, 8192, 128), (1, 2, 300, 128), (2, 3, 129, 64)]
 
 
+@pytest.mark.parametrize("variant", [0, 1, 3])
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 @pytest.mark.parametrize("shape", CAUSAL_SHAPES, ids=["x".join(map(str, s)) for s in CAUSAL_SHAPES])
-def test_causal_workload(cuda_device, dtype, shape):
+def test_causal_workload(cuda_device, dtype, shape, variant):
     b, h, s, d = shape
     scale = 1.0 / math.sqrt(d)
     inp = cases.attention_bench_inputs(shape, dtype, seed=cases.SEARCH_SEED)
     q, k, v = (inp[n].to(cuda_device) for n in ("q", "k", "v"))
     o = torch.full_like(q, float("nan"))
-    ops.flash_attention(q, k, v, scale, causal=True, out=o)
+    ops.flash_attention(q, k, v, scale, causal=True, out=o, variant=variant)
     torch.cuda.synchronize()
     _status_ok()
     rng = np.random.default_rng(0)
