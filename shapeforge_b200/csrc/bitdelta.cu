@@ -48,6 +48,9 @@ constexpr int BK = 64;
 constexpr int TILE_ROWS = 128;
 constexpr int ROW_TILE_BYTES = TILE_ROWS * BK * 2;  // 16 KB: 128 rows x 128 bytes
 constexpr int NUM_THREADS = 192;
+// The base kernel adds a seventh warp: warp 1 issues the W_base MMAs and warp 6 the sign MMAs,
+// into their separate accumulators (one thread's tcgen05.mma issue is the per-K-block limit).
+constexpr int BASE_THREADS = 224;
 constexpr int SMEM_LIMIT = 227 * 1024;
 // Neither kernel has static shared memory (the sign tables are dynamic).
 constexpr int BASE_SMEM_LIMIT = SMEM_LIMIT;
@@ -128,7 +131,7 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
 // W_base variant (swap-AB, split-K over a cluster)
 // ------------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(BASE_THREADS, 1)
     bitdelta_base_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                          const uint32_t* __restrict__ s_words, const T* __restrict__ alpha, T* __restrict__ y, int M, int N,
                          int K, int nm, int stages, int vec_words, int tile_n, sm100::KernelStatus* status) {
@@ -154,13 +157,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             sm100::mbar_init(&bars->full_w[s], 1);
-            sm100::mbar_init(&bars->empty_w[s], 1);
+            sm100::mbar_init(&bars->empty_w[s], 2);  // both MMA issuers read the stage's x tile
         }
         for (int s = 0; s < BASE_SSTAGES; ++s) {
             sm100::mbar_init(&bars->full_s[s], 128);
             sm100::mbar_init(&bars->empty_s[s], 1);
         }
-        sm100::mbar_init(&bars->acc_full, 1);
+        sm100::mbar_init(&bars->acc_full, 2);
         sm100::fence_mbar_init();
     }
     // Sign words of the first 16 K-blocks are requested first, then (after a CTA barrier, so the
@@ -173,9 +176,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         sm100::tma_load_2d(st, &tmap_w, &bars->full_w[s], kb * BK, n0);
         sm100::tma_load_2d(st + ROW_TILE_BYTES, &tmap_x, &bars->full_w[s], kb * BK, 0);
     };
+    const bool expander = warp >= 2 && warp < 6;  // warps 2..5: sign expansion and the epilogue
     const int t = threadIdx.x - 64;
     const int n = n0 + t;
-    const bool row_live = warp >= 2 && t < tile_n && n < N;
+    const bool row_live = expander && t < tile_n && n < N;
     uint32_t wv[32];
     auto load_words = [&](int kc) {
         const int w0 = 2 * kc;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int i = 0; i < 32; ++i) wv[i] = (row_live && w0 + i < 2 * kb_end && w0 + i < kw) ? __ldg(src + i) : 0u;
         }
     };
-    if (warp >= 2 && kb_end > kb_begin) load_words(kb_begin);
+    if (expander && kb_end > kb_begin) load_words(kb_begin);
     __syncthreads();  // barrier initialisation visible; the sign-word loads issued
     if (threadIdx.x == 0) {
         sm100::tma_prefetch_desc(&tmap_w);
@@ -221,30 +225,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (++s == stages) { s = 0; ph ^= 1u; }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == 6) {
+        // Warp 1: D1 = W_base . x^T; warp 6: D2 = S . x^T (waits for the expanded S tile too).
+        // Each releases the W_base / x stage (two arrivals) and warp 6 the S stage.
         if (lane == 0 && kb_end > kb_begin) {
+            const bool sign = warp == 6;
             const uint32_t idesc = sm100::idesc_f16(128, (uint32_t)nm, std::is_same<T, __nv_bfloat16>::value);
+            const uint32_t dst = tmem + (sign ? (uint32_t)nm : 0u);
             int s = 0, e = 0;
             uint32_t ph = 0, phe = 0;
             bool ok = true;
             for (int kb = kb_begin; kb < kb_end; ++kb) {
-                if (!sm100::mbar_wait(&bars->full_w[s], ph, status, 12) || !sm100::mbar_wait(&bars->full_s[e], phe, status, 13)) {
+                if (!sm100::mbar_wait(&bars->full_w[s], ph, status, 12) ||
+                    (sign && !sm100::mbar_wait(&bars->full_s[e], phe, status, 13))) {
                     ok = false;
                     break;
                 }
                 sm100::tc_fence_after();
                 const uint32_t sw = sm100::smem_u32(smem + s * stage_bytes);
                 const uint32_t sx = sw + ROW_TILE_BYTES;
-                const uint32_t ss = sm100::smem_u32(sring + e * ROW_TILE_BYTES);
+                const uint32_t sa = sign ? sm100::smem_u32(sring + e * ROW_TILE_BYTES) : sw;
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k) {
-                    const uint64_t bx = sm100::smem_desc_k_sw128(sx + k * 32);
-                    const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
-                    sm100::mma_f16(tmem, sm100::smem_desc_k_sw128(sw + k * 32), bx, idesc, acc);
-                    sm100::mma_f16(tmem + (uint32_t)nm, sm100::smem_desc_k_sw128(ss + k * 32), bx, idesc, acc);
-                }
+                for (int k = 0; k < BK / 16; ++k)
+                    sm100::mma_f16(dst, sm100::smem_desc_k_sw128(sa + k * 32), sm100::smem_desc_k_sw128(sx + k * 32), idesc,
+                                   (kb > kb_begin || k > 0) ? 1u : 0u);
                 sm100::mma_commit(&bars->empty_w[s]);
-                sm100::mma_commit(&bars->empty_s[e]);
+                if (sign) sm100::mma_commit(&bars->empty_s[e]);
                 if (++s == stages) { s = 0; ph ^= 1u; }
                 if (++e == BASE_SSTAGES) { e = 0; phe ^= 1u; }
             }
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---- epilogue: partial p[row][m] = D1 + alpha[n] * D2 into shared memory (the pipeline
     // buffers are free once acc_full has fired: every MMA reading them has completed).
     float* red = reinterpret_cast<float*>(smem);
-    if (warp >= 2) {
+    if (expander) {
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const int n = n0 + row;
@@ -312,7 +318,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     sm100::cluster_sync();  // every CTA's partial is in its shared memory
     // Reduce-scatter over the cluster: CTA `rank` sums the columns [c0, c1) of all partials
     // (16-byte loads through distributed shared memory) and writes those rows of y.
-    if (warp >= 2) {
+    if (expander) {
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const int n = n0 + row;
@@ -632,7 +638,7 @@ int launch_base_tc(const void* x, const void* wb, const void* sw, const void* al
             cudaFuncSetAttribute(bitdelta_base_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, BASE_SMEM_LIMIT);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)tiles, (unsigned)sk, 1);
-        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.blockDim = dim3(BASE_THREADS, 1, 1);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
