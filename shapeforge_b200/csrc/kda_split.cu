@@ -20,9 +20,10 @@
 //       EL  e^{b_31} fp32 [128]                                             512 B
 //  3. kda_chain_kernel: one CTA per (sequence, head) chain, the fp32 state [Dv, Dk] in TMEM.  A
 //     producer warp streams the chain's slots (one bulk copy each) and V (cp.async, zero-filled past
-//     the chain's end) through a 3-stage ring.  An MMA warp issues, per chunk,
+//     the chain's end) through a 3-stage ring.  Two MMA warps issue, per chunk, the two K halves of
 //     ACC += S [-K2 ; Q2]^T into the chunk's accumulator (already holding V^T [T ; MT]^T, so it ends
-//     as w^T | o^T), then the next chunk's V^T [T ; MT]^T into the other accumulator buffer while
+//     as w^T | o^T) and a second accumulator; the first then issues the next chunk's
+//     V^T [T ; MT]^T into the other accumulator buffer while
 //     eight state warps write W^T as 16-bit high | low parts and decay S, then S += W^T Kend; the
 //     state warps store o after handing W^T over.
 //
@@ -674,7 +675,7 @@ __global__ void __launch_bounds__(P_NT, 3)
 // ---------------------------------------------------------------------------------------------
 // 3. chain: one (sequence, head) per CTA
 // ---------------------------------------------------------------------------------------------
-constexpr int K_NT = 320;  // warps 0-7 state, warp 8 producer, warp 9 MMA issue
+constexpr int K_NT = 352;  // warps 0-7 state, warp 8 producer, warps 9 and 10 MMA issue
 constexpr int NSTAGE = 3;
 constexpr int STAGE_V = 50176;  // V of the chunk, 16-bit MN-major 2 x (32 x 128 B), after the slot image
 constexpr int STAGE_BYTES = STAGE_V + 8192;
@@ -690,7 +691,7 @@ static_assert(SLOT_BYTES <= STAGE_V, "slot image fits before V");
 struct __align__(8) ChainBars {
     uint64_t full[NSTAGE];   // slot (transaction bytes) and V (32 cp.async arrivals) of a chunk landed
     uint64_t empty[NSTAGE];  // the chunk's state update done (commit): the stage may be refilled
-    uint64_t m1;             // w | o accumulator ready (commit)
+    uint64_t m1;             // w | o accumulator ready (a commit from each MMA-issuing warp)
     uint64_t wready;         // W^T written and S decayed (one arrival per state warp)
     uint64_t oread[2];       // o read out of accumulator buffer b (one arrival per o warp); one
                              // barrier per buffer, so a wait can never alias a later chunk's phase
@@ -698,8 +699,9 @@ struct __align__(8) ChainBars {
     uint32_t tmem_base;
 };
 // TMEM: the state, then the w | o accumulator in two buffers (chunk parity), so the o warps can read
-// a chunk's o after the hand-off while the next chunk's MMAs fill the other buffer.
-constexpr uint32_t TM_S = 0, TM_ACC = 128, K_TMEM_COLS = 256;
+// a chunk's o after the hand-off while the next chunk's MMAs fill the other buffer; the S-product's
+// second K half goes to a second accumulator pair (its own issuing warp), summed in the epilogue.
+constexpr uint32_t TM_S = 0, TM_ACC = 128, TM_ACC2 = 256, K_TMEM_COLS = 512;
 
 // r[j] *= e[j] for 32 state columns (e: 16-byte aligned shared memory).
 __device__ __forceinline__ void decay32(uint32_t (&r)[32], const float* e) {
@@ -741,7 +743,7 @@ __global__ void __launch_bounds__(K_NT, 1)
             sm100::mbar_init(&bars->full[i], 33);
             sm100::mbar_init(&bars->empty[i], 1);
         }
-        sm100::mbar_init(&bars->m1, 1);
+        sm100::mbar_init(&bars->m1, 2);
         sm100::mbar_init(&bars->wready, 8);
         sm100::mbar_init(&bars->oread[0], 4);
         sm100::mbar_init(&bars->oread[1], 4);
@@ -785,10 +787,12 @@ __global__ void __launch_bounds__(K_NT, 1)
             if (!sm100::mbar_wait(&bars->full[ci % NSTAGE], (ci / NSTAGE) & 1, status, 104)) ok = false;
     } else if (warp == 9) {
         // ======================= MMA issue (lane 0) =======================
-        // Per chunk: S [-K2 ; Q2]^T into the chunk's accumulator (which already holds
-        // V^T [T ; MT]^T), then -- while the state warps run the chunk's epilogue -- the next
-        // chunk's V^T [T ; MT]^T into the other accumulator buffer, then S += W^T Kend once the
-        // epilogue hands W^T over.  The tensor pipe executes one thread's MMAs in issue order.
+        // Per chunk: the first K half of S [-K2 ; Q2]^T into the chunk's accumulator (which already
+        // holds V^T [T ; MT]^T; warp 10 issues the second half into the second accumulator at the
+        // same time), then -- while the state warps run the chunk's epilogue -- the next chunk's
+        // V^T [T ; MT]^T into the other accumulator buffer, then S += W^T Kend once the epilogue
+        // hands W^T over.  The tensor pipe executes one thread's MMAs in issue order; MMA issue is
+        // per issuing thread, so the two halves take half the time of one thread's 16 MMAs.
         if (lane == 0 && nch > 0) {
             constexpr uint32_t idv = sm100::idesc_f16_major(128, 64, BF16, true, false);
             constexpr uint32_t idt = sm100::idesc_tf32(128, 64) | (1u << 16);  // B MN-major
@@ -818,7 +822,7 @@ __global__ void __launch_bounds__(K_NT, 1)
                     const uint32_t acc_t = tmem + TM_ACC + (uint32_t)(64 * (ci & 1));
                     const uint64_t b1d = sm100::smem_desc_mn_b32(sm100::smem_u32(stg + SL_B1), 16384, 512);
 #pragma unroll
-                    for (int kk = 0; kk < D / 8; ++kk)
+                    for (int kk = 0; kk < D / 16; ++kk)
                         sm100::mma_tf32_ta(acc_t, tmem + TM_S + (uint32_t)(kk * 8), b1d + (uint64_t)((kk * 1024) >> 4), idt, 1u);
                 }
                 sm100::mma_commit(&bars->m1);
@@ -847,6 +851,33 @@ __global__ void __launch_bounds__(K_NT, 1)
             }
         }
         __syncwarp();
+    } else if (warp == 10) {
+        // ======================= second MMA issuer (lane 0) =======================
+        // The second K half of the chunk's S-product into its second accumulator (initialised by
+        // the first MMA).  Another thread's MMAs are not ordered with this one's, so it waits for
+        // the state it reads: the initial state, then each chunk's update completed (empty), and
+        // for the buffer's previous o having been read out.
+        if (lane == 0 && nch > 0) {
+            constexpr uint32_t idt = sm100::idesc_tf32(128, 64) | (1u << 16);  // B MN-major
+            if (!sm100::mbar_wait_spin(&bars->sinit, 0, status, 109)) ok = false;
+            for (int ci = 0; ci < nch; ++ci) {
+                const int st = ci % NSTAGE;
+                if (ci > 0 && !sm100::mbar_wait_spin(&bars->empty[(ci - 1) % NSTAGE], ((ci - 1) / NSTAGE) & 1, status, 110)) ok = false;
+                if (!sm100::mbar_wait_spin(&bars->full[st], (ci / NSTAGE) & 1, status, 111)) ok = false;
+                if (ci >= 2 && !sm100::mbar_wait_spin(&bars->oread[ci & 1], ((ci - 2) >> 1) & 1, status, 112)) ok = false;
+                sm100::tc_fence_after();
+                if (ok) {
+                    const uint32_t acc2 = tmem + TM_ACC2 + (uint32_t)(64 * (ci & 1));
+                    const uint64_t b1d = sm100::smem_desc_mn_b32(sm100::smem_u32(smem + st * STAGE_BYTES + SL_B1), 16384, 512);
+#pragma unroll
+                    for (int kk = D / 16; kk < D / 8; ++kk)
+                        sm100::mma_tf32_ta(acc2, tmem + TM_S + (uint32_t)(kk * 8), b1d + (uint64_t)((kk * 1024) >> 4), idt,
+                                           kk > D / 16 ? 1u : 0u);
+                }
+                sm100::mma_commit(&bars->m1);
+            }
+        }
+        __syncwarp();
     } else {
         // ======================= state: value row v, S columns [64 * role, 64 * role + 64) =======================
         const int qd = warp & 3, role = warp >> 2;  // role 0: w, role 1: o
@@ -870,6 +901,7 @@ __global__ void __launch_bounds__(K_NT, 1)
             const int t0 = begin + ci * C, nt = min(C, end - t0);
             uint8_t* stg = smem + st * STAGE_BYTES;
             const uint32_t acc_t = tmem + TM_ACC + (uint32_t)(64 * (ci & 1));
+            const uint32_t acc2_t = tmem + TM_ACC2 + (uint32_t)(64 * (ci & 1));
             // Thread 0 waits for the chunk's slot (its e^{b_31}) and accumulator; the other seven
             // warps sleep at the barrier instead of polling.
             if (tid == 0) {
@@ -884,11 +916,14 @@ __global__ void __launch_bounds__(K_NT, 1)
             // the hand-off, off the critical path.
             const float* el = reinterpret_cast<const float*>(stg + SL_EL) + 64 * role;
             const uint32_t scol = tmem + lane_q + TM_S + (uint32_t)(64 * role);
-            uint32_t wv[16], r0[32], r1[32];
+            uint32_t wv[16], wv2[16], r0[32], r1[32];
             sm100::tmem_ld_32x32b_x16(acc_t + lane_q + (uint32_t)(16 * role), wv);
+            sm100::tmem_ld_32x32b_x16(acc2_t + lane_q + (uint32_t)(16 * role), wv2);
             sm100::tmem_ld_32x32b_x32(scol, r0);
             sm100::tmem_ld_32x32b_x32(scol + 32u, r1);
             sm100::tmem_ld_wait();
+#pragma unroll
+            for (int u = 0; u < 16; ++u) wv[u] = __float_as_uint(__uint_as_float(wv[u]) + __uint_as_float(wv2[u]));
             {
                 uint32_t hi[8], lo[8];
 #pragma unroll
@@ -915,9 +950,12 @@ __global__ void __launch_bounds__(K_NT, 1)
                 // o^T row v (this chunk's accumulator buffer, which the next chunk's MMAs do not
                 // touch) -> o [t][v] in shared memory, then whole 256-byte token rows to global
                 // with 16-byte stores (rows past the chain's end are not stored).
-                uint32_t a[32];
+                uint32_t a[32], a2[32];
                 sm100::tmem_ld_32x32b_x32(acc_t + lane_q + (uint32_t)C, a);
+                sm100::tmem_ld_32x32b_x32(acc2_t + lane_q + (uint32_t)C, a2);
                 sm100::tmem_ld_wait();
+#pragma unroll
+                for (int t = 0; t < C; ++t) a[t] = __float_as_uint(__uint_as_float(a[t]) + __uint_as_float(a2[t]));
                 sm100::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) sm100::mbar_arrive(&bars->oread[ci & 1]);  // the buffer may take chunk ci + 2
