@@ -240,6 +240,135 @@ __device__ __forceinline__ void softmax_tile(uint32_t tmem, uint32_t tmem_o, uin
     l += t.x + t.y;
 }
 
+// softmax_tile with keys [64, 128) kept in registers between the two passes and that half of P
+// published first (one TMEM reload of keys [0, 64) instead of two of all keys); it needs ~64 more
+// registers, which the two-CTA kernel's bf16 instantiations do not have without spilling.
+// One score tile of one query row (the calling thread's TMEM lane): row max, lazy rescale of O,
+// exponentials, P_j (high + residual) over the score columns, published a half at a time on
+// p_full[0] / p_full[1].  MASK: keys past `lim` (tile-relative) score -inf.  `o_ready` (when not
+// null) completes a phase per P.V: a warp that must rescale O first waits for P_{j-1}.V_{j-1}
+// (the kernel that double-buffers S issues S_{j+1} before P_j.V_j, so S_j does not imply it).
+template <typename T, int D, bool MASK>
+__device__ __forceinline__ void softmax_tile_kh(uint32_t tmem, uint32_t tmem_o, uint32_t lane_off, int lim, int j, float scale_log2,
+                                             float& m, float& l, uint64_t* p_full, uint64_t* o_ready = nullptr,
+                                             sm100::KernelStatus* status = nullptr) {
+    constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+    // Pass 1: row max of the raw scores (scale > 0 commutes with max); NaN propagates.  Keys
+    // [64, 128) stay in registers (rb) for pass 2, which writes that half of P first; keys [0, 64)
+    // are read again.
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    uint32_t rb[64];
+    {
+        uint32_t r[64];
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 32u, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 64u, *reinterpret_cast<uint32_t(*)[32]>(&rb[0]));
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 96u, *reinterpret_cast<uint32_t(*)[32]>(&rb[32]));
+        sm100::tmem_ld_wait();
+        if (MASK) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                if (c > lim) r[c] = 0xff800000u;  // -inf
+                if (64 + c > lim) rb[c] = 0xff800000u;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+            const float a = fmax3_nan(__uint_as_float(r[c]), __uint_as_float(r[c + 1]), __uint_as_float(r[c + 2]));
+            const float b = fmax3_nan(__uint_as_float(r[c + 3]), __uint_as_float(r[c + 4]), __uint_as_float(r[c + 5]));
+            const int k = (c >> 3) & 3;
+            mx[k] = fmax3_nan(mx[k], a, fmax3_nan(b, __uint_as_float(r[c + 6]), __uint_as_float(r[c + 7])));
+        }
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+            const float a = fmax3_nan(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1]), __uint_as_float(rb[c + 2]));
+            const float b = fmax3_nan(__uint_as_float(rb[c + 3]), __uint_as_float(rb[c + 4]), __uint_as_float(rb[c + 5]));
+            const int k = (c >> 3) & 3;
+            mx[k] = fmax3_nan(mx[k], a, fmax3_nan(b, __uint_as_float(rb[c + 6]), __uint_as_float(rb[c + 7])));
+        }
+    }
+    const float rmax = fmax3_nan(mx[0], mx[1], fmax_nan(mx[2], mx[3]));
+    const float m_new = fmax_nan(m, rmax * scale_log2);
+    const bool need = !(m_new <= m + 8.0f);
+    const float m_old = m;
+    if (need) m = m_new;
+    // P.V_{j-1} has completed: the commit that published S_j was issued after it (or, with
+    // o_ready, once that barrier's phase j - 1 is complete).
+    if (j > 0) {
+        const float alpha = need ? ex2_approx(m_old - m_new) : 1.0f;
+        if (__any_sync(0xffffffffu, need)) {
+            if (o_ready) {
+                sm100::mbar_wait(o_ready, (uint32_t)(j - 1) & 1u, status, 40);
+                sm100::tc_fence_after();
+            }
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+                sm100::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                sm100::tmem_st_32x32b_x32(tmem_o + lane_off + (uint32_t)(c * 32), r);
+            }
+        }
+        if (need) l *= alpha;
+    }
+    // Pass 2: p = 2^(s * scale * log2(e) - m), one FFMA2 per two scores and one MUFU.EX2 per score;
+    // P over the score columns just read, a quarter of the keys at a time; each half of the keys is
+    // published as soon as it is in TMEM (keys [64, 128) first, from registers).
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
+    const float2 nm2 = make_float2(-m, -m);
+    const float2 neg1 = make_float2(-1.f, -1.f);
+    float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    auto half_p = [&](const uint32_t (&r)[64], int h) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            uint32_t hv[16], lv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float2 x = ffma2(make_float2(__uint_as_float(r[32 * e + 2 * i]), __uint_as_float(r[32 * e + 2 * i + 1])), sc2, nm2);
+                const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                acc[i & 3] = fadd2(acc[i & 3], pp);
+                if (BF16) {
+                    // bf16: the high part is the upper half of the fp32 bits (truncation, one byte
+                    // permute for two values) and the residual p - high is exact in fp32, so only the
+                    // residual is rounded: ~16 significant bits in total.
+                    const uint32_t b0 = __float_as_uint(pp.x), b1 = __float_as_uint(pp.y);
+                    hv[i] = __byte_perm(b0, b1, 0x7632);
+                    const float2 res = ffma2(make_float2(__uint_as_float(b0 & 0xFFFF0000u), __uint_as_float(b1 & 0xFFFF0000u)), neg1, pp);
+                    lv[i] = pack2<T>(res.x, res.y);
+                } else {
+                    hv[i] = pack2<T>(pp.x, pp.y);
+                    const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hv[i]));
+                    const float2 res = ffma2(hf, neg1, pp);
+                    lv[i] = pack2<T>(res.x, res.y);
+                }
+            }
+            const uint32_t col = (uint32_t)(64 * h + 32 * e);
+            sm100::tmem_st_32x32b_x16(tmem + lane_off + col, hv);
+            sm100::tmem_st_32x32b_x16(tmem + lane_off + col + 16u, lv);
+        }
+        sm100::tmem_st_wait();
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&p_full[h]);
+    };
+    half_p(rb, 1);
+    {
+        uint32_t r[64];
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        sm100::tmem_ld_32x32b_x32(tmem + lane_off + 32u, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        sm100::tmem_ld_wait();
+        if (MASK) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (c > lim) r[c] = 0xff800000u;
+        }
+        half_p(r, 0);
+    }
+    const float2 t = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+    l += t.x + t.y;
+}
+
 template <typename T, int D, bool CAUSAL>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -248,6 +377,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     constexpr int DB = L::DB;
     constexpr int NST = L::NST;
     constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+    constexpr bool KH = !BF16;  // keys [64, 128) kept in registers between the softmax passes
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars* bars = reinterpret_cast<Bars*>(smem + L::BARS);
@@ -339,8 +469,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                     break;
                 }
                 const uint32_t sv = sm100::smem_u32(smem + L::V + st * L::TILE);
+                // The half of P the softmax publishes first: keys [64, 128) with softmax_tile_kh
+                // (fp16), keys [0, 64) with softmax_tile (bf16, whose registers do not allow it).
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int half = KH ? 1 - hh : hh;
                     if (!sm100::mbar_wait(&bars->p_full[half], (uint32_t)j & 1u, status, 35)) {
                         ok = false;
                         break;
@@ -349,7 +482,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 #pragma unroll
                     for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
                         const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
-                        sm100::mma_f16_ta(tmem_o, tmem + p_hi_col(kk), bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                        sm100::mma_f16_ta(tmem_o, tmem + p_hi_col(kk), bd, idesc_o, (j > 0 || hh > 0 || kk > 4 * half) ? 1u : 0u);
                     }
 #pragma unroll
                     for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
@@ -380,10 +513,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             const int key0 = j * BN;
             const bool masked = (CAUSAL && j == qt) || key0 + BN > S;
             const int lim = masked ? min(CAUSAL && j == qt ? row : BN - 1, S - 1 - key0) : BN - 1;
-            if (masked)
-                softmax_tile<T, D, true>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
-            else
-                softmax_tile<T, D, false>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
+            if (KH) {
+                if (masked)
+                    softmax_tile_kh<T, D, true>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
+                else
+                    softmax_tile_kh<T, D, false>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
+            } else {
+                if (masked)
+                    softmax_tile<T, D, true>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
+                else
+                    softmax_tile<T, D, false>(tmem, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[0]);
+            }
         }
         // ---------------- epilogue: O / l ----------------
         if (ok && nkv > 0 && sm100::mbar_wait(&bars->o_done, 0, status, 39)) {
@@ -553,8 +693,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const uint32_t sv = sm100::smem_u32(smem + L::V + st * L::TILE);
                 const uint32_t pb = tmem + 128u * (uint32_t)(j & 1);
+                // Keys [64, 128) first: the softmax publishes that half of P first.
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int half = 1 - hh;
                     if (!sm100::mbar_wait(&bars->p_full[j & 1][half], (uint32_t)(j >> 1) & 1u, status, 45)) {
                         ok = false;
                         break;
@@ -563,7 +705,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
                         const uint64_t bd = sm100::smem_desc_mn_sw128(sv + (uint32_t)(kk * 16 * 128), BOX_BYTES, 1024);
-                        sm100::mma_f16_ta(tmem_o, pb + p_hi_col(kk), bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                        sm100::mma_f16_ta(tmem_o, pb + p_hi_col(kk), bd, idesc_o, (j > 0 || hh > 0 || kk > 4) ? 1u : 0u);
                     }
 #pragma unroll
                     for (int kk = 4 * half; kk < 4 * half + 4; ++kk) {
@@ -595,9 +737,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int lim = masked ? min(CAUSAL && j == qt ? row : BN - 1, S - 1 - key0) : BN - 1;
             const uint32_t sb = tmem + 128u * (uint32_t)(j & 1);
             if (masked)
-                softmax_tile<T, D, true>(sb, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[j & 1][0], &bars->o_ready, status);
+                softmax_tile_kh<T, D, true>(sb, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[j & 1][0], &bars->o_ready, status);
             else
-                softmax_tile<T, D, false>(sb, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[j & 1][0], &bars->o_ready, status);
+                softmax_tile_kh<T, D, false>(sb, tmem_o, lane_off, lim, j, scale_log2, m, l, &bars->p_full[j & 1][0], &bars->o_ready, status);
         }
         if (ok && nkv > 0 && sm100::mbar_wait(&bars->o_done, 0, status, 49)) {
             sm100::tc_fence_after();
