@@ -78,3 +78,26 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_native, "_lib", None)
     with pytest.raises(_native.NativeUnavailable):
         _native.load()
+
+
+def test_kda_workspace_sizes_without_a_device():
+    """The two-pass KDA workspace: a 1 KB-aligned header of nseq + 1 int32 chunk offsets, then one
+    49,664-byte slot per (32-token chunk, head) bound, floor((T + 31 N) / 32) * H slots; the task op
+    and the gated workload use the same layout; 0 when the shape does not qualify (D != 128)."""
+    lib = _native.load()
+    slot = 49664
+    for t, n, h in ((8192, 6, 64), (16552, 8, 16), (1, 1, 1), (0, 3, 2), (1000, 1025, 4)):
+        header = ((4 * (n + 1) + 1023) // 1024) * 1024
+        want = header + ((t + 31 * n) // 32) * h * slot
+        assert lib.sf_varlen_kda_workspace_bytes(t, n, h, 128) == want, (t, n, h)
+        assert lib.sf_varlen_kda_gated_workspace_bytes(t, n, h, 128) == want, (t, n, h)
+    for d in (64, 32, 256):
+        assert lib.sf_varlen_kda_workspace_bytes(8192, 6, 64, d) == 0
+    assert lib.sf_varlen_kda_workspace_bytes(8192, 0, 64, 128) == 0
+
+
+def test_kda_op_takes_a_workspace_argument():
+    """SF_OP_KDA carries the two-pass workspace as its 13th tensor argument (NULL: single pass)."""
+    lib = _native.load()
+    assert lib.sf_op_nargs(_native.OPS["varlen_kda"]) == 13
+    assert lib.sf_op_nargs(_native.OPS["varlen_kda_gated"]) == 10
