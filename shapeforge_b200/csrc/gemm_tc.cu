@@ -65,7 +65,7 @@ struct __align__(8) Barriers {
 
 // Grouped rasterisation: tiles are visited in column-major groups of GROUP_M tile rows so
 // concurrently running CTAs share A and B panels in L2.
-constexpr int GROUP_M = 8;
+constexpr int GROUP_M = 16;
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
     const int per_group = GROUP_M * tiles_n;
