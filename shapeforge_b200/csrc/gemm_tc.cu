@@ -347,6 +347,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
+            int issued = 0;
             for (int kb = 0; kb < num_kb; ++kb) {
                 const int stage = kb % S_STAGES;
                 // Reuse of a stage (K > 512) waits for the MMAs that read it; the first round passes.
@@ -355,7 +356,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 sm100::mbar_arrive_expect_tx(&bars->full[stage], S_STAGE_BYTES);
                 sm100::tma_load_2d(sa, &tmap_a, &bars->full[stage], kb * BK, tm * BM);
                 sm100::tma_load_2d(sa + A_BYTES, &tmap_b, &bars->full[stage], kb * BK, tn * SBN);
+                issued = kb + 1;
             }
+            // Drain: the last ring of loads has landed (bounded), so no TMA write into shared memory
+            // is in flight at teardown even if a wait elsewhere gave up.
+            for (int kb = max(0, issued - S_STAGES); kb < issued; ++kb)
+                if (!sm100::mbar_wait(&bars->full[kb % S_STAGES], (uint32_t)(kb / S_STAGES) & 1u, status, 14)) break;
         }
     } else if (warp == 1) {
         if (lane == 0) {
