@@ -80,15 +80,19 @@ int current_context_id(unsigned long long* id, char* err, uint64_t cap) {
         g_ctx_get_current = (CtxGetCurrentFn)p1;
         g_ctx_get_id = (CtxGetIdFn)p2;
     }
-    // cudaSetDevice on the current device makes its primary context current (and creates it if
-    // this thread has none yet).
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaSetDevice(dev);
-    if (e != cudaSuccess) return sf::fail(SF_EDEVICE, err, cap, "gemm_nn_noalloc: no CUDA context: %s", cudaGetErrorString(e));
+    // A context the caller made current (primary or its own) is used as it is.  Only a thread
+    // with none gets the current device's primary context, through cudaSetDevice, exactly as the
+    // runtime's kernel launches below would bind it.
     CUcontext ctx = nullptr;
-    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx)
-        return sf::fail(SF_EDEVICE, err, cap, "gemm_nn_noalloc: no current CUDA context");
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) return sf::fail(SF_EDEVICE, err, cap, "gemm_nn_noalloc: cuCtxGetCurrent failed");
+    if (!ctx) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaSetDevice(dev);
+        if (e != cudaSuccess) return sf::fail(SF_EDEVICE, err, cap, "gemm_nn_noalloc: no CUDA context: %s", cudaGetErrorString(e));
+        if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx)
+            return sf::fail(SF_EDEVICE, err, cap, "gemm_nn_noalloc: no current CUDA context");
+    }
     if (g_ctx_get_id(ctx, id) != CUDA_SUCCESS) return sf::fail(SF_EDEVICE, err, cap, "gemm_nn_noalloc: cuCtxGetId failed");
     return SF_OK;
 }
