@@ -22,6 +22,8 @@
 // their final_state rows are left untouched.
 #include "sf_common.cuh"
 
+#include <type_traits>
+
 namespace {
 
 constexpr int VR = 16;       // state rows per CTA
@@ -64,24 +66,59 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
     for (int c = 0; c < CPT; ++c) st[c] = (state0 && row_live) ? state0[sbase + (size_t)c * TPR] : 0.f;
 
     // Staging layout: thread = (token tt = tid / 8, lane-part p = tid % 8) covering D/8 columns.
+    // The raw inputs of the next 16-token group are loaded into registers in their storage
+    // types before the current group is consumed, so their global-memory latency overlaps the
+    // sequential per-token work; they are converted and transformed into shared memory only
+    // after that group's tokens are done.
+    using GT = typename std::conditional<TASK, T, float>::type;  // storage type of g and beta
     const int stt = tid / TPR;
     const int sp = tid % TPR;
     float decay_scale = 0.f;
     if (TASK) decay_scale = __expf(a_log[h]);
+    float dtb[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) dtb[c] = TASK ? dt_bias[h * D + sp + c * TPR] : 0.f;
+
+    const T zt = sf::Dt<T>::from_f(0.f);
+    GT zg;
+    if constexpr (TASK) zg = zt;
+    else zg = 0.f;
+    T rq[CPT], rk[CPT], rv[VR / TPR];
+    GT rg[CPT], rb = zg;
+    auto load_group = [&](int t0) {
+        const int t = t0 + stt;
+        const bool live = t < end;
+        const size_t base = ((size_t)(live ? t : begin) * H + h) * D + sp;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+            rq[c] = live ? q[base + (size_t)c * TPR] : zt;
+            rk[c] = live ? k[base + (size_t)c * TPR] : zt;
+            rg[c] = live ? reinterpret_cast<const GT*>(g_)[base + (size_t)c * TPR] : zg;
+        }
+        if (sp == 0) rb = live ? reinterpret_cast<const GT*>(beta_)[(size_t)t * H + h] : zg;
+#pragma unroll
+        for (int i = 0; i < VR / TPR; ++i) {
+            const int r = sp * (VR / TPR) + i;
+            rv[i] = (live && v0 + r < D) ? v[((size_t)t * H + h) * D + v0 + r] : zt;
+        }
+    };
+    auto to_f = [](auto x) -> float {
+        if constexpr (std::is_same<decltype(x), float>::value) return x;
+        else return sf::Dt<T>::to_f(x);
+    };
+    if (begin < end) load_group(begin);
 
     for (int t0 = begin; t0 < end; t0 += TS) {
         const int nt = min(TS, end - t0);
         __syncthreads();  // previous group fully consumed
         {
-            const int t = t0 + stt;
             const bool live = stt < nt;
             float qv[CPT], kv[CPT];
             float qq = 0.f, kk = 0.f;
-            const size_t base = ((size_t)t * H + h) * D + sp;
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
-                qv[c] = live ? sf::Dt<T>::to_f(q[base + (size_t)c * TPR]) : 0.f;
-                kv[c] = live ? sf::Dt<T>::to_f(k[base + (size_t)c * TPR]) : 0.f;
+                qv[c] = live ? sf::Dt<T>::to_f(rq[c]) : 0.f;
+                kv[c] = live ? sf::Dt<T>::to_f(rk[c]) : 0.f;
                 qq = fmaf(qv[c], qv[c], qq);
                 kk = fmaf(kv[c], kv[c], kk);
             }
@@ -103,36 +140,29 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
                 float e = 1.f;
                 if (live) {
                     if (TASK) {
-                        const float gv = sf::Dt<T>::to_f(reinterpret_cast<const T*>(g_)[base + (size_t)c * TPR]);
-                        const float z = decay_scale * (gv + dt_bias[h * D + col]);
+                        const float z = decay_scale * (to_f(rg[c]) + dtb[c]);
                         const float ld = lower_bound / (1.f + __expf(-z));
                         e = __expf(ld);
                     } else {
-                        e = __expf(reinterpret_cast<const float*>(g_)[base + (size_t)c * TPR]);
+                        e = __expf(to_f(rg[c]));
                     }
                 }
                 es[stt][col] = e;
             }
             if (sp == 0) {
                 float b = 0.f;
-                if (live) {
-                    if (TASK) {
-                        const float bv = sf::Dt<T>::to_f(reinterpret_cast<const T*>(beta_)[(size_t)t * H + h]);
-                        b = 1.f / (1.f + __expf(-bv));
-                    } else {
-                        b = reinterpret_cast<const float*>(beta_)[(size_t)t * H + h];
-                    }
-                }
+                if (live) b = TASK ? 1.f / (1.f + __expf(-to_f(rb))) : to_f(rb);
                 bs[stt] = b;
             }
             // v slice: VR rows of token stt, threads sp 0..7 cover VR columns (2 each).
 #pragma unroll
             for (int i = 0; i < VR / TPR; ++i) {
                 const int r = sp * (VR / TPR) + i;
-                vs[stt][r] = (live && v0 + r < D) ? sf::Dt<T>::to_f(v[((size_t)t * H + h) * D + v0 + r]) : 0.f;
+                vs[stt][r] = (live && v0 + r < D) ? sf::Dt<T>::to_f(rv[i]) : 0.f;
             }
         }
         __syncthreads();
+        if (t0 + TS < end) load_group(t0 + TS);
         for (int tt = 0; tt < nt; ++tt) {
             float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
