@@ -735,7 +735,9 @@ def _kda_fixed_task_workload(n: int = 256, h: int = 8, d: int = 64, dtype: str =
                      "input stream", "shape": [n, h, d]},
         "kda_fwd_kernel", "kda", make_inputs, ["q", "k", "v", "g", "beta", "A_log", "dt_bias", "initial_state", "scale"],
         [((n, h, d), td), ((h, d, d), torch.float32), ((3, 2), torch.int32), ((1,), torch.int32), ((2, h, d, d), torch.float32)],
-        (n, h, d), (-5.0,), cpu_rows=cpu_rows, total_rows=h)
+        (n, h, d), (-5.0,), cpu_rows=cpu_rows, total_rows=h, launches_per_step=2,
+        roofline_note="step of 2 launches (kda_fixed_items_kernel writes the one-piece work list, kda_fwd_kernel runs the "
+                      "recurrence): achieved = algorithmic bytes / step time")
 
 
 def _bitdelta_task_workload(m: int = 512, n: int = 4096, k: int = 4096, dtype: str = "fp16", scale: float = 0.02) -> Workload:

@@ -163,6 +163,7 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
         }
         __syncthreads();
         if (t0 + TS < end) load_group(t0 + TS);
+#pragma unroll 4
         for (int tt = 0; tt < nt; ++tt) {
             float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
