@@ -14,9 +14,11 @@
 // Parallel structure: the recurrence never mixes state rows (each row v evolves from k, q, ld, b
 // and v_t[v] alone), so a (sequence, head) chain is split over CTAs of 16 state rows each.  A
 // CTA has 128 threads: 8 per row, each holding D/8 key columns of the row in registers (thread
-// part p owns columns p, p+8, ..., so staged rows are read without bank conflicts); per token
-// the row dot products S.k and S.q are 3-shuffle reductions over those 8 threads.  Tokens are
-// staged 16 at a time in shared memory (normalised q/k, exp(ld), b, this CTA's v slice) by all
+// part p owns columns p, p+8, ..., so staged rows are read without bank conflicts).  Per token
+// both row dot products of the decayed state S' (S'.k and S'.q) come from one pass and share
+// their 3-shuffle reductions over those 8 threads; the output is S_new.q = S'.q + r (k.q), so the
+// token-to-token chain carries one reduction.  Tokens are staged 16 at a time in shared memory
+// (normalised q/k, their dot product k.q, exp(ld), b, this CTA's v slice) by all
 // threads, then consumed sequentially; outputs are staged and written 16 tokens at a time.
 // Sentinel offsets (cu < 0, the L2 capacity padding) end the sequence list: such sequences and
 // their final_state rows are left untouched.
@@ -43,6 +45,7 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
     __shared__ float qs[TS][D];
     __shared__ float es[TS][D];
     __shared__ float bs[TS];
+    __shared__ float kqs[TS];  // k.q of each staged token (normalised and scaled as staged)
     __shared__ float vs[TS][VR];
     __shared__ float os[TS][VR];
 
@@ -114,14 +117,17 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
         {
             const bool live = stt < nt;
             float qv[CPT], kv[CPT];
-            float qq = 0.f, kk = 0.f;
+            float qq = 0.f, kk = 0.f, kq = 0.f;
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
                 qv[c] = live ? sf::Dt<T>::to_f(rq[c]) : 0.f;
                 kv[c] = live ? sf::Dt<T>::to_f(rk[c]) : 0.f;
                 qq = fmaf(qv[c], qv[c], qq);
                 kk = fmaf(kv[c], kv[c], kk);
+                kq = fmaf(kv[c], qv[c], kq);
             }
+#pragma unroll
+            for (int o = 1; o < TPR; o <<= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
             float qn = scale, kn = 1.f;
             if (TASK) {
 #pragma unroll
@@ -153,6 +159,7 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
                 float b = 0.f;
                 if (live) b = TASK ? 1.f / (1.f + __expf(-to_f(rb))) : to_f(rb);
                 bs[stt] = b;
+                kqs[stt] = kq * kn * qn;
             }
             // v slice: VR rows of token stt, threads sp 0..7 cover VR columns (2 each).
 #pragma unroll
@@ -165,34 +172,31 @@ __global__ void __launch_bounds__(NT) kda_fwd_kernel(const T* __restrict__ q, co
         if (t0 + TS < end) load_group(t0 + TS);
 #pragma unroll 4
         for (int tt = 0; tt < nt; ++tt) {
-            float acc0 = 0.f, acc1 = 0.f;
+            // One pass over the decayed state S' gives both S'.k and S'.q; the output is then
+            // S_new.q = S'.q + r (k.q) with k.q staged per token, so the only dependent reduction
+            // on the token-to-token chain is S'.k (the two reductions share their shuffle levels).
+            float acc0 = 0.f, acc1 = 0.f, oq0 = 0.f, oq1 = 0.f;
 #pragma unroll
             for (int c = 0; c < CPT; c += 2) {
                 st[c] *= es[tt][part + c * TPR];
                 acc0 = fmaf(st[c], ks[tt][part + c * TPR], acc0);
+                oq0 = fmaf(st[c], qs[tt][part + c * TPR], oq0);
                 if (c + 1 < CPT) {
                     st[c + 1] *= es[tt][part + (c + 1) * TPR];
                     acc1 = fmaf(st[c + 1], ks[tt][part + (c + 1) * TPR], acc1);
+                    oq1 = fmaf(st[c + 1], qs[tt][part + (c + 1) * TPR], oq1);
                 }
             }
-            float acc = acc0 + acc1;
+            float acc = acc0 + acc1, oq = oq0 + oq1;
 #pragma unroll
-            for (int o = 1; o < TPR; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            for (int o = 1; o < TPR; o <<= 1) {
+                acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                oq += __shfl_xor_sync(0xffffffffu, oq, o);
+            }
             const float r = (vs[tt][row] - acc) * bs[tt];
-            float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-            for (int c = 0; c < CPT; c += 2) {
-                st[c] = fmaf(r, ks[tt][part + c * TPR], st[c]);
-                o0 = fmaf(st[c], qs[tt][part + c * TPR], o0);
-                if (c + 1 < CPT) {
-                    st[c + 1] = fmaf(r, ks[tt][part + (c + 1) * TPR], st[c + 1]);
-                    o1 = fmaf(st[c + 1], qs[tt][part + (c + 1) * TPR], o1);
-                }
-            }
-            float o = o0 + o1;
-#pragma unroll
-            for (int w = 1; w < TPR; w <<= 1) o += __shfl_xor_sync(0xffffffffu, o, w);
-            if (part == 0) os[tt][row] = o;
+            for (int c = 0; c < CPT; ++c) st[c] = fmaf(r, ks[tt][part + c * TPR], st[c]);
+            if (part == 0) os[tt][row] = fmaf(r, kqs[tt], oq);
         }
         __syncthreads();
         // Write the group's outputs: token-major, VR contiguous values per token.
