@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import importlib
 import os
+import time
 import traceback
 from typing import Any, Mapping, Sequence
 
@@ -87,7 +88,8 @@ def measure_on_gpus(parent: Any, opspec: Mapping[str, Any], points: Sequence[Any
     in domain order (one per benchmark point).
 
     ``devices`` are the workers' ``CUDA_VISIBLE_DEVICES`` values (default: every GPU this process
-    sees, ``device_masks()``); at most one worker per benchmark point is started."""
+    sees, ``device_masks()``); at most one worker per benchmark point is started.  ``timeout_s``
+    bounds the whole fan-out: a worker that has not answered by then is killed and reported."""
     import multiprocessing as mp
 
     bench = [p for p in points if p.usage == "benchmark"]
@@ -112,9 +114,10 @@ def measure_on_gpus(parent: Any, opspec: Mapping[str, Any], points: Sequence[Any
         procs.append((mask, proc, recv))
     results: dict[str, Any] = {}
     errors = []
+    deadline = time.monotonic() + timeout_s  # one limit for the whole fan-out, not per worker
     for mask, proc, recv in procs:
         try:
-            if not recv.poll(timeout_s):
+            if not recv.poll(max(0.0, deadline - time.monotonic())):
                 errors.append(f"GPU {mask}: no answer within {timeout_s:.0f} s")
                 proc.kill()
                 continue

@@ -80,3 +80,24 @@ def test_device_masks_follow_the_visible_devices(monkeypatch):
     assert fanout.device_masks(2) == ["2", "5"]
     monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
     assert fanout.device_masks(3) == ["0", "1", "2"]
+
+
+def stalled_measure(parent, opspec, points, *, make_inputs, baseline, verify, reps):
+    import time
+
+    time.sleep(120)  # a worker that never answers; the parent kills it at the deadline
+    return []
+
+
+def test_silent_workers_share_one_deadline(tmp_path):
+    import time
+
+    points = pp.domain(GEMV_OPSPEC, "fp16")
+    parent = pp.pack(make_tree(tmp_path, {"wide": (WIDE_GUARD, GEMV_VEC)}), points)
+    t0 = time.monotonic()
+    with pytest.raises(fanout.FanoutError) as exc:
+        fanout.measure_on_gpus(parent, GEMV_OPSPEC, points, recipe="tests.test_fanout:stand_in_recipe", devices=["0", "1"],
+                               measure="tests.test_fanout:stalled_measure", timeout_s=4)
+    elapsed = time.monotonic() - t0
+    assert str(exc.value).count("no answer within 4 s") == 2
+    assert elapsed < 7.5  # one 4 s limit for both workers, not 4 s each
