@@ -8,6 +8,8 @@ missing native library raises.
 
 from __future__ import annotations
 
+import functools
+
 import torch
 
 from . import _native
@@ -37,6 +39,29 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _tensor_device(fn):
+    """Run an operator on the GPU its tensors live on.
+
+    The C ABI launches on the calling thread's current CUDA device and caches per-device state
+    (SM count, kernel attributes) under it, while the stream comes from the tensors' device; so the
+    call is made with that device current.  Tensors on two different GPUs are refused (a kernel
+    would read the other GPU's memory); CPU tensors are left to each operator's own check, which
+    refuses them."""
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        devices = {a.device for a in (*args, *kwargs.values()) if isinstance(a, torch.Tensor) and a.is_cuda}
+        if len(devices) > 1:
+            raise ValueError(f"{fn.__name__}: tensors on more than one device ({', '.join(sorted(map(str, devices)))})")
+        if not devices:
+            return fn(*args, **kwargs)
+        with torch.cuda.device(devices.pop()):
+            return fn(*args, **kwargs)
+
+    return wrapper
+
+
+@_tensor_device
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
     """``y = x * rsqrt(mean(x^2, -1) + eps) * w`` (tasks/rmsnorm/reference.py:110-115)."""
     _check(x, "x")
@@ -62,6 +87,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tens
     return out
 
 
+@_tensor_device
 def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``C = A @ B^T`` with A ``[M, K]`` and B ``[N, K]`` (fp32 accumulation, one rounding)."""
     _check(a, "A")
@@ -78,6 +104,7 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, v
     return out
 
 
+@_tensor_device
 def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
             variant: int = 0) -> torch.Tensor:
     """``C = A @ B`` with A ``[M, K]`` and B ``[K, N]`` (tasks/gemm/reference.py:110-114).
@@ -88,6 +115,7 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, w
     return _gemm_kn("gemm_nn", a, b, out, workspace, variant)
 
 
+@_tensor_device
 def gemm_silu(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
               variant: int = 0) -> torch.Tensor:
     """``C = silu(A @ B)``, silu(v) = v * sigmoid(v) on the fp32 product (tasks/gemm_silu/reference.py,
@@ -121,9 +149,12 @@ def gemm_nn_workspace_bytes(m: int, n: int, k: int, dtype: str) -> int:
 
 
 def kernel_status(device: torch.device | None = None) -> tuple[int, int]:
-    """Read and clear the tensor-core kernels' status word (synchronises the current stream)."""
-    stream = torch.cuda.current_stream(device).cuda_stream
-    return _native.kernel_status(stream)
+    """Read and clear the tensor-core kernels' status word of ``device`` (default: the current
+    device; synchronises that device's current stream)."""
+    if device is None:
+        return _native.kernel_status(torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.device(device):
+        return _native.kernel_status(torch.cuda.current_stream(device).cuda_stream)
 
 
 def _run(op: str, t: torch.Tensor, ptrs, dims=(), attrs=(), variant: int = 0, flags: int = 0) -> None:
@@ -131,6 +162,7 @@ def _run(op: str, t: torch.Tensor, ptrs, dims=(), attrs=(), variant: int = 0, fl
     _native.run_op(desc, ptrs, _stream(t))
 
 
+@_tensor_device
 def silu(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y = x * sigmoid(x)`` (tasks/silu/reference.py:105-108), any shape, element-wise."""
     _check(x, "x")
@@ -140,6 +172,7 @@ def silu(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> 
     return out
 
 
+@_tensor_device
 def swiglu(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y = gate * sigmoid(gate) * up`` (tasks/swiglu/reference.py:109-113)."""
     _check(gate, "gate")
@@ -162,21 +195,25 @@ def _unary(op: str, x: torch.Tensor, out: torch.Tensor | None, variant: int) -> 
     return out
 
 
+@_tensor_device
 def relu(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y = max(x, 0)``; values <= 0 map to +0 and NaN propagates (tasks/relu/reference.py, ``reference``)."""
     return _unary("relu", x, out, variant)
 
 
+@_tensor_device
 def sigmoid(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y = 1 / (1 + exp(-x))`` (tasks/sigmoid/reference.py, ``reference``)."""
     return _unary("sigmoid", x, out, variant)
 
 
+@_tensor_device
 def sigmoid_shift(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y = sigmoid(x) + 1`` (tasks/sigmoid_shift/reference.py, ``reference``)."""
     return _unary("sigmoid_shift", x, out, variant)
 
 
+@_tensor_device
 def lion(p: torch.Tensor, g: torch.Tensor, m: torch.Tensor, lr: float = 1e-3, wd: float = 0.1, beta1: float = 0.9,
          beta2: float = 0.99, p_out: torch.Tensor | None = None, m_out: torch.Tensor | None = None,
          variant: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
@@ -197,6 +234,7 @@ def lion(p: torch.Tensor, g: torch.Tensor, m: torch.Tensor, lr: float = 1e-3, wd
     return p_out, m_out
 
 
+@_tensor_device
 def gemv(a: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y[r] = sum_k A[r, k] * x[k]`` with A ``[M, K]`` row-major (tasks/gemv/reference.py, ``reference``)."""
     _check(a, "A")
@@ -210,6 +248,7 @@ def gemv(a: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None, vari
     return out
 
 
+@_tensor_device
 def softmax(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """Row softmax over the last axis (tasks/softmax/reference.py:104-106)."""
     _check(x, "x")
@@ -221,6 +260,7 @@ def softmax(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) 
     return out
 
 
+@_tensor_device
 def reduction_sum(x: torch.Tensor, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """Row sum over the last axis (tasks/reduction_sum/reference.py:104-106)."""
     _check(x, "x")
@@ -232,6 +272,7 @@ def reduction_sum(x: torch.Tensor, out: torch.Tensor | None = None, variant: int
     return out
 
 
+@_tensor_device
 def rope(x: torch.Tensor, base: float = 10000.0, out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """Rotate-half RoPE over ``[B, H, S, D]`` (tasks/rope/reference.py:105-115)."""
     _check(x, "x")
@@ -244,6 +285,7 @@ def rope(x: torch.Tensor, base: float = 10000.0, out: torch.Tensor | None = None
     return out
 
 
+@_tensor_device
 def bitdelta_gemm(x: torch.Tensor, bits: torch.Tensor, scale: float = 0.02, out: torch.Tensor | None = None,
                   variant: int = 0) -> torch.Tensor:
     """``y = scale * x @ W`` with W ``[K, N]`` of +-1 from ``bits [K/32, N]`` (int32/uint32 words;
@@ -262,6 +304,7 @@ def bitdelta_gemm(x: torch.Tensor, bits: torch.Tensor, scale: float = 0.02, out:
     return out
 
 
+@_tensor_device
 def bitdelta_gemm_base(x: torch.Tensor, w_base: torch.Tensor, s_words: torch.Tensor, alpha: torch.Tensor,
                        out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``y = x @ (W_base + diag(alpha) S)^T`` with S in {-1,+1} packed along K as ``s_words [N, K/32]``."""
@@ -280,6 +323,7 @@ def bitdelta_gemm_base(x: torch.Tensor, w_base: torch.Tensor, s_words: torch.Ten
     return out
 
 
+@_tensor_device
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool = False,
                     out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
     """``softmax(q k^T * scale [+ causal mask]) v`` over ``[B, H, S, D]``
@@ -297,6 +341,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     return out
 
 
+@_tensor_device
 def varlen_kda(q, k, v, g, beta, a_log, dt_bias, initial_state, cu_seqlens, scale, lower_bound: float = -5.0,
                output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0,
                workspace: torch.Tensor | None = None):
@@ -330,6 +375,7 @@ def varlen_kda_workspace_bytes(total_tokens: int, num_seqs: int, heads: int, dim
     return int(_native.load().sf_varlen_kda_workspace_bytes(total_tokens, num_seqs, heads, dim))
 
 
+@_tensor_device
 def kda(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound: float = -5.0,
         output: torch.Tensor | None = None, final_state: torch.Tensor | None = None,
         work_items: torch.Tensor | None = None, item_counts: torch.Tensor | None = None,
@@ -359,6 +405,7 @@ def kda(q, k, v, g, beta, a_log, dt_bias, initial_state, scale, lower_bound: flo
     return output, final_state
 
 
+@_tensor_device
 def varlen_kda_gated(q, k, v, g, beta, cu_seqlens, scale: float, initial_state: torch.Tensor | None = None,
                      output: torch.Tensor | None = None, final_state: torch.Tensor | None = None, variant: int = 0,
                      workspace: torch.Tensor | None = None):
@@ -397,6 +444,7 @@ def varlen_kda_gated_workspace_bytes(total_tokens: int, num_seqs: int, heads: in
     return int(_native.load().sf_varlen_kda_gated_workspace_bytes(total_tokens, num_seqs, heads, dim))
 
 
+@_tensor_device
 def mamba2_chunk_scan(x, dt, dA_cumsum, b_mat, c_mat, d_skip, states, out: torch.Tensor | None = None,
                       variant: int = 0) -> torch.Tensor:
     """Mamba-2 SSD chunk scan of one B/C group (tasks/mamba2_chunk_scan/reference.py:106-127).

@@ -101,3 +101,48 @@ def test_kda_op_takes_a_workspace_argument():
     lib = _native.load()
     assert lib.sf_op_nargs(_native.OPS["varlen_kda"]) == 13
     assert lib.sf_op_nargs(_native.OPS["varlen_kda_gated"]) == 10
+
+
+def _on(index: int):
+    """Stand-in for a CUDA tensor on GPU ``index`` on a machine without a GPU: only ``is_cuda`` and
+    ``device`` are read before an operator reaches the library."""
+    import torch
+
+    class FakeCuda(torch.Tensor):
+        @property
+        def is_cuda(self):
+            return True
+
+        @property
+        def device(self):
+            return self._fake_device
+
+    t = torch.Tensor._make_subclass(FakeCuda, torch.zeros(4))
+    t._fake_device = torch.device("cuda", index)
+    return t
+
+
+def test_operators_run_with_their_tensors_device_current(monkeypatch):
+    import contextlib
+
+    import torch
+
+    from shapeforge_b200 import ops
+
+    entered = []
+
+    @contextlib.contextmanager
+    def device(d):
+        entered.append(d)
+        yield
+
+    monkeypatch.setattr(torch.cuda, "device", device)
+    body = ops._tensor_device(lambda *a, **k: "ran")
+    assert body(_on(1), w=_on(1), eps=1e-6) == "ran" and entered == [torch.device("cuda", 1)]
+    assert body(torch.zeros(1), 3) == "ran" and len(entered) == 1  # CPU tensors: the operator's own check refuses them
+    # Tensors on two GPUs are refused before anything reaches the library.
+    for call in (lambda: ops.rmsnorm(_on(0), _on(1)), lambda: ops.gemm_nt(_on(0), _on(1)),
+                 lambda: ops.flash_attention(_on(1), _on(1), _on(0), 0.125)):
+        with pytest.raises(ValueError, match="more than one device"):
+            call()
+    assert len(entered) == 1
